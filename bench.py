@@ -1,0 +1,450 @@
+"""Paged-decode microbench of the B200 paged-KV path (one JSON line on stdout).
+
+Workload (the paged-KV kernel microbench at the Qwen2.5-1.5B attention shape):
+one decode step = append one token per sequence + paged GQA attention, one
+layer, bf16, 12 query / 2 KV heads, head_dim 128, block size 16, 256
+sequences per GPU with context lengths U[64, 2048] (seeded), a 40 000-block
+pool with every sequence's blocks drawn from a random permutation of it, and
+K/V/Q ~ N(0, 1).  After each step the allocator rolls every sequence back by
+the token it appended, so every timed step sees the configured length
+distribution whatever --steps is.
+
+Arms:
+  ours (default)     ``value``: device-timed steps through PagedKVCacheStore
+                     (host allocator step + one descriptor upload + the fused
+                     sm_100a decode kernel) with inputs resident in HBM;
+                     ``e2e``: the same steps with q/k/v copied from pinned host
+                     memory and the output copied back inside the timed region.
+  --impl reference   the reference's CPU path (the oracle's restatement of the
+                     resident-cache decode step) on the host cores, rank 0 only.
+
+Multi-GPU (torchrun): every rank owns its own 256 sequences and KV pool (weak
+scaling, no data-path collective); the timed region is bracketed by NCCL
+barriers and the elapsed time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "paged-decode tokens/s/GPU at Qwen2.5-1.5B shape; paged-attn HBM GB/s vs peak"
+HQ, HKV, D, BS, POOL_BLOCKS, SEQS = 12, 2, 128, 16, 40000, 256
+L2_BYTES = 126 * 2**20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "paged KV microbench: one decode step (append 1 token/seq + paged GQA attention), 1 layer, "
+                    f"{SEQS} seqs/GPU, ctx U[64,2048], {HQ}q/{HKV}kv heads, head_dim {D}, block {BS}, "
+                    f"{POOL_BLOCKS}-block pool, random-permutation block placement, seed 0",
+        "seqs_per_gpu": SEQS,
+        "global_batch": SEQS * n_gpus,
+        "l2": "inputs larger than L2: ~277 MB of K/V read per step vs 126 MB L2",
+        "parallelism": f"replicas{n_gpus}: disjoint sequences and KV pool per GPU, no data-path collective",
+    }
+
+
+def algorithmic_bytes(lens: np.ndarray) -> int:
+    """HBM bytes one fused decode launch must move (bf16): K/V read incl. the new token,
+    the append (read k/v, write the slot), q read + o write, block-table and length reads."""
+    b = len(lens)
+    kv = int(lens.sum()) * HKV * D * 2 * 2
+    append = b * HKV * D * 2 * 2 * 2
+    qo = b * HQ * D * 2 * 2
+    tables = int(((lens + BS - 1) // BS).sum()) * 4 + b * 4
+    return kv + append + qo + tables
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic() -> float | None:
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "paged_decode_microbench.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock, power and throttle reasons via NVML during the timed region."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.002) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self) -> None:
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        active = 0
+        for _, r in self.samples:
+            active |= r
+        reasons = [k for k, bit in self.REASONS.items() if active & bit and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+def build_workload(device: torch.device, seed: int):
+    """Store + 256 sequences whose blocks follow a random permutation of the pool."""
+    from randomrepo_b200 import PagedKVAllocator, PagedKVCacheStore
+    from randomrepo_b200._lib import lib, raise_for_status
+
+    gen = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(64, 2049, (SEQS,), generator=gen).numpy().astype(np.int64)
+    perm = torch.randperm(POOL_BLOCKS, generator=gen).numpy()
+    alloc = PagedKVAllocator(POOL_BLOCKS, BS)
+    store = PagedKVCacheStore(alloc, num_layers=1, num_kv_heads=HKV, head_dim=D, dtype=torch.bfloat16,
+                              device=device)
+    h = alloc._handle
+    # Placement through the public allocator: hold every block with a filler
+    # sequence, then free exactly the block wanted next and grow into it (the
+    # allocator always hands out the lowest free id, here the only one).
+    filler0 = 1 << 40
+    for b in range(POOL_BLOCKS):
+        raise_for_status(lib.pkv_allocator_reserve(h, filler0 + b, 1))
+    cursor = 0
+    for sid, n in enumerate(lengths.tolist()):
+        raise_for_status(lib.pkv_allocator_reserve(h, sid, 0))
+        left = n
+        while left > 0:
+            raise_for_status(lib.pkv_allocator_release(h, filler0 + int(perm[cursor])))
+            raise_for_status(lib.pkv_allocator_append_tokens(h, sid, min(BS, left)))
+            cursor += 1
+            left -= BS
+    for b in perm[cursor:].tolist():
+        raise_for_status(lib.pkv_allocator_release(h, filler0 + int(b)))
+    store.pool.pool.normal_(generator=torch.Generator(device=device).manual_seed(seed))
+    store._sync()
+    dgen = torch.Generator(device=device).manual_seed(seed + 1)
+    q = torch.randn((SEQS, HQ, D), device=device, generator=dgen).to(torch.bfloat16)
+    kn = torch.randn((SEQS, HKV, D), device=device, generator=dgen).to(torch.bfloat16)
+    vn = torch.randn((SEQS, HKV, D), device=device, generator=dgen).to(torch.bfloat16)
+    return store, lengths, q, kn, vn, perm[:cursor]
+
+
+def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
+    import torch.distributed as dist
+
+    store, lengths, q, kn, vn, _ = build_workload(device, args.seed + rank)
+    ids = np.arange(SEQS, dtype=np.int64)
+    out = torch.empty_like(q)
+    alloc = store.allocator
+    pool = store.pool
+
+    def step(kernel_events=None, qq=q, kk=kn, vv=vn, oo=out):
+        st = store.decode_step(ids)
+        if kernel_events is not None:
+            kernel_events[0].record()
+        store.decode_attention(st, 0, qq, kk, vv, out=oo)
+        if kernel_events is not None:
+            kernel_events[1].record()
+        alloc.truncate(ids, lengths)
+        return st
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---- device-resident timing --------------------------------------------
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches0 = pool.launches
+    bytes_per_launch = []
+    with ClockSampler(device.index or 0) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(args.steps):
+            st = step(kev[i])
+            bytes_per_launch.append(algorithmic_bytes(st.host_lens))
+        t1.record()
+        torch.cuda.synchronize(device)
+    launches = pool.launches - launches0
+    elapsed_ms = t0.elapsed_time(t1)
+    kernel_ms = [a.elapsed_time(b) for a, b in kev]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    barrier()
+    err = pool.decode_error_flag()
+    if err:
+        raise RuntimeError(f"decode kernel reported device error {err}")
+
+    # ---- end to end through the public API with host buffers ---------------
+    q_h = q.cpu().pin_memory()
+    kn_h = kn.cpu().pin_memory()
+    vn_h = vn.cpu().pin_memory()
+    out_h = torch.empty_like(q_h).pin_memory()
+    q_d, kn_d, vn_d = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        kn_d.copy_(kn_h, non_blocking=True)
+        vn_d.copy_(vn_h, non_blocking=True)
+        step(None, q_d, kn_d, vn_d, out)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    barrier()
+    h2d = q_h.numel() * 2 + kn_h.numel() * 2 * 2 + (6 * SEQS + 1) * 4
+    d2h = out_h.numel() * 2
+
+    if rank != 0:
+        return None
+    ms_per_step = elapsed_ms / args.steps
+    value = world * SEQS * 1000.0 / ms_per_step
+    mean_kernel_ms = statistics.mean(kernel_ms)
+    achieved = statistics.mean(bytes_per_launch) / (mean_kernel_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/Q, ctx U[64,2048])",
+        "config": workload_config(world),
+        "per_gpu_tokens_per_s": value / world,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "paged_decode_kernel<128, bf16> (fused append + split-K GQA decode)",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_source": f"{peak_kind} hbm_gbs" + (" (MEASURED_PEAKS.json)" if peak_kind == "measured" else ""),
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": ncu_traffic(),
+            "algorithmic_bytes_per_launch": statistics.mean(bytes_per_launch),
+            "kernel_ms_mean": mean_kernel_ms,
+            "kernel_ms_min": min(kernel_ms),
+        },
+        "e2e": {
+            "value": world * SEQS * 1000.0 / (e2e_ms / args.steps),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "path": "PagedKVCacheStore.decode_step + decode_attention with pinned host q/k/v in, output out",
+        },
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
+    return result
+
+
+def cpu_baseline(lengths: np.ndarray, seconds: float, sample: int = 32, steps: int | None = None) -> dict:
+    """The reference's resident-cache decode step (oracle restatement) on a bounded sample."""
+    from oracle.decode_step import ResidentDecodeBatch
+
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(7)
+    idx = np.sort(rng.choice(len(lengths), size=sample, replace=False))
+    sub = lengths[idx]
+    batch = ResidentDecodeBatch(sub.tolist(), HQ, HKV, D, seed=3, threads=cores)
+    q = rng.standard_normal((sample, HQ, D), dtype=np.float32)
+    kn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
+    vn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
+    ids = list(range(sample))
+    batch.step(ids, q, kn, vn)
+    batch.rollback(ids)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
+        t = time.perf_counter()
+        batch.step(ids, q, kn, vn)
+        times.append(time.perf_counter() - t)
+        batch.rollback(ids)
+    batch.close()
+    per_step = statistics.mean(times)
+    return {
+        "value": sample / per_step,
+        "unit": "tokens/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": f"{sample} of the {SEQS} sequences (ctx from the same U[64,2048] draw), {len(times)} decode "
+                  "steps of the reference's resident-cache path: cat append, fp32 GQA attention, clone, "
+                  "append_tokens; fp16 caches",
+        "seconds_per_step": per_step,
+    }
+
+
+def run_reference(args) -> dict:
+    gen = torch.Generator().manual_seed(args.seed)
+    lengths = torch.randint(64, 2049, (SEQS,), generator=gen).numpy().astype(np.int64)
+    from oracle.decode_step import ResidentDecodeBatch
+
+    cores = len(os.sched_getaffinity(0))
+    sample = 32
+    rng = np.random.default_rng(7)
+    idx = np.sort(rng.choice(SEQS, size=sample, replace=False))
+    batch = ResidentDecodeBatch(lengths[idx].tolist(), HQ, HKV, D, seed=3, threads=cores)
+    q = rng.standard_normal((sample, HQ, D), dtype=np.float32)
+    kn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
+    vn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
+    ids = list(range(sample))
+    for _ in range(args.warmup):
+        batch.step(ids, q, kn, vn)
+        batch.rollback(ids)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        batch.step(ids, q, kn, vn)
+        batch.rollback(ids)
+    elapsed = time.perf_counter() - t
+    batch.close()
+    value = sample * args.steps / elapsed
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "impl": "reference",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed * 1000.0 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded, ctx U[64,2048])",
+        "config": workload_config(1),
+        "cpu_baseline": {
+            "value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"each step: {sample} of the {SEQS} sequences through the reference's resident-cache "
+                      "decode step (oracle restatement: cat append, fp32 GQA attention, clone, append_tokens)",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    sys.path.insert(0, str(ROOT))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    try:
+        result = run_ours(args, rank, world, device)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,246 @@
+/*
+ * pkv_b200.h -- C ABI of the B200 paged-KV library (libpkv_b200.so).
+ *
+ * The library implements AgentRL's paged-KV hot path: the block allocator and
+ * its block tables (host C++), and the device kernels for sm_100a that append
+ * K/V into pages, gather pages back into contiguous caches, run paged GQA
+ * decode attention, chunked-prefill and speculative-verify attention over
+ * pages, and apply copy-on-write forks and frees to the device block tables.
+ *
+ * The reference (AgentRL, Python) has no native code, so there is no existing
+ * FFI to keep; each entry point below names the Python call it replaces.  The
+ * Python package `randomrepo_b200` binds these through ctypes and exposes the
+ * reference's own classes (`PagedKVAllocator`, `PagedKVCacheStore`,
+ * `PagedKVSequenceView`) on top.
+ *
+ * Conventions
+ *  - Every function returns a status (0 = success).  On failure
+ *    pkv_last_error() returns a message for the calling thread.  The status
+ *    tells the binding which Python exception the reference raises:
+ *    PKV_ERR_VALUE -> ValueError, PKV_ERR_KEY -> KeyError,
+ *    PKV_ERR_RUNTIME -> RuntimeError, PKV_ERR_INDEX -> IndexError.
+ *  - Device pointers are plain CUDA device addresses; `stream` is a
+ *    cudaStream_t passed as void* (NULL = legacy default stream).  Kernels are
+ *    asynchronous on that stream and never synchronize the host.
+ *  - KV pool layout (one allocation for all layers):
+ *        pool[layer][block][state(0=K,1=V)][kv_head][slot][head_dim]
+ *    i.e. the K (or V) rows of one block and one KV head are one contiguous
+ *    run of block_size * head_dim elements.
+ *  - Block tables: int32 [rows][table_stride]; row r belongs to the sequence
+ *    the allocator mapped to row r; entries past the sequence's block count
+ *    are unspecified.  Context lengths: int32 [rows].
+ */
+#ifndef PKV_B200_H
+#define PKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is
+ * exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+enum pkv_status {
+  PKV_OK = 0,
+  PKV_ERR_VALUE = 1,    /* ValueError in the reference */
+  PKV_ERR_KEY = 2,      /* KeyError */
+  PKV_ERR_RUNTIME = 3,  /* RuntimeError (pool exhausted) */
+  PKV_ERR_INDEX = 4,    /* IndexError (logical block past the table) */
+  PKV_ERR_ARG = 5,      /* invalid argument to a kernel entry point */
+  PKV_ERR_CUDA = 6,     /* CUDA launch / runtime error */
+  PKV_ERR_UNSUPPORTED = 7 /* shape or dtype the kernels are not built for */
+};
+
+enum pkv_dtype { PKV_F32 = 0, PKV_F16 = 1, PKV_BF16 = 2 };
+
+/* Message of the last failure on this thread ("" if none). */
+const char* pkv_last_error(void);
+
+/* Library version string, e.g. "pkv_b200 1.0 sm_100a". */
+const char* pkv_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Host block allocator                                                      */
+/* ------------------------------------------------------------------------ */
+
+typedef struct pkv_allocator pkv_allocator;
+
+typedef struct pkv_allocator_stats {
+  int64_t total_blocks;
+  int64_t block_size_tokens;
+  int64_t free_block_count;        /* PagedKVAllocator.free_block_count */
+  int64_t used_block_count;        /* .used_block_count */
+  int64_t block_reuse_count;       /* .block_reuse_count */
+  int64_t max_blocks_in_use;       /* .max_blocks_in_use (high watermark) */
+  int64_t resident_sequence_count; /* .resident_sequence_count */
+  int64_t row_capacity;            /* rows the device table must have */
+  int64_t max_blocks_per_row;      /* columns the device table must have */
+  int64_t shared_block_count;      /* blocks with refcount > 1 (forks) */
+} pkv_allocator_stats;
+
+/* PagedKVAllocator.__init__ (agentrl/generation/paged_kv.py:34-48).
+ * Returns NULL and sets *status on invalid sizes. */
+pkv_allocator* pkv_allocator_create(int64_t total_blocks, int64_t block_size_tokens, int32_t* status);
+void pkv_allocator_destroy(pkv_allocator* a);
+
+/* PagedKVAllocator.reserve (paged_kv.py:78-91): lowest free ids first. */
+int32_t pkv_allocator_reserve(pkv_allocator* a, int64_t sequence_id, int64_t token_count);
+/* PagedKVAllocator.append_tokens (paged_kv.py:93-110).  A shared partial
+ * tail block (after pkv_allocator_fork) is first replaced by a private copy. */
+int32_t pkv_allocator_append_tokens(pkv_allocator* a, int64_t sequence_id, int64_t token_count);
+/* PagedKVAllocator.release (paged_kv.py:112-120); shared blocks are freed
+ * when their last owner releases them. */
+int32_t pkv_allocator_release(pkv_allocator* a, int64_t sequence_id);
+/* Copy-on-write fork: `child` shares all of `parent`'s blocks (no reference
+ * counterpart; used to share a GRPO group's prompt pages). */
+int32_t pkv_allocator_fork(pkv_allocator* a, int64_t parent_id, int64_t child_id);
+/* PagedKVAllocator.logical_to_physical (paged_kv.py:122-127). */
+int32_t pkv_allocator_logical_to_physical(pkv_allocator* a, int64_t sequence_id, int64_t logical_block_index,
+                                          int64_t* block_out);
+/* PagedKVAllocator.view (paged_kv.py:129-139).  Writes up to `capacity`
+ * block ids; *num_blocks gets the full count. */
+int32_t pkv_allocator_view(pkv_allocator* a, int64_t sequence_id, int64_t* token_count, int32_t* blocks,
+                           int64_t capacity, int64_t* num_blocks);
+/* PagedKVAllocator.has_sequence (paged_kv.py:154-157): 1 or 0. */
+int32_t pkv_allocator_has_sequence(pkv_allocator* a, int64_t sequence_id);
+/* Counters behind PagedKVAllocator's properties and metrics() (paged_kv.py:50-76,141-152). */
+int32_t pkv_allocator_get_stats(pkv_allocator* a, pkv_allocator_stats* out);
+/* Refcount of one block (0 = free). */
+int32_t pkv_allocator_refcount(pkv_allocator* a, int64_t block, int32_t* out);
+/* Device block-table row of a sequence. */
+int32_t pkv_allocator_row(pkv_allocator* a, int64_t sequence_id, int32_t* row_out);
+
+/* One decode step: append one token to each of `n` sequences, in order
+ * (the per-token append_tokens(seq, 1) calls of agentrl/generation/continuous.py:492-493).
+ * Per entry i it writes the table row, the new token count, the block
+ * newly allocated for the token (-1 if the token fits the current tail) and
+ * (if token_blocks_out is not NULL) the block that holds the token.
+ * rows/lens/new_blocks are what pkv_decode_attention consumes; the fused
+ * kernel itself stores the new block and length into the device tables, so
+ * they are not recorded as pending device updates (pkv_allocator_touch_rows
+ * records them when no fused kernel will run).  On failure (unknown id, pool
+ * exhausted) the steps already taken stay applied (as with the reference's
+ * sequential calls) and *done gets their count. */
+int32_t pkv_allocator_decode_step(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int32_t* rows_out,
+                                  int32_t* lens_out, int32_t* new_blocks_out, int32_t* token_blocks_out,
+                                  int64_t* done);
+/* Shrink sequences to token_counts[i] tokens (no reference counterpart: it
+ * rolls back speculative drafts a verify step rejected).  Blocks past the new
+ * end are released (a shared block only drops one reference).  A count above
+ * the current one is a ValueError; an unknown id a KeyError. */
+int32_t pkv_allocator_truncate(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* token_counts,
+                               int64_t n);
+/* Record the length and last table entry of the given rows as pending device
+ * updates. */
+int32_t pkv_allocator_touch_rows(pkv_allocator* a, const int32_t* rows, int64_t n);
+
+/* Device-mirror synchronisation.  Every allocator call records which table
+ * entries, refcounts and lengths changed and which blocks must be copied
+ * (copy-on-write).  pkv_allocator_pending_updates reports the sizes;
+ * pkv_allocator_drain_updates writes them into one int32 buffer laid out as
+ *   [n_table, n_ref, n_len, n_copy,
+ *    n_table x (row, col, block), n_ref x (block, refcount),
+ *    n_len x (row, len), n_copy x (src_block, dst_block)]
+ * with the CURRENT host values, and clears the record.  The buffer is what
+ * pkv_apply_updates (device) consumes.  Returns the number of int32 written. */
+int32_t pkv_allocator_pending_updates(pkv_allocator* a, int64_t* n_table, int64_t* n_ref, int64_t* n_len,
+                                      int64_t* n_copy);
+int32_t pkv_allocator_drain_updates(pkv_allocator* a, int32_t* out, int64_t capacity, int64_t* written);
+
+/* ------------------------------------------------------------------------ */
+/* Device kernels (sm_100a)                                                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct pkv_pool_geom {
+  int32_t num_layers;
+  int32_t num_blocks;
+  int32_t num_kv_heads;
+  int32_t block_size;   /* tokens per block */
+  int32_t head_dim;
+  int32_t dtype;        /* enum pkv_dtype */
+} pkv_pool_geom;
+
+/* Bytes of the KV pool for a geometry. */
+int64_t pkv_pool_bytes(const pkv_pool_geom* g);
+
+/* Apply a drained update buffer (pkv_allocator_drain_updates) to the device
+ * block tables, refcounts and lengths, then copy whole blocks (all layers,
+ * K and V) for the copy-on-write pairs, in order.  `updates` is a DEVICE copy
+ * of the buffer and `host_updates` the host buffer it was copied from (read
+ * for the counts and to order chained copies).
+ * Replaces nothing in the reference (whose tables live in Python dicts,
+ * paged_kv.py:44-45); it is the fork/free/COW table and refcount kernel. */
+int32_t pkv_apply_updates(const pkv_pool_geom* g, void* pool, int32_t* block_tables, int32_t table_stride,
+                          int32_t num_rows, int32_t* refcounts, int32_t* context_lens, const int32_t* updates,
+                          const int32_t* host_updates, void* stream);
+
+/* Scatter `n_tokens` token rows of K and V into their pool slots, for layers
+ * [layer0, layer0 + n_layers).  Token t of layer l, head h is read from
+ *   src + l*src_layer_stride + h*src_head_stride + t*src_token_stride
+ * (element strides, innermost head_dim contiguous) and written to slot
+ * slot_mapping[t] = block * block_size + offset.  A slot < 0 is skipped.
+ * Replaces the per-block clone of write_sequence_cache (paged_kv.py:259-269)
+ * and the per-step K/V append DynamicLayer.update (transformers
+ * cache_utils.py:119-120). */
+int32_t pkv_scatter_tokens(const pkv_pool_geom* g, void* pool, int32_t layer0, int32_t n_layers, const void* k_src,
+                           const void* v_src, int64_t src_layer_stride, int64_t src_head_stride,
+                           int64_t src_token_stride, const int64_t* slot_mapping, int64_t n_tokens, void* stream);
+
+/* Gather: the inverse of pkv_scatter_tokens into dst buffers with the same
+ * stride convention.  Replaces read_sequence_legacy_cache's torch.cat of the
+ * block chunks (paged_kv.py:302-321). */
+int32_t pkv_gather_tokens(const pkv_pool_geom* g, const void* pool, int32_t layer0, int32_t n_layers, void* k_dst,
+                          void* v_dst, int64_t dst_layer_stride, int64_t dst_head_stride, int64_t dst_token_stride,
+                          const int64_t* slot_mapping, int64_t n_tokens, void* stream);
+
+/* Copy whole blocks (every layer, K and V) src[i] -> dst[i]. */
+int32_t pkv_copy_blocks(const pkv_pool_geom* g, void* pool, const int32_t* src_blocks, const int32_t* dst_blocks,
+                        int64_t n, void* stream);
+
+/* Bytes of device workspace pkv_decode_attention needs for `batch`
+ * sequences and at most `max_splits_total` split work items. */
+int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t head_dim, int64_t max_splits_total);
+
+/* Paged GQA decode attention for one layer, optionally fused with the K/V
+ * append of the step's token.
+ *   q      [batch][num_q_heads][head_dim] (bf16 or f16, same as the pool)
+ *   k_new, v_new [batch][num_kv_heads][head_dim] or NULL (no append)
+ *   rows[b]       table row of entry b
+ *   seq_lens[b]   tokens in the cache INCLUDING the step's token
+ *   new_blocks[b] block allocated for the step's token or -1 (may be NULL)
+ *   split_offsets [batch+1]: entry b owns split work items
+ *                 split_offsets[b] .. split_offsets[b+1]-1, each covering
+ *                 `pages_per_split` blocks of its context
+ *   out    [batch][num_q_heads][head_dim]
+ *   workspace: pkv_decode_workspace_bytes() bytes, zeroed once before first
+ *              use; every launch leaves it ready for the next one.
+ * With k_new != NULL the kernel writes the token's K/V into its slot
+ * (position seq_lens[b]-1), and stores new_blocks[b] (when >= 0) into the
+ * table and seq_lens[b] into context_lens[rows[b]].
+ * Replaces HF sdpa_attention_forward with GQA (transformers
+ * integrations/sdpa_attention.py:40-62) over the stacked resident caches of
+ * agentrl/generation/continuous.py:476-483, and the torch.cat append of
+ * cache_utils.py:119-120.  Requires block_size 16, head_dim 64 or 128,
+ * num_q_heads / num_kv_heads <= 8. */
+int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q, const void* k_new,
+                             const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t* context_lens,
+                             const int32_t* rows, const int32_t* seq_lens, const int32_t* new_blocks,
+                             const int32_t* split_offsets, int32_t batch, int32_t num_q_heads,
+                             int32_t pages_per_split, int64_t total_splits, float scale, void* out,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_B200_H */

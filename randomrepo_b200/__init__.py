@@ -1,0 +1,37 @@
+"""B200-native paged-KV path of AgentRL's continuous-batching rollout.
+
+Public API (drop-in for ``agentrl.generation.paged_kv``):
+
+* ``PagedKVSequenceView``, ``PagedKVAllocator``, ``PagedKVCacheStore``;
+* the device decode path ``PagedKVCacheStore.decode_step`` /
+  ``decode_attention`` and copy-on-write ``fork``;
+* KV geometry helpers of ``agentrl.generation.scheduler`` in
+  ``randomrepo_b200.scheduler``.
+
+All device work runs in ``libpkv_b200.so`` (hand-written sm_100a kernels),
+built in-tree by ``python -m randomrepo_b200.build``.  The library is loaded
+on first use of these names (so the build module itself imports without it);
+if it is missing that first use raises ImportError -- there is no fallback.
+"""
+
+from __future__ import annotations
+
+_EXPORTS = {
+    "DecodeStep": "paged_kv",
+    "PagedKVAllocator": "paged_kv",
+    "PagedKVCacheStore": "paged_kv",
+    "PagedKVSequenceView": "paged_kv",
+}
+
+__all__ = sorted(_EXPORTS)
+
+
+def __getattr__(name: str):
+    module = _EXPORTS.get(name)
+    if module is None:
+        raise AttributeError(f"module 'randomrepo_b200' has no attribute {name!r}")
+    import importlib
+
+    value = getattr(importlib.import_module(f".{module}", __name__), name)
+    globals()[name] = value
+    return value

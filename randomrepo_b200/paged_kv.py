@@ -1,0 +1,592 @@
+"""Drop-in paged-KV allocator and store over libpkv_b200.
+
+The classes keep the names, signatures, properties, metric keys, exceptions
+and messages of AgentRL's ``agentrl/generation/paged_kv.py`` so that the
+continuous-batching loop, the scheduler admission code and the telemetry
+that call them run unchanged:
+
+* ``PagedKVSequenceView`` -- paged_kv.py:11-22;
+* ``PagedKVAllocator`` -- paged_kv.py:25-175, here a handle to the C++ block
+  allocator (lowest free id first, so block tables equal the reference's);
+* ``PagedKVCacheStore`` -- paged_kv.py:178-360, here backed by one device KV
+  pool per store instead of a dict of cloned per-block tensors.
+
+Additions that the reference does not have: ``fork`` (copy-on-write sharing of
+a sequence's blocks, for the members of a GRPO group that share one prompt),
+and the device decode path (``decode_step`` + ``decode_attention``) that
+appends each step's K/V into the pages and runs paged GQA attention on them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import lib
+from .device import KVPool, plan_splits
+
+
+@dataclass(frozen=True, slots=True)
+class PagedKVSequenceView:
+    """Read-only sequence mapping inside the paged-KV allocator (paged_kv.py:11-22)."""
+
+    sequence_id: int
+    token_count: int
+    block_size_tokens: int
+    physical_blocks: tuple[int, ...]
+
+    @property
+    def logical_block_count(self) -> int:
+        return len(self.physical_blocks)
+
+
+class PagedKVAllocator:
+    """Fixed pool of equal blocks with a per-sequence block table (paged_kv.py:25-175).
+
+    Allocation pops the lowest free block id; a release returns a sequence's
+    blocks (a block shared by forks returns when its last owner releases it).
+    """
+
+    def __init__(self, total_blocks: int, block_size_tokens: int) -> None:
+        status = ctypes.c_int32(0)
+        handle = lib.pkv_allocator_create(int(total_blocks), int(block_size_tokens), ctypes.byref(status))
+        if not handle:
+            _lib.raise_for_status(status.value)
+        self._handle = handle
+        self.total_blocks = int(total_blocks)
+        self.block_size_tokens = int(block_size_tokens)
+        self._view_buf = np.zeros(64, dtype=np.int32)
+        weakref.finalize(self, lib.pkv_allocator_destroy, handle)
+
+    def _stats(self) -> _lib.AllocatorStats:
+        st = _lib.AllocatorStats()
+        lib.pkv_allocator_get_stats(self._handle, ctypes.byref(st))
+        return st
+
+    # paged_kv.py:50-76
+    @property
+    def free_block_count(self) -> int:
+        return int(self._stats().free_block_count)
+
+    @property
+    def used_block_count(self) -> int:
+        return int(self._stats().used_block_count)
+
+    @property
+    def block_reuse_count(self) -> int:
+        return int(self._stats().block_reuse_count)
+
+    @property
+    def max_blocks_in_use(self) -> int:
+        return int(self._stats().max_blocks_in_use)
+
+    @property
+    def resident_sequence_count(self) -> int:
+        return int(self._stats().resident_sequence_count)
+
+    @property
+    def allocator_occupancy(self) -> float:
+        return self.used_block_count / self.total_blocks
+
+    @property
+    def allocator_pressure(self) -> float:
+        return self.allocator_occupancy
+
+    def reserve(self, sequence_id: int, token_count: int) -> PagedKVSequenceView:
+        """Reserve enough blocks for a fresh sequence (paged_kv.py:78-91)."""
+        _lib.raise_for_status(lib.pkv_allocator_reserve(self._handle, int(sequence_id), int(token_count)))
+        return self.view(sequence_id)
+
+    def append_tokens(self, sequence_id: int, token_count: int) -> PagedKVSequenceView:
+        """Grow a sequence by the provided number of tokens (paged_kv.py:93-110)."""
+        _lib.raise_for_status(lib.pkv_allocator_append_tokens(self._handle, int(sequence_id), int(token_count)))
+        return self.view(sequence_id)
+
+    def release(self, sequence_id: int) -> None:
+        """Release all blocks owned by one sequence (paged_kv.py:112-120)."""
+        _lib.raise_for_status(lib.pkv_allocator_release(self._handle, int(sequence_id)))
+
+    def fork(self, parent_id: int, child_id: int) -> PagedKVSequenceView:
+        """Share all of ``parent_id``'s blocks with a new sequence ``child_id``.
+
+        No reference counterpart.  The child's first append into a shared,
+        partially filled tail block gets a private copy of that block first.
+        """
+        _lib.raise_for_status(lib.pkv_allocator_fork(self._handle, int(parent_id), int(child_id)))
+        return self.view(child_id)
+
+    def logical_to_physical(self, sequence_id: int, logical_block_index: int) -> int:
+        """Resolve one logical block index to its physical block id (paged_kv.py:122-127)."""
+        out = ctypes.c_int64()
+        st = lib.pkv_allocator_logical_to_physical(self._handle, int(sequence_id), int(logical_block_index),
+                                                   ctypes.byref(out))
+        _lib.raise_for_status(st, key=sequence_id)
+        return int(out.value)
+
+    def view(self, sequence_id: int) -> PagedKVSequenceView:
+        """Return a read-only snapshot for one sequence (paged_kv.py:129-139)."""
+        count = ctypes.c_int64()
+        n = ctypes.c_int64()
+        buf = self._view_buf
+        st = lib.pkv_allocator_view(self._handle, int(sequence_id), ctypes.byref(count), buf.ctypes.data,
+                                    buf.size, ctypes.byref(n))
+        _lib.raise_for_status(st)
+        if n.value > buf.size:
+            self._view_buf = buf = np.zeros(max(n.value, 2 * buf.size), dtype=np.int32)
+            lib.pkv_allocator_view(self._handle, int(sequence_id), ctypes.byref(count), buf.ctypes.data, buf.size,
+                                   ctypes.byref(n))
+        return PagedKVSequenceView(
+            sequence_id=sequence_id,
+            token_count=int(count.value),
+            block_size_tokens=self.block_size_tokens,
+            physical_blocks=tuple(int(b) for b in buf[: n.value]),
+        )
+
+    def metrics(self) -> dict[str, float]:
+        """Allocator metrics for runtime reporting (paged_kv.py:141-152)."""
+        st = self._stats()
+        occupancy = st.used_block_count / self.total_blocks
+        return {
+            "paged_kv_free_block_count": float(st.free_block_count),
+            "paged_kv_used_block_count": float(st.used_block_count),
+            "paged_kv_allocator_occupancy": float(occupancy),
+            "paged_kv_block_reuse_count": float(st.block_reuse_count),
+            "paged_kv_allocator_pressure": float(occupancy),
+            "paged_kv_max_blocks_in_use": float(st.max_blocks_in_use),
+            "paged_kv_resident_sequences": float(st.resident_sequence_count),
+        }
+
+    def has_sequence(self, sequence_id: int) -> bool:
+        """Whether the allocator still tracks the sequence (paged_kv.py:154-157)."""
+        return bool(lib.pkv_allocator_has_sequence(self._handle, int(sequence_id)))
+
+    # -- extension ------------------------------------------------------------
+    def truncate(self, sequence_ids, token_counts) -> None:
+        """Shrink each sequence to its token count, releasing blocks past the end.
+
+        No reference counterpart: it rolls back rejected speculative drafts.
+        """
+        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
+        counts = np.ascontiguousarray(np.atleast_1d(np.asarray(token_counts, dtype=np.int64)))
+        if ids.shape != counts.shape:
+            raise ValueError("sequence_ids and token_counts must have the same length")
+        _lib.raise_for_status(lib.pkv_allocator_truncate(self._handle, ids.ctypes.data, counts.ctypes.data, ids.size))
+
+    def refcount(self, block_id: int) -> int:
+        out = ctypes.c_int32()
+        _lib.raise_for_status(lib.pkv_allocator_refcount(self._handle, int(block_id), ctypes.byref(out)))
+        return int(out.value)
+
+    def row(self, sequence_id: int) -> int:
+        """Row of the sequence in the device block table."""
+        out = ctypes.c_int32()
+        _lib.raise_for_status(lib.pkv_allocator_row(self._handle, int(sequence_id), ctypes.byref(out)))
+        return int(out.value)
+
+    @property
+    def shared_block_count(self) -> int:
+        return int(self._stats().shared_block_count)
+
+
+@dataclass
+class DecodeStep:
+    """Device descriptor of one decode step (one token appended per sequence).
+
+    ``rows``, ``seq_lens`` (token counts including the step's token),
+    ``new_blocks`` and ``split_offsets`` are int32 device tensors;
+    ``pages_per_split`` and ``total_splits`` describe the split-K work items.
+    The same step serves every layer.
+    """
+
+    sequence_ids: tuple[int, ...]
+    rows: torch.Tensor
+    seq_lens: torch.Tensor
+    new_blocks: torch.Tensor
+    split_offsets: torch.Tensor
+    slots: torch.Tensor
+    pages_per_split: int
+    total_splits: int
+    host_rows: np.ndarray
+    host_lens: np.ndarray
+    committed: bool = False
+
+    @property
+    def batch(self) -> int:
+        return len(self.sequence_ids)
+
+
+class PagedKVCacheStore:
+    """Block-backed KV store (paged_kv.py:178-360) on a device KV pool.
+
+    The pool is created on the first write from the cache's geometry (layers,
+    KV heads, head dim, dtype, device), or up front when all of
+    ``num_layers``, ``num_kv_heads``, ``head_dim`` and ``dtype`` are given.
+    Reads return new tensors on the device the sequence was written from.
+    """
+
+    def __init__(self, allocator: PagedKVAllocator, *, num_layers: int | None = None,
+                 num_kv_heads: int | None = None, head_dim: int | None = None, dtype: torch.dtype | None = None,
+                 device: torch.device | str | int | None = None) -> None:
+        self.allocator = allocator
+        self._cache_templates: dict[int, Any] = {}
+        self._resident_caches: dict[int, Any] = {}
+        self._io_device: dict[int, torch.device] = {}
+        # Tokens stored in each block's chunk (-1: the block holds no stored chunk).
+        self._block_fill = np.full(allocator.total_blocks, -1, dtype=np.int32)
+        self._pool: KVPool | None = None
+        if None not in (num_layers, num_kv_heads, head_dim, dtype):
+            self._pool = KVPool(allocator, num_layers, num_kv_heads, head_dim, dtype, device)
+
+    # -- reference API (paged_kv.py:192-216) ------------------------------------
+    @property
+    def resident_sequence_count(self) -> int:
+        return self.allocator.resident_sequence_count
+
+    @property
+    def pool(self) -> KVPool | None:
+        return self._pool
+
+    def reserve(self, sequence_id: int, token_count: int) -> PagedKVSequenceView:
+        return self.allocator.reserve(sequence_id, token_count)
+
+    def append_tokens(self, sequence_id: int, token_count: int) -> PagedKVSequenceView:
+        return self.allocator.append_tokens(sequence_id, token_count)
+
+    def has_sequence(self, sequence_id: int) -> bool:
+        return self.allocator.has_sequence(sequence_id)
+
+    def release(self, sequence_id: int) -> None:
+        """paged_kv.py:205-213: drop the resident cache, the stored blocks and the table."""
+        view = self.allocator.view(sequence_id)
+        self._resident_caches.pop(sequence_id, None)
+        self._cache_templates.pop(sequence_id, None)
+        self._io_device.pop(sequence_id, None)
+        self.allocator.release(sequence_id)
+        for block_id in view.physical_blocks:
+            if self.allocator.refcount(block_id) == 0:
+                self._block_fill[block_id] = -1
+
+    def metrics(self) -> dict[str, float]:
+        return self.allocator.metrics()
+
+    # -- resident caches (paged_kv.py:218-243) ------------------------------------
+    def cache_template(self, sequence_id: int) -> Any:
+        return self._cache_templates[sequence_id]
+
+    def set_resident_cache(self, sequence_id: int, cache: Any, cache_template: Any | None = None) -> None:
+        if not self.allocator.has_sequence(sequence_id):
+            raise KeyError(f"Unknown sequence_id {sequence_id}.")
+        self._resident_caches[sequence_id] = cache
+        if cache_template is not None:
+            self._cache_templates[sequence_id] = cache_template
+
+    def resident_cache(self, sequence_id: int) -> Any:
+        return self._resident_caches[sequence_id]
+
+    def has_resident_cache(self, sequence_id: int) -> bool:
+        return sequence_id in self._resident_caches
+
+    def clear_resident_cache(self, sequence_id: int) -> None:
+        resident_cache = self._resident_caches.get(sequence_id)
+        if resident_cache is not None and self.allocator.has_sequence(sequence_id):
+            cache_template = self._cache_templates.get(sequence_id, resident_cache)
+            self.write_sequence_cache(
+                sequence_id=sequence_id,
+                legacy_cache=self._as_legacy_cache(resident_cache, sequence_id),
+                cache_template=cache_template,
+            )
+        self._resident_caches.pop(sequence_id, None)
+
+    # -- block storage (paged_kv.py:245-347) --------------------------------------
+    def write_sequence_cache(self, sequence_id: int, legacy_cache: tuple[tuple[torch.Tensor, ...], ...],
+                             cache_template: Any) -> None:
+        """paged_kv.py:245-269: trim to token_count, split into blocks, store each block's chunk."""
+        view = self.allocator.view(sequence_id)
+        token_count = view.token_count
+        bs = view.block_size_tokens
+        self._cache_templates[sequence_id] = cache_template
+        if token_count == 0:
+            return
+        n_written = None
+        for layer_cache in legacy_cache:
+            for tensor in layer_cache:
+                n = int(tensor[:, :, :token_count, ...].shape[2])
+                chunks = max(1, -(-n // bs))
+                if chunks != view.logical_block_count:
+                    raise ValueError(
+                        "Cache chunk count does not match allocated block count "
+                        f"for sequence {sequence_id}: {chunks} vs {view.logical_block_count}."
+                    )
+                if n_written is not None and n != n_written:
+                    raise ValueError("every layer and state of a sequence cache must hold the same token count")
+                n_written = n
+        first = legacy_cache[0][0]
+        if any(len(layer) != 2 for layer in legacy_cache):
+            raise ValueError("the paged pool stores (key, value) pairs per layer")
+        pool = self._ensure_pool(len(legacy_cache), first.shape[1], first.shape[3], first.dtype, first.device)
+        self._io_device[sequence_id] = first.device
+        if n_written:
+            src = torch.stack([torch.stack([layer[0][0, :, :n_written], layer[1][0, :, :n_written]])
+                               for layer in legacy_cache]).to(pool.device)
+            slots = self._slots(view.physical_blocks, [min(bs, n_written - j * bs)
+                                                       for j in range(view.logical_block_count)], bs)
+            self._sync()
+            pool.scatter(0, src[:, 0], src[:, 1], slots)
+        for j, block_id in enumerate(view.physical_blocks):
+            self._block_fill[block_id] = max(0, min(bs, (n_written or 0) - j * bs))
+
+    def write_batched_legacy_cache(self, sequence_ids: list[int], legacy_cache: tuple[tuple[torch.Tensor, ...], ...],
+                                   cache_template: Any) -> None:
+        """paged_kv.py:271-281."""
+        split_caches = self._split_legacy_cache(legacy_cache)
+        if len(split_caches) != len(sequence_ids):
+            raise ValueError("Batched legacy cache does not match the number of sequence ids.")
+        for sequence_id, sequence_cache in zip(sequence_ids, split_caches, strict=True):
+            self.write_sequence_cache(sequence_id, sequence_cache, cache_template)
+
+    def read_sequence_legacy_cache(self, sequence_id: int) -> tuple[tuple[torch.Tensor, ...], ...]:
+        """paged_kv.py:283-321: resident cache, else the stored blocks, else the template."""
+        view = self.allocator.view(sequence_id)
+        token_count = view.token_count
+        resident_cache = self._resident_caches.get(sequence_id)
+        if resident_cache is not None:
+            legacy_cache = self._as_legacy_cache(resident_cache, sequence_id)
+            return tuple(
+                tuple(tensor[:, :, :token_count, ...].clone() for tensor in layer_cache)
+                for layer_cache in legacy_cache
+            )
+        fills = self._block_fill[list(view.physical_blocks)] if view.physical_blocks else np.zeros(0, np.int32)
+        if self._pool is None or not (fills >= 0).any():
+            legacy_template = self._as_legacy_cache(self._cache_templates[sequence_id], sequence_id)
+            return tuple(
+                tuple(tensor[:, :, :token_count, ...].clone() for tensor in layer_template)
+                for layer_template in legacy_template
+            )
+        missing = np.flatnonzero(fills < 0)
+        if missing.size:
+            raise KeyError((view.physical_blocks[int(missing[0])], 0, 0))
+        n = min(int(fills.sum()), token_count)
+        return self._gather_legacy(view.physical_blocks, fills, n, self._io_device.get(sequence_id))
+
+    def read_batched_legacy_cache(self, sequence_ids: list[int]) -> tuple[tuple[torch.Tensor, ...], ...]:
+        """paged_kv.py:331-333."""
+        sequence_caches = [self.read_sequence_legacy_cache(sequence_id) for sequence_id in sequence_ids]
+        return self._stack_legacy_cache(sequence_caches)
+
+    @staticmethod
+    def _as_legacy_cache(cache: Any, sequence_id: int) -> tuple[tuple[torch.Tensor, ...], ...]:
+        """paged_kv.py:323-329."""
+        if isinstance(cache, tuple):
+            return cache
+        if hasattr(cache, "to_legacy_cache"):
+            return cache.to_legacy_cache()
+        layers = getattr(cache, "layers", None)
+        if layers is not None and all(hasattr(layer, "keys") and hasattr(layer, "values") for layer in layers):
+            # transformers >= 5 caches dropped to_legacy_cache; their layers hold keys/values.
+            return tuple((layer.keys, layer.values) for layer in layers)
+        raise TypeError(f"Unsupported cache template for sequence {sequence_id}: {type(cache)!r}")
+
+    @staticmethod
+    def _stack_legacy_cache(caches: list[tuple[tuple[torch.Tensor, ...], ...]]) -> tuple[tuple[torch.Tensor, ...], ...]:
+        """paged_kv.py:335-347."""
+        stacked_layers = []
+        for layer_caches in zip(*caches, strict=True):
+            stacked_layers.append(tuple(torch.cat(items, dim=0) for items in zip(*layer_caches, strict=True)))
+        return tuple(stacked_layers)
+
+    @staticmethod
+    def _split_legacy_cache(cache: tuple[tuple[torch.Tensor, ...], ...]) -> list[tuple[tuple[torch.Tensor, ...], ...]]:
+        """paged_kv.py:349-360."""
+        batch_size = cache[0][0].shape[0]
+        return [
+            tuple(tuple(state[batch_index : batch_index + 1] for state in layer_cache) for layer_cache in cache)
+            for batch_index in range(batch_size)
+        ]
+
+    # -- copy-on-write fork (extension) ----------------------------------------
+    def fork(self, parent_id: int, child_id: int) -> PagedKVSequenceView:
+        """Give ``child_id`` the parent's blocks (shared, copy-on-write) and cache template."""
+        view = self.allocator.fork(parent_id, child_id)
+        if parent_id in self._cache_templates:
+            self._cache_templates[child_id] = self._cache_templates[parent_id]
+        if parent_id in self._io_device:
+            self._io_device[child_id] = self._io_device[parent_id]
+        return view
+
+    def truncate(self, sequence_ids, token_counts) -> None:
+        """Shrink sequences (see ``PagedKVAllocator.truncate``); stored chunks are trimmed to match."""
+        ids = np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64))
+        counts = np.atleast_1d(np.asarray(token_counts, dtype=np.int64))
+        bs = self.allocator.block_size_tokens
+        tails = []
+        for sid, n in zip(ids.tolist(), counts.tolist()):
+            view = self.allocator.view(sid)
+            keep = -(-n // bs)
+            tails.append((view.physical_blocks[:keep], view.physical_blocks[keep:], n))
+        self.allocator.truncate(ids, counts)
+        for kept, dropped, n in tails:
+            for b in dropped:
+                if self.allocator.refcount(b) == 0:
+                    self._block_fill[b] = -1
+            if kept and n % bs and self._block_fill[kept[-1]] > n % bs:
+                self._block_fill[kept[-1]] = n % bs
+
+    # -- device decode path (extension) -----------------------------------------
+    def decode_step(self, sequence_ids) -> DecodeStep:
+        """Append one token to each sequence and describe the step for the decode kernel.
+
+        The allocator side equals calling ``append_tokens(seq, 1)`` for each id in
+        order (agentrl/generation/continuous.py:492-493).
+        """
+        pool = self._require_pool()
+        ids = np.ascontiguousarray(np.asarray(sequence_ids, dtype=np.int64))
+        n = ids.size
+        if n == 0:
+            raise ValueError("decode_step needs at least one sequence")
+        desc = np.empty(4 * n, dtype=np.int32)
+        rows, lens, newb, tok_blocks = desc[:n], desc[n : 2 * n], desc[2 * n : 3 * n], desc[3 * n :]
+        done = ctypes.c_int64()
+        st = lib.pkv_allocator_decode_step(self.allocator._handle, ids.ctypes.data, n, rows.ctypes.data,
+                                           lens.ctypes.data, newb.ctypes.data, tok_blocks.ctypes.data,
+                                           ctypes.byref(done))
+        k = done.value
+        bs = self.allocator.block_size_tokens
+        if st != _lib.PKV_OK:
+            lib.pkv_allocator_touch_rows(self.allocator._handle, rows.ctypes.data, k)
+            self._sync()
+            self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
+            _lib.raise_for_status(st)
+        # Copy-on-write copies first (they carry the source block's fill), then
+        # the fill of the blocks that receive this step's tokens.
+        self._sync()
+        self._block_fill[tok_blocks] = (lens - 1) % bs + 1
+        pps, offsets = plan_splits(lens, pool.num_kv_heads, bs)
+        slots = tok_blocks.astype(np.int64) * bs + (lens - 1) % bs
+        # One pinned upload: [slots (int64) | rows | lens | new_blocks | split_offsets]
+        host = torch.empty(2 * n + 3 * n + n + 1, dtype=torch.int32, pin_memory=True)
+        h = host.numpy()
+        h[: 2 * n] = slots.view(np.int32)
+        h[2 * n : 5 * n] = desc[: 3 * n]
+        h[5 * n :] = offsets
+        dev = host.to(pool.device, non_blocking=True)
+        return DecodeStep(
+            sequence_ids=tuple(int(x) for x in ids),
+            rows=dev[2 * n : 3 * n],
+            seq_lens=dev[3 * n : 4 * n],
+            new_blocks=dev[4 * n : 5 * n],
+            split_offsets=dev[5 * n :],
+            slots=dev[: 2 * n].view(torch.int64),
+            pages_per_split=pps,
+            total_splits=int(offsets[-1]),
+            host_rows=rows.copy(),
+            host_lens=lens.copy(),
+        )
+
+    def decode_attention(self, step: DecodeStep, layer: int, q: torch.Tensor, k_new: torch.Tensor | None = None,
+                         v_new: torch.Tensor | None = None, *, scale: float | None = None,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+        """Paged GQA decode for one layer: ``q [B, Hq, D]`` -> ``[B, Hq, D]``.
+
+        With ``k_new``/``v_new`` ``[B, Hkv, D]`` the kernel first appends the
+        step's token into its page (and updates the device block table and
+        lengths); without them the step's K/V must already be in the pool.
+        """
+        pool = self._require_pool()
+        b = step.batch
+        if q.dim() != 3 or q.shape[0] != b or q.shape[2] != pool.head_dim:
+            raise ValueError("q must be [batch, num_q_heads, head_dim]")
+        if q.dtype != pool.dtype or not q.is_contiguous() or q.device != pool.device:
+            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
+        for t in (k_new, v_new):
+            if t is not None and (t.shape != (b, pool.num_kv_heads, pool.head_dim) or t.dtype != pool.dtype
+                                  or not t.is_contiguous() or t.device != pool.device):
+                raise ValueError("k_new/v_new must be contiguous [batch, num_kv_heads, head_dim] pool-dtype tensors")
+        if (k_new is None) != (v_new is None):
+            raise ValueError("pass both k_new and v_new or neither")
+        if k_new is None and not step.committed:
+            lib.pkv_allocator_touch_rows(self.allocator._handle, step.host_rows.ctypes.data, b)
+            step.committed = True
+        self._sync()
+        if out is None:
+            out = torch.empty_like(q)
+        hq = q.shape[1]
+        ws_bytes = lib.pkv_decode_workspace_bytes(b, pool.num_kv_heads, pool.head_dim, step.total_splits)
+        ws = pool.workspace(ws_bytes)
+        rows_t, cols_t = pool.tables.shape
+        st = lib.pkv_decode_attention(
+            pool._geom_ref, pool.pool.data_ptr(), int(layer), q.data_ptr(),
+            k_new.data_ptr() if k_new is not None else None, v_new.data_ptr() if v_new is not None else None,
+            pool.tables.data_ptr(), cols_t, pool.context_lens.data_ptr(), step.rows.data_ptr(),
+            step.seq_lens.data_ptr(), step.new_blocks.data_ptr(), step.split_offsets.data_ptr(), b, hq,
+            step.pages_per_split, step.total_splits, float(scale if scale is not None else pool.head_dim ** -0.5),
+            out.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        _lib.raise_for_status(st)
+        pool.launches += 1
+        if k_new is not None:
+            step.committed = True
+        return out
+
+    def append_step_kv(self, step: DecodeStep, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
+        """Write the step's K/V ``[B, Hkv, D]`` into the pool without attention."""
+        pool = self._require_pool()
+        pool.scatter(layer, k_new.permute(1, 0, 2).unsqueeze(0), v_new.permute(1, 0, 2).unsqueeze(0), step.slots)
+
+    # -- helpers -----------------------------------------------------------------
+    def _ensure_pool(self, num_layers: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype,
+                     device: torch.device) -> KVPool:
+        if self._pool is None:
+            dev = device if device.type == "cuda" else None
+            self._pool = KVPool(self.allocator, num_layers, num_kv_heads, head_dim, dtype, dev)
+        p = self._pool
+        if (p.num_layers, p.num_kv_heads, p.head_dim, p.dtype) != (num_layers, num_kv_heads, head_dim, dtype):
+            raise ValueError(
+                f"cache geometry (layers={num_layers}, kv_heads={num_kv_heads}, head_dim={head_dim}, {dtype}) does "
+                f"not match the pool (layers={p.num_layers}, kv_heads={p.num_kv_heads}, head_dim={p.head_dim}, "
+                f"{p.dtype})"
+            )
+        return p
+
+    def _require_pool(self) -> KVPool:
+        if self._pool is None:
+            raise RuntimeError("the KV pool does not exist yet: write a cache first or pass its geometry")
+        return self._pool
+
+    def _sync(self) -> None:
+        pool = self._pool
+        if pool is None:
+            return
+        buf = pool.drain()
+        if buf is not None:
+            self._note_copies(buf)
+        pool.sync(buf)
+
+    def _note_copies(self, buf: torch.Tensor) -> None:
+        h = buf.numpy()
+        nt, nr, nl, nc = (int(x) for x in h[:4])
+        if nc:
+            pairs = h[4 + 3 * nt + 2 * nr + 2 * nl :].reshape(nc, 2)
+            for src, dst in pairs:
+                self._block_fill[dst] = self._block_fill[src]
+
+    def _slots(self, blocks, fills, bs: int) -> torch.Tensor:
+        parts = [np.arange(f, dtype=np.int64) + int(b) * bs for b, f in zip(blocks, fills) if f > 0]
+        host = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+        return torch.from_numpy(host).to(self._pool.device)
+
+    def _gather_legacy(self, blocks, fills, n: int, io_device) -> tuple[tuple[torch.Tensor, ...], ...]:
+        pool = self._pool
+        self._sync()
+        slots = self._slots(blocks, fills, pool.block_size)[:n]
+        out = torch.empty((pool.num_layers, 2, pool.num_kv_heads, n, pool.head_dim), dtype=pool.dtype,
+                          device=pool.device)
+        if n:
+            pool.gather(0, out[:, 0], out[:, 1], slots)
+        if io_device is not None and io_device != pool.device:
+            out = out.to(io_device)
+        return tuple((out[layer, 0].unsqueeze(0), out[layer, 1].unsqueeze(0)) for layer in range(pool.num_layers))
