@@ -195,13 +195,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     alloc = store.allocator
     pool = store.pool
 
-    def step(kernel_events=None, qq=q, kk=kn, vv=vn, oo=out):
-        st = store.decode_step(ids)
-        if kernel_events is not None:
-            kernel_events[0].record()
-        store.decode_attention(st, 0, qq, kk, vv, out=oo)
-        if kernel_events is not None:
-            kernel_events[1].record()
+    def step(qq=q, kk=kn, vv=vn, oo=out):
+        _, st = store.decode(ids, qq, kk, vv, layer=0, out=oo)
         alloc.truncate(ids, lengths)
         return st
 
@@ -214,21 +209,22 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     for _ in range(args.warmup):
         step()
     barrier()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    launches0 = pool.launches
+    pool.time_launches(args.steps)  # events recorded by the library right around the decode kernels
+    launches0 = pool.launch_count()
     bytes_per_launch = []
     with ClockSampler(device.index or 0) as clocks:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for i in range(args.steps):
-            st = step(kev[i])
+            st = step()
             bytes_per_launch.append(algorithmic_bytes(st.host_lens))
         t1.record()
         torch.cuda.synchronize(device)
-    launches = pool.launches - launches0
+    launches = pool.launch_count() - launches0
     elapsed_ms = t0.elapsed_time(t1)
-    kernel_ms = [a.elapsed_time(b) for a, b in kev]
+    kernel_ms = pool.launch_times_ms().tolist()
+    pool.time_launches(0)
     if world > 1:
         t = torch.tensor([elapsed_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -249,7 +245,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         q_d.copy_(q_h, non_blocking=True)
         kn_d.copy_(kn_h, non_blocking=True)
         vn_d.copy_(vn_h, non_blocking=True)
-        step(None, q_d, kn_d, vn_d, out)
+        step(q_d, kn_d, vn_d, out)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -295,7 +291,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "per_gpu_tokens_per_s": value / world,
         "roofline": {
             "bound": "hbm",
-            "kernel": "paged_decode_kernel<128, bf16> (fused append + split-K GQA decode)",
+            "kernel": "pkv_decode_attention: paged_decode_kernel<128, 2, bf16> (fused append + split-K GQA "
+                      "decode) + paged_decode_combine_kernel, timed together per launch",
             "achieved": achieved,
             "peak": peak,
             "peak_source": f"{peak_kind} hbm_gbs" + (" (MEASURED_PEAKS.json)" if peak_kind == "measured" else ""),

@@ -23,9 +23,14 @@
  *    cudaStream_t passed as void* (NULL = legacy default stream).  Kernels are
  *    asynchronous on that stream and never synchronize the host.
  *  - KV pool layout (one allocation for all layers):
- *        pool[layer][block][state(0=K,1=V)][kv_head][slot][head_dim]
- *    i.e. the K (or V) rows of one block and one KV head are one contiguous
- *    run of block_size * head_dim elements.
+ *        pool[layer][block][kv_head][state(0=K,1=V)][slot][head_dim]
+ *    The K (or V) rows of one block and one KV head form a "page"; the pages
+ *    of one block are contiguous.  When a row is a multiple of 128 bytes and
+ *    block_size a multiple of 8, each page is stored pre-swizzled: cut into
+ *    128-byte column slabs, each slab holding the page's rows at 128 bytes
+ *    apiece with the 16-byte chunks of row t permuted by XOR (t mod 8) (the
+ *    layout TMA's 128-byte swizzle produces).  Otherwise pages are row-major.
+ *    Read and write the pool through pkv_scatter_tokens / pkv_gather_tokens.
  *  - Block tables: int32 [rows][table_stride]; row r belongs to the sequence
  *    the allocator mapped to row r; entries past the sequence's block count
  *    are unspecified.  Context lengths: int32 [rows].
@@ -54,7 +59,8 @@ enum pkv_status {
   PKV_ERR_INDEX = 4,    /* IndexError (logical block past the table) */
   PKV_ERR_ARG = 5,      /* invalid argument to a kernel entry point */
   PKV_ERR_CUDA = 6,     /* CUDA launch / runtime error */
-  PKV_ERR_UNSUPPORTED = 7 /* shape or dtype the kernels are not built for */
+  PKV_ERR_UNSUPPORTED = 7, /* shape or dtype the kernels are not built for */
+  PKV_ERR_CAPACITY = 8     /* device block tables must grow first (see pkv_step_info) */
 };
 
 enum pkv_dtype { PKV_F32 = 0, PKV_F16 = 1, PKV_BF16 = 2 };
@@ -203,37 +209,130 @@ int32_t pkv_gather_tokens(const pkv_pool_geom* g, const void* pool, int32_t laye
 int32_t pkv_copy_blocks(const pkv_pool_geom* g, void* pool, const int32_t* src_blocks, const int32_t* dst_blocks,
                         int64_t n, void* stream);
 
+/* KV heads one decode work item covers: 2 when num_kv_heads is even, else 1. */
+int32_t pkv_decode_heads_per_item(int32_t num_kv_heads);
+
+/* Plan one decode step (host): cut each sequence's pages into work items of
+ * at most *pages_per_split_out (<= 32) pages for one group of
+ * pkv_decode_heads_per_item KV heads, sized for the warps of `num_sms`
+ * persistent CTAs.  seq_lens[b] counts the step's token; a sequence may hold
+ * up to 32768 tokens.  With items_out == NULL only the counts are returned; else
+ * items_out (capacity in quadruples) receives *n_items_out int32 quadruples
+ *   {sequence, split << 8 | head_group, splits of the sequence, workspace slot of split 0}
+ * (full-size items first, then the rest by decreasing size), followed by
+ * *n_combine_out quadruples {sequence, head_group, splits, slot of split 0},
+ * one per (sequence, head group) cut into several items. */
+int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t num_sms, int32_t* pages_per_split_out, int32_t* items_out, int64_t items_capacity,
+                        int64_t* n_items_out, int64_t* n_combine_out);
+
 /* Bytes of device workspace pkv_decode_attention needs for `batch`
- * sequences and at most `max_splits_total` split work items. */
-int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t head_dim, int64_t max_splits_total);
+ * sequences and `n_items` work items. */
+int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t head_dim, int64_t n_items);
 
 /* Paged GQA decode attention for one layer, optionally fused with the K/V
  * append of the step's token.
  *   q      [batch][num_q_heads][head_dim] (bf16 or f16, same as the pool)
  *   k_new, v_new [batch][num_kv_heads][head_dim] or NULL (no append)
+ *   block_tables  int32 [table_rows][table_stride]
  *   rows[b]       table row of entry b
  *   seq_lens[b]   tokens in the cache INCLUDING the step's token
  *   new_blocks[b] block allocated for the step's token or -1 (may be NULL)
- *   split_offsets [batch+1]: entry b owns split work items
- *                 split_offsets[b] .. split_offsets[b+1]-1, each covering
- *                 `pages_per_split` blocks of its context
+ *   work_items    the plan of pkv_decode_plan for these seq_lens (device copy:
+ *                 n_items items then n_combine combine entries)
  *   out    [batch][num_q_heads][head_dim]
  *   workspace: pkv_decode_workspace_bytes() bytes, zeroed once before first
- *              use; every launch leaves it ready for the next one.
+ *              use; every launch leaves it ready for the next one.  Its first
+ *              int32 is an error word: 0, or 1 (a bounded wait gave up),
+ *              3 (a work item outside the launch was skipped), 4 (a block id
+ *              outside the pool was replaced by block 0).
  * With k_new != NULL the kernel writes the token's K/V into its slot
  * (position seq_lens[b]-1), and stores new_blocks[b] (when >= 0) into the
  * table and seq_lens[b] into context_lens[rows[b]].
  * Replaces HF sdpa_attention_forward with GQA (transformers
  * integrations/sdpa_attention.py:40-62) over the stacked resident caches of
  * agentrl/generation/continuous.py:476-483, and the torch.cat append of
- * cache_utils.py:119-120.  Requires block_size 16, head_dim 64 or 128,
- * num_q_heads / num_kv_heads <= 8. */
+ * transformers cache_utils.py:119-120.  Requires block_size 16, head_dim 64
+ * or 128, bf16/f16, num_q_heads / num_kv_heads <= 8. */
 int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q, const void* k_new,
-                             const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t* context_lens,
+                             const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                             int32_t* context_lens,
                              const int32_t* rows, const int32_t* seq_lens, const int32_t* new_blocks,
-                             const int32_t* split_offsets, int32_t batch, int32_t num_q_heads,
-                             int32_t pages_per_split, int64_t total_splits, float scale, void* out,
-                             void* workspace, int64_t workspace_bytes, void* stream);
+                             const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
+                             int32_t num_q_heads, int32_t pages_per_split, float scale, void* out, void* workspace,
+                             int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Native decode-step runtime                                                */
+/* ------------------------------------------------------------------------ */
+
+/* One decode step as uploaded to the device (device pointers are valid until
+ * the stepper's next upload). */
+typedef struct pkv_step_info {
+  int32_t batch;            /* sequences in the step (appended so far on failure) */
+  int32_t pages_per_split;
+  int32_t n_items;
+  int32_t n_combine;
+  int32_t n_copies;         /* copy-on-write block copies applied before the step */
+  int32_t need_rows;        /* device table rows / columns the step needs */
+  int32_t need_cols;
+  int32_t reserved;
+  const int32_t* rows;      /* device [batch] */
+  const int32_t* seq_lens;  /* device [batch] (tokens incl. the step's token) */
+  const int32_t* new_blocks;/* device [batch] */
+  const int32_t* items;     /* device: n_items work items, then n_combine entries */
+  const int64_t* slots;     /* device [batch]: pool slot of each step token */
+} pkv_step_info;
+
+typedef struct pkv_stepper pkv_stepper;
+
+/* A stepper runs decode steps of one allocator / pool on one stream: it owns
+ * a small ring of pinned staging buffers and the decode workspace.  It
+ * replaces the per-step Python work around AgentRL's decode loop
+ * (agentrl/generation/continuous.py:443-497: per-sequence append_tokens,
+ * cache stack / split) with one C call per step plus one per layer. */
+pkv_stepper* pkv_stepper_create(pkv_allocator* a, const pkv_pool_geom* g, void* pool, int32_t* status);
+void pkv_stepper_destroy(pkv_stepper* st);
+/* The device block tables (int32 [table_rows][table_stride]), lengths and
+ * refcounts the stepper keeps in sync; rebind after growing them. */
+int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                                int32_t* context_lens, int32_t* refcounts);
+/* Apply the allocator's pending updates on `stream` (as pkv_apply_updates);
+ * up to copies_cap copy-on-write (src, dst) pairs are reported.  Returns
+ * PKV_ERR_CAPACITY with *need_rows / *need_cols when the tables must grow. */
+int32_t pkv_stepper_sync(pkv_stepper* st, void* stream, int32_t* copies_out, int64_t copies_cap, int32_t* n_copies,
+                         int32_t* need_rows, int32_t* need_cols);
+/* Step phase 1 (host only): append one token to each sequence in order
+ * (pkv_allocator_decode_step).  Optional host outputs: table rows, new token
+ * counts and the block holding each step token. */
+int32_t pkv_stepper_begin(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, pkv_step_info* info,
+                          int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out);
+/* Step phase 2: apply pending updates, plan, upload the descriptor on
+ * `stream`.  PKV_ERR_CAPACITY (info->need_rows / need_cols set, nothing
+ * launched) asks the caller to grow and rebind the tables and call again. */
+int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, int32_t* copies_out,
+                           int64_t copies_cap);
+/* Fused append + paged decode attention of the uploaded step for one layer
+ * (pkv_decode_attention with the stepper's descriptor and workspace). */
+int32_t pkv_stepper_attention(pkv_stepper* st, int32_t layer, const void* q, const void* k_new, const void* v_new,
+                              int32_t num_q_heads, float scale, void* out, void* stream);
+/* begin + upload + attention of one layer in one call (a one-layer step, or
+ * a step and its first layer).  On PKV_ERR_CAPACITY the step is begun but
+ * nothing is launched: grow and rebind the tables, then call
+ * pkv_stepper_upload and pkv_stepper_attention. */
+int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer, const void* q,
+                         const void* k_new, const void* v_new, int32_t num_q_heads, float scale, void* out,
+                         void* stream, pkv_step_info* info, int32_t* rows_out, int32_t* lens_out,
+                         int32_t* token_blocks_out, int32_t* copies_out, int64_t copies_cap);
+/* The decode workspace's error word (synchronous read; 0 = no error). */
+int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error);
+/* Kernels the stepper has launched so far. */
+int64_t pkv_stepper_launches(pkv_stepper* st);
+/* Time the next `count` attention launches with CUDA events recorded right
+ * around the decode kernels on their stream (count 0 turns timing off). */
+int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count);
+/* Device milliseconds of the timed launches so far (waits for the last). */
+int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacity, int64_t* n_out);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

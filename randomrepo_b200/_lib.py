@@ -22,6 +22,7 @@ PKV_ERR_INDEX = 4
 PKV_ERR_ARG = 5
 PKV_ERR_CUDA = 6
 PKV_ERR_UNSUPPORTED = 7
+PKV_ERR_CAPACITY = 8
 
 PKV_F32 = 0
 PKV_F16 = 1
@@ -55,6 +56,26 @@ class AllocatorStats(ctypes.Structure):
         ("row_capacity", c_int64),
         ("max_blocks_per_row", c_int64),
         ("shared_block_count", c_int64),
+    ]
+
+
+class StepInfo(ctypes.Structure):
+    """``pkv_step_info``."""
+
+    _fields_ = [
+        ("batch", c_int32),
+        ("pages_per_split", c_int32),
+        ("n_items", c_int32),
+        ("n_combine", c_int32),
+        ("n_copies", c_int32),
+        ("need_rows", c_int32),
+        ("need_cols", c_int32),
+        ("reserved", c_int32),
+        ("rows", c_void_p),
+        ("seq_lens", c_void_p),
+        ("new_blocks", c_void_p),
+        ("items", c_void_p),
+        ("slots", c_void_p),
     ]
 
 
@@ -100,13 +121,35 @@ _SIGNATURES: dict[str, tuple] = {
          c_int64, c_void_p],
     ),
     "pkv_copy_blocks": (c_int32, [POINTER(PoolGeom), c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "pkv_decode_heads_per_item": (c_int32, [c_int32]),
+    "pkv_decode_plan": (
+        c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, I32P, c_void_p, c_int64, I64P, I64P]
+    ),
     "pkv_decode_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int64]),
     "pkv_decode_attention": (
         c_int32,
-        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
-         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int64, c_float, c_void_p, c_void_p, c_int64,
-         c_void_p],
+        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p,
+         c_void_p, c_int64, c_void_p],
     ),
+    "pkv_stepper_create": (c_void_p, [c_void_p, POINTER(PoolGeom), c_void_p, I32P]),
+    "pkv_stepper_destroy": (None, [c_void_p]),
+    "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "pkv_stepper_sync": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, I32P, I32P, I32P]),
+    "pkv_stepper_begin": (c_int32, [c_void_p, c_void_p, c_int32, POINTER(StepInfo), c_void_p, c_void_p, c_void_p]),
+    "pkv_stepper_upload": (c_int32, [c_void_p, c_void_p, POINTER(StepInfo), c_void_p, c_int64]),
+    "pkv_stepper_attention": (
+        c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_float, c_void_p, c_void_p]
+    ),
+    "pkv_stepper_step": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_float, c_void_p, c_void_p,
+         POINTER(StepInfo), c_void_p, c_void_p, c_void_p, c_void_p, c_int64],
+    ),
+    "pkv_stepper_error": (c_int32, [c_void_p, I32P]),
+    "pkv_stepper_launches": (c_int64, [c_void_p]),
+    "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64]),
+    "pkv_stepper_launch_times": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
 }
 
 # Entry points added after the first build; bound when present.

@@ -5,69 +5,86 @@
 // append into each resident cache (transformers cache_utils.py:119-120) and
 // sdpa_attention_forward with GQA (integrations/sdpa_attention.py:40-62).
 //
-// Work decomposition: one CTA per (split work item, KV head).  A work item is
-// `pages_per_split` consecutive 16-token pages of one sequence; the host lays
-// the items out with split_offsets.  The CTA serves all G = Hq/Hkv query heads
-// of its KV head from a single read of each page (GQA reuse).
+// Work: pkv_decode_plan (host) cuts every sequence's pages into work items of
+// at most `pages_per_split` (<= 32) pages for a group of HPC KV heads (HPC = 2
+// when the KV head count is even, else 1), largest items first.  A persistent
+// grid (one CTA per SM) runs independent warps; each warp takes the next item
+// from an atomic counter (dynamic, largest-first scheduling) and owns it
+// entirely, so no barrier ever couples warps.
 //
-// Inside the CTA, 4 warps take interleaved pages, each warp running its own
-// 3-stage TMA pipeline: one lane arms an mbarrier and issues 128-byte-swizzled
-// 3-D tensor loads of the page's K and V rows (no multicast).  Per page the
-// warp computes S^T[16 tokens x 8 heads] = K Q^T and O^T[D x 8] += V^T P^T
-// with mma.sync m16n8k16 (A fragments by ldmatrix from the swizzled stage,
-// P^T fragments by movmatrix.trans from the S^T accumulators), and keeps the
-// online softmax per head with warp shuffles (Milakov & Gimelshein 2018).
-// The 4 warps merge through shared memory; a sequence with several splits
-// writes (O, m, l) partials to the workspace and the last CTA to finish (an
-// atomic ticket, no spinning) combines them.
+// Per warp: a private ring of kStages shared-memory stages.  One stage holds
+// one block's K and V pages of the item's HPC heads -- adjacent in the pool
+// and stored pre-swizzled (pkv_device.cuh) -- filled by one cp.async.bulk
+// (no tensor map, no multicast) whose completion is counted on the stage's
+// mbarrier.  The warp keeps kStages copies in flight, and the stream runs on
+// across item boundaries: the next item's descriptor and block ids are
+// prefetched while the current item computes.  Per page and KV head the warp
+// computes S^T[16 tokens x 8 query heads] = K Q^T and O^T[D x 8] += V^T P^T
+// with mma.sync m16n8k16 (ldmatrix / ldmatrix.trans fragments straight from
+// the swizzled stage, P^T by movmatrix.trans) and keeps an online softmax per
+// query head with warp shuffles (Milakov & Gimelshein 2018); all G = Hq/Hkv
+// query heads of a KV head are served from one read of its pages.
+//
+// Item epilogue: a sequence with one item writes its output from registers;
+// otherwise the item writes its unnormalised (O, m, l) partial to the
+// workspace (plain stores, no fence) and a second, fully parallel kernel of the
+// same launch combines the partials of each such (sequence, head group).  An
+// in-kernel "last item combines" scheme puts a chain of dependent L2 reads on
+// one warp at the end of each sequence; it measured 2.5x slower here.
+//
+// Every mbarrier wait is bounded; on a timeout the warp records an error word
+// in the workspace, waits (bounded) for its copies in flight and exits.
 //
 // Arithmetic: fp32 scores and accumulation, P rounded to the input dtype for
 // the P.V product, output rounded once to the input dtype.
 #include "pkv_device.cuh"
 #include "pkv_error.h"
 
-#include <cudaTypedefs.h>
-
-#include <map>
-#include <mutex>
+#include <algorithm>
 #include <string>
-#include <tuple>
+#include <vector>
 
 namespace pkv {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kStages = 3;
 constexpr int kMaxSplitsPerSeq = 64;
+constexpr int kMaxPagesPerItem = 32;
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D>
-struct Geo {
-  static constexpr int kHalves = D / 64;            // 128-byte TMA boxes per row
-  static constexpr int kPageBytes = 16 * D * 2;     // one K (or V) page of one head
-  static constexpr int kStageBytes = 2 * kPageBytes;
+template <int D, int HPC>
+struct Cfg {
+  static constexpr int kPageBytes = 16 * D * 2;         // one K (or V) page of one head
+  static constexpr int kHeadBytes = 2 * kPageBytes;     // K + V of one head in one block
+  static constexpr int kStageBytes = HPC * kHeadBytes;  // one ring stage = one block, HPC heads
+  static constexpr int kWarps = kStageBytes >= 16384 ? 4 : 8;
+  static constexpr int kStages = (192 * 1024) / (kWarps * kStageBytes) > 8 ? 8 : (192 * 1024) / (kWarps * kStageBytes);
   static constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;
-  static constexpr int kVecsPerRow = D * 2 / 16;    // 16-byte chunks per token row
+  static constexpr int kVecsPerRow = D * 2 / 16;        // 16-byte chunks per token row
 };
 
+// Work item as laid out by pkv_decode_plan: {sequence, split << 8 | head_group,
+// nsplits, workspace slot of split 0}.  The splits of one (sequence, head
+// group) own consecutive workspace slots.
 struct DecodeParams {
   const void* q;
   const void* k_new;
   const void* v_new;
   void* out;
-  void* pool;
+  char* pool;
   int32_t* tables;
   int32_t* ctx_lens;
   const int32_t* rows;
   const int32_t* seq_lens;
   const int32_t* new_blocks;
-  const int32_t* split_offsets;
+  const int4* items;
   float* ws_ml;
   float* ws_o;
-  int32_t* ws_counters;
+  int32_t* ws_sched;     // [0] next item, [1] warps done
   int32_t* ws_error;
-  int32_t table_stride;
+  int32_t n_items;
   int32_t batch;
+  int32_t table_stride;
+  int32_t table_rows;
   int32_t hq;
   int32_t hkv;
   int32_t group;
@@ -77,406 +94,508 @@ struct DecodeParams {
   float scale_log2;
 };
 
-template <int D, typename T>
-__global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                                   const DecodeParams p) {
-  using G = Geo<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bars[kWarps * kStages];
-  __shared__ float s_m[kWarps][8];
-  __shared__ float s_l[kWarps][8];
-  __shared__ float s_w[kMaxSplitsPerSeq][8];
-  __shared__ int s_last;
+__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int item = blockIdx.x;
-  const int h = blockIdx.y;
-
-  // Sequence owning this work item: largest b with split_offsets[b] <= item.
-  int lo = 0, hi = p.batch - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(p.split_offsets + mid) <= item) lo = mid; else hi = mid - 1;
-  }
-  const int b = lo;
-  const int first_item = __ldg(p.split_offsets + b);
-  const int nsplits = __ldg(p.split_offsets + b + 1) - first_item;
-  const int split = item - first_item;
+// A work item must name a sequence of the batch whose table row exists, a
+// head group of the pool, a split inside the sequence's pages and a workspace
+// slot inside the item list.
+template <int HPC>
+__device__ __forceinline__ bool item_ok(const int4 item, const DecodeParams& p) {
+  const int b = item.x, split = item.y >> 8, hg = item.y & 0xff;
+  if (b < 0 || b >= p.batch || (hg + 1) * HPC > p.hkv || item.z < 1 || item.z > kMaxSplitsPerSeq) return false;
+  if (split < 0 || split >= item.z || item.w < 0 || item.w + item.z > p.n_items) return false;
   const int row = __ldg(p.rows + b);
   const int len = __ldg(p.seq_lens + b);
-  const int npages = (len + 15) >> 4;
-  const int pg0 = split * p.pages_per_split;
-  const int pg1 = min(pg0 + p.pages_per_split, npages);
-  const int last_page = npages - 1;
-  const int new_block = p.new_blocks ? __ldg(p.new_blocks + b) : -1;
-  int32_t* table_row = p.tables + (int64_t)row * p.table_stride;
-  if (nsplits > kMaxSplitsPerSeq) {  // the host never builds such offsets; refuse rather than overflow
-    if (tid == 0) atomicExch(p.ws_error, kDevBadSplits);
-    return;
-  }
-  const T* kn = static_cast<const T*>(p.k_new);
-  const T* vn = static_cast<const T*>(p.v_new);
+  return row >= 0 && row < p.table_rows && len > 0 && (len + 15) / 16 <= p.table_stride &&
+         split * p.pages_per_split < (len + 15) / 16;
+}
 
-  // Fused append: write the step's K/V row into its slot (for later steps;
-  // this step patches it into shared memory below).
-  if (kn != nullptr && pg1 == npages) {
-    const int pos = len - 1;
-    const int blk = new_block >= 0 ? new_block : table_row[pos >> 4];
-    const int slot = pos & 15;
-    if (tid < 2 * G::kVecsPerRow) {
-      const int state = tid / G::kVecsPerRow;
-      const int vec = tid % G::kVecsPerRow;
-      const T* src = (state == 0 ? kn : vn) + ((int64_t)b * p.hkv + h) * D;
-      const int64_t prow = pool_row_index(p.layer, blk, state, h, slot, p.num_blocks, p.hkv, 16);
-      reinterpret_cast<uint4*>(static_cast<T*>(p.pool) + prow * D)[vec] = reinterpret_cast<const uint4*>(src)[vec];
-    }
-    if (h == 0 && tid == 0) {
-      if (new_block >= 0) table_row[pos >> 4] = new_block;
-      p.ctx_lens[row] = len;
-    }
-  }
+// A block id from the table or the step descriptor must lie in the pool; a bad
+// one is replaced by block 0 (and reported) so that no copy leaves the pool.
+__device__ __forceinline__ int checked_block(int blk, const DecodeParams& p) {
+  if (blk >= 0 && blk < p.num_blocks) return blk;
+  atomicExch(p.ws_error, kDevBadBlock);
+  return 0;
+}
 
-  if (tid == 0) {
-    prefetch_tmap(&tmap);
-    for (int i = 0; i < kWarps * kStages; ++i) mbar_init(&bars[i], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
+// Everything a warp needs about one item, in registers (warp-uniform except blk).
+struct Item {
+  int idx;  // -1: none
+  int b, split, hg, nsplits, slot0, len, npages, pg0, pg1, row, newb;
+  int blk;  // this lane's block: page pg0 + lane
+};
 
-  // Q^T fragments (B operand, col layout): head = lane/4, dims 2*(lane%4)+{0,1} (+8).
-  constexpr int KK = D / 16;
-  uint32_t qf[KK][2];
-  {
-    const int g = lane >> 2;
-    const T* qrow = static_cast<const T*>(p.q) + ((int64_t)b * p.hq + h * p.group + g) * D;
-#pragma unroll
-    for (int kk = 0; kk < KK; ++kk) {
-      if (g < p.group) {
-        qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * (lane & 3));
-        qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * (lane & 3));
-      } else {
-        qf[kk][0] = 0u;
-        qf[kk][1] = 0u;
+// Take the next item from the launch's counter.  The warp that takes the
+// last out-of-range index resets the counters for the next launch (by then
+// no warp of this launch fetches again).
+__device__ __forceinline__ int fetch_item(const DecodeParams& p, int lane, int total_warps) {
+  int idx = 0;
+  if (lane == 0) {
+    idx = atomicAdd(p.ws_sched, 1);
+    if (idx >= p.n_items) {
+      const int done = atomicAdd(p.ws_sched + 1, 1);
+      if (done == total_warps - 1) {
+        atomicExch(p.ws_sched, 0);
+        atomicExch(p.ws_sched + 1, 0);
       }
     }
   }
+  idx = __shfl_sync(0xffffffffu, idx, 0);
+  return idx < p.n_items ? idx : -1;
+}
 
-  const int span = pg1 - pg0;
-  const int n_my = span > warp ? (span - warp + kWarps - 1) / kWarps : 0;
-  uint8_t* wsm = smem + warp * kStages * G::kStageBytes;
-  uint64_t* wbar = bars + warp * kStages;
-
-  auto issue = [&](int i) {
-    const int pg = pg0 + warp + i * kWarps;
-    const int st = i % kStages;
-    const int blk = (pg == last_page && new_block >= 0) ? new_block : table_row[pg];
-    uint8_t* dst = wsm + st * G::kStageBytes;
-    const int rk = ((blk * 2 + 0) * p.hkv + h) * 16;
-    const int rv = ((blk * 2 + 1) * p.hkv + h) * 16;
-    mbar_arrive_expect_tx(&wbar[st], G::kStageBytes);
-#pragma unroll
-    for (int j = 0; j < G::kHalves; ++j) {
-      tma_load_3d(dst + j * 2048, &tmap, 64 * j, rk, p.layer, &wbar[st]);
-      tma_load_3d(dst + G::kPageBytes + j * 2048, &tmap, 64 * j, rv, p.layer, &wbar[st]);
+template <int HPC>
+__device__ __forceinline__ Item next_item(const DecodeParams& p, int lane, int total_warps) {
+  Item m;
+  for (;;) {
+    m.idx = fetch_item(p, lane, total_warps);
+    if (m.idx < 0) return m;
+    const int4 it = p.items[m.idx];
+    if (item_ok<HPC>(it, p)) {
+      m.b = it.x;
+      m.split = it.y >> 8;
+      m.hg = it.y & 0xff;
+      m.nsplits = it.z;
+      m.slot0 = it.w;
+      break;
     }
-  };
+    if (lane == 0) atomicExch(p.ws_error, kDevBadItem);
+  }
+  m.len = __ldg(p.seq_lens + m.b);
+  m.row = __ldg(p.rows + m.b);
+  m.newb = p.new_blocks ? __ldg(p.new_blocks + m.b) : -1;
+  m.npages = (m.len + 15) >> 4;
+  m.pg0 = m.split * p.pages_per_split;
+  m.pg1 = min(m.pg0 + p.pages_per_split, m.npages);
+  const int pg = m.pg0 + lane;
+  m.blk = 0;
+  if (pg < m.pg1)
+    m.blk = checked_block((pg == m.npages - 1 && m.newb >= 0) ? m.newb
+                                                              : p.tables[(int64_t)m.row * p.table_stride + pg],
+                          p);
+  return m;
+}
 
-  int issued = min(kStages, n_my);
+template <int D, int HPC, typename T>
+__global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kernel(const DecodeParams p) {
+  using C = Cfg<D, HPC>;
+  constexpr int KK = D / 16;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bars[C::kWarps * S];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_warps = gridDim.x * C::kWarps;
+  uint8_t* ring = smem + warp * S * C::kStageBytes;
+  uint64_t* full = bars + warp * S;
   if (lane == 0) {
-    for (int i = 0; i < issued; ++i) issue(i);
+    for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+    fence_barrier_init();
   }
   __syncwarp();
 
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  float oacc[KK][4];
+  const T* kn = static_cast<const T*>(p.k_new);
+  const T* vn = static_cast<const T*>(p.v_new);
+  T* out = static_cast<T*>(p.out);
+  const int group = p.group;
+  const char* layer_base = p.pool + (int64_t)p.layer * p.num_blocks * p.hkv * C::kHeadBytes;
+
+  Item cur = next_item<HPC>(p, lane, total_warps);
+  Item nxt;
+  nxt.idx = -1;
+  if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, total_warps);
+  int issued = 0, consumed = 0;
+  bool iss_next = false;
+  int iss_pg = cur.pg0;
+
+  // Keep kStages copies in flight along the stream cur -> nxt.
+  auto issue_ahead = [&]() {
+    while (issued - consumed < S) {
+      const Item& m = iss_next ? nxt : cur;
+      if (m.idx < 0) break;
+      if (iss_pg >= m.pg1) {
+        if (iss_next) break;
+        iss_next = true;
+        iss_pg = nxt.pg0;
+        continue;
+      }
+      const int blk = __shfl_sync(0xffffffffu, m.blk, iss_pg - m.pg0);
+      if (lane == 0) {
+        const int st = issued % S;
+        mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+        bulk_copy_g2s(ring + st * C::kStageBytes,
+                      layer_base + ((int64_t)blk * p.hkv + m.hg * HPC) * C::kHeadBytes, C::kStageBytes, &full[st]);
+      }
+      ++issued;
+      ++iss_pg;
+    }
+  };
+
+  while (cur.idx >= 0) {
+    // Q^T fragments (B operand, col layout): query head lane/4, dims 2*(lane%4)+{0,1} (+8).
+    uint32_t qf[HPC][KK][2];
 #pragma unroll
-  for (int mt = 0; mt < KK; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
-
-  int failed_at = -1;
-  for (int i = 0; i < n_my; ++i) {
-    const int st = i % kStages;
-    const bool ok = mbar_wait_bounded(&wbar[st], (i / kStages) & 1);
-    if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform exit
-      failed_at = i;
-      break;
-    }
-    const int pg = pg0 + warp + i * kWarps;
-    const int valid = min(16, len - pg * 16);
-    uint8_t* stage = wsm + st * G::kStageBytes;
-    const uint32_t sk = smem_u32(stage);
-    const uint32_t sv = sk + G::kPageBytes;
-
-    if (pg == last_page) {
-      // Patch the step's token (the slot may have been read before the
-      // append above landed) and zero V rows past the context so that
-      // masked probabilities multiply finite values.
-      if (kn != nullptr && lane < 2 * G::kVecsPerRow) {
-        const int state = lane / G::kVecsPerRow;
-        const int vec = lane % G::kVecsPerRow;
-        const T* src = (state == 0 ? kn : vn) + ((int64_t)b * p.hkv + h) * D;
-        const int slot = valid - 1;
-        uint8_t* dst = stage + state * G::kPageBytes + (vec >> 3) * 2048 + swz128(slot, vec & 7);
-        *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(src)[vec];
-      }
-      for (int c = lane; c < (16 - valid) * G::kVecsPerRow; c += 32) {
-        const int r = valid + c / G::kVecsPerRow;
-        const int vec = c % G::kVecsPerRow;
-        *reinterpret_cast<uint4*>(stage + G::kPageBytes + (vec >> 3) * 2048 + swz128(r, vec & 7)) =
-            make_uint4(0u, 0u, 0u, 0u);
-      }
-      __syncwarp();
-    }
-
-    // S^T = K Q^T  (M = 16 tokens, N = 8 heads, K = D)
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const int tok = (lane & 7) + 8 * ((lane >> 3) & 1);
+    for (int hh = 0; hh < HPC; ++hh) {
+      const int gq = lane >> 2;
+      const bool in = gq < group;
+      const T* qrow =
+          static_cast<const T*>(p.q) + ((int64_t)cur.b * p.hq + (cur.hg * HPC + hh) * group + (in ? gq : 0)) * D;
 #pragma unroll
       for (int kk = 0; kk < KK; ++kk) {
-        const int dim = kk * 16 + 8 * (lane >> 4);
-        uint32_t a[4];
-        ldmatrix_x4(sk + (dim >> 6) * 2048 + swz128(tok, (dim & 63) >> 3), a[0], a[1], a[2], a[3]);
-        MmaOp<T>::run(sacc, a, qf[kk]);
+        qf[hh][kk][0] = in ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * (lane & 3)) : 0u;
+        qf[hh][kk][1] = in ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * (lane & 3)) : 0u;
       }
     }
-
-    // Online softmax per head column (heads 2*(lane%4) and +1).
-    const bool va = (lane >> 2) < valid;
-    const bool vb = (lane >> 2) + 8 < valid;
-    const float s0 = va ? sacc[0] * p.scale_log2 : -INFINITY;
-    const float s1 = va ? sacc[1] * p.scale_log2 : -INFINITY;
-    const float s2 = vb ? sacc[2] * p.scale_log2 : -INFINITY;
-    const float s3 = vb ? sacc[3] * p.scale_log2 : -INFINITY;
-    float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
+    float m_a[HPC], m_b[HPC], l_a[HPC], l_b[HPC];
+    float oacc[HPC][KK][4];
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+    for (int hh = 0; hh < HPC; ++hh) {
+      m_a[hh] = m_b[hh] = -INFINITY;
+      l_a[hh] = l_b[hh] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < KK; ++mt) oacc[hh][mt][0] = oacc[hh][mt][1] = oacc[hh][mt][2] = oacc[hh][mt][3] = 0.f;
     }
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float al_a = exp2f(m_a - mn_a), al_b = exp2f(m_b - mn_b);
-    const float p0 = exp2f(s0 - mn_a), p1 = exp2f(s1 - mn_b);
-    const float p2 = exp2f(s2 - mn_a), p3 = exp2f(s3 - mn_b);
-    l_a = l_a * al_a + p0 + p2;
-    l_b = l_b * al_b + p1 + p3;
-    m_a = mn_a;
-    m_b = mn_b;
-#pragma unroll
-    for (int mt = 0; mt < KK; ++mt) {
-      oacc[mt][0] *= al_a;
-      oacc[mt][1] *= al_b;
-      oacc[mt][2] *= al_a;
-      oacc[mt][3] *= al_b;
-    }
-    uint32_t pb[2];
-    pb[0] = movmatrix_trans(MmaOp<T>::pack(p0, p1));
-    pb[1] = movmatrix_trans(MmaOp<T>::pack(p2, p3));
 
-    // O^T += V^T P^T  (M = D dims in tiles of 16, N = 8 heads, K = 16 tokens)
-    {
-      const int tok = (lane & 7) + 8 * (lane >> 4);
-#pragma unroll
-      for (int mt = 0; mt < KK; ++mt) {
-        const int dim = mt * 16 + 8 * ((lane >> 3) & 1);
-        uint32_t a[4];
-        ldmatrix_x4_trans(sv + (dim >> 6) * 2048 + swz128(tok, (dim & 63) >> 3), a[0], a[1], a[2], a[3]);
-        MmaOp<T>::run(oacc[mt], a, pb);
+    for (int pg = cur.pg0; pg < cur.pg1; ++pg) {
+      issue_ahead();
+      const int st = consumed % S;
+      const bool ok = mbar_wait_bounded(&full[st], (consumed / S) & 1);
+      if (!__all_sync(0xffffffffu, ok)) {
+        // Record the failure, wait (bounded) for the copies still in flight, leave.
+        if (lane == 0) {
+          atomicExch(p.ws_error, kDevWaitTimeout);
+          for (int k = consumed + 1; k < issued; ++k) mbar_wait_bounded(&full[k % S], (k / S) & 1);
+        }
+        __syncwarp();
+        return;
       }
-    }
+      uint8_t* stage = ring + st * C::kStageBytes;
+      const int valid = min(16, cur.len - pg * 16);
 
-    if (i + kStages < n_my) {
+      if (pg == cur.npages - 1) {
+        // The step's token: write it to its slot in the pool (for later steps)
+        // and patch it into the stage (the copy may predate that write); then
+        // zero V rows past the context so masked probabilities multiply finite
+        // values.
+        const int slot = valid - 1;
+#pragma unroll
+        for (int hh = 0; hh < HPC; ++hh) {
+          if (kn != nullptr && lane < 2 * C::kVecsPerRow) {
+            const int state = lane / C::kVecsPerRow, vec = lane % C::kVecsPerRow;
+            const int h = cur.hg * HPC + hh;
+            const uint4 val =
+                reinterpret_cast<const uint4*>((state == 0 ? kn : vn) + ((int64_t)cur.b * p.hkv + h) * D)[vec];
+            const int64_t inpage = row_byte_offset(slot, vec * 16, 16, D * 2, true);
+            *reinterpret_cast<uint4*>(stage + hh * C::kHeadBytes + state * C::kPageBytes + inpage) = val;
+            const int blk = checked_block(
+                cur.newb >= 0 ? cur.newb : p.tables[(int64_t)cur.row * p.table_stride + pg], p);
+            *reinterpret_cast<uint4*>(p.pool + page_offset(p.layer, blk, h, state, p.num_blocks, p.hkv, 16, D * 2) +
+                                      inpage) = val;
+          }
+          for (int c = lane; c < (16 - valid) * C::kVecsPerRow; c += 32) {
+            const int r = valid + c / C::kVecsPerRow, vec = c % C::kVecsPerRow;
+            *reinterpret_cast<uint4*>(stage + hh * C::kHeadBytes + C::kPageBytes +
+                                      row_byte_offset(r, vec * 16, 16, D * 2, true)) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        if (kn != nullptr && cur.hg == 0 && lane == 0) {
+          if (cur.newb >= 0) p.tables[(int64_t)cur.row * p.table_stride + pg] = cur.newb;
+          p.ctx_lens[cur.row] = cur.len;
+        }
+        __syncwarp();
+      }
+
+      const bool va = (lane >> 2) < valid;
+      const bool vb = (lane >> 2) + 8 < valid;
+#pragma unroll
+      for (int hh = 0; hh < HPC; ++hh) {
+        const uint32_t sk = smem_u32(stage + hh * C::kHeadBytes);
+        const uint32_t sv = sk + C::kPageBytes;
+        // S^T = K Q^T  (M = 16 tokens, N = 8 query heads, K = D), two accumulator chains.
+        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          const int tok = (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+          for (int kk = 0; kk < KK; ++kk) {
+            const int dim = kk * 16 + 8 * (lane >> 4);
+            uint32_t a[4];
+            ldmatrix_x4(sk + (dim >> 6) * 2048 + swz128(tok, (dim & 63) >> 3), a[0], a[1], a[2], a[3]);
+            MmaOp<T>::run((kk & 1) ? s1 : s0, a, qf[hh][kk]);
+          }
+        }
+        const float x0 = va ? (s0[0] + s1[0]) * p.scale_log2 : -INFINITY;
+        const float x1 = va ? (s0[1] + s1[1]) * p.scale_log2 : -INFINITY;
+        const float x2 = vb ? (s0[2] + s1[2]) * p.scale_log2 : -INFINITY;
+        const float x3 = vb ? (s0[3] + s1[3]) * p.scale_log2 : -INFINITY;
+        float mx_a = fmaxf(x0, x2), mx_b = fmaxf(x1, x3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+          mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+        }
+        const float mn_a = fmaxf(m_a[hh], mx_a), mn_b = fmaxf(m_b[hh], mx_b);
+        const float al_a = exp2f(m_a[hh] - mn_a), al_b = exp2f(m_b[hh] - mn_b);
+        const float p0 = exp2f(x0 - mn_a), p1 = exp2f(x1 - mn_b);
+        const float p2 = exp2f(x2 - mn_a), p3 = exp2f(x3 - mn_b);
+        l_a[hh] = l_a[hh] * al_a + p0 + p2;
+        l_b[hh] = l_b[hh] * al_b + p1 + p3;
+        m_a[hh] = mn_a;
+        m_b[hh] = mn_b;
+        uint32_t pb[2];
+        pb[0] = movmatrix_trans(MmaOp<T>::pack(p0, p1));
+        pb[1] = movmatrix_trans(MmaOp<T>::pack(p2, p3));
+        // O^T += V^T P^T  (M = D dims in tiles of 16, N = 8 query heads, K = 16 tokens)
+        const int tok = (lane & 7) + 8 * (lane >> 4);
+#pragma unroll
+        for (int mt = 0; mt < KK; ++mt) {
+          oacc[hh][mt][0] *= al_a;
+          oacc[hh][mt][1] *= al_b;
+          oacc[hh][mt][2] *= al_a;
+          oacc[hh][mt][3] *= al_b;
+          const int dim = mt * 16 + 8 * ((lane >> 3) & 1);
+          uint32_t a[4];
+          ldmatrix_x4_trans(sv + (dim >> 6) * 2048 + swz128(tok, (dim & 63) >> 3), a[0], a[1], a[2], a[3]);
+          MmaOp<T>::run(oacc[hh][mt], a, pb);
+        }
+      }
+      // The stage is read; order those reads before the next bulk copy into it.
       __syncwarp();
       fence_proxy_async_smem();
-      if (lane == 0) issue(i + kStages);
-      ++issued;
-      __syncwarp();
+      ++consumed;
     }
-  }
 
-  if (failed_at >= 0) {
-    // Record the failure, then give the loads still in flight one more
-    // bounded wait each before this warp's stages are reused or released.
-    if (lane == 0) atomicExch(p.ws_error, kDevWaitTimeout);
-    for (int i = failed_at; i < issued; ++i) mbar_wait_bounded(&wbar[i % kStages], (i / kStages) & 1);
-  }
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
-  }
-  __syncthreads();  // every warp is done with its stages: reuse them for the merge
-
-  float* red = reinterpret_cast<float*>(smem);  // [kWarps][8][D]
-  {
-    float* wr = red + warp * 8 * D;
+    // ---- item epilogue ----
     const int ha = 2 * (lane & 3), hb = ha + 1;
+    if (cur.nsplits == 1) {
 #pragma unroll
-    for (int mt = 0; mt < KK; ++mt) {
-      const int d0 = mt * 16 + (lane >> 2);
-      wr[ha * D + d0] = oacc[mt][0];
-      wr[hb * D + d0] = oacc[mt][1];
-      wr[ha * D + d0 + 8] = oacc[mt][2];
-      wr[hb * D + d0 + 8] = oacc[mt][3];
-    }
-    if (lane < 4) {
-      s_m[warp][ha] = n_my > 0 ? m_a : -INFINITY;
-      s_m[warp][hb] = n_my > 0 ? m_b : -INFINITY;
-      s_l[warp][ha] = n_my > 0 ? l_a : 0.f;
-      s_l[warp][hb] = n_my > 0 ? l_b : 0.f;
-    }
-  }
-  __syncthreads();
-
-  const int group = p.group;
-  T* out = static_cast<T*>(p.out);
-  const int64_t wi = (int64_t)item * p.hkv + h;
-  for (int idx = tid; idx < group * D; idx += kWarps * 32) {
-    const int g = idx / D, d = idx % D;
-    float mm = -INFINITY;
+      for (int hh = 0; hh < HPC; ++hh) {
+        float la = l_a[hh], lb = l_b[hh];
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
-    float o = 0.f, l = 0.f;
+        for (int off = 4; off < 32; off <<= 1) {
+          la += __shfl_xor_sync(0xffffffffu, la, off);
+          lb += __shfl_xor_sync(0xffffffffu, lb, off);
+        }
+        const float ia = 1.f / la, ib = 1.f / lb;
+        T* oa = out + ((int64_t)cur.b * p.hq + (cur.hg * HPC + hh) * group + ha) * D;
+        T* ob = oa + D;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float wgt = exp2f(s_m[w][g] - mm);
-      o += wgt * red[(w * 8 + g) * D + d];
-      l += wgt * s_l[w][g];
-    }
-    if (nsplits == 1) {
-      out[((int64_t)b * p.hq + h * group + g) * D + d] = MmaOp<T>::from_float(o / l);
+        for (int mt = 0; mt < KK; ++mt) {
+          const int d0 = mt * 16 + (lane >> 2);
+          if (ha < group) {
+            oa[d0] = MmaOp<T>::from_float(oacc[hh][mt][0] * ia);
+            oa[d0 + 8] = MmaOp<T>::from_float(oacc[hh][mt][2] * ia);
+          }
+          if (hb < group) {
+            ob[d0] = MmaOp<T>::from_float(oacc[hh][mt][1] * ib);
+            ob[d0 + 8] = MmaOp<T>::from_float(oacc[hh][mt][3] * ib);
+          }
+        }
+      }
     } else {
-      p.ws_o[(wi * 8 + g) * D + d] = o;
-      if (d == 0) {
-        p.ws_ml[wi * 16 + g] = mm;
-        p.ws_ml[wi * 16 + 8 + g] = l;
+      const int64_t slot = (int64_t)cur.slot0 + cur.split;
+#pragma unroll
+      for (int hh = 0; hh < HPC; ++hh) {
+        float la = l_a[hh], lb = l_b[hh];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          la += __shfl_xor_sync(0xffffffffu, la, off);
+          lb += __shfl_xor_sync(0xffffffffu, lb, off);
+        }
+        float* wo = p.ws_o + (slot * HPC + hh) * 8 * D;
+#pragma unroll
+        for (int mt = 0; mt < KK; ++mt) {
+          const int d0 = mt * 16 + (lane >> 2);
+          wo[ha * D + d0] = oacc[hh][mt][0];
+          wo[hb * D + d0] = oacc[hh][mt][1];
+          wo[ha * D + d0 + 8] = oacc[hh][mt][2];
+          wo[hb * D + d0 + 8] = oacc[hh][mt][3];
+        }
+        if (lane < 4) {
+          float* ml = p.ws_ml + (slot * HPC + hh) * 16;
+          ml[ha] = m_a[hh];
+          ml[hb] = m_b[hh];
+          ml[8 + ha] = la;
+          ml[8 + hb] = lb;
+        }
       }
     }
-  }
-  if (nsplits == 1) return;
 
-  // Split-K combine by the last CTA of this (sequence, KV head).
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int ticket = atomicAdd(p.ws_counters + (int64_t)b * p.hkv + h, 1);
-    s_last = ticket == nsplits - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int64_t base = (int64_t)first_item * p.hkv + h;
-  if (tid < group) {
-    const int g = tid;
-    float mm = -INFINITY;
-    for (int s = 0; s < nsplits; ++s) mm = fmaxf(mm, __ldcg(p.ws_ml + (base + (int64_t)s * p.hkv) * 16 + g));
-    float l = 0.f;
-    for (int s = 0; s < nsplits; ++s) {
-      const int64_t si = base + (int64_t)s * p.hkv;
-      const float wgt = exp2f(__ldcg(p.ws_ml + si * 16 + g) - mm);
-      s_w[s][g] = wgt;
-      l += wgt * __ldcg(p.ws_ml + si * 16 + 8 + g);
+    // ---- advance the stream ----
+    cur = nxt;
+    if (iss_next) {
+      iss_next = false;
+    } else {
+      iss_pg = cur.pg0;
     }
-    s_l[0][g] = 1.f / l;
+    nxt.idx = -1;
+    if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, total_warps);
+  }
+}
+
+// Split-K combine: one CTA per (sequence, head group) that has several items.
+// Entries {sequence, head_group, nsplits, workspace slot of split 0} follow the
+// decode items in the plan.  out = sum_s w_s O_s / sum_s w_s l_s with
+// w_s = 2^(m_s - max_s m_s), for every query head of the group and dim.
+// Latency, not bandwidth, bounds this kernel (a few MB from L2), so every
+// phase issues all of its loads before it uses any: the splits' (m, l) go to
+// shared memory in one parallel pass, and each thread loads the float4 of every
+// split for its outputs back to back.
+constexpr int kCombineThreads = 128;
+
+template <int D, int HPC, typename T>
+__global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(const DecodeParams p,
+                                                                               const int4* entries, int n_entries) {
+  __shared__ float s_ml[kMaxSplitsPerSeq][HPC][16];
+  __shared__ float s_w[kMaxSplitsPerSeq][HPC][8];
+  __shared__ float s_inv[HPC][8];
+  const int e = blockIdx.x;
+  if (e >= n_entries) return;
+  const int4 en = entries[e];
+  const int b = en.x, hg = en.y, ns = en.z, slot0 = en.w;
+  if (b < 0 || b >= p.batch || (hg + 1) * HPC > p.hkv || ns < 2 || ns > kMaxSplitsPerSeq || slot0 < 0 ||
+      slot0 + ns > p.n_items) {
+    if (threadIdx.x == 0) atomicExch(p.ws_error, kDevBadItem);
+    return;
+  }
+  const int group = p.group;
+  // (m, l) of every split: ns * HPC * 16 consecutive floats.
+  const float* ml = p.ws_ml + (int64_t)slot0 * HPC * 16;
+  for (int i = threadIdx.x; i < ns * HPC * 16; i += kCombineThreads) (&s_ml[0][0][0])[i] = __ldcg(ml + i);
+  __syncthreads();
+  if (threadIdx.x < HPC * group) {
+    const int hh = threadIdx.x / group, gq = threadIdx.x - hh * group;
+    float mm = -INFINITY;
+    for (int s = 0; s < ns; ++s) mm = fmaxf(mm, s_ml[s][hh][gq]);
+    float l = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float w = exp2f(s_ml[s][hh][gq] - mm);
+      s_w[s][hh][gq] = w;
+      l += w * s_ml[s][hh][8 + gq];
+    }
+    s_inv[hh][gq] = 1.f / l;
   }
   __syncthreads();
-  for (int idx = tid; idx < group * D; idx += kWarps * 32) {
-    const int g = idx / D, d = idx % D;
-    float o = 0.f;
-    for (int s = 0; s < nsplits; ++s)
-      o += s_w[s][g] * __ldcg(p.ws_o + ((base + (int64_t)s * p.hkv) * 8 + g) * D + d);
-    out[((int64_t)b * p.hq + h * group + g) * D + d] = MmaOp<T>::from_float(o * s_l[0][g]);
+  T* out = static_cast<T*>(p.out);
+  constexpr int kVec = 4;
+  const int n_vec = HPC * group * (D / kVec);
+  for (int v = threadIdx.x; v < n_vec; v += kCombineThreads) {
+    const int hh = v / (group * (D / kVec));
+    const int r = v - hh * group * (D / kVec);
+    const int gq = r / (D / kVec), d = (r - gq * (D / kVec)) * kVec;
+    const float4* src = reinterpret_cast<const float4*>(p.ws_o + (((int64_t)slot0 * HPC + hh) * 8 + gq) * D + d);
+    const int64_t stride4 = (int64_t)HPC * 8 * D / kVec;  // one split further
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int s = 0;
+    for (; s + 8 <= ns; s += 8) {
+      float4 x[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (s + k) * stride4);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = s_w[s + k][hh][gq];
+        acc.x += w * x[k].x;
+        acc.y += w * x[k].y;
+        acc.z += w * x[k].z;
+        acc.w += w * x[k].w;
+      }
+    }
+    {
+      float4 x[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = s + k < ns ? __ldcg(src + (s + k) * stride4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = s + k < ns ? s_w[s + k][hh][gq] : 0.f;
+        acc.x += w * x[k].x;
+        acc.y += w * x[k].y;
+        acc.z += w * x[k].z;
+        acc.w += w * x[k].w;
+      }
+    }
+    const float inv = s_inv[hh][gq];
+    T* dst = out + ((int64_t)b * p.hq + (hg * HPC + hh) * group + gq) * D + d;
+    dst[0] = MmaOp<T>::from_float(acc.x * inv);
+    dst[1] = MmaOp<T>::from_float(acc.y * inv);
+    dst[2] = MmaOp<T>::from_float(acc.z * inv);
+    dst[3] = MmaOp<T>::from_float(acc.w * inv);
   }
-  if (tid == 0) p.ws_counters[(int64_t)b * p.hkv + h] = 0;
 }
 
 // ---------------------------------------------------------------------------
-// Host side: tensor maps and launch.
+// Host side.
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
+int num_sms_cached() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
 }
 
-// Pool viewed as a 3-D tensor {head_dim, rows of one layer, layers} with
-// 128-byte-swizzled boxes of {64 elements, 16 rows, 1}: one box is one half
-// (64 dims) of one K or V page of one KV head.
-bool make_pool_map(const pkv_pool_geom* g, void* pool, CUtensorMap* out) {
-  using Key = std::tuple<uintptr_t, int, int, int, int, int>;
-  static std::map<Key, CUtensorMap> cache;
-  static std::mutex mu;
-  Key key{(uintptr_t)pool, g->num_layers, g->num_blocks, g->num_kv_heads, g->head_dim, g->dtype};
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(key);
-  if (it != cache.end()) {
-    *out = it->second;
-    return true;
-  }
-  auto encode = get_encode_fn();
-  if (!encode) {
-    pkv_set_error("cuTensorMapEncodeTiled is unavailable from the driver");
-    return false;
-  }
-  const uint64_t rows = (uint64_t)g->num_blocks * 2 * g->num_kv_heads * 16;
-  cuuint64_t dims[3] = {(cuuint64_t)g->head_dim, rows, (cuuint64_t)g->num_layers};
-  cuuint64_t strides[2] = {(cuuint64_t)g->head_dim * 2, rows * g->head_dim * 2};
-  cuuint32_t box[3] = {64, 16, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUtensorMap map;
-  CUresult r = encode(&map, g->dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                      3, pool, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    pkv_set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
-    return false;
-  }
-  if (cache.size() > 64) cache.clear();
-  cache.emplace(key, map);
-  *out = map;
-  return true;
-}
+int heads_per_item(int num_kv_heads) { return num_kv_heads % 2 == 0 ? 2 : 1; }
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+int warps_per_cta(int head_dim, int hpc) {
+  const int stage = hpc * 2 * 16 * head_dim * 2;
+  return stage >= 16384 ? 4 : 8;
+}
+
 struct WsLayout {
-  int64_t counters, ml, o, total;
+  int64_t sched, ml, o, total;
 };
 
-WsLayout ws_layout(int32_t batch, int32_t hkv, int32_t head_dim, int64_t splits) {
+// Workspace: [error word][scheduler counters][partial m, l][partial O].
+WsLayout ws_layout(int32_t batch, int32_t hkv, int32_t head_dim, int64_t n_items) {
+  (void)batch;
+  const int hpc = heads_per_item(hkv);
   WsLayout w;
-  w.counters = 256;
-  w.ml = w.counters + align256((int64_t)batch * hkv * 4);
-  w.o = w.ml + align256(splits * hkv * 16 * 4);
-  w.total = w.o + align256(splits * hkv * 8 * head_dim * 4);
+  w.sched = 64;
+  w.ml = 256;
+  w.o = w.ml + align256(n_items * hpc * 16 * 4);
+  w.total = w.o + align256(n_items * hpc * 8 * head_dim * 4);
   return w;
 }
 
-template <int D, typename T>
-int32_t launch_decode(const CUtensorMap& map, const DecodeParams& prm, int64_t total_splits, cudaStream_t s) {
-  using G = Geo<D>;
+template <int D, int HPC, typename T>
+int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entries, cudaStream_t s) {
+  using C = Cfg<D, HPC>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<D, HPC, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) {
+      pkv_set_error(std::string("pkv_decode_attention: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      return PKV_ERR_CUDA;
+    }
     attr_set = true;
   }
-  dim3 grid((unsigned)total_splits, (unsigned)prm.hkv);
-  paged_decode_kernel<D, T><<<grid, kWarps * 32, G::kSmemBytes, s>>>(map, prm);
+  const int grid = std::max(1, std::min((prm.n_items + C::kWarps - 1) / C::kWarps, num_sms_cached()));
+  paged_decode_kernel<D, HPC, T><<<grid, C::kWarps * 32, C::kSmemBytes, s>>>(prm);
+  if (n_entries > 0)
+    paged_decode_combine_kernel<D, HPC, T><<<n_entries, kCombineThreads, 0, s>>>(prm, entries, n_entries);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     pkv_set_error(std::string("pkv_decode_attention launch: ") + cudaGetErrorString(e));
     return PKV_ERR_CUDA;
   }
   return PKV_OK;
+}
+
+template <int D, typename T>
+int32_t launch_for_heads(const DecodeParams& prm, const int4* entries, int n_entries, cudaStream_t s) {
+  return heads_per_item(prm.hkv) == 2 ? launch_decode<D, 2, T>(prm, entries, n_entries, s)
+                                      : launch_decode<D, 1, T>(prm, entries, n_entries, s);
 }
 
 }  // namespace
@@ -486,16 +605,121 @@ using namespace pkv;
 
 extern "C" {
 
-int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t head_dim, int64_t max_splits_total) {
-  return ws_layout(batch, num_kv_heads, head_dim, max_splits_total).total;
+int32_t pkv_decode_heads_per_item(int32_t num_kv_heads) { return heads_per_item(num_kv_heads); }
+
+int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t num_sms, int32_t* pages_per_split_out, int32_t* items_out, int64_t items_capacity,
+                        int64_t* n_items_out, int64_t* n_combine_out) {
+  pkv_clear_error();
+  if (batch <= 0 || num_kv_heads <= 0 || !seq_lens || !pages_per_split_out || !n_items_out || !n_combine_out) {
+    pkv_set_error("pkv_decode_plan: invalid arguments");
+    return PKV_ERR_ARG;
+  }
+  const int hpc = heads_per_item(num_kv_heads);
+  const int groups = num_kv_heads / hpc;
+  if (num_sms <= 0) num_sms = 148;
+  int64_t total_pages = 0;
+  int32_t max_pages = 1;
+  for (int b = 0; b < batch; ++b) {
+    if (seq_lens[b] <= 0) {
+      pkv_set_error("pkv_decode_plan: every sequence needs at least one token (the step's token)");
+      return PKV_ERR_ARG;
+    }
+    const int32_t pages = (seq_lens[b] + 15) / 16;
+    total_pages += pages;
+    max_pages = std::max(max_pages, pages);
+  }
+  if (max_pages > kMaxPagesPerItem * kMaxSplitsPerSeq) {
+    pkv_set_error("pkv_decode_plan: a sequence exceeds " + std::to_string(16 * kMaxPagesPerItem * kMaxSplitsPerSeq) +
+                  " tokens");
+    return PKV_ERR_UNSUPPORTED;
+  }
+  // About 3 items per warp of the persistent grid (dynamic scheduling evens
+  // out the rest), 4..32 pages per item, at most kMaxSplitsPerSeq items per
+  // sequence and head group.
+  const int64_t work = total_pages * groups;
+  const int64_t warps = (int64_t)num_sms * warps_per_cta(head_dim, hpc);
+  int32_t pps = (int32_t)std::min<int64_t>(kMaxPagesPerItem,
+                                           std::max<int64_t>(4, (work + warps * 3 - 1) / (warps * 3)));
+  pps = std::max(pps, (max_pages + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq);
+  int64_t n = 0, nc = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int64_t ns = ((seq_lens[b] + 15) / 16 + pps - 1) / pps;
+    n += groups * ns;
+    if (ns > 1) nc += groups;
+  }
+  *pages_per_split_out = pps;
+  *n_items_out = n;
+  *n_combine_out = nc;
+  if (!items_out) return PKV_OK;
+  if (items_capacity < n + nc) {
+    pkv_set_error("pkv_decode_plan: item buffer too small");
+    return PKV_ERR_ARG;
+  }
+  // Full items first, then the partial last splits by decreasing size: the
+  // warps take items in this order, largest first.
+  struct Item {
+    int32_t pages, b, split, hg, nsplits, slot0;
+  };
+  std::vector<Item> full, part;
+  full.reserve(n);
+  int32_t slot = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int32_t pages = (seq_lens[b] + 15) / 16;
+    const int32_t ns = (pages + pps - 1) / pps;
+    for (int hg = 0; hg < groups; ++hg) {
+      for (int s = 0; s < ns; ++s) {
+        const int32_t pg = std::min(pps, pages - s * pps);
+        Item it{pg, b, s, hg, ns, slot};
+        (pg == pps ? full : part).push_back(it);
+      }
+      slot += ns;
+    }
+  }
+  if ((int64_t)(full.size() + part.size()) != n) {
+    pkv_set_error("pkv_decode_plan: internal item count mismatch");
+    return PKV_ERR_ARG;
+  }
+  std::stable_sort(part.begin(), part.end(), [](const Item& x, const Item& y) { return x.pages > y.pages; });
+  int32_t* o = items_out;
+  for (const auto* v : {&full, &part}) {
+    for (const Item& it : *v) {
+      o[0] = it.b;
+      o[1] = (it.split << 8) | it.hg;
+      o[2] = it.nsplits;
+      o[3] = it.slot0;
+      o += 4;
+    }
+  }
+  // Combine entries {sequence, head_group, nsplits, slot of split 0}.
+  slot = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int32_t ns = ((seq_lens[b] + 15) / 16 + pps - 1) / pps;
+    for (int hg = 0; hg < groups; ++hg) {
+      if (ns > 1) {
+        o[0] = b;
+        o[1] = hg;
+        o[2] = ns;
+        o[3] = slot;
+        o += 4;
+      }
+      slot += ns;
+    }
+  }
+  return PKV_OK;
+}
+
+int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t head_dim, int64_t n_items) {
+  return ws_layout(batch, num_kv_heads, head_dim, n_items).total;
 }
 
 int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q, const void* k_new,
-                             const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t* context_lens,
+                             const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                             int32_t* context_lens,
                              const int32_t* rows, const int32_t* seq_lens, const int32_t* new_blocks,
-                             const int32_t* split_offsets, int32_t batch, int32_t num_q_heads,
-                             int32_t pages_per_split, int64_t total_splits, float scale, void* out,
-                             void* workspace, int64_t workspace_bytes, void* stream) {
+                             const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
+                             int32_t num_q_heads, int32_t pages_per_split, float scale, void* out, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
   pkv_clear_error();
   if (!g || g->block_size != 16) {
     pkv_set_error("paged decode attention needs block_size 16");
@@ -509,56 +733,52 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
     pkv_set_error("paged decode attention supports head_dim 64 and 128");
     return PKV_ERR_UNSUPPORTED;
   }
-  if (num_q_heads <= 0 || num_q_heads % g->num_kv_heads != 0 || num_q_heads / g->num_kv_heads > 8) {
+  if (num_q_heads <= 0 || num_q_heads % g->num_kv_heads != 0 || num_q_heads / g->num_kv_heads > 8 ||
+      g->num_kv_heads > 255 * 2) {
     pkv_set_error("num_q_heads must be a multiple of num_kv_heads with at most 8 query heads per KV head");
     return PKV_ERR_UNSUPPORTED;
   }
-  if (layer < 0 || layer >= g->num_layers || batch <= 0 || pages_per_split <= 0 || total_splits < batch ||
-      total_splits > INT32_MAX) {
-    pkv_set_error("invalid layer, batch or split arguments");
+  if (layer < 0 || layer >= g->num_layers || batch <= 0 || pages_per_split <= 0 ||
+      pages_per_split > kMaxPagesPerItem || n_items < batch || n_combine < 0 || n_combine > n_items) {
+    pkv_set_error("invalid layer, batch, item or split arguments");
     return PKV_ERR_ARG;
   }
-  if (!pool || !q || !out || !block_tables || !rows || !seq_lens || !split_offsets || !workspace ||
+  if (!pool || !q || !out || !block_tables || !rows || !seq_lens || !work_items || !workspace ||
       (k_new != nullptr) != (v_new != nullptr) || (k_new && !context_lens)) {
     pkv_set_error("null pointer argument");
     return PKV_ERR_ARG;
   }
   if ((uintptr_t)pool % 16 != 0 || (uintptr_t)q % 16 != 0 || (uintptr_t)out % 16 != 0 ||
-      (k_new && ((uintptr_t)k_new % 16 || (uintptr_t)v_new % 16))) {
-    pkv_set_error("pool, q, out, k_new and v_new must be 16-byte aligned");
+      (uintptr_t)work_items % 16 != 0 || (k_new && ((uintptr_t)k_new % 16 || (uintptr_t)v_new % 16))) {
+    pkv_set_error("pool, q, out, work_items, k_new and v_new must be 16-byte aligned");
     return PKV_ERR_ARG;
   }
-  if ((int64_t)g->num_blocks * 2 * g->num_kv_heads * 16 >= INT32_MAX) {
-    pkv_set_error("pool too large for 32-bit TMA row coordinates");
-    return PKV_ERR_UNSUPPORTED;
-  }
-  const WsLayout wl = ws_layout(batch, g->num_kv_heads, g->head_dim, total_splits);
+  const WsLayout wl = ws_layout(batch, g->num_kv_heads, g->head_dim, n_items);
   if (workspace_bytes < wl.total) {
     pkv_set_error("workspace too small: need " + std::to_string(wl.total) + " bytes");
     return PKV_ERR_ARG;
   }
-  CUtensorMap map;
-  if (!make_pool_map(g, pool, &map)) return PKV_ERR_CUDA;
-
   DecodeParams prm;
   prm.q = q;
   prm.k_new = k_new;
   prm.v_new = v_new;
   prm.out = out;
-  prm.pool = pool;
+  prm.pool = static_cast<char*>(pool);
   prm.tables = block_tables;
   prm.ctx_lens = context_lens;
   prm.rows = rows;
   prm.seq_lens = seq_lens;
   prm.new_blocks = new_blocks;
-  prm.split_offsets = split_offsets;
+  prm.items = reinterpret_cast<const int4*>(work_items);
   char* ws = static_cast<char*>(workspace);
   prm.ws_error = reinterpret_cast<int32_t*>(ws);
-  prm.ws_counters = reinterpret_cast<int32_t*>(ws + wl.counters);
+  prm.ws_sched = reinterpret_cast<int32_t*>(ws + wl.sched);
   prm.ws_ml = reinterpret_cast<float*>(ws + wl.ml);
   prm.ws_o = reinterpret_cast<float*>(ws + wl.o);
-  prm.table_stride = table_stride;
+  prm.n_items = n_items;
   prm.batch = batch;
+  prm.table_stride = table_stride;
+  prm.table_rows = table_rows;
   prm.hq = num_q_heads;
   prm.hkv = g->num_kv_heads;
   prm.group = num_q_heads / g->num_kv_heads;
@@ -567,12 +787,12 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
   prm.pages_per_split = pages_per_split;
   prm.scale_log2 = scale * kLog2e;
   auto s = static_cast<cudaStream_t>(stream);
-  if (g->head_dim == 128) {
-    return g->dtype == PKV_BF16 ? launch_decode<128, __nv_bfloat16>(map, prm, total_splits, s)
-                                : launch_decode<128, __half>(map, prm, total_splits, s);
-  }
-  return g->dtype == PKV_BF16 ? launch_decode<64, __nv_bfloat16>(map, prm, total_splits, s)
-                              : launch_decode<64, __half>(map, prm, total_splits, s);
+  const int4* entries = reinterpret_cast<const int4*>(work_items) + n_items;
+  if (g->head_dim == 128)
+    return g->dtype == PKV_BF16 ? launch_for_heads<128, __nv_bfloat16>(prm, entries, n_combine, s)
+                                : launch_for_heads<128, __half>(prm, entries, n_combine, s);
+  return g->dtype == PKV_BF16 ? launch_for_heads<64, __nv_bfloat16>(prm, entries, n_combine, s)
+                              : launch_for_heads<64, __half>(prm, entries, n_combine, s);
 }
 
 }  // extern "C"

@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(256) move_tokens_kernel(char* __restrict__ poo
                                                           int64_t head_stride_b, int64_t token_stride_b) {
   using V = typename VecT<W>::type;
   const int64_t vecs = row_bytes / W;
+  const bool swizzled = page_swizzled(block_size, row_bytes);
   const int64_t total = (int64_t)n_layers * n_tokens * 2 * num_kv_heads * vecs;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     int64_t r = i;
@@ -90,9 +91,9 @@ __global__ void __launch_bounds__(256) move_tokens_kernel(char* __restrict__ poo
     if (slot < 0) continue;
     const int64_t block = slot / block_size;
     const int64_t off = slot % block_size;
-    const int64_t prow =
-        pool_row_index(layer0 + layer, block, state, head, off, num_blocks, num_kv_heads, block_size);
-    V* p = reinterpret_cast<V*>(pool + prow * row_bytes) + vec;
+    const int64_t page = page_offset(layer0 + layer, block, head, state, num_blocks, num_kv_heads, block_size,
+                                     row_bytes);
+    V* p = reinterpret_cast<V*>(pool + page + row_byte_offset(off, vec * W, block_size, row_bytes, swizzled));
     char* base = state == 0 ? k_buf : v_buf;
     V* b = reinterpret_cast<V*>(base + layer * layer_stride_b + head * head_stride_b + tok * token_stride_b) + vec;
     if (kToPool) {
@@ -146,8 +147,8 @@ int32_t move_tokens(const pkv_pool_geom* g, void* pool, int32_t layer0, int32_t 
   return launch_status(kToPool ? "pkv_scatter_tokens" : "pkv_gather_tokens");
 }
 
-// Copy whole blocks: per (pair, layer) the (state, head, slot, dim) sub-array
-// of a block is one contiguous run of 2*Hkv*bs*D elements.
+// Copy whole blocks: per (pair, layer) the (head, state, slot, dim) sub-array
+// of a block is one contiguous run of Hkv*2*bs*D elements.
 __global__ void __launch_bounds__(256) copy_blocks_kernel(uint4* __restrict__ pool, const int32_t* __restrict__ src,
                                                           const int32_t* __restrict__ dst, int64_t n_pairs,
                                                           int32_t pair_stride, int32_t num_layers,

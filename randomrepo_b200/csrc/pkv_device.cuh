@@ -20,6 +20,8 @@ enum DeviceError : int32_t {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // an mbarrier wait hit its iteration limit
   kDevBadSplits = 2,    // a sequence was given more split work items than a kernel supports
+  kDevBadItem = 3,      // a work item named a sequence, head group or split outside the launch
+  kDevBadBlock = 4,     // a block id outside the pool (replaced by block 0, no access left the pool)
 };
 
 // Upper bound of one mbarrier wait, in SM clock cycles (~1 s at 2 GHz).
@@ -148,10 +150,37 @@ struct MmaOp<__half> {
   __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
 };
 
-__host__ __device__ __forceinline__ int64_t pool_row_index(int64_t layer, int64_t block, int64_t state, int64_t head,
-                                                           int64_t slot, int64_t num_blocks, int64_t num_kv_heads,
-                                                           int64_t block_size) {
-  return (((layer * num_blocks + block) * 2 + state) * num_kv_heads + head) * block_size + slot;
+// KV pool layout: pool[layer][block][kv_head][state (0=K, 1=V)][slot][head_dim].
+// One (layer, block, kv_head, state) run of block_size rows is a "page"; the
+// K and V pages of one head in one block are adjacent, and so are the heads
+// of one block, so a block's pages for a group of heads move with one bulk copy.
+//
+// When a row is a multiple of 128 bytes and block_size a multiple of 8, a page
+// is stored pre-swizzled: it is cut into 128-byte column slabs (64 bf16 dims
+// each), a slab holds the page's rows at 128 bytes apiece, and the 16-byte
+// chunks of row t are permuted by XOR with (t mod 8).  That is the 128-byte
+// swizzle TMA applies, so a linear copy of a page into 1024-byte aligned shared
+// memory is directly bank-conflict free for ldmatrix and is the canonical
+// SWIZZLE_128B operand layout of tcgen05 (K-major for K, MN-major for V).
+// Other geometries (rows of 64 bytes, block sizes such as 2) use plain
+// row-major pages.
+__host__ __device__ __forceinline__ bool page_swizzled(int64_t block_size, int64_t row_bytes) {
+  return row_bytes % 128 == 0 && block_size % 8 == 0;
+}
+
+// Byte offset of page (layer, block, head, state) from the pool base.
+__host__ __device__ __forceinline__ int64_t page_offset(int64_t layer, int64_t block, int64_t head, int64_t state,
+                                                        int64_t num_blocks, int64_t num_kv_heads, int64_t block_size,
+                                                        int64_t row_bytes) {
+  return (((layer * num_blocks + block) * num_kv_heads + head) * 2 + state) * block_size * row_bytes;
+}
+
+// Byte offset, inside a page, of byte `b` of row `t`.
+__host__ __device__ __forceinline__ int64_t row_byte_offset(int64_t t, int64_t b, int64_t block_size, int64_t row_bytes,
+                                                            bool swizzled) {
+  if (!swizzled) return t * row_bytes + b;
+  const int64_t chunk = b >> 4;
+  return (chunk >> 3) * block_size * 128 + t * 128 + (((chunk & 7) ^ (t & 7)) << 4) + (b & 15);
 }
 
 }  // namespace pkv

@@ -1,0 +1,373 @@
+// Native host path of one decode step (C ABI in include/pkv_b200.h).
+//
+// One call per step does what the Python layer would otherwise do in many:
+// the allocator's per-token append for every sequence of the batch, the
+// device upload and application of any pending block-table updates, the
+// split-K plan, and one staged upload of the step descriptor; one call per
+// layer then launches the fused decode kernels.  Host buffers are pinned and
+// recycled through a small ring guarded by CUDA events, device buffers are
+// recycled in stream order, so a step costs a few microseconds of host time
+// and never synchronises the host with the device.
+//
+// Everything a stepper launches goes to the stream passed to begin(); use one
+// stream per stepper.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "pkv_b200.h"
+#include "pkv_error.h"
+
+namespace {
+
+constexpr int kRing = 8;
+
+struct Slot {
+  int32_t* host = nullptr;
+  int32_t* dev = nullptr;
+  int64_t cap = 0;  // int32 elements
+  cudaEvent_t done = nullptr;
+  bool pending = false;
+};
+
+int32_t cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PKV_OK;
+  pkv_set_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return PKV_ERR_CUDA;
+}
+
+}  // namespace
+
+struct pkv_stepper {
+  pkv_allocator* alloc = nullptr;
+  pkv_pool_geom geom{};
+  void* pool = nullptr;
+  int num_sms = 148;
+  int32_t* tables = nullptr;
+  int32_t stride = 0;
+  int32_t rows = 0;
+  int32_t* lens = nullptr;
+  int32_t* refs = nullptr;
+  Slot slot[kRing];
+  int next = 0;
+  std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
+  pkv_step_info info{};
+  bool step_ready = false;
+  void* ws = nullptr;
+  int64_t ws_bytes = 0;
+  cudaStream_t ws_stream = nullptr;
+  int64_t launches = 0;
+  // Optional per-launch timing of the decode kernels (events around them).
+  std::vector<cudaEvent_t> t_start, t_stop;
+  int64_t t_cap = 0, t_count = 0;
+
+  ~pkv_stepper() {
+    for (auto& s : slot) {
+      if (s.done) {
+        cudaEventSynchronize(s.done);
+        cudaEventDestroy(s.done);
+      }
+      if (s.host) cudaFreeHost(s.host);
+      if (s.dev) cudaFree(s.dev);
+    }
+    if (ws) cudaFree(ws);
+    for (auto e : t_start) cudaEventDestroy(e);
+    for (auto e : t_stop) cudaEventDestroy(e);
+  }
+
+  // A ring slot with room for `n` int32, its previous upload finished.
+  int32_t take_slot(int64_t n, Slot** out) {
+    Slot& s = slot[next];
+    next = (next + 1) % kRing;
+    if (s.pending) {
+      int32_t st = cuda_status(cudaEventSynchronize(s.done), "stepper ring");
+      if (st) return st;
+      s.pending = false;
+    }
+    if (s.cap < n) {
+      const int64_t cap = std::max<int64_t>(n, 2 * s.cap);
+      if (s.host) cudaFreeHost(s.host);
+      if (s.dev) cudaFree(s.dev);  // implicit device sync: only when a slot grows
+      s.host = nullptr;
+      s.dev = nullptr;
+      int32_t st = cuda_status(cudaHostAlloc((void**)&s.host, cap * 4, cudaHostAllocDefault), "cudaHostAlloc");
+      if (!st) st = cuda_status(cudaMalloc((void**)&s.dev, cap * 4), "cudaMalloc");
+      if (st) return st;
+      s.cap = cap;
+    }
+    if (!s.done) {
+      int32_t st = cuda_status(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "cudaEventCreate");
+      if (st) return st;
+    }
+    *out = &s;
+    return PKV_OK;
+  }
+
+  int32_t upload(Slot* s, int64_t n, cudaStream_t stream) {
+    int32_t st = cuda_status(cudaMemcpyAsync(s->dev, s->host, n * 4, cudaMemcpyHostToDevice, stream), "H2D");
+    if (!st) st = cuda_status(cudaEventRecord(s->done, stream), "cudaEventRecord");
+    if (!st) s->pending = true;
+    return st;
+  }
+
+  bool capacity_ok(pkv_step_info* out) {
+    pkv_allocator_stats stats;
+    pkv_allocator_get_stats(alloc, &stats);
+    out->need_rows = (int32_t)stats.row_capacity;
+    out->need_cols = (int32_t)stats.max_blocks_per_row;
+    return tables && stats.row_capacity <= rows && stats.max_blocks_per_row <= stride;
+  }
+
+  // Drain the allocator's pending table / refcount / length updates and
+  // copy-on-write copies, and apply them on `stream`.
+  int32_t apply_pending(cudaStream_t stream, int32_t* copies_out, int64_t copies_cap, int32_t* n_copies) {
+    int64_t nt, nr, nl, nc;
+    pkv_allocator_pending_updates(alloc, &nt, &nr, &nl, &nc);
+    *n_copies = 0;
+    if (nt + nr + nl + nc == 0) return PKV_OK;
+    const int64_t cap = 4 + 3 * nt + 2 * nr + 2 * nl + 2 * nc;
+    Slot* s;
+    int32_t st = take_slot(cap, &s);
+    if (st) return st;
+    int64_t written = 0;
+    st = pkv_allocator_drain_updates(alloc, s->host, cap, &written);
+    if (st) return st;
+    if (copies_out && s->host[3] > 0) {
+      const int64_t off = 4 + 3 * (int64_t)s->host[0] + 2 * (int64_t)s->host[1] + 2 * (int64_t)s->host[2];
+      const int64_t n = std::min<int64_t>(s->host[3], copies_cap);
+      std::memcpy(copies_out, s->host + off, n * 2 * 4);
+    }
+    *n_copies = s->host[3];
+    st = cuda_status(cudaMemcpyAsync(s->dev, s->host, written * 4, cudaMemcpyHostToDevice, stream), "H2D");
+    if (st) return st;
+    st = pkv_apply_updates(&geom, pool, tables, stride, rows, refs, lens, s->dev, s->host, stream);
+    // The host copy is read by pkv_apply_updates synchronously; the event only
+    // guards the pinned buffer against reuse before the H2D completes.
+    int32_t st2 = cuda_status(cudaEventRecord(s->done, stream), "cudaEventRecord");
+    s->pending = true;
+    launches += 1 + (s->host[3] > 0 ? 1 : 0);
+    return st ? st : st2;
+  }
+};
+
+extern "C" {
+
+pkv_stepper* pkv_stepper_create(pkv_allocator* a, const pkv_pool_geom* g, void* pool, int32_t* status) {
+  pkv_clear_error();
+  if (!a || !g || !pool) {
+    pkv_set_error("pkv_stepper_create: null argument");
+    if (status) *status = PKV_ERR_ARG;
+    return nullptr;
+  }
+  auto* st = new pkv_stepper();
+  st->alloc = a;
+  st->geom = *g;
+  st->pool = pool;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&st->num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (st->num_sms <= 0) st->num_sms = 148;
+  if (status) *status = PKV_OK;
+  return st;
+}
+
+void pkv_stepper_destroy(pkv_stepper* st) { delete st; }
+
+int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                                int32_t* context_lens, int32_t* refcounts) {
+  st->tables = block_tables;
+  st->stride = table_stride;
+  st->rows = table_rows;
+  st->lens = context_lens;
+  st->refs = refcounts;
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_sync(pkv_stepper* st, void* stream, int32_t* copies_out, int64_t copies_cap, int32_t* n_copies,
+                         int32_t* need_rows, int32_t* need_cols) {
+  pkv_clear_error();
+  pkv_step_info probe{};
+  if (!st->capacity_ok(&probe)) {
+    *need_rows = probe.need_rows;
+    *need_cols = probe.need_cols;
+    pkv_set_error("device block tables too small");
+    return PKV_ERR_CAPACITY;
+  }
+  return st->apply_pending(static_cast<cudaStream_t>(stream), copies_out, copies_cap, n_copies);
+}
+
+int32_t pkv_stepper_begin(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, pkv_step_info* info,
+                          int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out) {
+  pkv_clear_error();
+  st->step_ready = false;
+  if (n <= 0 || !sequence_ids || !info) {
+    pkv_set_error("pkv_stepper_begin: invalid arguments");
+    return PKV_ERR_ARG;
+  }
+  st->rows_h.resize(n);
+  st->lens_h.resize(n);
+  st->newb_h.resize(n);
+  st->tokb_h.resize(n);
+  int64_t done = 0;
+  int32_t s = pkv_allocator_decode_step(st->alloc, sequence_ids, n, st->rows_h.data(), st->lens_h.data(),
+                                        st->newb_h.data(), st->tokb_h.data(), &done);
+  std::memset(info, 0, sizeof(*info));
+  info->batch = (int32_t)done;
+  if (rows_out) std::memcpy(rows_out, st->rows_h.data(), done * 4);
+  if (lens_out) std::memcpy(lens_out, st->lens_h.data(), done * 4);
+  if (token_blocks_out) std::memcpy(token_blocks_out, st->tokb_h.data(), done * 4);
+  if (s != PKV_OK) {
+    // The appends already made stay (as with the reference's sequential
+    // append_tokens calls); record their rows so the next sync uploads them.
+    pkv_allocator_touch_rows(st->alloc, st->rows_h.data(), done);
+    st->rows_h.clear();
+    return s;
+  }
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, int32_t* copies_out,
+                           int64_t copies_cap) {
+  pkv_clear_error();
+  auto cs = static_cast<cudaStream_t>(stream);
+  const int32_t n = info->batch;
+  if (n <= 0 || (size_t)n != st->rows_h.size()) {
+    pkv_set_error("pkv_stepper_upload: no step begun");
+    return PKV_ERR_ARG;
+  }
+  if (!st->capacity_ok(info)) {
+    pkv_set_error("device block tables too small");
+    return PKV_ERR_CAPACITY;
+  }
+  int32_t n_copies = 0;
+  int32_t s = st->apply_pending(cs, copies_out, copies_cap, &n_copies);
+  if (s) return s;
+  info->n_copies = n_copies;
+  int32_t pps = 0;
+  int64_t n_items = 0, n_combine = 0;
+  s = pkv_decode_plan(st->lens_h.data(), n, st->geom.num_kv_heads, st->geom.head_dim, st->num_sms, &pps, nullptr, 0,
+                      &n_items, &n_combine);
+  if (s) return s;
+  // Descriptor: [items + combine entries (int4) | slots (int64) | rows | lens | new_blocks]
+  const int64_t n_quads = n_items + n_combine;
+  const int64_t total = 4 * n_quads + 2 * n + 3 * n;
+  Slot* sl;
+  s = st->take_slot(total, &sl);
+  if (s) return s;
+  int32_t* h = sl->host;
+  s = pkv_decode_plan(st->lens_h.data(), n, st->geom.num_kv_heads, st->geom.head_dim, st->num_sms, &pps, h, n_quads,
+                      &n_items, &n_combine);
+  if (s) return s;
+  int64_t* slots = reinterpret_cast<int64_t*>(h + 4 * n_quads);
+  const int32_t bs = st->geom.block_size;
+  for (int i = 0; i < n; ++i) slots[i] = (int64_t)st->tokb_h[i] * bs + (st->lens_h[i] - 1) % bs;
+  int32_t* tail = h + 4 * n_quads + 2 * n;
+  std::memcpy(tail, st->rows_h.data(), n * 4);
+  std::memcpy(tail + n, st->lens_h.data(), n * 4);
+  std::memcpy(tail + 2 * n, st->newb_h.data(), n * 4);
+  s = st->upload(sl, total, cs);
+  if (s) return s;
+  int32_t* d = sl->dev;
+  info->pages_per_split = pps;
+  info->n_items = (int32_t)n_items;
+  info->n_combine = (int32_t)n_combine;
+  info->items = d;
+  info->slots = reinterpret_cast<const int64_t*>(d + 4 * n_quads);
+  info->rows = d + 4 * n_quads + 2 * n;
+  info->seq_lens = info->rows + n;
+  info->new_blocks = info->rows + 2 * n;
+  // Workspace for this plan (grown rarely; a new one starts zeroed).
+  const int64_t need = pkv_decode_workspace_bytes(n, st->geom.num_kv_heads, st->geom.head_dim, n_items);
+  if (need > st->ws_bytes) {
+    if (st->ws) {
+      s = cuda_status(cudaStreamSynchronize(cs), "stepper workspace");
+      if (s) return s;
+      cudaFree(st->ws);
+      st->ws = nullptr;
+    }
+    const int64_t bytes = std::max<int64_t>(need, (int64_t)1 << 20) * 2;
+    s = cuda_status(cudaMalloc(&st->ws, bytes), "cudaMalloc workspace");
+    if (!s) s = cuda_status(cudaMemsetAsync(st->ws, 0, bytes, cs), "cudaMemsetAsync workspace");
+    if (s) return s;
+    st->ws_bytes = bytes;
+  }
+  st->info = *info;
+  st->step_ready = true;
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_attention(pkv_stepper* st, int32_t layer, const void* q, const void* k_new, const void* v_new,
+                              int32_t num_q_heads, float scale, void* out, void* stream) {
+  if (!st->step_ready) {
+    pkv_clear_error();
+    pkv_set_error("pkv_stepper_attention: no step uploaded");
+    return PKV_ERR_ARG;
+  }
+  const pkv_step_info& in = st->info;
+  const bool timed = st->t_count < st->t_cap;
+  if (timed) cudaEventRecord(st->t_start[st->t_count], static_cast<cudaStream_t>(stream));
+  int32_t s = pkv_decode_attention(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride, st->rows,
+                                   st->lens, in.rows, in.seq_lens, in.new_blocks, in.items, in.n_items, in.n_combine,
+                                   in.batch, num_q_heads, in.pages_per_split, scale, out, st->ws, st->ws_bytes,
+                                   stream);
+  if (timed) cudaEventRecord(st->t_stop[st->t_count++], static_cast<cudaStream_t>(stream));
+  if (s == PKV_OK) st->launches += 1 + (in.n_combine > 0 ? 1 : 0);
+  return s;
+}
+
+int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer, const void* q,
+                         const void* k_new, const void* v_new, int32_t num_q_heads, float scale, void* out,
+                         void* stream, pkv_step_info* info, int32_t* rows_out, int32_t* lens_out,
+                         int32_t* token_blocks_out, int32_t* copies_out, int64_t copies_cap) {
+  int32_t s = pkv_stepper_begin(st, sequence_ids, n, info, rows_out, lens_out, token_blocks_out);
+  if (s) return s;
+  s = pkv_stepper_upload(st, stream, info, copies_out, copies_cap);
+  if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention
+  return pkv_stepper_attention(st, layer, q, k_new, v_new, num_q_heads, scale, out, stream);
+}
+
+int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error) {
+  pkv_clear_error();
+  *device_error = 0;
+  if (!st->ws) return PKV_OK;
+  return cuda_status(cudaMemcpy(device_error, st->ws, 4, cudaMemcpyDeviceToHost), "pkv_stepper_error");
+}
+
+int64_t pkv_stepper_launches(pkv_stepper* st) { return st->launches; }
+
+int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count) {
+  pkv_clear_error();
+  for (auto e : st->t_start) cudaEventDestroy(e);
+  for (auto e : st->t_stop) cudaEventDestroy(e);
+  st->t_start.assign(count, nullptr);
+  st->t_stop.assign(count, nullptr);
+  for (int64_t i = 0; i < count; ++i) {
+    int32_t s = cuda_status(cudaEventCreate(&st->t_start[i]), "cudaEventCreate");
+    if (!s) s = cuda_status(cudaEventCreate(&st->t_stop[i]), "cudaEventCreate");
+    if (s) {
+      st->t_cap = 0;
+      return s;
+    }
+  }
+  st->t_cap = count;
+  st->t_count = 0;
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacity, int64_t* n_out) {
+  pkv_clear_error();
+  const int64_t n = std::min(st->t_count, capacity);
+  for (int64_t i = 0; i < n; ++i) {
+    int32_t s = cuda_status(cudaEventSynchronize(st->t_stop[i]), "cudaEventSynchronize");
+    if (!s) s = cuda_status(cudaEventElapsedTime(&ms_out[i], st->t_start[i], st->t_stop[i]), "cudaEventElapsedTime");
+    if (s) return s;
+  }
+  *n_out = n;
+  return PKV_OK;
+}
+
+}  // extern "C"

@@ -2,9 +2,11 @@
 
 ``KVPool`` owns, on one CUDA device:
 
-* the pool ``[layers, blocks, 2 (K/V), kv_heads, block_size, head_dim]`` --
-  a block's K (or V) rows for one KV head are one contiguous run, which is
-  what the decode kernel's TMA boxes read;
+* the pool ``[layers, blocks, kv_heads, 2 (K/V), block_size, head_dim]`` --
+  a block's K and V pages of all KV heads are one contiguous run, which the
+  decode kernel moves with one bulk copy per head group; pages whose rows are
+  a multiple of 128 bytes are stored pre-swizzled (see include/pkv_b200.h), so
+  the pool is read and written through the scatter / gather kernels only;
 * the device mirror of the allocator's state: block tables
   ``int32 [rows, cols]``, context lengths ``int32 [rows]`` and refcounts
   ``int32 [blocks]``.
@@ -19,7 +21,7 @@ torch stream without host synchronisation.
 from __future__ import annotations
 
 import ctypes
-import math
+import weakref
 
 import numpy as np
 import torch
@@ -67,19 +69,34 @@ class KVPool:
         nbytes = lib.pkv_pool_bytes(self._geom_ref)
         elem = torch.tensor([], dtype=dtype).element_size()
         self.pool = torch.zeros(nbytes // elem, dtype=dtype, device=self.device).view(
-            self.num_layers, self.num_blocks, 2, self.num_kv_heads, self.block_size, self.head_dim)
+            self.num_layers, self.num_blocks, self.num_kv_heads, 2, self.block_size, self.head_dim)
         self.refcounts = torch.zeros(self.num_blocks, dtype=torch.int32, device=self.device)
-        self.tables = torch.full((0, 0), -1, dtype=torch.int32, device=self.device)
-        self.context_lens = torch.zeros(0, dtype=torch.int32, device=self.device)
-        self._workspace = torch.zeros(0, dtype=torch.uint8, device=self.device)
-        # Kernel launches issued through this pool (for launch accounting).
+        self.tables = torch.full((64, 64), -1, dtype=torch.int32, device=self.device)
+        self.context_lens = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        # Kernel launches issued from Python through this pool (the stepper counts its own).
         self.launches = 0
+        status = ctypes.c_int32()
+        with torch.cuda.device(self.device):
+            self.stepper = lib.pkv_stepper_create(allocator._handle, self._geom_ref, self.pool.data_ptr(),
+                                                  ctypes.byref(status))
+        if not self.stepper:
+            _lib.raise_for_status(status.value)
+        weakref.finalize(self, lib.pkv_stepper_destroy, self.stepper)
+        self.step_serial = 0
+        self._timing_cap = 0
+        self._pending = [ctypes.pointer(ctypes.c_int64()) for _ in range(4)]
+        self._bind()
         self.sync()
 
     # -- device tables ------------------------------------------------------
-    def ensure_capacity(self) -> None:
-        st = self.allocator._stats()
-        rows_need, cols_need = int(st.row_capacity), int(st.max_blocks_per_row)
+    def _bind(self) -> None:
+        rows, cols = self.tables.shape
+        lib.pkv_stepper_bind_tables(self.stepper, self.tables.data_ptr(), cols, rows, self.context_lens.data_ptr(),
+                                    self.refcounts.data_ptr())
+
+    def grow(self, rows_need: int, cols_need: int) -> None:
+        """Grow the device tables to at least rows_need x cols_need (contents kept)."""
         rows, cols = self.tables.shape
         if rows_need <= rows and cols_need <= cols:
             return
@@ -90,43 +107,64 @@ class KVPool:
         lens = torch.zeros(new_rows, dtype=torch.int32, device=self.device)
         lens[:rows] = self.context_lens
         self.tables, self.context_lens = tables, lens
+        self._bind()
 
-    def drain(self) -> torch.Tensor | None:
-        """Drain the allocator's pending updates into a pinned int32 buffer."""
-        a = self.allocator._handle
-        nt, nr, nl, nc = (ctypes.c_int64() for _ in range(4))
-        lib.pkv_allocator_pending_updates(a, ctypes.byref(nt), ctypes.byref(nr), ctypes.byref(nl), ctypes.byref(nc))
-        if nt.value + nr.value + nl.value + nc.value == 0:
-            return None
-        cap = 4 + 3 * nt.value + 2 * nr.value + 2 * nl.value + 2 * nc.value
-        buf = torch.empty(cap, dtype=torch.int32, pin_memory=True)
-        written = ctypes.c_int64()
-        _lib.raise_for_status(lib.pkv_allocator_drain_updates(a, buf.data_ptr(), cap, ctypes.byref(written)))
-        return buf[: written.value]
+    def pending_copies(self) -> int:
+        c = self._pending
+        lib.pkv_allocator_pending_updates(self.allocator._handle, c[0], c[1], c[2], c[3])
+        return int(c[3].contents.value)
 
-    def sync(self, drained: torch.Tensor | None = None) -> torch.Tensor | None:
-        """Bring the device tables, lengths and refcounts up to the host state."""
-        self.ensure_capacity()
-        buf = self.drain() if drained is None else drained
-        if buf is None:
-            return None
-        dev = buf.to(self.device, non_blocking=True)
-        rows, cols = self.tables.shape
-        st = lib.pkv_apply_updates(self._geom_ref, self.pool.data_ptr(), self.tables.data_ptr(), cols, rows,
-                                   self.refcounts.data_ptr(), self.context_lens.data_ptr(), dev.data_ptr(),
-                                   buf.data_ptr(), _stream_ptr())
+    def sync(self) -> np.ndarray:
+        """Bring the device tables, lengths and refcounts up to the host allocator's state.
+
+        Returns the copy-on-write (src, dst) block pairs applied, int32 [n, 2].
+        """
+        cap = self.pending_copies()
+        copies = np.empty((max(cap, 1), 2), dtype=np.int32)
+        n, need_r, need_c = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        with torch.cuda.device(self.device):
+            stream = _stream_ptr()
+            st = lib.pkv_stepper_sync(self.stepper, stream, copies.ctypes.data, cap, ctypes.byref(n),
+                                      ctypes.byref(need_r), ctypes.byref(need_c))
+            if st == _lib.PKV_ERR_CAPACITY:
+                self.grow(need_r.value, need_c.value)
+                st = lib.pkv_stepper_sync(self.stepper, stream, copies.ctypes.data, cap, ctypes.byref(n),
+                                          ctypes.byref(need_r), ctypes.byref(need_c))
         _lib.raise_for_status(st)
-        self.launches += 1 + _copy_waves(buf)
-        return buf
+        return copies[: n.value]
+
+    def time_launches(self, count: int) -> None:
+        """Time the next ``count`` decode-attention launches on the device (0 = off)."""
+        _lib.raise_for_status(lib.pkv_stepper_time_launches(self.stepper, int(count)))
+        self._timing_cap = int(count)
+
+    def launch_times_ms(self) -> np.ndarray:
+        """Device milliseconds of the launches timed since ``time_launches``."""
+        out = np.zeros(max(1, int(self._timing_cap)), dtype=np.float32)
+        n = ctypes.c_int64()
+        _lib.raise_for_status(lib.pkv_stepper_launch_times(self.stepper, out.ctypes.data, out.size, ctypes.byref(n)))
+        return out[: n.value]
+
+    def launch_count(self) -> int:
+        return self.launches + int(lib.pkv_stepper_launches(self.stepper))
+
+    def decode_error_flag(self) -> int:
+        """Error word the decode kernels write (0 = none); synchronises with the device."""
+        err = ctypes.c_int32()
+        _lib.raise_for_status(lib.pkv_stepper_error(self.stepper, ctypes.byref(err)))
+        return int(err.value)
 
     # -- data movement --------------------------------------------------------
-    def scatter(self, layer0: int, k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor) -> None:
+    def scatter(self, layer0: int, k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor | int,
+                n_tokens: int | None = None) -> None:
         """Write token rows: k/v ``[n_layers, kv_heads, n_tokens, head_dim]`` (any strides with a
-        contiguous innermost dim, equal strides for k and v) into ``slots`` (int64 device)."""
+        contiguous innermost dim, equal strides for k and v) into ``slots`` (int64 device tensor,
+        or a device pointer with ``n_tokens``)."""
         self._check_rows(k, v)
+        ptr = slots if isinstance(slots, int) else slots.data_ptr()
+        n = n_tokens if isinstance(slots, int) else slots.numel()
         st = lib.pkv_scatter_tokens(self._geom_ref, self.pool.data_ptr(), layer0, k.shape[0], k.data_ptr(),
-                                    v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), slots.data_ptr(),
-                                    slots.numel(), _stream_ptr())
+                                    v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), ptr, n, _stream_ptr())
         _lib.raise_for_status(st)
         self.launches += 1
 
@@ -149,49 +187,22 @@ class KVPool:
         if k.shape[1] != self.num_kv_heads or k.shape[3] != self.head_dim or k.stride(3) != 1:
             raise ValueError("K/V rows do not match the pool geometry")
 
-    # -- decode ---------------------------------------------------------------
-    def workspace(self, nbytes: int) -> torch.Tensor:
-        if self._workspace.numel() < nbytes:
-            self._workspace = torch.zeros(_round_up(nbytes, 1 << 20), dtype=torch.uint8, device=self.device)
-        return self._workspace
 
-    def decode_error_flag(self) -> int:
-        """Error word the decode kernel writes on a bounded-wait timeout (0 = none). Synchronises."""
-        if self._workspace.numel() < 4:
-            return 0
-        return int(self._workspace[:4].view(torch.int32).item())
+def plan_decode(lens: np.ndarray, num_kv_heads: int, num_sms: int,
+                head_dim: int = 128) -> tuple[int, np.ndarray, int, int]:
+    """Plan one decode step (``pkv_decode_plan``).
 
-
-def _copy_waves(buf: torch.Tensor) -> int:
-    """Launches pkv_apply_updates issues for the copy-on-write pairs of a drained buffer."""
-    h = buf.numpy()
-    nt, nr, nl, nc = (int(x) for x in h[:4])
-    if nc == 0:
-        return 0
-    pairs = h[4 + 3 * nt + 2 * nr + 2 * nl :].reshape(nc, 2)
-    waves, touched = 1, set()
-    for src, dst in pairs.tolist():
-        if src in touched or dst in touched:
-            waves += 1
-            touched = set()
-        touched.update((src, dst))
-    return waves
-
-
-def plan_splits(lens: np.ndarray, num_kv_heads: int, block_size: int = 16, sms: int = 148,
-                max_splits_per_seq: int = 64) -> tuple[int, np.ndarray]:
-    """Choose pages per split work item and lay out the work items.
-
-    Aims at several waves of CTAs over the GPU (2 resident CTAs per SM) while
-    keeping each work item at 4..32 pages so its 4 warps stream enough data.
-    Returns (pages_per_split, split_offsets[int32, n+1]).
+    Returns (pages_per_split, int32 [n_items + n_combine, 4], n_items,
+    n_combine): the work items followed by the split-K combine entries.
     """
-    pages = (lens.astype(np.int64) + block_size - 1) // block_size
-    total = int(pages.sum()) * num_kv_heads
-    target_ctas = sms * 2 * 4
-    pps = max(4, min(32, math.ceil(total / target_ctas)))
-    pps = max(pps, math.ceil(int(pages.max(initial=1)) / max_splits_per_seq))
-    nsplits = np.maximum((pages + pps - 1) // pps, 1)
-    offsets = np.zeros(len(lens) + 1, dtype=np.int32)
-    np.cumsum(nsplits, out=offsets[1:])
-    return pps, offsets
+    lens = np.ascontiguousarray(lens, dtype=np.int32)
+    pps = ctypes.c_int32()
+    n = ctypes.c_int64()
+    nc = ctypes.c_int64()
+    _lib.raise_for_status(lib.pkv_decode_plan(lens.ctypes.data, lens.size, num_kv_heads, head_dim, num_sms,
+                                              ctypes.byref(pps), None, 0, ctypes.byref(n), ctypes.byref(nc)))
+    items = np.empty((n.value + nc.value, 4), dtype=np.int32)
+    _lib.raise_for_status(lib.pkv_decode_plan(lens.ctypes.data, lens.size, num_kv_heads, head_dim, num_sms,
+                                              ctypes.byref(pps), items.ctypes.data, items.shape[0], ctypes.byref(n),
+                                              ctypes.byref(nc)))
+    return int(pps.value), items, int(n.value), int(nc.value)

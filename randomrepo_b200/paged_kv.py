@@ -29,7 +29,28 @@ import torch
 
 from . import _lib
 from ._lib import lib
-from .device import KVPool, plan_splits
+from .device import KVPool
+
+
+class _on_device:
+    """Make ``device`` current only if it is not (the common case costs one query)."""
+
+    __slots__ = ("_device", "_prev")
+
+    def __init__(self, device: torch.device) -> None:
+        self._device = device
+        self._prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self._device.index:
+            self._prev = cur
+            torch.cuda.set_device(self._device)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self._prev is not None:
+            torch.cuda.set_device(self._prev)
 
 
 @dataclass(frozen=True, slots=True)
@@ -196,29 +217,32 @@ class PagedKVAllocator:
 
 @dataclass
 class DecodeStep:
-    """Device descriptor of one decode step (one token appended per sequence).
+    """One decode step (one token appended per sequence) as uploaded to the device.
 
-    ``rows``, ``seq_lens`` (token counts including the step's token),
-    ``new_blocks`` and ``split_offsets`` are int32 device tensors;
-    ``pages_per_split`` and ``total_splits`` describe the split-K work items.
-    The same step serves every layer.
+    ``info`` is the native step descriptor (device pointers to the table rows,
+    token counts, new blocks, work items and slots of the step); it is valid
+    until the store's next ``decode_step``.  ``host_rows`` / ``host_lens`` are
+    the same rows and token counts on the host.
     """
 
-    sequence_ids: tuple[int, ...]
-    rows: torch.Tensor
-    seq_lens: torch.Tensor
-    new_blocks: torch.Tensor
-    split_offsets: torch.Tensor
-    slots: torch.Tensor
-    pages_per_split: int
-    total_splits: int
+    sequence_ids: np.ndarray
+    info: _lib.StepInfo
+    serial: int
     host_rows: np.ndarray
     host_lens: np.ndarray
     committed: bool = False
 
     @property
     def batch(self) -> int:
-        return len(self.sequence_ids)
+        return int(self.info.batch)
+
+    @property
+    def n_items(self) -> int:
+        return int(self.info.n_items)
+
+    @property
+    def pages_per_split(self) -> int:
+        return int(self.info.pages_per_split)
 
 
 class PagedKVCacheStore:
@@ -240,6 +264,7 @@ class PagedKVCacheStore:
         # Tokens stored in each block's chunk (-1: the block holds no stored chunk).
         self._block_fill = np.full(allocator.total_blocks, -1, dtype=np.int32)
         self._pool: KVPool | None = None
+        self._copies = np.empty((64, 2), dtype=np.int32)
         if None not in (num_layers, num_kv_heads, head_dim, dtype):
             self._pool = KVPool(allocator, num_layers, num_kv_heads, head_dim, dtype, device)
 
@@ -438,55 +463,61 @@ class PagedKVCacheStore:
                 self._block_fill[kept[-1]] = n % bs
 
     # -- device decode path (extension) -----------------------------------------
-    def decode_step(self, sequence_ids) -> DecodeStep:
-        """Append one token to each sequence and describe the step for the decode kernel.
+    def decode(self, sequence_ids, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, *, layer: int = 0,
+               scale: float | None = None, out: torch.Tensor | None = None) -> tuple[torch.Tensor, DecodeStep]:
+        """One decode step and its fused append + paged attention for one layer, in one native call.
 
-        The allocator side equals calling ``append_tokens(seq, 1)`` for each id in
-        order (agentrl/generation/continuous.py:492-493).
+        Equivalent to ``decode_step(sequence_ids)`` followed by
+        ``decode_attention(step, layer, q, k_new, v_new)``; the returned step
+        serves the model's other layers.
         """
         pool = self._require_pool()
-        ids = np.ascontiguousarray(np.asarray(sequence_ids, dtype=np.int64))
+        ids = self._step_ids(sequence_ids)
         n = ids.size
-        if n == 0:
-            raise ValueError("decode_step needs at least one sequence")
-        desc = np.empty(4 * n, dtype=np.int32)
-        rows, lens, newb, tok_blocks = desc[:n], desc[n : 2 * n], desc[2 * n : 3 * n], desc[3 * n :]
-        done = ctypes.c_int64()
-        st = lib.pkv_allocator_decode_step(self.allocator._handle, ids.ctypes.data, n, rows.ctypes.data,
-                                           lens.ctypes.data, newb.ctypes.data, tok_blocks.ctypes.data,
-                                           ctypes.byref(done))
-        k = done.value
-        bs = self.allocator.block_size_tokens
-        if st != _lib.PKV_OK:
-            lib.pkv_allocator_touch_rows(self.allocator._handle, rows.ctypes.data, k)
-            self._sync()
-            self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
-            _lib.raise_for_status(st)
-        # Copy-on-write copies first (they carry the source block's fill), then
-        # the fill of the blocks that receive this step's tokens.
-        self._sync()
-        self._block_fill[tok_blocks] = (lens - 1) % bs + 1
-        pps, offsets = plan_splits(lens, pool.num_kv_heads, bs)
-        slots = tok_blocks.astype(np.int64) * bs + (lens - 1) % bs
-        # One pinned upload: [slots (int64) | rows | lens | new_blocks | split_offsets]
-        host = torch.empty(2 * n + 3 * n + n + 1, dtype=torch.int32, pin_memory=True)
-        h = host.numpy()
-        h[: 2 * n] = slots.view(np.int32)
-        h[2 * n : 5 * n] = desc[: 3 * n]
-        h[5 * n :] = offsets
-        dev = host.to(pool.device, non_blocking=True)
-        return DecodeStep(
-            sequence_ids=tuple(int(x) for x in ids),
-            rows=dev[2 * n : 3 * n],
-            seq_lens=dev[3 * n : 4 * n],
-            new_blocks=dev[4 * n : 5 * n],
-            split_offsets=dev[5 * n :],
-            slots=dev[: 2 * n].view(torch.int64),
-            pages_per_split=pps,
-            total_splits=int(offsets[-1]),
-            host_rows=rows.copy(),
-            host_lens=lens.copy(),
-        )
+        out = self._check_decode_io(pool, n, q, k_new, v_new, out)
+        info = _lib.StepInfo()
+        host = np.empty((3, n), dtype=np.int32)
+        copies, cap = self._copy_buffer(pool, n)
+        with _on_device(pool.device):
+            stream = torch.cuda.current_stream().cuda_stream
+            sc = float(scale if scale is not None else pool.head_dim ** -0.5)
+            st = lib.pkv_stepper_step(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(), k_new.data_ptr(),
+                                      v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream, ctypes.byref(info),
+                                      host[0].ctypes.data, host[1].ctypes.data, host[2].ctypes.data,
+                                      copies.ctypes.data, cap)
+            if st == _lib.PKV_ERR_CAPACITY:
+                pool.grow(info.need_rows, info.need_cols)
+                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
+                if st == _lib.PKV_OK:
+                    st = lib.pkv_stepper_attention(pool.stepper, int(layer), q.data_ptr(), k_new.data_ptr(),
+                                                   v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream)
+        step = self._finish_step(pool, st, ids, info, host, copies)
+        step.committed = True
+        return out, step
+
+    def decode_step(self, sequence_ids) -> DecodeStep:
+        """Append one token to each sequence and upload the step for the decode kernels.
+
+        The allocator side equals calling ``append_tokens(seq, 1)`` for each id in
+        order (agentrl/generation/continuous.py:492-493); the host work runs in
+        the native stepper (one call to append, one to plan and upload).
+        """
+        pool = self._require_pool()
+        ids = self._step_ids(sequence_ids)
+        n = ids.size
+        info = _lib.StepInfo()
+        host = np.empty((3, n), dtype=np.int32)
+        st = lib.pkv_stepper_begin(pool.stepper, ids.ctypes.data, n, ctypes.byref(info), host[0].ctypes.data,
+                                   host[1].ctypes.data, host[2].ctypes.data)
+        copies, cap = self._copy_buffer(pool, n)
+        if st == _lib.PKV_OK:
+            with _on_device(pool.device):
+                stream = torch.cuda.current_stream().cuda_stream
+                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
+                if st == _lib.PKV_ERR_CAPACITY:
+                    pool.grow(info.need_rows, info.need_cols)
+                    st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
+        return self._finish_step(pool, st, ids, info, host, copies)
 
     def decode_attention(self, step: DecodeStep, layer: int, q: torch.Tensor, k_new: torch.Tensor | None = None,
                          v_new: torch.Tensor | None = None, *, scale: float | None = None,
@@ -495,39 +526,28 @@ class PagedKVCacheStore:
 
         With ``k_new``/``v_new`` ``[B, Hkv, D]`` the kernel first appends the
         step's token into its page (and updates the device block table and
-        lengths); without them the step's K/V must already be in the pool.
+        lengths); without them the step's K/V must already be in the pool
+        (``append_step_kv``).
         """
         pool = self._require_pool()
-        b = step.batch
-        if q.dim() != 3 or q.shape[0] != b or q.shape[2] != pool.head_dim:
-            raise ValueError("q must be [batch, num_q_heads, head_dim]")
-        if q.dtype != pool.dtype or not q.is_contiguous() or q.device != pool.device:
-            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
-        for t in (k_new, v_new):
-            if t is not None and (t.shape != (b, pool.num_kv_heads, pool.head_dim) or t.dtype != pool.dtype
-                                  or not t.is_contiguous() or t.device != pool.device):
-                raise ValueError("k_new/v_new must be contiguous [batch, num_kv_heads, head_dim] pool-dtype tensors")
+        if step.serial != pool.step_serial:
+            raise RuntimeError("this decode step is stale: a later decode_step replaced its device descriptor")
         if (k_new is None) != (v_new is None):
             raise ValueError("pass both k_new and v_new or neither")
+        out = self._check_decode_io(pool, step.batch, q, k_new, v_new, out)
         if k_new is None and not step.committed:
-            lib.pkv_allocator_touch_rows(self.allocator._handle, step.host_rows.ctypes.data, b)
+            # The step's new blocks and lengths reach the device tables here,
+            # since no fused append will store them.
+            lib.pkv_allocator_touch_rows(self.allocator._handle, step.host_rows.ctypes.data, step.batch)
+            self._sync()
             step.committed = True
-        self._sync()
-        if out is None:
-            out = torch.empty_like(q)
-        hq = q.shape[1]
-        ws_bytes = lib.pkv_decode_workspace_bytes(b, pool.num_kv_heads, pool.head_dim, step.total_splits)
-        ws = pool.workspace(ws_bytes)
-        rows_t, cols_t = pool.tables.shape
-        st = lib.pkv_decode_attention(
-            pool._geom_ref, pool.pool.data_ptr(), int(layer), q.data_ptr(),
-            k_new.data_ptr() if k_new is not None else None, v_new.data_ptr() if v_new is not None else None,
-            pool.tables.data_ptr(), cols_t, pool.context_lens.data_ptr(), step.rows.data_ptr(),
-            step.seq_lens.data_ptr(), step.new_blocks.data_ptr(), step.split_offsets.data_ptr(), b, hq,
-            step.pages_per_split, step.total_splits, float(scale if scale is not None else pool.head_dim ** -0.5),
-            out.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        with _on_device(pool.device):
+            st = lib.pkv_stepper_attention(
+                pool.stepper, int(layer), q.data_ptr(), k_new.data_ptr() if k_new is not None else None,
+                v_new.data_ptr() if v_new is not None else None, q.shape[1],
+                float(scale if scale is not None else pool.head_dim ** -0.5), out.data_ptr(),
+                torch.cuda.current_stream().cuda_stream)
         _lib.raise_for_status(st)
-        pool.launches += 1
         if k_new is not None:
             step.committed = True
         return out
@@ -535,7 +555,56 @@ class PagedKVCacheStore:
     def append_step_kv(self, step: DecodeStep, layer: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
         """Write the step's K/V ``[B, Hkv, D]`` into the pool without attention."""
         pool = self._require_pool()
-        pool.scatter(layer, k_new.permute(1, 0, 2).unsqueeze(0), v_new.permute(1, 0, 2).unsqueeze(0), step.slots)
+        if step.serial != pool.step_serial:
+            raise RuntimeError("this decode step is stale: a later decode_step replaced its device descriptor")
+        pool.scatter(layer, k_new.permute(1, 0, 2).unsqueeze(0), v_new.permute(1, 0, 2).unsqueeze(0),
+                     int(step.info.slots), step.batch)
+
+    @staticmethod
+    def _step_ids(sequence_ids) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(sequence_ids, dtype=np.int64).reshape(-1))
+        if ids.size == 0:
+            raise ValueError("a decode step needs at least one sequence")
+        return ids
+
+    @staticmethod
+    def _check_decode_io(pool: KVPool, n: int, q, k_new, v_new, out):
+        if q.dim() != 3 or q.shape[0] != n or q.shape[2] != pool.head_dim:
+            raise ValueError("q must be [batch, num_q_heads, head_dim]")
+        if q.dtype != pool.dtype or q.device != pool.device or not q.is_contiguous():
+            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
+        shape = (n, pool.num_kv_heads, pool.head_dim)
+        for t in (k_new, v_new):
+            if t is not None and (t.shape != shape or t.dtype != pool.dtype or t.device != pool.device
+                                  or not t.is_contiguous()):
+                raise ValueError("k_new/v_new must be contiguous [batch, num_kv_heads, head_dim] pool-dtype tensors")
+        if out is None:
+            return torch.empty_like(q)
+        if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or not out.is_contiguous():
+            raise ValueError("out must be a contiguous tensor shaped and typed like q")
+        return out
+
+    def _copy_buffer(self, pool: KVPool, n: int) -> tuple[np.ndarray, int]:
+        cap = max(pool.pending_copies(), n)
+        if self._copies.shape[0] < cap:
+            self._copies = np.empty((2 * cap, 2), dtype=np.int32)
+        return self._copies, self._copies.shape[0]
+
+    def _finish_step(self, pool: KVPool, st: int, ids, info, host, copies) -> DecodeStep:
+        rows, lens, tok_blocks = host[0], host[1], host[2]
+        bs = self.allocator.block_size_tokens
+        k = int(info.batch)
+        if st != _lib.PKV_OK:
+            self._sync()
+            self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
+            _lib.raise_for_status(st)
+        # Copy-on-write copies first (they carry the source block's fill), then
+        # the fill of the blocks that receive this step's tokens.
+        for src, dst in copies[: info.n_copies].tolist():
+            self._block_fill[dst] = self._block_fill[src]
+        self._block_fill[tok_blocks] = (lens - 1) % bs + 1
+        pool.step_serial += 1
+        return DecodeStep(sequence_ids=ids, info=info, serial=pool.step_serial, host_rows=rows, host_lens=lens)
 
     # -- helpers -----------------------------------------------------------------
     def _ensure_pool(self, num_layers: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype,
@@ -561,18 +630,8 @@ class PagedKVCacheStore:
         pool = self._pool
         if pool is None:
             return
-        buf = pool.drain()
-        if buf is not None:
-            self._note_copies(buf)
-        pool.sync(buf)
-
-    def _note_copies(self, buf: torch.Tensor) -> None:
-        h = buf.numpy()
-        nt, nr, nl, nc = (int(x) for x in h[:4])
-        if nc:
-            pairs = h[4 + 3 * nt + 2 * nr + 2 * nl :].reshape(nc, 2)
-            for src, dst in pairs:
-                self._block_fill[dst] = self._block_fill[src]
+        for src, dst in pool.sync().tolist():
+            self._block_fill[dst] = self._block_fill[src]
 
     def _slots(self, blocks, fills, bs: int) -> torch.Tensor:
         parts = [np.arange(f, dtype=np.int64) + int(b) * bs for b, f in zip(blocks, fills) if f > 0]

@@ -119,7 +119,7 @@ def test_decode_microbench_shape_and_append_bits(cuda_device):
     lengths = torch.randint(64, 2049, (256,), generator=gen).tolist()
     store, q, kn, vn, ks, vs = _batch_case(cuda_device, lengths, 12, 2, 128, torch.bfloat16, seed=1)
     step = store.decode_step(list(range(256)))
-    assert step.total_splits > 256  # split-K is exercised
+    assert step.n_items > 256  # split-K is exercised
     out = store.decode_attention(step, 0, q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
     torch.cuda.synchronize()
     _close(out, _oracle(q, ks, vs, 128 ** -0.5))
