@@ -262,6 +262,30 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
                              int32_t num_q_heads, int32_t pages_per_split, float scale, void* out, void* workspace,
                              int64_t workspace_bytes, void* stream);
 
+/* pkv_decode_attention for callers that may not allocate device memory (no
+ * counterpart in the reference).  Some hosts of this library -- a serving
+ * framework that owns all GPU memory through its own arena so that its
+ * accounting stays exact and no cudaMalloc/cudaFree stalls the device, or a
+ * plugin interface that only passes buffers it allocated -- provide inputs
+ * and outputs but no workspace.  This entry point takes the same arguments
+ * minus the workspace and uses a 16 MiB scratch array that lives in the
+ * library's device memory on every GPU that loads it, until process exit.  It
+ * never calls cudaMalloc, cudaFree or any allocating routine.
+ *  - A step whose workspace (pkv_decode_workspace_bytes) exceeds 16 MiB is
+ *    rejected with PKV_ERR_ARG and a message; nothing is launched.
+ *  - The first call on a device looks up the scratch's device address (with
+ *    that device current); make that first call before any stream capture.
+ *  - All calls share the one scratch: calls that overlap on the GPU (other
+ *    streams, other threads) race and corrupt each other's results.  Each call
+ *    clears the parts that must start at zero. */
+int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q,
+                                     const void* k_new, const void* v_new, int32_t* block_tables,
+                                     int32_t table_stride, int32_t table_rows, int32_t* context_lens,
+                                     const int32_t* rows, const int32_t* seq_lens, const int32_t* new_blocks,
+                                     const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
+                                     int32_t num_q_heads, int32_t pages_per_split, float scale, void* out,
+                                     void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Native decode-step runtime                                                */
 /* ------------------------------------------------------------------------ */

@@ -132,6 +132,12 @@ _SIGNATURES: dict[str, tuple] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p,
          c_void_p, c_int64, c_void_p],
     ),
+    "pkv_decode_attention_noalloc": (
+        c_int32,
+        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p,
+         c_void_p],
+    ),
     "pkv_stepper_create": (c_void_p, [c_void_p, POINTER(PoolGeom), c_void_p, I32P]),
     "pkv_stepper_destroy": (None, [c_void_p]),
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),

@@ -41,6 +41,7 @@
 #include "pkv_error.h"
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -793,6 +794,84 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
                                 : launch_for_heads<128, __half>(prm, entries, n_combine, s);
   return g->dtype == PKV_BF16 ? launch_for_heads<64, __nv_bfloat16>(prm, entries, n_combine, s)
                               : launch_for_heads<64, __half>(prm, entries, n_combine, s);
+}
+
+// ---------------------------------------------------------------------------
+// Decode without a caller-provided workspace.
+//
+// Some callers of this library may not allocate device memory while they
+// run: an inference server or framework that owns every byte of the GPU
+// through its own arena (so that memory accounting stays exact and no
+// cudaMalloc / cudaFree ever stalls the device), or a plugin interface that
+// only hands the library buffers it allocated itself.  They can pass their
+// inputs and outputs but cannot provide the decode workspace.  For them,
+// pkv_decode_attention_noalloc takes its scratch (error word, scheduler
+// counters, split-K partials) from a fixed array in this file's device
+// memory instead.  The array exists on every GPU that loads this library and
+// stays allocated until the process exits.
+namespace {
+constexpr int64_t kStaticScratchBytes = 16ll << 20;  // 16 MiB
+__device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[kMaxDevices] = {};
+}  // namespace
+
+int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q,
+                                     const void* k_new, const void* v_new, int32_t* block_tables,
+                                     int32_t table_stride, int32_t table_rows, int32_t* context_lens,
+                                     const int32_t* rows, const int32_t* seq_lens, const int32_t* new_blocks,
+                                     const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
+                                     int32_t num_q_heads, int32_t pages_per_split, float scale, void* out,
+                                     void* stream) {
+  pkv_clear_error();
+  if (!g) {
+    pkv_set_error("null pool geometry");
+    return PKV_ERR_ARG;
+  }
+  const int64_t need = ws_layout(batch, g->num_kv_heads, g->head_dim, n_items).total;
+  if (need > kStaticScratchBytes) {
+    pkv_set_error("pkv_decode_attention_noalloc: this step needs " + std::to_string(need) +
+                  " bytes of scratch, more than the 16 MiB static scratch (fewer or shorter sequences per "
+                  "call, or pkv_decode_attention with a workspace)");
+    return PKV_ERR_ARG;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    pkv_set_error(std::string("pkv_decode_attention_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    pkv_set_error("pkv_decode_attention_noalloc: device index out of range");
+    return PKV_ERR_UNSUPPORTED;
+  }
+  void* scratch = nullptr;
+  {
+    // The array's name is only a host-side stand-in: its device address must
+    // be looked up, once per device, with that device current.
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+      e = cudaGetSymbolAddress(&g_scratch_addr[dev], g_decode_scratch);
+      if (e != cudaSuccess) {
+        g_scratch_addr[dev] = nullptr;
+        pkv_set_error(std::string("pkv_decode_attention_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        return PKV_ERR_CUDA;
+      }
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  // The scratch keeps the previous call's contents: clear the error word and
+  // the scheduler counters, which the kernels expect at zero.  (The split-K
+  // partials are always written before they are read.)
+  e = cudaMemsetAsync(scratch, 0, 256, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    pkv_set_error(std::string("pkv_decode_attention_noalloc: cudaMemsetAsync: ") + cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
+  }
+  return pkv_decode_attention(g, pool, layer, q, k_new, v_new, block_tables, table_stride, table_rows, context_lens,
+                              rows, seq_lens, new_blocks, work_items, n_items, n_combine, batch, num_q_heads,
+                              pages_per_split, scale, out, scratch, kStaticScratchBytes, stream);
 }
 
 }  // extern "C"
