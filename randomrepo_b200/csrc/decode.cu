@@ -27,10 +27,11 @@
 //
 // Item epilogue: a sequence with one item writes its output from registers;
 // otherwise the item writes its unnormalised (O, m, l) partial to the
-// workspace (plain stores, no fence) and a second, fully parallel kernel of the
-// same launch combines the partials of each such (sequence, head group).  An
-// in-kernel "last item combines" scheme puts a chain of dependent L2 reads on
-// one warp at the end of each sequence; it measured 2.5x slower here.
+// workspace (plain stores, no fence) and a second, fully parallel kernel --
+// a programmatic dependent of the decode grid -- combines the partials of each
+// such (sequence, head group).  Combining inside the decode kernel (the last
+// item of a sequence, by atomic ticket) put one warp on a chain of L2 round
+// trips while HBM was saturated and cost ~45% more time.
 //
 // Every mbarrier wait is bounded; on a timeout the warp records an error word
 // in the workspace, waits (bounded) for its copies in flight and exits.
@@ -39,6 +40,7 @@
 // the P.V product, output rounded once to the input dtype.
 #include "pkv_device.cuh"
 #include "pkv_error.h"
+#include "pkv_internal.h"
 
 #include <algorithm>
 #include <mutex>
@@ -81,6 +83,13 @@ struct DecodeParams {
   float* ws_ml;
   float* ws_o;
   int32_t* ws_sched;     // [0] next item, [1] warps done
+  // Length / refcount updates the decode does not read, applied on the way
+  // (the stepper defers them here instead of launching a table kernel):
+  // n_ref (block, refcount) pairs then n_len (row, length) pairs.
+  const int32_t* deferred;
+  int32_t deferred_refs;
+  int32_t deferred_lens;
+  int32_t* refcounts;
   int32_t* ws_error;
   int32_t n_items;
   int32_t batch;
@@ -201,6 +210,22 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
     fence_barrier_init();
   }
   __syncwarp();
+
+  // Let the split-K combine grid get resident now; it waits in hardware for
+  // this grid to complete before it reads the partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (p.deferred) {
+    const int n = p.deferred_refs + p.deferred_lens;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+      const int32_t a = p.deferred[2 * i], v = p.deferred[2 * i + 1];
+      if (i < p.deferred_refs) {
+        if (a >= 0 && a < p.num_blocks) p.refcounts[a] = v;
+      } else if (a >= 0 && a < p.table_rows) {
+        p.ctx_lens[a] = v;
+      }
+    }
+  }
 
   const T* kn = static_cast<const T*>(p.k_new);
   const T* vn = static_cast<const T*>(p.v_new);
@@ -440,93 +465,80 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
   }
 }
 
-// Split-K combine: one CTA per (sequence, head group) that has several items.
-// Entries {sequence, head_group, nsplits, workspace slot of split 0} follow the
-// decode items in the plan.  out = sum_s w_s O_s / sum_s w_s l_s with
-// w_s = 2^(m_s - max_s m_s), for every query head of the group and dim.
-// Latency, not bandwidth, bounds this kernel (a few MB from L2), so every
-// phase issues all of its loads before it uses any: the splits' (m, l) go to
-// shared memory in one parallel pass, and each thread loads the float4 of every
-// split for its outputs back to back.
-constexpr int kCombineThreads = 128;
+// Split-K combine: entries {sequence, head_group, nsplits, workspace slot of
+// split 0} follow the decode items in the plan; grid = (entry, query head of
+// the group), one warp each.  out = sum_s w_s O_s / sum_s w_s l_s with
+// w_s = 2^(m_s - max_s m_s).  Lane s (and s + 32) reads split s's max and sum,
+// warp shuffles give the weights, then lane i loads dims 4i..4i+3 of every
+// split at once: about two memory round trips per warp.  Launched as a
+// programmatic dependent of the decode grid: its CTAs become resident early
+// and griddepcontrol.wait holds them (in hardware, no spinning) until the
+// decode grid has completed and its partials are visible.
+constexpr int kCombineThreads = 32;
 
 template <int D, int HPC, typename T>
 __global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(const DecodeParams p,
                                                                                const int4* entries, int n_entries) {
-  __shared__ float s_ml[kMaxSplitsPerSeq][HPC][16];
-  __shared__ float s_w[kMaxSplitsPerSeq][HPC][8];
-  __shared__ float s_inv[HPC][8];
-  const int e = blockIdx.x;
-  if (e >= n_entries) return;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int e = blockIdx.x, pi = blockIdx.y;
+  const int hh = pi >> 3, gq = pi & 7;
+  if (e >= n_entries || gq >= p.group) return;
   const int4 en = entries[e];
   const int b = en.x, hg = en.y, ns = en.z, slot0 = en.w;
+  const int lane = threadIdx.x;
   if (b < 0 || b >= p.batch || (hg + 1) * HPC > p.hkv || ns < 2 || ns > kMaxSplitsPerSeq || slot0 < 0 ||
       slot0 + ns > p.n_items) {
-    if (threadIdx.x == 0) atomicExch(p.ws_error, kDevBadItem);
+    if (lane == 0) atomicExch(p.ws_error, kDevBadItem);
     return;
   }
-  const int group = p.group;
-  // (m, l) of every split: ns * HPC * 16 consecutive floats.
-  const float* ml = p.ws_ml + (int64_t)slot0 * HPC * 16;
-  for (int i = threadIdx.x; i < ns * HPC * 16; i += kCombineThreads) (&s_ml[0][0][0])[i] = __ldcg(ml + i);
-  __syncthreads();
-  if (threadIdx.x < HPC * group) {
-    const int hh = threadIdx.x / group, gq = threadIdx.x - hh * group;
-    float mm = -INFINITY;
-    for (int s = 0; s < ns; ++s) mm = fmaxf(mm, s_ml[s][hh][gq]);
-    float l = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float w = exp2f(s_ml[s][hh][gq] - mm);
-      s_w[s][hh][gq] = w;
-      l += w * s_ml[s][hh][8 + gq];
-    }
-    s_inv[hh][gq] = 1.f / l;
+  float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+  if (lane < ns) {
+    const float* ml = p.ws_ml + ((int64_t)(slot0 + lane) * HPC + hh) * 16;
+    m0 = ml[gq];
+    l0 = ml[8 + gq];
   }
-  __syncthreads();
-  T* out = static_cast<T*>(p.out);
-  constexpr int kVec = 4;
-  const int n_vec = HPC * group * (D / kVec);
-  for (int v = threadIdx.x; v < n_vec; v += kCombineThreads) {
-    const int hh = v / (group * (D / kVec));
-    const int r = v - hh * group * (D / kVec);
-    const int gq = r / (D / kVec), d = (r - gq * (D / kVec)) * kVec;
-    const float4* src = reinterpret_cast<const float4*>(p.ws_o + (((int64_t)slot0 * HPC + hh) * 8 + gq) * D + d);
-    const int64_t stride4 = (int64_t)HPC * 8 * D / kVec;  // one split further
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int s = 0;
-    for (; s + 8 <= ns; s += 8) {
-      float4 x[8];
+  if (lane + 32 < ns) {
+    const float* ml = p.ws_ml + ((int64_t)(slot0 + lane + 32) * HPC + hh) * 16;
+    m1 = ml[gq];
+    l1 = ml[8 + gq];
+  }
+  float mm = fmaxf(m0, m1);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = __ldcg(src + (s + k) * stride4);
+  for (int off = 16; off > 0; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+  const float w0 = lane < ns ? exp2f(m0 - mm) : 0.f;
+  const float w1 = lane + 32 < ns ? exp2f(m1 - mm) : 0.f;
+  float l = w0 * l0 + w1 * l1;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float w = s_w[s + k][hh][gq];
+  for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+  const float inv = 1.f / l;
+  constexpr int kQuads = D / 4;
+  const bool active = lane < kQuads;
+  const float4* src = reinterpret_cast<const float4*>(p.ws_o + (((int64_t)slot0 * HPC + hh) * 8 + gq) * D) + lane;
+  const int64_t stride = (int64_t)HPC * 8 * D / 4;  // float4s from one split to the next
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < ns; s0 += 16) {
+    float4 x[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      x[k] = (active && s0 + k < ns) ? src[(s0 + k) * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int sidx = s0 + k;
+      const float w = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
+      if (sidx < ns) {
         acc.x += w * x[k].x;
         acc.y += w * x[k].y;
         acc.z += w * x[k].z;
         acc.w += w * x[k].w;
       }
     }
-    {
-      float4 x[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = s + k < ns ? __ldcg(src + (s + k) * stride4) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float w = s + k < ns ? s_w[s + k][hh][gq] : 0.f;
-        acc.x += w * x[k].x;
-        acc.y += w * x[k].y;
-        acc.z += w * x[k].z;
-        acc.w += w * x[k].w;
-      }
-    }
-    const float inv = s_inv[hh][gq];
-    T* dst = out + ((int64_t)b * p.hq + (hg * HPC + hh) * group + gq) * D + d;
-    dst[0] = MmaOp<T>::from_float(acc.x * inv);
-    dst[1] = MmaOp<T>::from_float(acc.y * inv);
-    dst[2] = MmaOp<T>::from_float(acc.z * inv);
-    dst[3] = MmaOp<T>::from_float(acc.w * inv);
   }
+  if (!active) return;
+  T* dst = static_cast<T*>(p.out) + ((int64_t)b * p.hq + (hg * HPC + hh) * p.group + gq) * D + 4 * lane;
+  dst[0] = MmaOp<T>::from_float(acc.x * inv);
+  dst[1] = MmaOp<T>::from_float(acc.y * inv);
+  dst[2] = MmaOp<T>::from_float(acc.z * inv);
+  dst[3] = MmaOp<T>::from_float(acc.w * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -583,8 +595,23 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entrie
   }
   const int grid = std::max(1, std::min((prm.n_items + C::kWarps - 1) / C::kWarps, num_sms_cached()));
   paged_decode_kernel<D, HPC, T><<<grid, C::kWarps * 32, C::kSmemBytes, s>>>(prm);
-  if (n_entries > 0)
-    paged_decode_combine_kernel<D, HPC, T><<<n_entries, kCombineThreads, 0, s>>>(prm, entries, n_entries);
+  if (n_entries > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_entries, HPC * 8);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel<D, HPC, T>, prm, entries, n_entries);
+    if (le != cudaSuccess) {
+      pkv_set_error(std::string("pkv_decode_attention combine launch: ") + cudaGetErrorString(le));
+      return PKV_ERR_CUDA;
+    }
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     pkv_set_error(std::string("pkv_decode_attention launch: ") + cudaGetErrorString(e));
@@ -657,43 +684,40 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
     pkv_set_error("pkv_decode_plan: item buffer too small");
     return PKV_ERR_ARG;
   }
-  // Full items first, then the partial last splits by decreasing size: the
-  // warps take items in this order, largest first.
-  struct Item {
-    int32_t pages, b, split, hg, nsplits, slot0;
-  };
-  std::vector<Item> full, part;
-  full.reserve(n);
-  int32_t slot = 0;
-  for (int b = 0; b < batch; ++b) {
+  // Order: sequences by decreasing length, each sequence's items together
+  // (head group, then split).  The items of one sequence are taken by several
+  // warps at about the same time, so its split-K combine (done by the item
+  // that finishes last) overlaps other sequences' streaming instead of piling
+  // up at the end of the kernel; the shortest sequences (one or two small
+  // items) come last and even out the tail.
+  std::vector<int32_t> order(batch);
+  for (int b = 0; b < batch; ++b) order[b] = b;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int32_t x, int32_t y) { return seq_lens[x] > seq_lens[y]; });
+  std::vector<int32_t> slot_of(batch);
+  {
+    int32_t sl = 0;
+    for (int b = 0; b < batch; ++b) {
+      slot_of[b] = sl;
+      sl += groups * (((seq_lens[b] + 15) / 16 + pps - 1) / pps);
+    }
+  }
+  int32_t* o = items_out;
+  for (int32_t b : order) {
     const int32_t pages = (seq_lens[b] + 15) / 16;
     const int32_t ns = (pages + pps - 1) / pps;
     for (int hg = 0; hg < groups; ++hg) {
-      for (int s = 0; s < ns; ++s) {
-        const int32_t pg = std::min(pps, pages - s * pps);
-        Item it{pg, b, s, hg, ns, slot};
-        (pg == pps ? full : part).push_back(it);
+      for (int sp = 0; sp < ns; ++sp) {
+        o[0] = b;
+        o[1] = (sp << 8) | hg;
+        o[2] = ns;
+        o[3] = slot_of[b] + hg * ns;
+        o += 4;
       }
-      slot += ns;
-    }
-  }
-  if ((int64_t)(full.size() + part.size()) != n) {
-    pkv_set_error("pkv_decode_plan: internal item count mismatch");
-    return PKV_ERR_ARG;
-  }
-  std::stable_sort(part.begin(), part.end(), [](const Item& x, const Item& y) { return x.pages > y.pages; });
-  int32_t* o = items_out;
-  for (const auto* v : {&full, &part}) {
-    for (const Item& it : *v) {
-      o[0] = it.b;
-      o[1] = (it.split << 8) | it.hg;
-      o[2] = it.nsplits;
-      o[3] = it.slot0;
-      o += 4;
     }
   }
   // Combine entries {sequence, head_group, nsplits, slot of split 0}.
-  slot = 0;
+  int32_t slot = 0;
   for (int b = 0; b < batch; ++b) {
     const int32_t ns = ((seq_lens[b] + 15) / 16 + pps - 1) / pps;
     for (int hg = 0; hg < groups; ++hg) {
@@ -721,7 +745,27 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
                              const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
                              int32_t num_q_heads, int32_t pages_per_split, float scale, void* out, void* workspace,
                              int64_t workspace_bytes, void* stream) {
+  return pkv_decode_attention_ex(g, pool, layer, q, k_new, v_new, block_tables, table_stride, table_rows,
+                                 context_lens, rows, seq_lens, new_blocks, work_items, n_items, n_combine, batch,
+                                 num_q_heads, pages_per_split, scale, out, workspace, workspace_bytes, stream,
+                                 nullptr, 0, 0, nullptr);
+}
+
+}  // extern "C"
+
+int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q, const void* k_new,
+                                const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                                int32_t* context_lens, const int32_t* rows, const int32_t* seq_lens,
+                                const int32_t* new_blocks, const int32_t* work_items, int32_t n_items,
+                                int32_t n_combine, int32_t batch, int32_t num_q_heads, int32_t pages_per_split,
+                                float scale, void* out, void* workspace, int64_t workspace_bytes, void* stream,
+                                const int32_t* deferred, int32_t deferred_refs, int32_t deferred_lens,
+                                int32_t* refcounts) {
   pkv_clear_error();
+  if (deferred && (!refcounts || !context_lens || deferred_refs < 0 || deferred_lens < 0)) {
+    pkv_set_error("deferred updates need the refcount and length arrays");
+    return PKV_ERR_ARG;
+  }
   if (!g || g->block_size != 16) {
     pkv_set_error("paged decode attention needs block_size 16");
     return PKV_ERR_UNSUPPORTED;
@@ -774,6 +818,10 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
   char* ws = static_cast<char*>(workspace);
   prm.ws_error = reinterpret_cast<int32_t*>(ws);
   prm.ws_sched = reinterpret_cast<int32_t*>(ws + wl.sched);
+  prm.deferred = deferred;
+  prm.deferred_refs = deferred ? deferred_refs : 0;
+  prm.deferred_lens = deferred ? deferred_lens : 0;
+  prm.refcounts = refcounts;
   prm.ws_ml = reinterpret_cast<float*>(ws + wl.ml);
   prm.ws_o = reinterpret_cast<float*>(ws + wl.o);
   prm.n_items = n_items;
@@ -795,6 +843,8 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
   return g->dtype == PKV_BF16 ? launch_for_heads<64, __nv_bfloat16>(prm, entries, n_combine, s)
                               : launch_for_heads<64, __half>(prm, entries, n_combine, s);
 }
+
+extern "C" {
 
 // ---------------------------------------------------------------------------
 // Decode without a caller-provided workspace.

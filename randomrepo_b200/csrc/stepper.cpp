@@ -21,6 +21,7 @@
 
 #include "pkv_b200.h"
 #include "pkv_error.h"
+#include "pkv_internal.h"
 
 namespace {
 
@@ -61,6 +62,11 @@ struct pkv_stepper {
   int64_t ws_bytes = 0;
   cudaStream_t ws_stream = nullptr;
   int64_t launches = 0;
+  // Length / refcount updates uploaded with the step descriptor, applied by
+  // the step's first decode launch (device pointer past the drain header).
+  const int32_t* def_dev = nullptr;
+  int32_t def_refs = 0, def_lens = 0;
+  bool def_pending = false;
   // Optional per-launch timing of the decode kernels (events around them).
   std::vector<cudaEvent_t> t_start, t_stop;
   int64_t t_cap = 0, t_count = 0;
@@ -122,9 +128,21 @@ struct pkv_stepper {
     return tables && stats.row_capacity <= rows && stats.max_blocks_per_row <= stride;
   }
 
+  // Deferred updates that no decode launch consumed go through the table
+  // kernel before anything else reads the mirror.
+  int32_t flush_deferred(cudaStream_t stream) {
+    if (!def_pending) return PKV_OK;
+    def_pending = false;
+    const int32_t header[4] = {0, def_refs, def_lens, 0};
+    launches += 1;
+    return pkv_apply_updates(&geom, pool, tables, stride, rows, refs, lens, def_dev - 4, header, stream);
+  }
+
   // Drain the allocator's pending table / refcount / length updates and
   // copy-on-write copies, and apply them on `stream`.
   int32_t apply_pending(cudaStream_t stream, int32_t* copies_out, int64_t copies_cap, int32_t* n_copies) {
+    int32_t fs = flush_deferred(stream);
+    if (fs) return fs;
     int64_t nt, nr, nl, nc;
     pkv_allocator_pending_updates(alloc, &nt, &nr, &nl, &nc);
     *n_copies = 0;
@@ -244,8 +262,17 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
     return PKV_ERR_CAPACITY;
   }
   int32_t n_copies = 0;
-  int32_t s = st->apply_pending(cs, copies_out, copies_cap, &n_copies);
+  int32_t s = st->flush_deferred(cs);
   if (s) return s;
+  int64_t pt, pr, pl, pc;
+  pkv_allocator_pending_updates(st->alloc, &pt, &pr, &pl, &pc);
+  // Only lengths / refcounts pending (the decode never reads them): they ride
+  // in the descriptor upload and the decode kernel applies them.
+  const bool defer = pt == 0 && pc == 0 && pr + pl > 0;
+  if (!defer) {
+    s = st->apply_pending(cs, copies_out, copies_cap, &n_copies);
+    if (s) return s;
+  }
   info->n_copies = n_copies;
   int32_t pps = 0;
   int64_t n_items = 0, n_combine = 0;
@@ -254,7 +281,9 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
   if (s) return s;
   // Descriptor: [items + combine entries (int4) | slots (int64) | rows | lens | new_blocks]
   const int64_t n_quads = n_items + n_combine;
-  const int64_t total = 4 * n_quads + 2 * n + 3 * n;
+  const int64_t def_off = 4 * n_quads + 2 * n + 3 * n;
+  const int64_t def_cap = defer ? 4 + 2 * (pr + pl) : 0;
+  const int64_t total = def_off + def_cap;
   Slot* sl;
   s = st->take_slot(total, &sl);
   if (s) return s;
@@ -269,9 +298,20 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
   std::memcpy(tail, st->rows_h.data(), n * 4);
   std::memcpy(tail + n, st->lens_h.data(), n * 4);
   std::memcpy(tail + 2 * n, st->newb_h.data(), n * 4);
-  s = st->upload(sl, total, cs);
+  int64_t written = 0;
+  if (defer) {
+    s = pkv_allocator_drain_updates(st->alloc, h + def_off, def_cap, &written);
+    if (s) return s;
+  }
+  s = st->upload(sl, def_off + written, cs);
   if (s) return s;
   int32_t* d = sl->dev;
+  if (defer) {
+    st->def_dev = d + def_off + 4;
+    st->def_refs = h[def_off + 1];
+    st->def_lens = h[def_off + 2];
+    st->def_pending = true;
+  }
   info->pages_per_split = pps;
   info->n_items = (int32_t)n_items;
   info->n_combine = (int32_t)n_combine;
@@ -309,11 +349,13 @@ int32_t pkv_stepper_attention(pkv_stepper* st, int32_t layer, const void* q, con
   }
   const pkv_step_info& in = st->info;
   const bool timed = st->t_count < st->t_cap;
+  const int32_t* def = st->def_pending ? st->def_dev : nullptr;
   if (timed) cudaEventRecord(st->t_start[st->t_count], static_cast<cudaStream_t>(stream));
-  int32_t s = pkv_decode_attention(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride, st->rows,
-                                   st->lens, in.rows, in.seq_lens, in.new_blocks, in.items, in.n_items, in.n_combine,
-                                   in.batch, num_q_heads, in.pages_per_split, scale, out, st->ws, st->ws_bytes,
-                                   stream);
+  int32_t s = pkv_decode_attention_ex(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride, st->rows,
+                                      st->lens, in.rows, in.seq_lens, in.new_blocks, in.items, in.n_items,
+                                      in.n_combine, in.batch, num_q_heads, in.pages_per_split, scale, out, st->ws,
+                                      st->ws_bytes, stream, def, st->def_refs, st->def_lens, st->refs);
+  if (s == PKV_OK && def) st->def_pending = false;
   if (timed) cudaEventRecord(st->t_stop[st->t_count++], static_cast<cudaStream_t>(stream));
   if (s == PKV_OK) st->launches += 1 + (in.n_combine > 0 ? 1 : 0);
   return s;

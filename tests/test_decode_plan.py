@@ -44,8 +44,11 @@ def test_plan_covers_every_page_once(hkv, seed):
     for b in range(n):
         for hg in range(groups):
             assert sum(v for (bb, gg, _), v in seen.items() if bb == b and gg == hg) == pages[b]
-    full = [min(pps, pages[b] - (sh >> 8) * pps) == pps for b, sh, _, _ in items.tolist()]
-    assert full == sorted(full, reverse=True)  # full-size items first
+    # sequences by decreasing length, each sequence's items contiguous and in split order
+    order = [b for b, _, _, _ in items.tolist()]
+    firsts = [order[i] for i in range(len(order)) if i == 0 or order[i] != order[i - 1]]
+    assert len(firsts) == n and sorted(firsts) == list(range(n))
+    assert [lens[b] for b in firsts] == sorted(lens.tolist(), reverse=True)
     # one combine entry per (sequence, head group) cut into several items, naming its slots
     want = {(b, hg) for (b, hg, s) in seen if -(-pages[b] // pps) > 1}
     got = set()
