@@ -348,6 +348,9 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
                          const void* k_new, const void* v_new, int32_t num_q_heads, float scale, void* out,
                          void* stream, pkv_step_info* info, int32_t* rows_out, int32_t* lens_out,
                          int32_t* token_blocks_out, int32_t* copies_out, int64_t copies_cap);
+/* The copy-on-write (src, dst) block pairs the last sync / upload applied
+ * (*n_pairs gets their count; up to `capacity` pairs are written). */
+int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs);
 /* The decode workspace's error word (synchronous read; 0 = no error). */
 int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error);
 /* Kernels the stepper has launched so far. */

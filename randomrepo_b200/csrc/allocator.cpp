@@ -65,6 +65,12 @@ struct pkv_allocator {
 
   std::unordered_map<int64_t, Sequence> seqs;
   std::vector<Sequence*> row_owner;
+  // Bumped whenever a sequence is created or destroyed; a decode step over
+  // the same ids as the previous one reuses that step's id -> sequence lookup.
+  uint64_t generation = 0;
+  std::vector<int64_t> step_ids;
+  std::vector<Sequence*> step_seqs;
+  uint64_t step_generation = ~0ull;
   std::priority_queue<int32_t, std::vector<int32_t>, std::greater<int32_t>> free_rows;
   int64_t max_cols = 0;
 
@@ -247,6 +253,7 @@ int32_t pkv_allocator_reserve(pkv_allocator* a, int64_t sequence_id, int64_t tok
     blocks.push_back(b);
   }
   Sequence& s = a->seqs[sequence_id];
+  ++a->generation;
   s.tokens = token_count;
   s.blocks = std::move(blocks);
   s.row = a->take_row(&s);
@@ -290,6 +297,7 @@ int32_t pkv_allocator_release(pkv_allocator* a, int64_t sequence_id) {
   a->free_rows.push(s.row);
   a->mark_len(s.row);
   a->seqs.erase(it);
+  ++a->generation;
   return PKV_OK;
 }
 
@@ -307,6 +315,7 @@ int32_t pkv_allocator_fork(pkv_allocator* a, int64_t parent_id, int64_t child_id
   std::vector<int32_t> blocks = it->second.blocks;
   int64_t tokens = it->second.tokens;
   Sequence& c = a->seqs[child_id];  // may rehash; `it` is not used after this
+  ++a->generation;
   c.tokens = tokens;
   c.blocks = std::move(blocks);
   c.row = a->take_row(&c);
@@ -401,13 +410,25 @@ int32_t pkv_allocator_decode_step(pkv_allocator* a, const int64_t* sequence_ids,
                                   int64_t* done) {
   pkv_clear_error();
   if (done) *done = 0;
+  const bool cached = a->step_generation == a->generation && (int64_t)a->step_ids.size() == n &&
+                      std::memcmp(a->step_ids.data(), sequence_ids, n * sizeof(int64_t)) == 0;
+  if (!cached) {
+    a->step_generation = ~0ull;
+    a->step_ids.assign(sequence_ids, sequence_ids + n);
+    a->step_seqs.assign(n, nullptr);
+  }
   for (int64_t i = 0; i < n; ++i) {
-    auto it = a->seqs.find(sequence_ids[i]);
-    if (it == a->seqs.end()) {
-      pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
-      return PKV_ERR_KEY;
+    Sequence* sp = cached ? a->step_seqs[i] : nullptr;
+    if (!sp) {
+      auto it = a->seqs.find(sequence_ids[i]);
+      if (it == a->seqs.end()) {
+        pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
+        return PKV_ERR_KEY;
+      }
+      sp = &it->second;
+      a->step_seqs[i] = sp;
     }
-    Sequence& s = it->second;
+    Sequence& s = *sp;
     int32_t nb = -1;
     int32_t st = a->append(s, 1, /*track=*/false, &nb);
     if (st != PKV_OK) return st;
@@ -417,6 +438,7 @@ int32_t pkv_allocator_decode_step(pkv_allocator* a, const int64_t* sequence_ids,
     if (token_blocks_out) token_blocks_out[i] = s.blocks.back();
     if (done) *done = i + 1;
   }
+  a->step_generation = a->generation;
   return PKV_OK;
 }
 

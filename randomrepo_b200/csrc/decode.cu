@@ -686,24 +686,26 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
   }
   // Order: sequences by decreasing length, each sequence's items together
   // (head group, then split).  The items of one sequence are taken by several
-  // warps at about the same time, so its split-K combine (done by the item
-  // that finishes last) overlaps other sequences' streaming instead of piling
-  // up at the end of the kernel; the shortest sequences (one or two small
-  // items) come last and even out the tail.
-  std::vector<int32_t> order(batch);
-  for (int b = 0; b < batch; ++b) order[b] = b;
-  std::stable_sort(order.begin(), order.end(),
-                   [&](int32_t x, int32_t y) { return seq_lens[x] > seq_lens[y]; });
-  std::vector<int32_t> slot_of(batch);
+  // warps at about the same time, so its split-K partials are complete early
+  // and the shortest sequences (one or two small items) come last and even
+  // out the tail.  One sort of packed (pages, sequence) keys.
+  thread_local std::vector<int64_t> keys;
+  thread_local std::vector<int32_t> slot_of;
+  keys.resize(batch);
+  slot_of.resize(batch);
   {
     int32_t sl = 0;
     for (int b = 0; b < batch; ++b) {
+      const int64_t pages = (seq_lens[b] + 15) / 16;
+      keys[b] = ((int64_t)(0x7fffffff - pages) << 32) | b;  // ascending key = descending length
       slot_of[b] = sl;
-      sl += groups * (((seq_lens[b] + 15) / 16 + pps - 1) / pps);
+      sl += groups * (int32_t)((pages + pps - 1) / pps);
     }
   }
+  std::sort(keys.begin(), keys.end());
   int32_t* o = items_out;
-  for (int32_t b : order) {
+  for (int64_t key : keys) {
+    const int32_t b = (int32_t)(key & 0xffffffff);
     const int32_t pages = (seq_lens[b] + 15) / 16;
     const int32_t ns = (pages + pps - 1) / pps;
     for (int hg = 0; hg < groups; ++hg) {

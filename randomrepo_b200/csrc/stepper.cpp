@@ -56,6 +56,7 @@ struct pkv_stepper {
   Slot slot[kRing];
   int next = 0;
   std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
+  std::vector<int32_t> last_copies;  // (src, dst) pairs applied by the last sync / upload
   pkv_step_info info{};
   bool step_ready = false;
   void* ws = nullptr;
@@ -154,10 +155,14 @@ struct pkv_stepper {
     int64_t written = 0;
     st = pkv_allocator_drain_updates(alloc, s->host, cap, &written);
     if (st) return st;
-    if (copies_out && s->host[3] > 0) {
+    last_copies.clear();
+    if (s->host[3] > 0) {
       const int64_t off = 4 + 3 * (int64_t)s->host[0] + 2 * (int64_t)s->host[1] + 2 * (int64_t)s->host[2];
-      const int64_t n = std::min<int64_t>(s->host[3], copies_cap);
-      std::memcpy(copies_out, s->host + off, n * 2 * 4);
+      last_copies.assign(s->host + off, s->host + off + 2 * (int64_t)s->host[3]);
+      if (copies_out) {
+        const int64_t n = std::min<int64_t>(s->host[3], copies_cap);
+        std::memcpy(copies_out, s->host + off, n * 2 * 4);
+      }
     }
     *n_copies = s->host[3];
     st = cuda_status(cudaMemcpyAsync(s->dev, s->host, written * 4, cudaMemcpyHostToDevice, stream), "H2D");
@@ -269,6 +274,7 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
   // Only lengths / refcounts pending (the decode never reads them): they ride
   // in the descriptor upload and the decode kernel applies them.
   const bool defer = pt == 0 && pc == 0 && pr + pl > 0;
+  st->last_copies.clear();
   if (!defer) {
     s = st->apply_pending(cs, copies_out, copies_cap, &n_copies);
     if (s) return s;
@@ -370,6 +376,13 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
   s = pkv_stepper_upload(st, stream, info, copies_out, copies_cap);
   if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention
   return pkv_stepper_attention(st, layer, q, k_new, v_new, num_q_heads, scale, out, stream);
+}
+
+int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs) {
+  const int64_t n = (int64_t)st->last_copies.size() / 2;
+  *n_pairs = n;
+  if (pairs_out) std::memcpy(pairs_out, st->last_copies.data(), std::min(n, capacity) * 2 * 4);
+  return PKV_OK;
 }
 
 int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error) {

@@ -32,6 +32,16 @@ from ._lib import lib
 from .device import KVPool
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream(device: torch.device) -> int:
+    """Raw cudaStream_t of the current torch stream on ``device``."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
 class _on_device:
     """Make ``device`` current only if it is not (the common case costs one query)."""
 
@@ -264,7 +274,6 @@ class PagedKVCacheStore:
         # Tokens stored in each block's chunk (-1: the block holds no stored chunk).
         self._block_fill = np.full(allocator.total_blocks, -1, dtype=np.int32)
         self._pool: KVPool | None = None
-        self._copies = np.empty((64, 2), dtype=np.int32)
         if None not in (num_layers, num_kv_heads, head_dim, dtype):
             self._pool = KVPool(allocator, num_layers, num_kv_heads, head_dim, dtype, device)
 
@@ -477,21 +486,19 @@ class PagedKVCacheStore:
         out = self._check_decode_io(pool, n, q, k_new, v_new, out)
         info = _lib.StepInfo()
         host = np.empty((3, n), dtype=np.int32)
-        copies, cap = self._copy_buffer(pool, n)
         with _on_device(pool.device):
-            stream = torch.cuda.current_stream().cuda_stream
+            stream = _current_stream(pool.device)
             sc = float(scale if scale is not None else pool.head_dim ** -0.5)
             st = lib.pkv_stepper_step(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(), k_new.data_ptr(),
                                       v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream, ctypes.byref(info),
-                                      host[0].ctypes.data, host[1].ctypes.data, host[2].ctypes.data,
-                                      copies.ctypes.data, cap)
+                                      host[0].ctypes.data, host[1].ctypes.data, host[2].ctypes.data, None, 0)
             if st == _lib.PKV_ERR_CAPACITY:
                 pool.grow(info.need_rows, info.need_cols)
-                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
+                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
                 if st == _lib.PKV_OK:
                     st = lib.pkv_stepper_attention(pool.stepper, int(layer), q.data_ptr(), k_new.data_ptr(),
                                                    v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream)
-        step = self._finish_step(pool, st, ids, info, host, copies)
+        step = self._finish_step(pool, st, ids, info, host)
         step.committed = True
         return out, step
 
@@ -509,15 +516,14 @@ class PagedKVCacheStore:
         host = np.empty((3, n), dtype=np.int32)
         st = lib.pkv_stepper_begin(pool.stepper, ids.ctypes.data, n, ctypes.byref(info), host[0].ctypes.data,
                                    host[1].ctypes.data, host[2].ctypes.data)
-        copies, cap = self._copy_buffer(pool, n)
         if st == _lib.PKV_OK:
             with _on_device(pool.device):
-                stream = torch.cuda.current_stream().cuda_stream
-                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
+                stream = _current_stream(pool.device)
+                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
                 if st == _lib.PKV_ERR_CAPACITY:
                     pool.grow(info.need_rows, info.need_cols)
-                    st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), copies.ctypes.data, cap)
-        return self._finish_step(pool, st, ids, info, host, copies)
+                    st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+        return self._finish_step(pool, st, ids, info, host)
 
     def decode_attention(self, step: DecodeStep, layer: int, q: torch.Tensor, k_new: torch.Tensor | None = None,
                          v_new: torch.Tensor | None = None, *, scale: float | None = None,
@@ -546,7 +552,7 @@ class PagedKVCacheStore:
                 pool.stepper, int(layer), q.data_ptr(), k_new.data_ptr() if k_new is not None else None,
                 v_new.data_ptr() if v_new is not None else None, q.shape[1],
                 float(scale if scale is not None else pool.head_dim ** -0.5), out.data_ptr(),
-                torch.cuda.current_stream().cuda_stream)
+                _current_stream(pool.device))
         _lib.raise_for_status(st)
         if k_new is not None:
             step.committed = True
@@ -584,13 +590,7 @@ class PagedKVCacheStore:
             raise ValueError("out must be a contiguous tensor shaped and typed like q")
         return out
 
-    def _copy_buffer(self, pool: KVPool, n: int) -> tuple[np.ndarray, int]:
-        cap = max(pool.pending_copies(), n)
-        if self._copies.shape[0] < cap:
-            self._copies = np.empty((2 * cap, 2), dtype=np.int32)
-        return self._copies, self._copies.shape[0]
-
-    def _finish_step(self, pool: KVPool, st: int, ids, info, host, copies) -> DecodeStep:
+    def _finish_step(self, pool: KVPool, st: int, ids, info, host) -> DecodeStep:
         rows, lens, tok_blocks = host[0], host[1], host[2]
         bs = self.allocator.block_size_tokens
         k = int(info.batch)
@@ -598,10 +598,14 @@ class PagedKVCacheStore:
             self._sync()
             self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
             _lib.raise_for_status(st)
-        # Copy-on-write copies first (they carry the source block's fill), then
-        # the fill of the blocks that receive this step's tokens.
-        for src, dst in copies[: info.n_copies].tolist():
-            self._block_fill[dst] = self._block_fill[src]
+        if info.n_copies:
+            n = ctypes.c_int64()
+            pairs = np.empty((info.n_copies, 2), dtype=np.int32)
+            lib.pkv_stepper_copies(pool.stepper, pairs.ctypes.data, info.n_copies, ctypes.byref(n))
+            for src, dst in pairs.tolist():
+                self._block_fill[dst] = self._block_fill[src]
+        # Copy-on-write copies came first (they carry the source block's fill);
+        # then the fill of the blocks that receive this step's tokens.
         self._block_fill[tok_blocks] = (lens - 1) % bs + 1
         pool.step_serial += 1
         return DecodeStep(sequence_ids=ids, info=info, serial=pool.step_serial, host_rows=rows, host_lens=lens)

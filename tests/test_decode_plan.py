@@ -48,7 +48,7 @@ def test_plan_covers_every_page_once(hkv, seed):
     order = [b for b, _, _, _ in items.tolist()]
     firsts = [order[i] for i in range(len(order)) if i == 0 or order[i] != order[i - 1]]
     assert len(firsts) == n and sorted(firsts) == list(range(n))
-    assert [lens[b] for b in firsts] == sorted(lens.tolist(), reverse=True)
+    assert [int(pages[b]) for b in firsts] == sorted(pages.tolist(), reverse=True)
     # one combine entry per (sequence, head group) cut into several items, naming its slots
     want = {(b, hg) for (b, hg, s) in seen if -(-pages[b] // pps) > 1}
     got = set()
