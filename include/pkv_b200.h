@@ -287,6 +287,46 @@ int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t
                                      void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Chunked prefill / speculative verify over pages                           */
+/* ------------------------------------------------------------------------ */
+
+/* Chunk positions one prefill work item covers: 128 / (num_q_heads /
+ * num_kv_heads) (the G query heads of a position share one 128-row tile);
+ * 0 for head counts the kernel does not support. */
+int32_t pkv_prefill_positions_per_item(int32_t num_q_heads, int32_t num_kv_heads);
+
+/* Plan a prefill / verify launch (host).  Sequence i has table row rows[i],
+ * past_lens[i] tokens before its chunk and q_lens[i] chunk queries, packed in
+ * q in sequence order.  Writes int32 [n][4] items (longest key range first)
+ * when items_out is non-NULL and the capacity suffices (else
+ * PKV_ERR_CAPACITY); *n_items_out is always the count needed. */
+int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const int32_t* q_lens, int32_t n_seqs,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t* work_items_out, int64_t items_capacity,
+                         int64_t* n_items_out);
+
+/* Causal paged attention for chunks of queries after cached tokens, one layer
+ * (tcgen05 tensor cores, fp32 accumulation in tensor memory).
+ *   q, out        [total_q][num_q_heads][head_dim], pool dtype (bf16 / f16)
+ *   block_tables  int32 [table_rows][table_stride] (device; every block of
+ *                 past + chunk tokens present, the chunk's K/V already
+ *                 written, e.g. by pkv_scatter_tokens)
+ *   work_items    device copy of pkv_prefill_plan's items
+ *   error_word    device int32, 0 before the call; afterwards 0, or 1 (a
+ *                 bounded wait gave up), 3 (an item outside the launch was
+ *                 skipped), 4 (a block id outside the pool was replaced by 0)
+ * Query i of a chunk after `past` tokens attends to keys 0 .. past + i.
+ * Replaces the attention of the HF forward per prefill chunk
+ * (agentrl/generation/prefill.py:96-104; transformers
+ * integrations/sdpa_attention.py:40-62 with a causal mask after a past) and
+ * of the speculative verify forward (agentrl/generation/speculative.py:229-264,
+ * rows prefix_len-1 .. prefix_len-1+k: a chunk of k+1 queries after
+ * prefix_len-1 tokens).  Requires block_size 16, head_dim 64 or 128. */
+int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* pool, int32_t layer, const void* q,
+                              const int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                              const int32_t* work_items, int32_t n_items, int64_t total_q, int32_t num_q_heads,
+                              float scale, void* out, int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Native decode-step runtime                                                */
 /* ------------------------------------------------------------------------ */
 

@@ -138,6 +138,15 @@ _SIGNATURES: dict[str, tuple] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p,
          c_void_p],
     ),
+    "pkv_prefill_positions_per_item": (c_int32, [c_int32, c_int32]),
+    "pkv_prefill_plan": (
+        c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, I64P]
+    ),
+    "pkv_prefill_attention": (
+        c_int32,
+        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int64,
+         c_int32, c_float, c_void_p, c_void_p, c_void_p],
+    ),
     "pkv_stepper_create": (c_void_p, [c_void_p, POINTER(PoolGeom), c_void_p, I32P]),
     "pkv_stepper_destroy": (None, [c_void_p]),
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),

@@ -104,13 +104,6 @@ struct DecodeParams {
   float scale_log2;
 };
 
-__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(smem_dst)),
-               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 // A work item must name a sequence of the batch whose table row exists, a
 // head group of the pool, a split inside the sequence's pages and a workspace
 // slot inside the item list.

@@ -73,6 +73,8 @@ class KVPool:
         self.refcounts = torch.zeros(self.num_blocks, dtype=torch.int32, device=self.device)
         self.tables = torch.full((64, 64), -1, dtype=torch.int32, device=self.device)
         self.context_lens = torch.zeros(64, dtype=torch.int32, device=self.device)
+        # Error word of the prefill / verify kernel (0 = none).
+        self.prefill_error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         # Kernel launches issued from Python through this pool (the stepper counts its own).
         self.launches = 0
@@ -154,6 +156,21 @@ class KVPool:
         _lib.raise_for_status(lib.pkv_stepper_error(self.stepper, ctypes.byref(err)))
         return int(err.value)
 
+    def prefill_error_flag(self) -> int:
+        """Error word the prefill / verify kernel writes (0 = none); synchronises with the device."""
+        return int(self.prefill_error.item())
+
+    def prefill(self, layer: int, q: torch.Tensor, items: torch.Tensor, n_items: int, num_q_heads: int,
+                scale: float, out: torch.Tensor) -> None:
+        """Launch paged prefill / verify attention (``pkv_prefill_attention``) on the current stream."""
+        rows, cols = self.tables.shape
+        st = lib.pkv_prefill_attention(self._geom_ref, self.pool.data_ptr(), int(layer), q.data_ptr(),
+                                       self.tables.data_ptr(), cols, rows, items.data_ptr(), int(n_items),
+                                       q.shape[0], int(num_q_heads), float(scale), out.data_ptr(),
+                                       self.prefill_error.data_ptr(), _stream_ptr())
+        _lib.raise_for_status(st)
+        self.launches += 1
+
     # -- data movement --------------------------------------------------------
     def scatter(self, layer0: int, k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor | int,
                 n_tokens: int | None = None) -> None:
@@ -206,3 +223,19 @@ def plan_decode(lens: np.ndarray, num_kv_heads: int, num_sms: int,
                                               ctypes.byref(pps), items.ctypes.data, items.shape[0], ctypes.byref(n),
                                               ctypes.byref(nc)))
     return int(pps.value), items, int(n.value), int(nc.value)
+
+
+def plan_prefill(rows: np.ndarray, past_lens: np.ndarray, q_lens: np.ndarray, num_q_heads: int,
+                 num_kv_heads: int) -> np.ndarray:
+    """Plan one prefill / verify launch (``pkv_prefill_plan``): int32 [n_items, 4] work items."""
+    rows = np.ascontiguousarray(rows, dtype=np.int32)
+    past_lens = np.ascontiguousarray(past_lens, dtype=np.int32)
+    q_lens = np.ascontiguousarray(q_lens, dtype=np.int32)
+    if not rows.size == past_lens.size == q_lens.size:
+        raise ValueError("rows, past_lens and q_lens must have one entry per sequence")
+    n = ctypes.c_int64()
+    args = (rows.ctypes.data, past_lens.ctypes.data, q_lens.ctypes.data, rows.size, num_q_heads, num_kv_heads)
+    _lib.raise_for_status(lib.pkv_prefill_plan(*args, None, 0, ctypes.byref(n)))
+    items = np.empty((n.value, 4), dtype=np.int32)
+    _lib.raise_for_status(lib.pkv_prefill_plan(*args, items.ctypes.data, items.shape[0], ctypes.byref(n)))
+    return items

@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 from ._lib import lib
-from .device import KVPool
+from .device import KVPool, plan_prefill
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -565,6 +565,93 @@ class PagedKVCacheStore:
             raise RuntimeError("this decode step is stale: a later decode_step replaced its device descriptor")
         pool.scatter(layer, k_new.permute(1, 0, 2).unsqueeze(0), v_new.permute(1, 0, 2).unsqueeze(0),
                      int(step.info.slots), step.batch)
+
+    # -- device chunked-prefill / speculative-verify path (extension) -----------
+    def prefill_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                          q_lens=None, layer: int = 0, scale: float | None = None,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+        """Causal attention of chunks of queries over the paged cache, one layer.
+
+        Sequence i's chunk is its last ``q_lens[i]`` tokens (already reserved /
+        appended in the allocator): ``k``/``v`` ``[total_q, Hkv, D]`` are
+        written into those slots, then each query ``[total_q, Hq, D]`` (packed in
+        ``sequence_ids`` order) attends to its sequence's earlier tokens and the
+        chunk up to itself -- the attention of one HF forward over a prefill
+        chunk with a past cache (agentrl/generation/prefill.py:96-104).
+        ``q_lens`` defaults to an equal split of ``total_q``.
+        """
+        pool = self._require_pool()
+        ids = self._step_ids(sequence_ids)
+        n = ids.size
+        total_q = q.shape[0] if q.dim() == 3 else -1
+        if q_lens is None:
+            if total_q % n:
+                raise ValueError("q_lens is required when the queries do not split evenly over the sequences")
+            q_lens = np.full(n, total_q // n, dtype=np.int64)
+        q_lens = np.asarray(q_lens, dtype=np.int64).reshape(-1)
+        if q_lens.size != n or (q_lens < 0).any() or int(q_lens.sum()) != total_q:
+            raise ValueError("q_lens must give one non-negative chunk length per sequence summing to q.shape[0]")
+        if q.dim() != 3 or q.shape[2] != pool.head_dim or q.shape[1] % pool.num_kv_heads:
+            raise ValueError("q must be [total_q, num_q_heads, head_dim] with num_q_heads a multiple of num_kv_heads")
+        if q.dtype != pool.dtype or q.device != pool.device or not q.is_contiguous():
+            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
+        shape = (total_q, pool.num_kv_heads, pool.head_dim)
+        for t in (k, v):
+            if t.shape != shape or t.dtype != pool.dtype or t.device != pool.device or not t.is_contiguous():
+                raise ValueError("k/v must be contiguous [total_q, num_kv_heads, head_dim] pool-dtype tensors")
+        if out is None:
+            out = torch.empty_like(q)
+        elif out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or not out.is_contiguous():
+            raise ValueError("out must be a contiguous tensor shaped and typed like q")
+        bs = self.allocator.block_size_tokens
+        # Device tables up to date and copy-on-write copies applied (they carry
+        # their source block's fill) before the chunk's fills are recorded.
+        self._sync()
+        rows = np.empty(n, dtype=np.int32)
+        past = np.empty(n, dtype=np.int32)
+        slot_parts = []
+        for i, sid in enumerate(ids.tolist()):
+            view = self.allocator.view(sid)
+            p0 = view.token_count - int(q_lens[i])
+            if p0 < 0:
+                raise ValueError(f"sequence {sid} holds {view.token_count} tokens, fewer than its chunk of {q_lens[i]}")
+            rows[i] = self.allocator.row(sid)
+            past[i] = p0
+            if q_lens[i]:
+                pos = np.arange(p0, view.token_count, dtype=np.int64)
+                blocks = np.asarray(view.physical_blocks, dtype=np.int64)[pos // bs]
+                slot_parts.append(blocks * bs + pos % bs)
+                np.maximum.at(self._block_fill, blocks, (pos % bs + 1).astype(np.int32))
+        if total_q == 0:
+            return out
+        slots = np.concatenate(slot_parts)
+        items = plan_prefill(rows, past, q_lens, q.shape[1], pool.num_kv_heads)
+        with _on_device(pool.device):
+            dev = pool.device
+            slots_d = torch.from_numpy(slots).to(dev, non_blocking=True)
+            items_d = torch.from_numpy(items).to(dev, non_blocking=True)
+            pool.scatter(layer, k.permute(1, 0, 2).unsqueeze(0), v.permute(1, 0, 2).unsqueeze(0), slots_d)
+            pool.prefill(layer, q, items_d, items.shape[0], q.shape[1],
+                         float(scale if scale is not None else pool.head_dim ** -0.5), out)
+        return out
+
+    def verify_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                         layer: int = 0, scale: float | None = None) -> torch.Tensor:
+        """The k+1-query speculative-verify read, one layer: ``q [B, k+1, Hq, D]`` -> same shape.
+
+        Each sequence already holds its last accepted token and k draft tokens
+        (appended in the allocator); ``k``/``v`` ``[B, k+1, Hkv, D]`` are their
+        K/V.  The rows equal rows ``prefix_len-1 .. prefix_len-1+k`` of the
+        reference's full causal verify forward (agentrl/generation/speculative.py:229-264).
+        Rejected drafts are dropped afterwards with ``truncate``.
+        """
+        if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+            raise ValueError("verify inputs are q [B, k+1, Hq, D] and k/v [B, k+1, Hkv, D]")
+        b, t = q.shape[0], q.shape[1]
+        out = self.prefill_attention(sequence_ids, q.reshape(b * t, q.shape[2], q.shape[3]),
+                                     k.reshape(b * t, k.shape[2], k.shape[3]), v.reshape(b * t, v.shape[2], v.shape[3]),
+                                     q_lens=np.full(b, t, dtype=np.int64), layer=layer, scale=scale)
+        return out.view(q.shape)
 
     @staticmethod
     def _step_ids(sequence_ids) -> np.ndarray:
