@@ -290,9 +290,10 @@ int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t
 /* Chunked prefill / speculative verify over pages                           */
 /* ------------------------------------------------------------------------ */
 
-/* Chunk positions one prefill work item covers: 128 / (num_q_heads /
- * num_kv_heads) (the G query heads of a position share one 128-row tile);
- * 0 for head counts the kernel does not support. */
+/* Chunk positions one prefill work item covers: 2 x 128 / G with G =
+ * num_q_heads / num_kv_heads (the G query heads of a position share a row
+ * block of a 128-row tile, and an item holds two tiles); 0 for head counts
+ * the kernel does not support. */
 int32_t pkv_prefill_positions_per_item(int32_t num_q_heads, int32_t num_kv_heads);
 
 /* Plan a prefill / verify launch (host).  Sequence i has table row rows[i],

@@ -11,27 +11,32 @@
 // KV head h / (Hq/Hkv)).  The chunk's own K/V are written into their pages
 // first (pkv_scatter_tokens), so every key is read from the pool.
 //
-// Tiles: a CTA owns one work item = (sequence, KV head, up to 128/G chunk
-// positions), whose G = Hq/Hkv query heads per position are packed into the
-// 128 rows of one tcgen05 tile (row = position * G + head), so the KV head's
-// pages are read once for all of its query heads.  Keys stream in tiles of
-// 128 (8 pages).  Roles (192 threads):
-//   warp 4      producer: per KV tile, 2 KB cp.async.bulk copies of every
-//               page's 64-dim K and V slabs into a 2-stage ring (the pool's
-//               pages are pre-swizzled, so the slabs land directly in the
-//               128-byte-swizzled canonical operand layouts; no tensor map,
-//               no multicast);
-//   warp 5      allocates 512 tensor-memory columns; lane 0 issues the MMAs:
-//               S_j = Q K_j^T into one of two S buffers (M=128, N=128,
-//               K-major A and B), and O += P_j V_j (K-major P, MN-major V)
-//               into the O accumulator, committing each to mbarriers;
-//   warps 0-3   one thread per tile row: Q load (swizzled into shared
-//               memory), online softmax on S read from tensor memory
-//               (tcgen05.ld), P written as 16-bit into a double-buffered
-//               shared tile, lazy rescaling of O in tensor memory (only
-//               when a row maximum grows by more than 2^8), and the
-//               epilogue O / l -> out.
-// S_{j+1} runs on the tensor cores while warps 0-3 turn S_j into P_j.
+// Tiles: a CTA owns one work item = (sequence, KV head, up to 2 x 128/G chunk
+// positions).  The G = Hq/Hkv query heads of a position are packed into the
+// rows of a 128-row tcgen05 tile (row = position * G + head), and the item's
+// positions fill two such query tiles, A and B, that share every K/V tile the
+// CTA loads: the KV head's pages are read once for 2 x 128 query rows.  Keys
+// stream in tiles of 128 (8 pages).  Roles (320 threads):
+//   warp 8      producer: per KV tile, 2 KB cp.async.bulk copies of every
+//               page's 64-dim K (then V) slabs into separate K and V rings
+//               (the pool's pages are pre-swizzled, so the slabs land directly
+//               in the 128-byte-swizzled canonical operand layouts; no tensor
+//               map, no multicast);
+//   warp 9      allocates all 512 tensor-memory columns (S_A, S_B, O_A, O_B);
+//               lane 0 issues S_X = Q_X K_j^T (M=128, N=128, both operands
+//               K-major in shared memory) and O_X += P_X V_j with P_X read
+//               from tensor memory (it overwrites S_X in place) and V
+//               MN-major in shared memory, in the order S_A(j), P_B V(j-1),
+//               S_B(j), P_A V(j), so the tensor cores work on one tile while
+//               the other tile's softmax runs;
+//   warps 0-3   softmax of tile A, warps 4-7 of tile B (thread = tile row):
+//               Q load (swizzled into shared memory), one 128-column
+//               tcgen05.ld of S per KV tile, online softmax in base 2 with a
+//               lazily kept row maximum (O is rescaled in tensor memory only
+//               when the maximum grows by more than 2^8), P stored back into
+//               tensor memory as packed 16-bit pairs, and the epilogue O / l.
+// Completion of S_X(j) also implies completion of P_X V(j-1) (MMAs complete
+// in issue order), so the O rescale needs no separate wait.
 //
 // Every mbarrier wait is bounded; a timed-out role records an error word and
 // skips the rest of its work, the MMA thread waits (bounded) for its last
@@ -47,13 +52,15 @@
 namespace pkv {
 namespace {
 
-constexpr int kRows = 128;             // tile rows (M)
+constexpr int kRows = 128;             // rows of one query tile (M)
 constexpr int kKeys = 128;             // keys per KV tile (N of S, K of P.V)
 constexpr int kPageRows = 16;          // block_size
 constexpr int kPagesPerTile = kKeys / kPageRows;
-constexpr int kThreads = 192;
-constexpr int kSoftmaxThreads = 128;
-constexpr int kTmemCols = 512;         // S buffers 2 x kKeys, O head_dim
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+constexpr int kTileThreads = 128;      // softmax threads per query tile
+constexpr int kTmemCols = 512;         // S_A, S_B (kKeys each), O_A, O_B (head_dim each)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;    // keep a stale row maximum while the new one exceeds it by <= 2^8
 
@@ -61,22 +68,21 @@ template <int D>
 struct PCfg {
   static constexpr int kSlabs = D / 64;                    // 64-dim (128-byte) slabs per row
   static constexpr int kQSlabBytes = kRows * 128;
-  static constexpr int kQBytes = kSlabs * kQSlabBytes;
+  static constexpr int kQBytes = kSlabs * kQSlabBytes;     // one query tile
   static constexpr int kKVSlabBytes = kKeys * 128;         // one slab of a KV tile
-  static constexpr int kKBytes = kSlabs * kKVSlabBytes;    // K (or V) of one KV tile
-  static constexpr int kStageBytes = 2 * kKBytes;
-  static constexpr int kPSlabBytes = kRows * 128;          // 64 keys of P
-  static constexpr int kPBytes = (kKeys / 64) * kPSlabBytes;
-  static constexpr int kOffKV = kQBytes;
-  static constexpr int kOffP = kOffKV + 2 * kStageBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  static constexpr int kTileBytes = kSlabs * kKVSlabBytes; // K (or V) of one KV tile
+  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kVStages = D == 128 ? 2 : 4;
+  static constexpr int kOffK = 2 * kQBytes;
+  static constexpr int kOffV = kOffK + kKStages * kTileBytes;
+  static constexpr int kOffBar = kOffV + kVStages * kTileBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
-  static constexpr int kCopiesPerPage = 2 * kSlabs;        // K and V slabs of one page
   static constexpr uint32_t kPageSlabBytes = kPageRows * 128;
 };
 
-// Work item (int4): {table row, position of the tile's first query, index of
-// that query in the packed q, kv_head << 16 | positions in the tile}.
+// Work item (int4): {table row, position of the item's first query, index of
+// that query in the packed q, kv_head << 16 | positions in the item}.  The
+// first `ppi` positions form query tile A, the rest tile B.
 struct PrefillParams {
   const void* q;    // [total_q][hq][D]
   void* out;        // [total_q][hq][D]
@@ -91,18 +97,22 @@ struct PrefillParams {
   int32_t hq;
   int32_t hkv;
   int32_t group;
+  int32_t ppi;      // positions per query tile: kRows / group
   int32_t layer;
   int32_t num_blocks;
   float scale_log2;
 };
 
+template <int NK, int NV>
 struct Bars {
-  uint64_t q_full;       // 128 Q-writer arrivals
-  uint64_t kv_full[2];   // producer expect_tx + bulk-copy bytes
-  uint64_t kv_empty[2];  // MMA commit after P_j V_j
-  uint64_t s_full[2];    // MMA commit after S_j
-  uint64_t p_full[2];    // 128 softmax arrivals: P_j written, O rescaled, S_j read
-  uint64_t o_done[2];    // MMA commit after P_j V_j
+  uint64_t q_full[2];    // 128 Q-writer arrivals per query tile
+  uint64_t k_full[NK];   // producer expect_tx + bulk-copy bytes
+  uint64_t k_empty[NK];  // MMA commit after the tile's last S MMA
+  uint64_t v_full[NV];
+  uint64_t v_empty[NV];  // MMA commit after the tile's last P.V MMA
+  uint64_t s_full[2];    // MMA commit after S_X(j)
+  uint64_t p_full[2];    // 128 softmax arrivals: P_X(j) stored, O_X rescaled
+  uint64_t o_done[2];    // MMA commit after the last P_X V MMA
   uint64_t mma_done;     // final commit of the MMA thread
   uint32_t tmem_base;
   int32_t abort;
@@ -125,6 +135,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
+  constexpr int NK = C::kKStages, NV = C::kVStages;
   constexpr uint32_t kAbFormat = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   constexpr uint32_t kIdescS = umma_idesc_f16(kAbFormat, 0, 0, kRows, kKeys);
   constexpr uint32_t kIdescO = umma_idesc_f16(kAbFormat, 0, 1, kRows, D);
@@ -133,9 +144,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   const uint32_t raw_s = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
   uint8_t* q_s = smem;
-  uint8_t* kv_s = smem + C::kOffKV;
-  uint8_t* p_s = smem + C::kOffP;
-  Bars* bars = reinterpret_cast<Bars*>(smem + C::kOffBar);
+  uint8_t* k_s = smem + C::kOffK;
+  uint8_t* v_s = smem + C::kOffV;
+  Bars<NK, NV>* bars = reinterpret_cast<Bars<NK, NV>*>(smem + C::kOffBar);
   volatile int32_t* abort = &bars->abort;
 
   const int tid = threadIdx.x;
@@ -144,252 +155,292 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
 
   const int4 item = p.items[blockIdx.x];
   const int row = item.x, pos0 = item.y, qrow0 = item.z, h = item.w >> 16, nt = item.w & 0xffff;
-  const int kv_len = pos0 + nt;  // keys the tile's last query sees
-  const bool ok = row >= 0 && row < p.table_rows && h >= 0 && h < p.hkv && nt >= 1 && nt * p.group <= kRows &&
-                  pos0 >= 0 && qrow0 >= 0 && (int64_t)qrow0 + nt <= p.total_q &&
+  const int group = p.group, ppi = p.ppi;
+  const int nt_a = min(nt, ppi), nt_b = nt - nt_a;
+  const bool has_b = nt_b > 0;
+  const int kv_len = pos0 + nt;  // keys the item's last query sees
+  const bool ok = row >= 0 && row < p.table_rows && h >= 0 && h < p.hkv && nt >= 1 && nt <= 2 * ppi &&
+                  ppi * group <= kRows && pos0 >= 0 && qrow0 >= 0 && (int64_t)qrow0 + nt <= p.total_q &&
                   (kv_len + kPageRows - 1) / kPageRows <= p.table_stride;
   if (!ok) {  // uniform across the CTA: nothing initialised yet
     if (tid == 0) atomicExch(p.error, kDevBadItem);
     return;
   }
-  const int n_tiles = (kv_len + kKeys - 1) / kKeys;
+  const int n_tiles = (kv_len + kKeys - 1) / kKeys;           // KV tiles of tile B (or A alone)
+  const int n_a = (pos0 + nt_a + kKeys - 1) / kKeys;          // KV tiles tile A needs
 
   if (tid == 0) {
-    mbar_init(&bars->q_full, kSoftmaxThreads);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->kv_full[i], 1);
-      mbar_init(&bars->kv_empty[i], 1);
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], kSoftmaxThreads);
-      mbar_init(&bars->o_done[i], 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->q_full[x], kTileThreads);
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->p_full[x], kTileThreads);
+      mbar_init(&bars->o_done[x], 1);
+    }
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
     }
     mbar_init(&bars->mma_done, 1);
     bars->abort = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(&bars->tmem_base, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(&bars->tmem_base, kTmemCols);
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_o = tmem + 2 * kKeys;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---------------- producer ----------------
-    const char* layer_base = p.pool;
     const int32_t* trow = p.tables + (int64_t)row * p.table_stride;
-    int issued = 0;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (j >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&bars->kv_empty[st], ((j >> 1) - 1) & 1, p, abort)))
-        break;
+    // K (state 0) or V (state 1) pages of KV tile j into one ring stage.
+    auto issue = [&](int state, int j, uint8_t* stage, uint64_t* full) {
       const int key0 = j * kKeys;
       const int pages = min(kPagesPerTile, (kv_len - key0 + kPageRows - 1) / kPageRows);
-      const int copies = pages * C::kCopiesPerPage;
-      if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[st], copies * C::kPageSlabBytes);
+      const int copies = pages * C::kSlabs;
+      if (lane == 0) mbar_arrive_expect_tx(full, copies * C::kPageSlabBytes);
       __syncwarp();
-      uint8_t* stage = kv_s + st * C::kStageBytes;
       for (int c = lane; c < copies; c += 32) {
-        const int pg = c / C::kCopiesPerPage;
-        const int kv = (c / C::kSlabs) & 1;
-        const int slab = c % C::kSlabs;
+        const int pg = c / C::kSlabs, slab = c % C::kSlabs;
         int blk = __ldg(trow + key0 / kPageRows + pg);
         if (blk < 0 || blk >= p.num_blocks) {
           atomicExch(p.error, kDevBadBlock);
           blk = 0;
         }
-        const char* src = layer_base +
-                          page_offset(p.layer, blk, h, kv, p.num_blocks, p.hkv, kPageRows, D * 2) +
+        const char* src = p.pool + page_offset(p.layer, blk, h, state, p.num_blocks, p.hkv, kPageRows, D * 2) +
                           slab * C::kPageSlabBytes;
-        bulk_copy_g2s(stage + kv * C::kKBytes + slab * C::kKVSlabBytes + pg * C::kPageSlabBytes, src,
-                      C::kPageSlabBytes, &bars->kv_full[st]);
+        bulk_copy_g2s(stage + slab * C::kKVSlabBytes + pg * C::kPageSlabBytes, src, C::kPageSlabBytes, full);
       }
-      issued = j + 1;
+    };
+    int k_issued = 0, v_issued = 0;
+    // K runs one tile ahead of V: S(j) needs K(j) before P V(j-1) needs V(j-1).
+    for (int s = 0; s <= n_tiles; ++s) {
+      if (s < n_tiles) {
+        const int st = s % NK;
+        if (s >= NK &&
+            !__all_sync(0xffffffffu, wait_or_abort(&bars->k_empty[st], ((s / NK) - 1) & 1, p, abort)))
+          break;
+        issue(0, s, k_s + st * C::kTileBytes, &bars->k_full[st]);
+        k_issued = s + 1;
+      }
+      if (s >= 1) {
+        const int j = s - 1, st = j % NV;
+        if (j >= NV && !__all_sync(0xffffffffu, wait_or_abort(&bars->v_empty[st], ((j / NV) - 1) & 1, p, abort)))
+          break;
+        issue(1, j, v_s + st * C::kTileBytes, &bars->v_full[st]);
+        v_issued = j + 1;
+      }
     }
     // Copies still in flight must land before the CTA frees its memory.
     if (lane == 0) {
-      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_bounded(&bars->kv_full[j & 1], (j >> 1) & 1);
+      for (int j = max(0, k_issued - NK); j < k_issued; ++j) mbar_wait_bounded(&bars->k_full[j % NK], (j / NK) & 1);
+      for (int j = max(0, v_issued - NV); j < v_issued; ++j) mbar_wait_bounded(&bars->v_full[j % NV], (j / NV) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(q_s);
-      const uint32_t kv_addr = smem_u32(kv_s);
-      const uint32_t p_addr = smem_u32(p_s);
-      auto issue_pv = [&](int i) -> bool {
-        if (!wait_or_abort(&bars->p_full[i & 1], (i >> 1) & 1, p, abort)) return false;
-        tc_fence_after_sync();
-        const int valid = min(kKeys, kv_len - i * kKeys);
-        const int steps = (valid + 15) / 16;
-        const uint32_t v_base = kv_addr + (i & 1) * C::kStageBytes + C::kKBytes;
-        const uint32_t pb = p_addr + (i & 1) * C::kPBytes;
-        for (int ks = 0; ks < steps; ++ks) {
-          const uint64_t adesc = umma_desc_sw128(pb + (ks >> 2) * C::kPSlabBytes + (ks & 3) * 32, 16, 1024);
-          const uint64_t bdesc = umma_desc_sw128(v_base + ks * 2048, C::kKVSlabBytes, 1024);
-          umma_f16_ss(tmem_o, adesc, bdesc, kIdescO, (i > 0 || ks > 0) ? 1u : 0u);
+      const uint32_t k_addr = smem_u32(k_s);
+      const uint32_t v_addr = smem_u32(v_s);
+      auto s_mma = [&](int x, int kst) {
+        const uint32_t qb = q_addr + x * C::kQBytes;
+        const uint32_t kb = k_addr + kst * C::kTileBytes;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * C::kQSlabBytes + (ks & 3) * 32;
+          const uint64_t adesc = umma_desc_sw128(qb + off, 16, 1024);
+          const uint64_t bdesc = umma_desc_sw128(kb + (ks >> 2) * C::kKVSlabBytes + (ks & 3) * 32, 16, 1024);
+          umma_f16_ss(tmem + x * kKeys, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->o_done[i & 1]);
-        umma_commit(&bars->kv_empty[i & 1]);
+        umma_commit(&bars->s_full[x]);
+      };
+      auto pv_mma = [&](int x, int j) -> bool {
+        if (!wait_or_abort(&bars->p_full[x], j & 1, p, abort)) return false;
+        if (!wait_or_abort(&bars->v_full[j % NV], (j / NV) & 1, p, abort)) return false;
+        tc_fence_after_sync();
+        const int steps = (min(kKeys, kv_len - j * kKeys) + 15) / 16;
+        const uint32_t vb = v_addr + (j % NV) * C::kTileBytes;
+        for (int ks = 0; ks < steps; ++ks) {
+          const uint64_t bdesc = umma_desc_sw128(vb + ks * 2048, C::kKVSlabBytes, 1024);
+          umma_f16_ts(tmem + 2 * kKeys + x * D, tmem + x * kKeys + ks * 8, bdesc, kIdescO,
+                      (j > 0 || ks > 0) ? 1u : 0u);
+        }
         return true;
       };
-      bool alive = wait_or_abort(&bars->q_full, 0, p, abort);
+      bool alive = wait_or_abort(&bars->q_full[0], 0, p, abort);
+      if (alive && has_b) alive = wait_or_abort(&bars->q_full[1], 0, p, abort);
       if (alive) tc_fence_after_sync();
       for (int j = 0; alive && j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (!wait_or_abort(&bars->kv_full[st], (j >> 1) & 1, p, abort)) {
+        const int kst = j % NK;
+        if (!wait_or_abort(&bars->k_full[kst], (j / NK) & 1, p, abort)) {
           alive = false;
           break;
         }
         tc_fence_after_sync();
-        const uint32_t k_base = kv_addr + st * C::kStageBytes;
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * C::kQSlabBytes + (ks & 3) * 32;
-          const uint64_t adesc = umma_desc_sw128(q_addr + off, 16, 1024);
-          const uint64_t bdesc = umma_desc_sw128(k_base + (ks >> 2) * C::kKVSlabBytes + (ks & 3) * 32, 16, 1024);
-          umma_f16_ss(tmem + st * kKeys, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
+        if (j < n_a) s_mma(0, kst);
+        if (has_b && j > 0) {
+          if (!pv_mma(1, j - 1)) {
+            alive = false;
+            break;
+          }
+          umma_commit(&bars->v_empty[(j - 1) % NV]);
         }
-        umma_commit(&bars->s_full[st]);
-        if (j > 0 && !issue_pv(j - 1)) alive = false;
+        if (has_b) s_mma(1, kst);
+        umma_commit(&bars->k_empty[kst]);
+        if (j < n_a) {
+          if (!pv_mma(0, j)) {
+            alive = false;
+            break;
+          }
+          if (!has_b) umma_commit(&bars->v_empty[j % NV]);
+          if (j == n_a - 1) umma_commit(&bars->o_done[0]);
+        }
       }
-      if (alive) issue_pv(n_tiles - 1);
+      if (alive && has_b && pv_mma(1, n_tiles - 1)) {
+        umma_commit(&bars->v_empty[(n_tiles - 1) % NV]);
+        umma_commit(&bars->o_done[1]);
+      }
       // Every MMA issued must complete before tensor memory is freed.
       umma_commit(&bars->mma_done);
       mbar_wait_bounded(&bars->mma_done, 0);
     }
     __syncwarp();
   } else {
-    // ---------------- softmax / epilogue (thread = tile row) ----------------
-    const int r = tid;
-    const int group = p.group;
-    const int rows_valid = nt * group;
-    const T* qbase = static_cast<const T*>(p.q);
-    {
-      const bool in = r < rows_valid;
-      const T* src = qbase + (((int64_t)qrow0 + r / group) * p.hq + (int64_t)h * group + r % group) * D;
+    // ---------------- softmax / epilogue: tile x, thread = tile row ----------------
+    const int x = warp >> 2;
+    const int r = tid & (kTileThreads - 1);
+    const int nt_x = x == 0 ? nt_a : nt_b;
+    const int n_x = x == 0 ? n_a : (has_b ? n_tiles : 0);
+    if (n_x > 0) {
+      const int rows_valid = nt_x * group;
+      const int pos_first = pos0 + x * ppi;                       // tile's first position
+      const int pos_r = pos_first + min(r / group, nt_x - 1);     // padding rows repeat the last position
+      const int64_t qrow = (int64_t)qrow0 + x * ppi + r / group;  // this row's query
+      {
+        const T* src = static_cast<const T*>(p.q) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
+        uint8_t* qt = q_s + x * C::kQBytes;
+        const bool in = r < rows_valid;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (in) v = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        *reinterpret_cast<uint4*>(q_s + (c >> 3) * C::kQSlabBytes + swz128(r, c & 7)) = v;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->q_full);
-    }
-    const int pos_r = pos0 + min(r / group, nt - 1);  // padding rows repeat the last position
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool alive = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[st], (j >> 1) & 1, p, abort))) {
-        alive = false;
-        break;
-      }
-      tc_fence_after_sync();
-      const uint32_t s_addr = tmem + lane_base + st * kKeys;
-      const int key0 = j * kKeys;
-      // Pass 1: row maximum over the visible keys.
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int cc = 0; cc < kKeys / 32; ++cc) {
-        float v[32];
-        tmem_ld32(s_addr + cc * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (key0 + cc * 32 + i <= pos_r) mx = fmaxf(mx, v[i]);
-      }
-      mx *= p.scale_log2;
-      float alpha = 1.f;
-      bool rescale = false;
-      if (mx > m_run + kRescaleLog2) {
-        alpha = exp2f(m_run - mx);
-        l_run *= alpha;
-        m_run = mx;
-        rescale = j > 0;
-      }
-      // P_j goes into the buffer P_{j-2} used: that product must be done.
-      if (j >= 2 &&
-          !__all_sync(0xffffffffu, wait_or_abort(&bars->o_done[st], ((j >> 1) - 1) & 1, p, abort))) {
-        alive = false;
-        break;
-      }
-      // Pass 2: P = exp2(S * scale * log2e - m) for visible keys, 0 elsewhere.
-      uint8_t* pb = p_s + st * C::kPBytes;
-#pragma unroll 1
-      for (int cc = 0; cc < kKeys / 32; ++cc) {
-        float v[32];
-        tmem_ld32(s_addr + cc * 32, v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = key0 + cc * 32 + i <= pos_r ? exp2f(fmaf(v[i], p.scale_log2, -m_run)) : 0.f;
-          const float p1 = key0 + cc * 32 + i + 1 <= pos_r ? exp2f(fmaf(v[i + 1], p.scale_log2, -m_run)) : 0.f;
-          l_run += p0 + p1;
-          pk[i >> 1] = MmaOp<T>::pack(p0, p1);
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (in) v = __ldg(reinterpret_cast<const uint4*>(src) + c);
+          *reinterpret_cast<uint4*>(qt + (c >> 3) * C::kQSlabBytes + swz128(r, c & 7)) = v;
         }
-        uint8_t* prow = pb + (cc >> 1) * C::kPSlabBytes;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(prow + swz128(r, (cc & 1) * 4 + c)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->q_full[x]);
       }
-      // Last tile: V rows past the sequence inside its last page are zeroed
-      // so that their zero probabilities multiply finite values.
-      if (j == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
-        if (!__all_sync(0xffffffffu, wait_or_abort(&bars->kv_full[st], (j >> 1) & 1, p, abort))) {
-          alive = false;
-          break;
-        }
-        const int first = kv_len - key0;                       // first stale row of the tile
-        const int last = (first + kPageRows - 1) & ~(kPageRows - 1);
-        uint8_t* vb = kv_s + st * C::kStageBytes + C::kKBytes;
-        for (int c = r; c < (last - first) * 8 * C::kSlabs; c += kSoftmaxThreads) {
-          const int slab = c / ((last - first) * 8);
-          const int rem = c % ((last - first) * 8);
-          *reinterpret_cast<uint4*>(vb + slab * C::kKVSlabBytes + swz128(first + rem / 8, rem & 7)) =
-              make_uint4(0, 0, 0, 0);
-        }
-      }
-      // O *= alpha for rows whose maximum moved (after P_{j-1} V_{j-1} is done).
-      if (__any_sync(0xffffffffu, rescale)) {
-        if (!__all_sync(0xffffffffu,
-                        wait_or_abort(&bars->o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p, abort))) {
+      const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+      const uint32_t s_addr = tmem + lane_base + x * kKeys;
+      const uint32_t o_addr = tmem + lane_base + 2 * kKeys + x * D;
+      // The tile that finishes last with the sequence's last (partial) page zeroes its stale V rows.
+      const bool zero_owner = (x == 0) == (n_a == n_tiles);
+      const float sl2 = p.scale_log2;
+      float m_run = -INFINITY, l_run = 0.f;
+      bool alive = true;
+      for (int j = 0; j < n_x; ++j) {
+        if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[x], j & 1, p, abort))) {
           alive = false;
           break;
         }
         tc_fence_after_sync();
-#pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          float v[32];
-          tmem_ld32(tmem_o + lane_base + cc * 32, v);
+        uint32_t sr[128];
+        tmem_ld128(s_addr, sr);
+        const int key0 = j * kKeys;
+        const bool masked = key0 + kKeys - 1 > pos_first;  // crosses the causal diagonal of this tile
+        const int lim = pos_r - key0;                      // visible columns: c <= lim
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (masked) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(tmem_o + lane_base + cc * 32, v);
+          for (int c = 0; c < kKeys; ++c)
+            if (c <= lim) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < kKeys; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c]));
         }
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_run + kRescaleLog2) {
+          alpha = ex2_approx(m_run - mx);
+          l_run *= alpha;
+          m_run = mx;
+          rescale = j > 0;
+        }
+        // P = 2^(S * scale * log2e - m) for visible keys, 0 elsewhere, packed
+        // 16-bit pairs over the first 64 columns of S (already read).
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = half * 64 + 2 * i;
+            float p0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sl2, -m_run));
+            float p1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sl2, -m_run));
+            if (masked) {
+              p0 = c <= lim ? p0 : 0.f;
+              p1 = c + 1 <= lim ? p1 : 0.f;
+            }
+            l4[i & 3] += p0 + p1;
+            pk[i] = MmaOp<T>::pack(p0, p1);
+          }
+          tmem_st32_nowait(s_addr + half * 32, pk);
+        }
+        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        // Last KV tile: V rows past the sequence inside its last page are
+        // zeroed so that their zero probabilities multiply finite values.
+        if (zero_owner && j == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
+          if (!__all_sync(0xffffffffu,
+                          wait_or_abort(&bars->v_full[j % NV], (j / NV) & 1, p, abort))) {
+            alive = false;
+            break;
+          }
+          const int first = kv_len - key0;                       // first stale row of the tile
+          const int last = (first + kPageRows - 1) & ~(kPageRows - 1);
+          uint8_t* vb = v_s + (j % NV) * C::kTileBytes;
+          for (int c = r; c < (last - first) * 8 * C::kSlabs; c += kTileThreads) {
+            const int slab = c / ((last - first) * 8);
+            const int rem = c % ((last - first) * 8);
+            *reinterpret_cast<uint4*>(vb + slab * C::kKVSlabBytes + swz128(first + rem / 8, rem & 7)) =
+                make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        // O *= alpha for rows whose maximum moved; P V(j-1) completed before S(j).
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            float v[32];
+            tmem_ld32(o_addr + cc * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st32(o_addr + cc * 32, v);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before_sync();
+        mbar_arrive(&bars->p_full[x]);
       }
-      fence_proxy_async_smem();
-      tc_fence_before_sync();
-      mbar_arrive(&bars->p_full[st]);
-    }
-    if (alive) {
-      const int last = n_tiles - 1;
-      if (__all_sync(0xffffffffu, wait_or_abort(&bars->o_done[last & 1], (last >> 1) & 1, p, abort))) {
+      if (alive && __all_sync(0xffffffffu, wait_or_abort(&bars->o_done[x], 0, p, abort))) {
         tc_fence_after_sync();
         const float inv_l = 1.f / l_run;
-        T* dst = static_cast<T*>(p.out) + (((int64_t)qrow0 + r / group) * p.hq + (int64_t)h * group + r % group) * D;
+        T* dst = static_cast<T*>(p.out) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
 #pragma unroll 1
         for (int cc = 0; cc < D / 32; ++cc) {
           float v[32];
-          tmem_ld32(tmem_o + lane_base + cc * 32, v);
+          tmem_ld32(o_addr + cc * 32, v);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) pk[i >> 1] = MmaOp<T>::pack(v[i] * inv_l, v[i + 1] * inv_l);
           if (r < rows_valid) {
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              reinterpret_cast<uint4*>(dst + cc * 32)[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
-                                                                      pk[4 * c + 3]);
+              reinterpret_cast<uint4*>(dst + cc * 32)[c] =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
           }
         }
       }
@@ -398,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
 
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -408,6 +459,7 @@ template <int D, typename T>
 cudaError_t launch_prefill(const PrefillParams& prm, cudaStream_t stream) {
   using C = PCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "prefill tile exceeds the shared memory of one CTA");
+  static_assert(sizeof(Bars<C::kKStages, C::kVStages>) <= 256, "barrier block overflows its slot");
   auto kern = paged_prefill_kernel<D, T>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (err != cudaSuccess) return err;
@@ -418,12 +470,13 @@ cudaError_t launch_prefill(const PrefillParams& prm, cudaStream_t stream) {
 }  // namespace
 }  // namespace pkv
 
+
 using namespace pkv;
 
 extern "C" int32_t pkv_prefill_positions_per_item(int32_t num_q_heads, int32_t num_kv_heads) {
   if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0) return 0;
   const int group = num_q_heads / num_kv_heads;
-  return group > kRows ? 0 : kRows / group;
+  return group > kRows ? 0 : 2 * (kRows / group);  // two query tiles of kRows / group positions
 }
 
 extern "C" int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const int32_t* q_lens,
@@ -527,6 +580,7 @@ extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* poo
   prm.hq = num_q_heads;
   prm.hkv = static_cast<int32_t>(g->num_kv_heads);
   prm.group = num_q_heads / static_cast<int32_t>(g->num_kv_heads);
+  prm.ppi = kRows / prm.group;
   prm.layer = layer;
   prm.num_blocks = static_cast<int32_t>(g->num_blocks);
   prm.scale_log2 = scale * kLog2e;
