@@ -63,6 +63,9 @@ constexpr int kTileThreads = 128;      // softmax threads per query tile
 constexpr int kTmemCols = 512;         // S_A, S_B (kKeys each), O_A, O_B (head_dim each)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;    // keep a stale row maximum while the new one exceeds it by <= 2^8
+#ifndef PKV_PREFILL_POLY_PAIRS
+#define PKV_PREFILL_POLY_PAIRS 0       // of every 8 probability pairs, those whose 2^x runs on the FMA pipes
+#endif
 
 template <int D>
 struct PCfg {
@@ -132,7 +135,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
   return false;
 }
 
-template <int D, typename T>
+template <int D, typename T, int kPoly>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid_constant__ PrefillParams p) {
   using C = PCfg<D>;
   constexpr int NK = C::kKStages, NV = C::kVStages;
@@ -347,21 +350,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           break;
         }
         tc_fence_after_sync();
-        uint32_t sr[128];
-        tmem_ld128(s_addr, sr);
         const int key0 = j * kKeys;
         const bool masked = key0 + kKeys - 1 > pos_first;  // crosses the causal diagonal of this tile
         const int lim = pos_r - key0;                      // visible columns: c <= lim
+        // Pass 1: row maximum of the visible keys (one 128-column read).
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        {
+        uint32_t sr[128];
+        tmem_ld128(s_addr, sr);
         if (masked) {
 #pragma unroll
-          for (int c = 0; c < kKeys; ++c)
-            if (c <= lim) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c]));
+          for (int c = 0; c < kKeys; c += 2)
+            m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], c <= lim ? __uint_as_float(sr[c]) : -INFINITY,
+                                     c + 1 <= lim ? __uint_as_float(sr[c + 1]) : -INFINITY);
         } else {
 #pragma unroll
-          for (int c = 0; c < kKeys; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c]));
+          for (int c = 0; c < kKeys; c += 2)
+            m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
         }
-        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+        }
+        const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
         float alpha = 1.f;
         bool rescale = false;
         if (mx > m_run + kRescaleLog2) {
@@ -370,27 +378,39 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           m_run = mx;
           rescale = j > 0;
         }
-        // P = 2^(S * scale * log2e - m) for visible keys, 0 elsewhere, packed
-        // 16-bit pairs over the first 64 columns of S (already read).
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        // Pass 2, per 32 columns: P = 2^(S * scale * log2e - m) for visible
+        // keys, 0 elsewhere, packed 16-bit pairs over the first 64 columns of
+        // S (each part is read before its pairs land on columns already read;
+        // re-reading S keeps the register peak low).  kPoly
+        // of every 8 pairs take 2^x from the FMA pipes, the rest from the
+        // multi-function unit, so that neither unit alone bounds the tile.
+        const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_run, -m_run);
+        float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+        for (int part = 0; part < kKeys / 32; ++part) {
+          uint32_t sr[32];
+          tmem_ld32_bits(s_addr + part * 32, sr);
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = half * 64 + 2 * i;
-            float p0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sl2, -m_run));
-            float p1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sl2, -m_run));
-            if (masked) {
-              p0 = c <= lim ? p0 : 0.f;
-              p1 = c + 1 <= lim ? p1 : 0.f;
+          for (int i = 0; i < 16; ++i) {
+            const int c = part * 32 + 2 * i;
+            const float2 xv = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2);
+            float2 pv;
+            if ((i & 7) < kPoly) {
+              pv = exp2_poly2(xv);
+            } else {
+              pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
             }
-            l4[i & 3] += p0 + p1;
-            pk[i] = MmaOp<T>::pack(p0, p1);
+            if (masked) {
+              pv.x = c <= lim ? pv.x : 0.f;
+              pv.y = c + 1 <= lim ? pv.y : 0.f;
+            }
+            l2[i & 1] = add2(l2[i & 1], pv);
+            pk[i] = MmaOp<T>::pack(pv.x, pv.y);
           }
-          tmem_st32_nowait(s_addr + half * 32, pk);
+          tmem_st16_nowait(s_addr + part * 16, pk);
         }
-        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        l_run += (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
         // Last KV tile: V rows past the sequence inside its last page are
         // zeroed so that their zero probabilities multiply finite values.
         if (zero_owner && j == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
@@ -460,7 +480,7 @@ cudaError_t launch_prefill(const PrefillParams& prm, cudaStream_t stream) {
   using C = PCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "prefill tile exceeds the shared memory of one CTA");
   static_assert(sizeof(Bars<C::kKStages, C::kVStages>) <= 256, "barrier block overflows its slot");
-  auto kern = paged_prefill_kernel<D, T>;
+  auto kern = paged_prefill_kernel<D, T, PKV_PREFILL_POLY_PAIRS>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (err != cudaSuccess) return err;
   kern<<<prm.n_items, kThreads, C::kSmemBytes, stream>>>(prm);
