@@ -18,6 +18,12 @@ Arms:
   --impl reference   the reference's CPU path (the oracle's restatement of the
                      resident-cache decode step) on the host cores, rank 0 only.
 
+At N=1 the line also carries ``tensor_tiles``: the tcgen05 chunked-prefill
+attention kernel (Qwen2.5-7B attention shape, 32 prompts of U[256,4096] tokens,
+every 512-token chunk in one launch) against the measured bf16 tensor peak, and
+the speculative-verify read (1.5B target shape, 64 sequences, k = 4) against
+the measured HBM bandwidth, each timed alone with CUDA events and L2 flushed.
+
 Multi-GPU (torchrun): every rank owns its own 256 sequences and KV pool (weak
 scaling, no data-path collective); the timed region is bracketed by NCCL
 barriers and the elapsed time is the max over ranks.
@@ -43,6 +49,7 @@ METRIC = "paged-decode tokens/s/GPU at Qwen2.5-1.5B shape; paged-attn HBM GB/s v
 HQ, HKV, D, BS, POOL_BLOCKS, SEQS = 12, 2, 128, 16, 40000, 256
 L2_BYTES = 126 * 2**20
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def workload_config(n_gpus: int) -> dict:
@@ -76,6 +83,17 @@ def measured_peaks() -> tuple[float, str]:
         except (KeyError, ValueError):
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s for a kernel timed on its own (the burst figure)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured bf16_tflops (MEASURED_PEAKS.json)"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_BF16_TFLOPS, "fallback bf16 TFLOP/s"
 
 
 def ncu_traffic() -> float | None:
@@ -313,9 +331,115 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_tiles:
+        del store, q, kn, vn, out, q_d, kn_d, vn_d
+        torch.cuda.empty_cache()
+        result["tensor_tiles"] = run_tensor_tiles(device, args.seed, args.steps, args.warmup)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
     return result
+
+
+PREFILL_SHAPE = {"model": "Qwen2.5-7B attention", "hq": 28, "hkv": 4, "d": 128, "prompts": 32, "len_lo": 256,
+                 "len_hi": 4096, "chunk": 512}
+VERIFY_SHAPE = {"model": "Qwen2.5-1.5B target attention", "hq": 12, "hkv": 2, "d": 128, "seqs": 64, "prefix_lo": 128,
+                "prefix_hi": 1280, "k": 4}
+
+
+def _tile_workload(device: torch.device, hq: int, hkv: int, d: int, seqs, seed: int):
+    """A store whose sequences hold ``total`` tokens of seeded N(0,1) K/V and the planned
+    prefill items for the chunks ``(past, q_len)`` of each sequence; q is seeded N(0,1)."""
+    from randomrepo_b200 import PagedKVAllocator, PagedKVCacheStore
+    from randomrepo_b200.device import plan_prefill
+
+    total = sum(n for n, _ in seqs)
+    store = PagedKVCacheStore(PagedKVAllocator(total // BS + len(seqs) + 64, BS), num_layers=1, num_kv_heads=hkv,
+                              head_dim=d, dtype=torch.bfloat16, device=device)
+    store.pool.pool.normal_(generator=torch.Generator(device=device).manual_seed(seed))
+    rows, past, qls = [], [], []
+    for sid, (n, chunks) in enumerate(seqs):
+        store.reserve(sid, n)
+        for p0, ql in chunks:
+            rows.append(store.allocator.row(sid))
+            past.append(p0)
+            qls.append(ql)
+    store._sync()
+    items = plan_prefill(np.array(rows), np.array(past), np.array(qls), hq, hkv)
+    q = torch.randn((sum(qls), hq, d), device=device,
+                    generator=torch.Generator(device=device).manual_seed(seed + 1)).to(torch.bfloat16)
+    pos_sum = sum(int((np.arange(p0, p0 + ql, dtype=np.int64) + 1).sum()) for p0, ql in zip(past, qls))
+    flops = 4 * hq * d * pos_sum
+    kv_bytes = sum((p0 + ql) * hkv * d * 2 * 2 for p0, ql in zip(past, qls))
+    return store, q, torch.from_numpy(items).to(device), items.shape[0], flops, kv_bytes
+
+
+def _time_prefill(store, q, items, n_items, steps: int, warmup: int) -> tuple[float, int]:
+    """Mean device ms of one pkv_prefill_attention launch (L2 flushed before each) and launches timed."""
+    pool = store.pool
+    out = torch.empty_like(q)
+    scale = q.shape[2] ** -0.5
+    for _ in range(warmup):
+        pool.prefill(0, q, items, n_items, q.shape[1], scale, out)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=q.device)
+    launches0 = pool.launch_count()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        pool.prefill(0, q, items, n_items, q.shape[1], scale, out)
+        e1.record()
+        torch.cuda.synchronize(q.device)
+        times.append(e0.elapsed_time(e1))
+    if pool.prefill_error_flag():
+        raise RuntimeError(f"prefill kernel reported device error {pool.prefill_error_flag()}")
+    return statistics.mean(times), pool.launch_count() - launches0
+
+
+def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -> dict:
+    """The tcgen05 chunked-prefill and speculative-verify attention kernels on their own workloads."""
+    hbm, hbm_kind = measured_peaks()
+    tflops_peak, tflops_kind = measured_tensor_peak()
+    rng = np.random.default_rng(seed)
+    res = {}
+    ps = PREFILL_SHAPE
+    lens = rng.integers(ps["len_lo"], ps["len_hi"] + 1, size=ps["prompts"])
+    seqs = [(int(n), [(c0, min(ps["chunk"], int(n) - c0)) for c0 in range(0, int(n), ps["chunk"])]) for n in lens]
+    store, q, items, n_items, flops, kv_bytes = _tile_workload(device, ps["hq"], ps["hkv"], ps["d"], seqs, seed)
+    ms, launches = _time_prefill(store, q, items, n_items, max(5, steps // 10), warmup)
+    achieved = flops / (ms * 1e-3) / 1e12
+    res["prefill"] = {
+        "workload": f"chunked-prefill attention, 1 layer, {ps['model']} ({ps['hq']}q/{ps['hkv']}kv heads, head_dim "
+                    f"{ps['d']}), {ps['prompts']} prompts of U[{ps['len_lo']},{ps['len_hi']}] tokens, every "
+                    f"{ps['chunk']}-token chunk of every prompt in one launch (causal after its past), bf16, "
+                    f"seed {seed}",
+        "ms": ms, "work_items": n_items, "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tflops_peak, "peak_source": tflops_kind,
+                     "flops_per_launch": flops, "flops_rule": "4 * Hq * D * sum over queries of (position + 1)"},
+        "kv_gb_per_launch": kv_bytes / 1e9,
+    }
+    del store, q, items
+    vs = VERIFY_SHAPE
+    pre = rng.integers(vs["prefix_lo"], vs["prefix_hi"] + 1, size=vs["seqs"])
+    seqs = [(int(p) + vs["k"], [(int(p) - 1, vs["k"] + 1)]) for p in pre]
+    store, q, items, n_items, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2)
+    ms, launches = _time_prefill(store, q, items, n_items, max(10, steps // 5), warmup)
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    res["verify"] = {
+        "workload": f"speculative-verify attention, 1 layer, {vs['model']} ({vs['hq']}q/{vs['hkv']}kv heads, "
+                    f"head_dim {vs['d']}), {vs['seqs']} sequences with prefix U[{vs['prefix_lo']},"
+                    f"{vs['prefix_hi']}], k={vs['k']} drafts: {vs['k'] + 1} causal queries each, bf16, seed {seed}",
+        "ms": ms, "work_items": n_items, "gpu_launches": launches,
+        "tokens_per_s": vs["seqs"] * (vs["k"] + 1) / (ms * 1e-3),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{hbm_kind} hbm_gbs", "bytes_per_launch": kv_bytes,
+                     "bytes_rule": "K and V of prefix + k tokens per sequence and KV head"},
+        "tflops": flops / (ms * 1e-3) / 1e12,
+    }
+    del store, q, items
+    torch.cuda.empty_cache()
+    return res
 
 
 def cpu_baseline(lengths: np.ndarray, seconds: float, sample: int = 32, steps: int | None = None) -> dict:
@@ -411,6 +535,7 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tiles", action="store_true", help="skip the prefill / verify kernel lines (N=1 only)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
