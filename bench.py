@@ -96,6 +96,17 @@ def measured_tensor_peak() -> tuple[float, str]:
     return FALLBACK_BF16_TFLOPS, "fallback bf16 TFLOP/s"
 
 
+def tiles_traffic(which: str) -> float | None:
+    """DRAM bytes per launch of the prefill / verify kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "tensor_tiles.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())[which]["dram_bytes_per_launch"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
 def ncu_traffic() -> float | None:
     """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any."""
     p = ROOT / "profiles" / "paged_decode_microbench.json"
@@ -415,7 +426,7 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
                     f"seed {seed}",
         "ms": ms, "work_items": n_items, "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
-                     "frac": achieved / tflops_peak, "peak_source": tflops_kind,
+                     "frac": achieved / tflops_peak, "peak_source": tflops_kind, "traffic": tiles_traffic("prefill"),
                      "flops_per_launch": flops, "flops_rule": "4 * Hq * D * sum over queries of (position + 1)"},
         "kv_gb_per_launch": kv_bytes / 1e9,
     }
@@ -433,7 +444,7 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
         "ms": ms, "work_items": n_items, "gpu_launches": launches,
         "tokens_per_s": vs["seqs"] * (vs["k"] + 1) / (ms * 1e-3),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": f"{hbm_kind} hbm_gbs", "bytes_per_launch": kv_bytes,
+                     "peak_source": f"{hbm_kind} hbm_gbs", "traffic": tiles_traffic("verify"), "bytes_per_launch": kv_bytes,
                      "bytes_rule": "K and V of prefix + k tokens per sequence and KV head"},
         "tflops": flops / (ms * 1e-3) / 1e12,
     }
