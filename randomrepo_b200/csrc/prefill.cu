@@ -159,8 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   const int4 item = p.items[blockIdx.x];
   const int row = item.x, pos0 = item.y, qrow0 = item.z, h = item.w >> 16, nt = item.w & 0xffff;
   const int group = p.group, ppi = p.ppi;
-  const int nt_a = min(nt, ppi), nt_b = nt - nt_a;
-  const bool has_b = nt_b > 0;
   const int kv_len = pos0 + nt;  // keys the item's last query sees
   const bool ok = row >= 0 && row < p.table_rows && h >= 0 && h < p.hkv && nt >= 1 && nt <= 2 * ppi &&
                   ppi * group <= kRows && pos0 >= 0 && qrow0 >= 0 && (int64_t)qrow0 + nt <= p.total_q &&
@@ -169,8 +167,27 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     if (tid == 0) atomicExch(p.error, kDevBadItem);
     return;
   }
-  const int n_tiles = (kv_len + kKeys - 1) / kKeys;           // KV tiles of tile B (or A alone)
-  const int n_a = (pos0 + nt_a + kKeys - 1) / kKeys;          // KV tiles tile A needs
+  const int n_tiles = (kv_len + kKeys - 1) / kKeys;
+  // Two modes.  Shared: tile A holds the first ppi positions, tile B the rest,
+  // and both read KV tile j at step j (one load serves both).  Split (all
+  // positions fit tile A and there are >= 2 KV tiles): tile B takes the same
+  // queries over the second half of the keys, each half streams its own K/V,
+  // and the two partial softmaxes are merged at the end.
+  const bool split = nt <= ppi && n_tiles >= 2;
+  const int nt_a = min(nt, ppi);
+  const int n_a = split ? (n_tiles + 1) / 2 : (pos0 + nt_a + kKeys - 1) / kKeys;  // KV tiles of tile A
+  const int n_b = split ? n_tiles - n_a : (nt > ppi ? n_tiles : 0);              // KV tiles of tile B
+  const int b_tile0 = split ? n_a : 0;                                             // B's first KV tile
+  const int n_steps = max(n_a, n_b);
+  const bool two_q = n_b > 0 && !split;  // tile B has queries of its own
+  // Index of tile x's step-j K (or V) tile in the order the MMAs consume them:
+  // shared mode one per step; split mode A(0), B(0), A(1), B(1), ... then A's rest.
+  auto use_idx = [&](int x, int j) { return split ? (x == 0 ? j + min(j, n_b) : 2 * j + 1) : j; };
+  const int n_loads = split ? n_a + n_b : n_tiles;
+  auto load_tile = [&](int c) {  // KV tile of load c
+    if (!split) return c;
+    return c < 2 * n_b ? ((c & 1) ? b_tile0 + (c >> 1) : (c >> 1)) : c - n_b;
+  };
 
   if (tid == 0) {
     for (int x = 0; x < 2; ++x) {
@@ -200,9 +217,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   if (warp == kProducerWarp) {
     // ---------------- producer ----------------
     const int32_t* trow = p.tables + (int64_t)row * p.table_stride;
-    // K (state 0) or V (state 1) pages of KV tile j into one ring stage.
-    auto issue = [&](int state, int j, uint8_t* stage, uint64_t* full) {
-      const int key0 = j * kKeys;
+    // K (state 0) or V (state 1) pages of KV tile t into one ring stage.
+    auto issue = [&](int state, int t, uint8_t* stage, uint64_t* full) {
+      const int key0 = t * kKeys;
       const int pages = min(kPagesPerTile, (kv_len - key0 + kPageRows - 1) / kPageRows);
       const int copies = pages * C::kSlabs;
       if (lane == 0) mbar_arrive_expect_tx(full, copies * C::kPageSlabBytes);
@@ -220,28 +237,28 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       }
     };
     int k_issued = 0, v_issued = 0;
-    // K runs one tile ahead of V: S(j) needs K(j) before P V(j-1) needs V(j-1).
-    for (int s = 0; s <= n_tiles; ++s) {
-      if (s < n_tiles) {
+    // K runs one load ahead of V: S(j) needs its K before P V(j-1) needs its V.
+    for (int s = 0; s <= n_loads; ++s) {
+      if (s < n_loads) {
         const int st = s % NK;
         if (s >= NK &&
             !__all_sync(0xffffffffu, wait_or_abort(&bars->k_empty[st], ((s / NK) - 1) & 1, p, abort)))
           break;
-        issue(0, s, k_s + st * C::kTileBytes, &bars->k_full[st]);
+        issue(0, load_tile(s), k_s + st * C::kTileBytes, &bars->k_full[st]);
         k_issued = s + 1;
       }
       if (s >= 1) {
-        const int j = s - 1, st = j % NV;
-        if (j >= NV && !__all_sync(0xffffffffu, wait_or_abort(&bars->v_empty[st], ((j / NV) - 1) & 1, p, abort)))
+        const int c = s - 1, st = c % NV;
+        if (c >= NV && !__all_sync(0xffffffffu, wait_or_abort(&bars->v_empty[st], ((c / NV) - 1) & 1, p, abort)))
           break;
-        issue(1, j, v_s + st * C::kTileBytes, &bars->v_full[st]);
-        v_issued = j + 1;
+        issue(1, load_tile(c), v_s + st * C::kTileBytes, &bars->v_full[st]);
+        v_issued = c + 1;
       }
     }
     // Copies still in flight must land before the CTA frees its memory.
     if (lane == 0) {
-      for (int j = max(0, k_issued - NK); j < k_issued; ++j) mbar_wait_bounded(&bars->k_full[j % NK], (j / NK) & 1);
-      for (int j = max(0, v_issued - NV); j < v_issued; ++j) mbar_wait_bounded(&bars->v_full[j % NV], (j / NV) & 1);
+      for (int c = max(0, k_issued - NK); c < k_issued; ++c) mbar_wait_bounded(&bars->k_full[c % NK], (c / NK) & 1);
+      for (int c = max(0, v_issued - NV); c < v_issued; ++c) mbar_wait_bounded(&bars->v_full[c % NV], (c / NV) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
@@ -249,8 +266,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       const uint32_t q_addr = smem_u32(q_s);
       const uint32_t k_addr = smem_u32(k_s);
       const uint32_t v_addr = smem_u32(v_s);
-      auto s_mma = [&](int x, int kst) {
-        const uint32_t qb = q_addr + x * C::kQBytes;
+      // S_x(j) = Q K^T; in split mode both tiles use tile A's queries.
+      auto s_mma = [&](int x, int j) -> bool {
+        const int c = use_idx(x, j), kst = c % NK;
+        if (!wait_or_abort(&bars->k_full[kst], (c / NK) & 1, p, abort)) return false;
+        tc_fence_after_sync();
+        const uint32_t qb = q_addr + (two_q ? x : 0) * C::kQBytes;
         const uint32_t kb = k_addr + kst * C::kTileBytes;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
@@ -260,53 +281,38 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           umma_f16_ss(tmem + x * kKeys, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full[x]);
+        // The K tile is free once every S that reads it is issued before this commit.
+        if (split || x == 1 || n_b == 0) umma_commit(&bars->k_empty[kst]);
+        return true;
       };
       auto pv_mma = [&](int x, int j) -> bool {
+        const int c = use_idx(x, j), vst = c % NV;
         if (!wait_or_abort(&bars->p_full[x], j & 1, p, abort)) return false;
-        if (!wait_or_abort(&bars->v_full[j % NV], (j / NV) & 1, p, abort)) return false;
+        if (!wait_or_abort(&bars->v_full[vst], (c / NV) & 1, p, abort)) return false;
         tc_fence_after_sync();
-        const int steps = (min(kKeys, kv_len - j * kKeys) + 15) / 16;
-        const uint32_t vb = v_addr + (j % NV) * C::kTileBytes;
+        const int t = x == 0 ? j : b_tile0 + j;
+        const int steps = (min(kKeys, kv_len - t * kKeys) + 15) / 16;
+        const uint32_t vb = v_addr + vst * C::kTileBytes;
         for (int ks = 0; ks < steps; ++ks) {
           const uint64_t bdesc = umma_desc_sw128(vb + ks * 2048, C::kKVSlabBytes, 1024);
           umma_f16_ts(tmem + 2 * kKeys + x * D, tmem + x * kKeys + ks * 8, bdesc, kIdescO,
                       (j > 0 || ks > 0) ? 1u : 0u);
         }
+        if (split || x == 1 || n_b == 0) umma_commit(&bars->v_empty[vst]);
+        if (j == (x == 0 ? n_a : n_b) - 1) umma_commit(&bars->o_done[x]);
         return true;
       };
       bool alive = wait_or_abort(&bars->q_full[0], 0, p, abort);
-      if (alive && has_b) alive = wait_or_abort(&bars->q_full[1], 0, p, abort);
-      if (alive) tc_fence_after_sync();
-      for (int j = 0; alive && j < n_tiles; ++j) {
-        const int kst = j % NK;
-        if (!wait_or_abort(&bars->k_full[kst], (j / NK) & 1, p, abort)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after_sync();
-        if (j < n_a) s_mma(0, kst);
-        if (has_b && j > 0) {
-          if (!pv_mma(1, j - 1)) {
-            alive = false;
-            break;
-          }
-          umma_commit(&bars->v_empty[(j - 1) % NV]);
-        }
-        if (has_b) s_mma(1, kst);
-        umma_commit(&bars->k_empty[kst]);
-        if (j < n_a) {
-          if (!pv_mma(0, j)) {
-            alive = false;
-            break;
-          }
-          if (!has_b) umma_commit(&bars->v_empty[j % NV]);
-          if (j == n_a - 1) umma_commit(&bars->o_done[0]);
-        }
+      if (alive && two_q) alive = wait_or_abort(&bars->q_full[1], 0, p, abort);
+      // Order per step: S_A(j), P_B V(j-1), S_B(j), P_A V(j): the tensor pipe
+      // runs one tile's products while the other tile's softmax works.
+      for (int j = 0; alive && j < n_steps; ++j) {
+        if (j < n_a && !s_mma(0, j)) alive = false;
+        if (alive && j > 0 && j - 1 < n_b && !pv_mma(1, j - 1)) alive = false;
+        if (alive && j < n_b && !s_mma(1, j)) alive = false;
+        if (alive && j < n_a && !pv_mma(0, j)) alive = false;
       }
-      if (alive && has_b && pv_mma(1, n_tiles - 1)) {
-        umma_commit(&bars->v_empty[(n_tiles - 1) % NV]);
-        umma_commit(&bars->o_done[1]);
-      }
+      if (alive && n_b == n_steps && n_b > 0) pv_mma(1, n_b - 1);
       // Every MMA issued must complete before tensor memory is freed.
       umma_commit(&bars->mma_done);
       mbar_wait_bounded(&bars->mma_done, 0);
@@ -316,14 +322,20 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
     // ---------------- softmax / epilogue: tile x, thread = tile row ----------------
     const int x = warp >> 2;
     const int r = tid & (kTileThreads - 1);
-    const int nt_x = x == 0 ? nt_a : nt_b;
-    const int n_x = x == 0 ? n_a : (has_b ? n_tiles : 0);
+    const int nt_x = (split || x == 0) ? nt_a : nt - nt_a;
+    const int n_x = x == 0 ? n_a : n_b;
+    const int row_block = split ? 0 : x;                         // which positions the tile's rows hold
+    const int rows_valid = nt_x * group;
+    const int pos_first = pos0 + row_block * ppi;                // tile's first position
+    const int pos_r = pos_first + min(r / group, nt_x - 1);      // padding rows repeat the last position
+    const int64_t qrow = (int64_t)qrow0 + row_block * ppi + r / group;  // this row's query
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + x * kKeys;
+    const uint32_t o_addr = tmem + lane_base + 2 * kKeys + x * D;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool alive = true;
     if (n_x > 0) {
-      const int rows_valid = nt_x * group;
-      const int pos_first = pos0 + x * ppi;                       // tile's first position
-      const int pos_r = pos_first + min(r / group, nt_x - 1);     // padding rows repeat the last position
-      const int64_t qrow = (int64_t)qrow0 + x * ppi + r / group;  // this row's query
-      {
+      if (x == 0 || two_q) {
         const T* src = static_cast<const T*>(p.q) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
         uint8_t* qt = q_s + x * C::kQBytes;
         const bool in = r < rows_valid;
@@ -336,38 +348,32 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         fence_proxy_async_smem();
         mbar_arrive(&bars->q_full[x]);
       }
-      const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-      const uint32_t s_addr = tmem + lane_base + x * kKeys;
-      const uint32_t o_addr = tmem + lane_base + 2 * kKeys + x * D;
-      // The tile that finishes last with the sequence's last (partial) page zeroes its stale V rows.
-      const bool zero_owner = (x == 0) == (n_a == n_tiles);
       const float sl2 = p.scale_log2;
-      float m_run = -INFINITY, l_run = 0.f;
-      bool alive = true;
       for (int j = 0; j < n_x; ++j) {
         if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[x], j & 1, p, abort))) {
           alive = false;
           break;
         }
         tc_fence_after_sync();
-        const int key0 = j * kKeys;
+        const int t = x == 0 ? j : b_tile0 + j;            // KV tile
+        const int key0 = t * kKeys;
         const bool masked = key0 + kKeys - 1 > pos_first;  // crosses the causal diagonal of this tile
         const int lim = pos_r - key0;                      // visible columns: c <= lim
         // Pass 1: row maximum of the visible keys (one 128-column read).
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         {
-        uint32_t sr[128];
-        tmem_ld128(s_addr, sr);
-        if (masked) {
+          uint32_t sr[128];
+          tmem_ld128(s_addr, sr);
+          if (masked) {
 #pragma unroll
-          for (int c = 0; c < kKeys; c += 2)
-            m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], c <= lim ? __uint_as_float(sr[c]) : -INFINITY,
-                                     c + 1 <= lim ? __uint_as_float(sr[c + 1]) : -INFINITY);
-        } else {
+            for (int c = 0; c < kKeys; c += 2)
+              m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], c <= lim ? __uint_as_float(sr[c]) : -INFINITY,
+                                       c + 1 <= lim ? __uint_as_float(sr[c + 1]) : -INFINITY);
+          } else {
 #pragma unroll
-          for (int c = 0; c < kKeys; c += 2)
-            m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        }
+            for (int c = 0; c < kKeys; c += 2)
+              m4[(c >> 1) & 3] = fmax3(m4[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          }
         }
         const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
         float alpha = 1.f;
@@ -381,9 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         // Pass 2, per 32 columns: P = 2^(S * scale * log2e - m) for visible
         // keys, 0 elsewhere, packed 16-bit pairs over the first 64 columns of
         // S (each part is read before its pairs land on columns already read;
-        // re-reading S keeps the register peak low).  kPoly
-        // of every 8 pairs take 2^x from the FMA pipes, the rest from the
-        // multi-function unit, so that neither unit alone bounds the tile.
+        // re-reading S keeps the register peak low).  kPoly of every 8 pairs
+        // take 2^x from the FMA pipes, the rest from the multi-function unit.
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_run, -m_run);
         float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -411,20 +416,22 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           tmem_st16_nowait(s_addr + part * 16, pk);
         }
         l_run += (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
-        // Last KV tile: V rows past the sequence inside its last page are
-        // zeroed so that their zero probabilities multiply finite values.
-        if (zero_owner && j == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
-          if (!__all_sync(0xffffffffu,
-                          wait_or_abort(&bars->v_full[j % NV], (j / NV) & 1, p, abort))) {
+        // The item's last KV tile: V rows past the sequence inside its last
+        // page are zeroed (by the tile whose product reads it first) so that
+        // their zero probabilities multiply finite values.
+        const bool zero_owner = split ? x == 1 : ((x == 0) == (n_a == n_tiles));
+        if (zero_owner && t == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
+          const int c = use_idx(x, j);
+          if (!__all_sync(0xffffffffu, wait_or_abort(&bars->v_full[c % NV], (c / NV) & 1, p, abort))) {
             alive = false;
             break;
           }
           const int first = kv_len - key0;                       // first stale row of the tile
           const int last = (first + kPageRows - 1) & ~(kPageRows - 1);
-          uint8_t* vb = v_s + (j % NV) * C::kTileBytes;
-          for (int c = r; c < (last - first) * 8 * C::kSlabs; c += kTileThreads) {
-            const int slab = c / ((last - first) * 8);
-            const int rem = c % ((last - first) * 8);
+          uint8_t* vb = v_s + (c % NV) * C::kTileBytes;
+          for (int e = r; e < (last - first) * 8 * C::kSlabs; e += kTileThreads) {
+            const int slab = e / ((last - first) * 8);
+            const int rem = e % ((last - first) * 8);
             *reinterpret_cast<uint4*>(vb + slab * C::kKVSlabBytes + swz128(first + rem / 8, rem & 7)) =
                 make_uint4(0, 0, 0, 0);
           }
@@ -445,17 +452,54 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         tc_fence_before_sync();
         mbar_arrive(&bars->p_full[x]);
       }
-      if (alive && __all_sync(0xffffffffu, wait_or_abort(&bars->o_done[x], 0, p, abort))) {
+    }
+    // Epilogue.  Split mode: tile B hands its row maximum and sum to tile A
+    // through shared memory (tile B's unused query buffer), and tile A merges
+    // the two partial results: O = (O_A 2^(m_A-m) + O_B 2^(m_B-m)) / (l_A
+    // 2^(m_A-m) + l_B 2^(m_B-m)), m = max(m_A, m_B).
+    float* xchg = reinterpret_cast<float*>(q_s + C::kQBytes);
+    if (split) {
+      if (x == 1) {
+        xchg[r] = m_run;
+        xchg[kTileThreads + r] = l_run;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps, once, on every path
+    }
+    if (x == 0 || two_q) {
+      bool done = alive && __all_sync(0xffffffffu, wait_or_abort(&bars->o_done[x], 0, p, abort));
+      if (split) done = done && __all_sync(0xffffffffu, wait_or_abort(&bars->o_done[1], 0, p, abort));
+      if (done) {
         tc_fence_after_sync();
-        const float inv_l = 1.f / l_run;
+        float wa = 1.f, wb = 0.f;
+        float inv_l;
+        if (split) {
+          const float m_b = xchg[r], l_b = xchg[kTileThreads + r];
+          const float m = fmaxf(m_run, m_b);
+          wa = ex2_approx(m_run - m);
+          wb = ex2_approx(m_b - m);
+          inv_l = 1.f / (l_run * wa + l_b * wb);
+        } else {
+          inv_l = 1.f / l_run;
+        }
+        wa *= inv_l;
+        wb *= inv_l;
         T* dst = static_cast<T*>(p.out) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
 #pragma unroll 1
         for (int cc = 0; cc < D / 32; ++cc) {
           float v[32];
           tmem_ld32(o_addr + cc * 32, v);
+          if (split) {
+            float vb[32];
+            tmem_ld32(o_addr + D + cc * 32, vb);  // O_B, same lanes
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = v[i] * wa + vb[i] * wb;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= wa;
+          }
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) pk[i >> 1] = MmaOp<T>::pack(v[i] * inv_l, v[i + 1] * inv_l);
+          for (int i = 0; i < 32; i += 2) pk[i >> 1] = MmaOp<T>::pack(v[i], v[i + 1]);
           if (r < rows_valid) {
 #pragma unroll
             for (int c = 0; c < 4; ++c)
