@@ -3,10 +3,14 @@
 Public API (drop-in for ``agentrl.generation.paged_kv``):
 
 * ``PagedKVSequenceView``, ``PagedKVAllocator``, ``PagedKVCacheStore``;
-* the device decode path ``PagedKVCacheStore.decode_step`` /
-  ``decode_attention`` and copy-on-write ``fork``;
-* KV geometry helpers of ``agentrl.generation.scheduler`` in
-  ``randomrepo_b200.scheduler``.
+* the device paths of the store: ``decode_step`` / ``decode_attention``
+  (fused append + paged GQA decode), ``prefill_attention`` /
+  ``verify_attention`` (chunked prefill and speculative verify on tcgen05),
+  copy-on-write ``fork`` and ``truncate``;
+* ``PagedGenerator`` (``randomrepo_b200.hf``): HF Qwen2-family models
+  prefilling and decoding through the store;
+* ``assign_groups`` / ``StepGather`` (``randomrepo_b200.sharding``): GRPO
+  groups per GPU and the per-step gather of sampled tokens and logprobs.
 
 All device work runs in ``libpkv_b200.so`` (hand-written sm_100a kernels),
 built in-tree by ``python -m randomrepo_b200.build``.  The library is loaded
@@ -21,6 +25,10 @@ _EXPORTS = {
     "PagedKVAllocator": "paged_kv",
     "PagedKVCacheStore": "paged_kv",
     "PagedKVSequenceView": "paged_kv",
+    "PagedGenerator": "hf",
+    "SamplingConfig": "hf",
+    "StepGather": "sharding",
+    "assign_groups": "sharding",
 }
 
 __all__ = sorted(_EXPORTS)

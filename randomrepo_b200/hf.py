@@ -1,0 +1,296 @@
+"""HF transformers models (Qwen2 family) decoding and prefilling through the paged KV store.
+
+AgentRL's continuous-batching loop (agentrl/generation/continuous.py:363-504)
+keeps one HF ``DynamicCache`` per sequence, stacks the caches of a length
+bucket, runs the model forward over one token and splits the caches again,
+every step.  Here the paged store is the cache:
+
+* ``register()`` adds the attention implementation ``"paged_b200"`` to HF's
+  ``AttentionInterface``.  A model switched to it runs its projections,
+  rotary embeddings and MLPs unchanged; each attention layer hands its fresh
+  q/k/v to the store, which appends k/v into the pages and attends over them
+  (``decode_attention`` for a decode step, ``prefill_attention`` for packed
+  prompt chunks).  HF builds no causal mask for an implementation it has no
+  mask function for, and no HF cache is passed, so nothing else is stored.
+* ``PagedGenerator`` is the rollout loop on top: packed (and chunked) prefill
+  of many prompts in one forward, copy-on-write forks of a GRPO group's
+  prompt pages, and decode steps over all active sequences at once (one
+  allocator step, one forward, no length buckets and no per-sequence cache
+  stacking), with greedy or temperature / top-p sampling as in
+  agentrl/core/rollout.py:307-329.
+
+Only ``last_hidden_state`` rows that need logits go through the LM head, so a
+long packed prefill never materialises [tokens, vocab] logits.  By default
+the head runs in fp32 on the model's final hidden state (an fp32 copy of its
+weight is kept): a bf16 head rounds logits to 8 bits of mantissa, which
+leaves exact ties in the argmax and coarse log-probabilities for the trainer.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import threading
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+ATTN_IMPLEMENTATION = "paged_b200"
+
+_local = threading.local()
+
+
+@dataclass
+class _Phase:
+    kind: str                    # "decode" or "prefill"
+    store: object
+    step: object = None          # DecodeStep for a decode phase
+    sequence_ids: list = field(default_factory=list)
+    q_lens: np.ndarray | None = None
+
+
+@contextlib.contextmanager
+def _phase(ph: _Phase):
+    prev = getattr(_local, "phase", None)
+    _local.phase = ph
+    try:
+        yield
+    finally:
+        _local.phase = prev
+
+
+def paged_attention_forward(module, query, key, value, attention_mask=None, scaling=None, dropout=0.0, **kwargs):
+    """HF attention-interface entry: q [B, Hq, T, D], k/v [B, Hkv, T, D] -> ([B, T, Hq, D], None)."""
+    ph = getattr(_local, "phase", None)
+    if ph is None:
+        raise RuntimeError("paged_b200 attention ran outside a PagedGenerator forward")
+    layer = int(module.layer_idx)
+    b, hq, t, d = query.shape
+    hkv = key.shape[1]
+    q = query.transpose(1, 2)
+    k = key.transpose(1, 2)
+    v = value.transpose(1, 2)
+    if ph.kind == "decode":
+        if t != 1:
+            raise ValueError("a decode step feeds one token per sequence")
+        out = ph.store.decode_attention(ph.step, layer, q.reshape(b, hq, d).contiguous(),
+                                        k.reshape(b, hkv, d).contiguous(), v.reshape(b, hkv, d).contiguous(),
+                                        scale=scaling)
+        return out.view(b, 1, hq, d), None
+    if b != 1:
+        raise ValueError("prefill runs packed: batch 1, the chunks of all sequences along the token axis")
+    out = ph.store.prefill_attention(ph.sequence_ids, q.reshape(t, hq, d).contiguous(),
+                                     k.reshape(t, hkv, d).contiguous(), v.reshape(t, hkv, d).contiguous(),
+                                     q_lens=ph.q_lens, layer=layer, scale=scaling)
+    return out.view(1, t, hq, d), None
+
+
+def register() -> None:
+    """Make ``"paged_b200"`` a valid ``config._attn_implementation`` (idempotent)."""
+    from transformers import AttentionInterface
+
+    AttentionInterface.register(ATTN_IMPLEMENTATION, paged_attention_forward)
+
+
+def use_paged_attention(model) -> None:
+    """Switch a loaded HF model to the paged attention implementation."""
+    register()
+    model.config._attn_implementation = ATTN_IMPLEMENTATION
+    for sub in model.modules():
+        cfg = getattr(sub, "config", None)
+        if cfg is not None and cfg is not model.config:
+            cfg._attn_implementation = ATTN_IMPLEMENTATION
+
+
+def kv_geometry(config) -> tuple[int, int, int]:
+    """(layers, KV heads, head dim) of a model config, by the rule of
+    agentrl/generation/scheduler.py:16-29: KV heads fall back to the attention
+    heads, head_dim to hidden_size / attention heads."""
+    layers = int(config.num_hidden_layers)
+    heads = int(getattr(config, "num_key_value_heads", None) or config.num_attention_heads)
+    head_dim = getattr(config, "head_dim", None)
+    if head_dim is None:
+        head_dim = int(config.hidden_size) // int(config.num_attention_heads)
+    return layers, heads, int(head_dim)
+
+
+def make_store(model, total_blocks: int, block_size: int = 16, device=None):
+    """A PagedKVCacheStore shaped for ``model`` (layers, KV heads, head dim, dtype)."""
+    from .paged_kv import PagedKVAllocator, PagedKVCacheStore
+
+    layers, heads, head_dim = kv_geometry(model.config)
+    dtype = next(model.parameters()).dtype
+    dev = device if device is not None else next(model.parameters()).device
+    return PagedKVCacheStore(PagedKVAllocator(total_blocks, block_size), num_layers=layers, num_kv_heads=heads,
+                             head_dim=head_dim, dtype=dtype, device=dev)
+
+
+@dataclass
+class SamplingConfig:
+    """agentrl/core/rollout.py:307-329: greedy unless do_sample with temperature > 0 (then top-p)."""
+
+    do_sample: bool = False
+    temperature: float = 1.0
+    top_p: float = 1.0
+    seed: int = 0
+
+
+def _top_p(logits: torch.Tensor, top_p: float) -> torch.Tensor:
+    if top_p >= 1.0:
+        return logits
+    sorted_logits, idx = torch.sort(logits, descending=True, dim=-1)
+    probs = torch.softmax(sorted_logits, dim=-1)
+    cum = probs.cumsum(dim=-1)
+    drop = cum - probs > top_p
+    sorted_logits = sorted_logits.masked_fill(drop, float("-inf"))
+    return torch.full_like(logits, float("-inf")).scatter(-1, idx, sorted_logits)
+
+
+class PagedGenerator:
+    """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches)."""
+
+    def __init__(self, model, store, *, prefill_chunk_size: int = 512, eos_token_id: int | None = None,
+                 fp32_logits: bool = True) -> None:
+        use_paged_attention(model)
+        self.model = model
+        self.store = store
+        self.prefill_chunk_size = int(prefill_chunk_size)
+        self.eos_token_id = eos_token_id
+        self.device = next(model.parameters()).device
+        self._base = model.get_decoder() if hasattr(model, "get_decoder") else model.model
+        self._head = model.get_output_embeddings()
+        self._head32 = None
+        if fp32_logits:
+            w = self._head.weight.detach().float()
+            b = None if getattr(self._head, "bias", None) is None else self._head.bias.detach().float()
+            self._head32 = (w, b)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """LM head on final hidden states [n, hidden] -> float32 logits [n, vocab]."""
+        with torch.inference_mode():
+            if self._head32 is not None:
+                return torch.nn.functional.linear(hidden.float(), *self._head32)
+            return self._head(hidden).float()
+
+    # -- forwards -------------------------------------------------------------
+    def _forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor, ph: _Phase) -> torch.Tensor:
+        with _phase(ph), torch.inference_mode():
+            out = self._base(input_ids=input_ids, position_ids=position_ids, use_cache=False)
+        return out.last_hidden_state
+
+    def prefill(self, sequence_ids, prompts) -> torch.Tensor:
+        """Reserve each prompt, write its K/V, return next-token logits [n, vocab] (float32).
+
+        All prompts go through one packed forward per round of chunks of at
+        most ``prefill_chunk_size`` tokens (continuous.py:944-976 prefills one
+        prompt at a time; prefill.py:65-111 chunks a long one).
+        """
+        ids = [int(s) for s in sequence_ids]
+        toks = [torch.as_tensor(p, dtype=torch.long).reshape(-1) for p in prompts]
+        if len(ids) != len(toks):
+            raise ValueError("one prompt per sequence id")
+        if any(t.numel() == 0 for t in toks):
+            raise ValueError("prompts must be non-empty")
+        for sid in ids:
+            self.store.reserve(sid, 0)
+        last_hidden = [None] * len(ids)
+        cs = self.prefill_chunk_size
+        rounds = max((t.numel() + cs - 1) // cs for t in toks)
+        for c in range(rounds):
+            members = [i for i, t in enumerate(toks) if t.numel() > c * cs]
+            chunks = [toks[i][c * cs:(c + 1) * cs] for i in members]
+            q_lens = np.array([ch.numel() for ch in chunks], dtype=np.int64)
+            for i, ch in zip(members, chunks):
+                self.store.append_tokens(ids[i], ch.numel())
+            input_ids = torch.cat(chunks).to(self.device).unsqueeze(0)
+            pos = torch.cat([torch.arange(c * cs, c * cs + ch.numel()) for ch in chunks]).to(self.device)
+            h = self._forward(input_ids, pos.unsqueeze(0),
+                              _Phase("prefill", self.store, sequence_ids=[ids[i] for i in members], q_lens=q_lens))
+            ends = np.cumsum(q_lens) - 1
+            for j, i in enumerate(members):
+                if (c + 1) * cs >= toks[i].numel():
+                    last_hidden[i] = h[0, int(ends[j])]
+        return self.logits(torch.stack(last_hidden))
+
+    def decode_step(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
+        """Feed one token per sequence; returns next-token logits [n, vocab] (float32)."""
+        step = self.store.decode_step(sequence_ids)
+        pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
+        h = self._forward(tokens.reshape(-1, 1).to(self.device), pos.reshape(-1, 1),
+                          _Phase("decode", self.store, step=step))
+        return self.logits(h[:, -1])
+
+    # -- sampling ---------------------------------------------------------------
+    @staticmethod
+    def sample(logits: torch.Tensor, cfg: SamplingConfig, gen: torch.Generator | None) -> torch.Tensor:
+        if cfg.do_sample and cfg.temperature > 0:
+            probs = torch.softmax(_top_p(logits / cfg.temperature, cfg.top_p), dim=-1)
+            return torch.multinomial(probs, 1, generator=gen).reshape(-1)
+        return torch.argmax(logits, dim=-1)
+
+    # -- rollout ----------------------------------------------------------------
+    def generate(self, prompts, *, group_size: int = 1, max_new_tokens: int = 16,
+                 sampling: SamplingConfig | None = None, force_tokens=None, first_id: int = 0,
+                 release: bool = True) -> dict:
+        """Roll out ``group_size`` completions per prompt.
+
+        Each prompt is prefilled once; the other members of its group fork the
+        prompt's pages (copy-on-write) and start from the same next-token
+        logits.  Returns ``{"sequence_ids", "tokens" (list per sequence),
+        "logprobs" (list per sequence), "argmax" (per step, the greedy token
+        of each sequence's logits)}``.  ``force_tokens[i]`` (optional) feeds
+        sequence i those tokens instead of sampled ones (teacher forcing).
+        """
+        cfg = sampling or SamplingConfig()
+        gen = None
+        if cfg.do_sample:
+            gen = torch.Generator(device=self.device).manual_seed(cfg.seed)
+        n_groups = len(prompts)
+        heads = [first_id + g * group_size for g in range(n_groups)]
+        logits = self.prefill(heads, prompts)
+        seq_ids, next_logits = [], []
+        for g in range(n_groups):
+            for m in range(group_size):
+                sid = heads[g] + m
+                if m:
+                    self.store.fork(heads[g], sid)
+                seq_ids.append(sid)
+                next_logits.append(logits[g])
+        cur = torch.stack(next_logits)
+        n = len(seq_ids)
+        tokens = [[] for _ in range(n)]
+        logprobs = [[] for _ in range(n)]
+        argmax = [[] for _ in range(n)]
+        active = list(range(n))
+        for step in range(max_new_tokens):
+            if not active:
+                break
+            lp = torch.log_softmax(cur, dim=-1)
+            am = torch.argmax(cur, dim=-1)
+            if force_tokens is not None:
+                nxt = torch.tensor([int(force_tokens[i][step]) for i in active], device=cur.device)
+            else:
+                nxt = self.sample(cur, cfg, gen)
+            chosen_lp = lp.gather(1, nxt.reshape(-1, 1)).reshape(-1)
+            nxt_h, lp_h, am_h = nxt.tolist(), chosen_lp.tolist(), am.tolist()
+            still = []
+            for j, i in enumerate(active):
+                tokens[i].append(nxt_h[j])
+                logprobs[i].append(lp_h[j])
+                argmax[i].append(am_h[j])
+                done = (self.eos_token_id is not None and nxt_h[j] == self.eos_token_id) or \
+                    len(tokens[i]) >= max_new_tokens
+                if not done:
+                    still.append(j)
+                elif release and self.store.has_sequence(seq_ids[i]):
+                    self.store.release(seq_ids[i])
+            if not still:
+                break
+            keep = torch.tensor(still, device=cur.device)
+            active = [active[j] for j in still]
+            cur = self.decode_step([seq_ids[i] for i in active], nxt[keep])
+        if release:
+            for sid in seq_ids:
+                if self.store.has_sequence(sid):
+                    self.store.release(sid)
+        return {"sequence_ids": seq_ids, "tokens": tokens, "logprobs": logprobs, "argmax": argmax}

@@ -1,0 +1,175 @@
+"""HF integration plumbing on CPU: PagedGenerator over a fake store equals HF's own greedy generate.
+
+The fake store below is test infrastructure: it keeps every sequence's K/V
+per layer in plain fp32 tensors (with copy-on-write forks, releases and the
+decode-step descriptor the real store returns) and attends with the oracle's
+arithmetic (oracle/attention.py).  Running a tiny fp32 Qwen2 through
+``PagedGenerator`` with it checks, without a GPU, everything the integration
+adds around the kernels: the attention-interface layouts, packed and chunked
+prefill positions, decode positions, group forks and sampling bookkeeping.
+The result must equal HF ``generate`` (SDPA, DynamicCache, greedy) token for
+token.  The same generator runs on the device store in tests/test_gpu_hf.py.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import gqa_attention
+
+
+@dataclass
+class _FakeStep:
+    host_lens: np.ndarray
+    ids: list
+
+
+class FakeStore:
+    def __init__(self, layers: int):
+        self.layers = layers
+        self.kv = {}    # sid -> list per layer of [k [T,Hkv,D], v]
+        self.count = {}
+
+    def reserve(self, sid, n):
+        assert sid not in self.count
+        self.count[sid] = n
+        self.kv[sid] = [[None, None] for _ in range(self.layers)]
+
+    def append_tokens(self, sid, n):
+        self.count[sid] += n
+
+    def fork(self, parent, child):
+        self.count[child] = self.count[parent]
+        self.kv[child] = [[k.clone(), v.clone()] for k, v in self.kv[parent]]
+
+    def has_sequence(self, sid):
+        return sid in self.count
+
+    def release(self, sid):
+        del self.count[sid], self.kv[sid]
+
+    def decode_step(self, ids):
+        for s in ids:
+            self.count[s] += 1
+        return _FakeStep(np.array([self.count[s] for s in ids]), list(ids))
+
+    def _append(self, sid, layer, k, v):
+        ent = self.kv[sid][layer]
+        ent[0] = k if ent[0] is None else torch.cat([ent[0], k])
+        ent[1] = v if ent[1] is None else torch.cat([ent[1], v])
+        assert ent[0].shape[0] == self.count[sid]
+
+    def decode_attention(self, step, layer, q, k, v, scale=None):
+        outs = []
+        for i, sid in enumerate(step.ids):
+            self._append(sid, layer, k[i:i + 1], v[i:i + 1])
+            kk, vv = self.kv[sid][layer]
+            o = gqa_attention(q[i:i + 1].numpy(), kk.numpy(), vv.numpy(), scale, past=kk.shape[0] - 1)
+            outs.append(torch.from_numpy(o))
+        return torch.cat(outs).to(q.dtype)
+
+    def prefill_attention(self, ids, q, k, v, q_lens=None, layer=0, scale=None):
+        outs, off = [], 0
+        for sid, n in zip(ids, q_lens):
+            n = int(n)
+            self._append(sid, layer, k[off:off + n], v[off:off + n])
+            kk, vv = self.kv[sid][layer]
+            past = kk.shape[0] - n
+            o = gqa_attention(q[off:off + n].numpy(), kk.numpy(), vv.numpy(), scale, past=past)
+            outs.append(torch.from_numpy(o))
+            off += n
+        return torch.cat(outs).to(q.dtype)
+
+
+def _tiny_model():
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=128, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                      rope_theta=10000.0, attn_implementation="sdpa")
+    return Qwen2ForCausalLM(cfg).eval()
+
+
+def test_paged_generator_equals_hf_greedy_generate_on_cpu():
+    import copy
+
+    from randomrepo_b200.hf import PagedGenerator
+
+    ref = _tiny_model()
+    ours = copy.deepcopy(ref)
+    gen = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 128, (n,), generator=gen) for n in (9, 23, 40)]
+    new = 12
+    want = []
+    for p in prompts:
+        out = ref.generate(p.unsqueeze(0), attention_mask=torch.ones(1, p.numel(), dtype=torch.long),
+                           max_new_tokens=new, do_sample=False, pad_token_id=0)
+        want.append(out[0, p.numel():].tolist())
+    g = PagedGenerator(ours, FakeStore(2), prefill_chunk_size=16)  # prompts of 23 / 40 tokens take 2-3 chunks
+    res = g.generate(prompts, group_size=2, max_new_tokens=new)
+    assert res["sequence_ids"] == [0, 1, 2, 3, 4, 5]
+    for gi in range(3):
+        for m in range(2):
+            assert res["tokens"][2 * gi + m] == want[gi]
+    assert ours.config._attn_implementation == "paged_b200"
+    assert not g.store.count  # every sequence released
+
+
+def test_teacher_forcing_and_sampling_bookkeeping():
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig
+
+    model = _tiny_model()
+    g = PagedGenerator(model, FakeStore(2), prefill_chunk_size=64, eos_token_id=None)
+    prompts = [torch.arange(5), torch.arange(7)]
+    forced = [[3, 4, 5, 6], [7, 8, 9, 10]]
+    res = g.generate(prompts, max_new_tokens=4, force_tokens=forced)
+    assert res["tokens"] == forced
+    assert all(len(a) == 4 for a in res["argmax"])
+    assert all(np.isfinite(res["logprobs"][i]).all() for i in range(2))
+    s1 = g.generate(prompts, max_new_tokens=6, sampling=SamplingConfig(do_sample=True, temperature=1.0, seed=5),
+                    first_id=100)
+    s2 = g.generate(prompts, max_new_tokens=6, sampling=SamplingConfig(do_sample=True, temperature=1.0, seed=5),
+                    first_id=200)
+    assert s1["tokens"] == s2["tokens"]  # seeded sampling is reproducible
+
+
+def test_eos_stops_and_releases():
+    from randomrepo_b200.hf import PagedGenerator
+
+    model = _tiny_model()
+    store = FakeStore(2)
+    g = PagedGenerator(model, store, eos_token_id=None)
+    first = g.generate([torch.arange(6)], max_new_tokens=3)["tokens"][0]
+    g2 = PagedGenerator(model, store, eos_token_id=first[1])
+    res = g2.generate([torch.arange(6)], max_new_tokens=8, first_id=10)
+    assert res["tokens"][0] == first[:2]  # stops right after emitting eos
+    assert not store.count
+
+
+def test_paged_attention_outside_a_generator_raises():
+    from randomrepo_b200.hf import paged_attention_forward
+
+    class M:
+        layer_idx = 0
+
+    with pytest.raises(RuntimeError):
+        paged_attention_forward(M(), torch.zeros(1, 4, 1, 16), torch.zeros(1, 2, 1, 16), torch.zeros(1, 2, 1, 16))
+
+
+def test_kv_geometry_follows_the_reference_rule():
+    from types import SimpleNamespace
+
+    from randomrepo_b200.hf import kv_geometry
+
+    # agentrl/generation/scheduler.py:16-29
+    assert kv_geometry(SimpleNamespace(num_hidden_layers=28, num_key_value_heads=2, num_attention_heads=12,
+                                       hidden_size=1536)) == (28, 2, 128)
+    assert kv_geometry(SimpleNamespace(num_hidden_layers=2, num_key_value_heads=None, num_attention_heads=4,
+                                       hidden_size=64, head_dim=None)) == (2, 4, 16)
+    assert kv_geometry(SimpleNamespace(num_hidden_layers=24, num_key_value_heads=2, num_attention_heads=14,
+                                       hidden_size=896, head_dim=64)) == (24, 2, 64)
