@@ -298,12 +298,21 @@ int32_t pkv_prefill_positions_per_item(int32_t num_q_heads, int32_t num_kv_heads
 
 /* Plan a prefill / verify launch (host).  Sequence i has table row rows[i],
  * past_lens[i] tokens before its chunk and q_lens[i] chunk queries, packed in
- * q in sequence order.  Writes int32 [n][4] items (longest key range first)
- * when items_out is non-NULL and the capacity suffices (else
- * PKV_ERR_CAPACITY); *n_items_out is always the count needed. */
+ * q in sequence order.  Output: int32 [n_items + n_combine][8] records, the
+ * work items (longest key range first) then the combine entries.  With
+ * split_waves > 0 and fewer than split_waves x num_sms items (a verify step),
+ * the keys of an item whose queries fit one tile are cut into ranges (about
+ * split_waves CTAs per SM in all) that each write a partial into one of
+ * *n_slots_out workspace slots, merged by a combine entry; 0 keeps one CTA
+ * per item.  Records are written when items_out is non-NULL and the capacity (in
+ * records) suffices (else PKV_ERR_CAPACITY); the counts are always set. */
 int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const int32_t* q_lens, int32_t n_seqs,
-                         int32_t num_q_heads, int32_t num_kv_heads, int32_t* work_items_out, int64_t items_capacity,
-                         int64_t* n_items_out);
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t num_sms, int32_t split_waves,
+                         int32_t* work_items_out, int64_t items_capacity, int64_t* n_items_out,
+                         int64_t* n_combine_out, int64_t* n_slots_out);
+
+/* Bytes of workspace pkv_prefill_attention needs for n_slots partials. */
+int64_t pkv_prefill_workspace_bytes(int64_t n_slots, int32_t head_dim);
 
 /* Causal paged attention for chunks of queries after cached tokens, one layer
  * (tcgen05 tensor cores, fp32 accumulation in tensor memory).
@@ -311,10 +320,13 @@ int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const in
  *   block_tables  int32 [table_rows][table_stride] (device; every block of
  *                 past + chunk tokens present, the chunk's K/V already
  *                 written, e.g. by pkv_scatter_tokens)
- *   work_items    device copy of pkv_prefill_plan's items
+ *   work_items    device copy of pkv_prefill_plan's records (n_items work
+ *                 items, then n_combine combine entries)
  *   error_word    device int32, 0 before the call; afterwards 0, or 1 (a
  *                 bounded wait gave up), 3 (an item outside the launch was
  *                 skipped), 4 (a block id outside the pool was replaced by 0)
+ *   workspace     pkv_prefill_workspace_bytes(n_slots) bytes (may be NULL
+ *                 when n_slots is 0); no initial contents needed
  * Query i of a chunk after `past` tokens attends to keys 0 .. past + i.
  * Replaces the attention of the HF forward per prefill chunk
  * (agentrl/generation/prefill.py:96-104; transformers
@@ -324,8 +336,9 @@ int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const in
  * prefix_len-1 tokens).  Requires block_size 16, head_dim 64 or 128. */
 int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* pool, int32_t layer, const void* q,
                               const int32_t* block_tables, int32_t table_stride, int32_t table_rows,
-                              const int32_t* work_items, int32_t n_items, int64_t total_q, int32_t num_q_heads,
-                              float scale, void* out, int32_t* error_word, void* stream);
+                              const int32_t* work_items, int32_t n_items, int32_t n_combine, int64_t total_q,
+                              int32_t num_q_heads, float scale, void* out, int32_t* error_word, void* workspace,
+                              int64_t workspace_bytes, int64_t n_slots, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Native decode-step runtime                                                */
@@ -362,6 +375,11 @@ void pkv_stepper_destroy(pkv_stepper* st);
  * refcounts the stepper keeps in sync; rebind after growing them. */
 int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
                                 int32_t* context_lens, int32_t* refcounts);
+/* Optional: a host int32 array [n_blocks] of tokens stored per block that the
+ * stepper keeps current -- a copy-on-write copy gives the new block its
+ * source's count, an uploaded step sets the count of the block each step
+ * token went to.  The array must outlive the stepper or be unbound (n 0). */
+int32_t pkv_stepper_bind_fill(pkv_stepper* st, int32_t* block_fill, int64_t n_blocks);
 /* Apply the allocator's pending updates on `stream` (as pkv_apply_updates);
  * up to copies_cap copy-on-write (src, dst) pairs are reported.  Returns
  * PKV_ERR_CAPACITY with *need_rows / *need_cols when the tables must grow. */
@@ -396,9 +414,11 @@ int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity
 int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error);
 /* Kernels the stepper has launched so far. */
 int64_t pkv_stepper_launches(pkv_stepper* st);
-/* Time the next `count` attention launches with CUDA events recorded right
- * around the decode kernels on their stream (count 0 turns timing off). */
-int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count);
+/* Time `count` of the following attention launches, every `every`-th one,
+ * with CUDA events recorded right around the decode kernels on their stream
+ * (count 0 turns timing off; sampling keeps the event calls' host time off
+ * most steps). */
+int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every);
 /* Device milliseconds of the timed launches so far (waits for the last). */
 int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacity, int64_t* n_out);
 

@@ -140,16 +140,19 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "pkv_prefill_positions_per_item": (c_int32, [c_int32, c_int32]),
     "pkv_prefill_plan": (
-        c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, I64P]
+        c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64,
+                  I64P, I64P, I64P]
     ),
+    "pkv_prefill_workspace_bytes": (c_int64, [c_int64, c_int32]),
     "pkv_prefill_attention": (
         c_int32,
-        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int64,
-         c_int32, c_float, c_void_p, c_void_p, c_void_p],
+        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32,
+         c_int64, c_int32, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
     ),
     "pkv_stepper_create": (c_void_p, [c_void_p, POINTER(PoolGeom), c_void_p, I32P]),
     "pkv_stepper_destroy": (None, [c_void_p]),
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "pkv_stepper_bind_fill": (c_int32, [c_void_p, c_void_p, c_int64]),
     "pkv_stepper_sync": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, I32P, I32P, I32P]),
     "pkv_stepper_begin": (c_int32, [c_void_p, c_void_p, c_int32, POINTER(StepInfo), c_void_p, c_void_p, c_void_p]),
     "pkv_stepper_upload": (c_int32, [c_void_p, c_void_p, POINTER(StepInfo), c_void_p, c_int64]),
@@ -164,7 +167,7 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_copies": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
     "pkv_stepper_error": (c_int32, [c_void_p, I32P]),
     "pkv_stepper_launches": (c_int64, [c_void_p]),
-    "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64]),
+    "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64, c_int64]),
     "pkv_stepper_launch_times": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
 }
 

@@ -83,9 +83,14 @@ struct PCfg {
   static constexpr uint32_t kPageSlabBytes = kPageRows * 128;
 };
 
-// Work item (int4): {table row, position of the item's first query, index of
-// that query in the packed q, kv_head << 16 | positions in the item}.  The
-// first `ppi` positions form query tile A, the rest tile B.
+// Work item (two int4): {table row, position of the item's first query, index
+// of that query in the packed q, kv_head << 16 | positions in the item} and
+// {first KV tile, one past the last KV tile (0: all of them), partial slot
+// (-1: write the output), 0}.  The first `ppi` positions form query tile A,
+// the rest tile B.  An item with a key range or a partial slot has one query
+// tile; it writes its unnormalised (m, l, O) into the workspace slot, and a
+// combine entry {first slot, slots, query index, kv_head << 16 | positions}
+// merges the slots of one query tile.
 struct PrefillParams {
   const void* q;    // [total_q][hq][D]
   void* out;        // [total_q][hq][D]
@@ -93,6 +98,8 @@ struct PrefillParams {
   const int32_t* tables;
   const int4* items;
   int32_t* error;
+  float* partials;  // n_slots x (m[128], l[128], O[128][D]) fp32
+  int32_t n_slots;
   int64_t total_q;
   int32_t n_items;
   int32_t table_stride;
@@ -156,37 +163,44 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  const int4 item = p.items[blockIdx.x];
+  const int4 item = p.items[2 * blockIdx.x];
+  const int4 ext = p.items[2 * blockIdx.x + 1];
   const int row = item.x, pos0 = item.y, qrow0 = item.z, h = item.w >> 16, nt = item.w & 0xffff;
   const int group = p.group, ppi = p.ppi;
   const int kv_len = pos0 + nt;  // keys the item's last query sees
+  const int n_tiles = (kv_len + kKeys - 1) / kKeys;    // KV tiles of the whole key range
+  const int kt_lo = ext.x, kt_hi = ext.y > 0 ? ext.y : n_tiles, slot = ext.z;
+  const bool ranged = kt_lo != 0 || kt_hi != n_tiles || slot >= 0;  // a key range of a one-tile item
   const bool ok = row >= 0 && row < p.table_rows && h >= 0 && h < p.hkv && nt >= 1 && nt <= 2 * ppi &&
                   ppi * group <= kRows && pos0 >= 0 && qrow0 >= 0 && (int64_t)qrow0 + nt <= p.total_q &&
-                  (kv_len + kPageRows - 1) / kPageRows <= p.table_stride;
+                  (kv_len + kPageRows - 1) / kPageRows <= p.table_stride && kt_lo >= 0 && kt_lo < kt_hi &&
+                  kt_hi <= n_tiles && slot >= -1 && slot < p.n_slots && (!ranged || nt <= ppi);
   if (!ok) {  // uniform across the CTA: nothing initialised yet
     if (tid == 0) atomicExch(p.error, kDevBadItem);
     return;
   }
-  const int n_tiles = (kv_len + kKeys - 1) / kKeys;
+  const int n_range = kt_hi - kt_lo;
   // Two modes.  Shared: tile A holds the first ppi positions, tile B the rest,
   // and both read KV tile j at step j (one load serves both).  Split (all
-  // positions fit tile A and there are >= 2 KV tiles): tile B takes the same
-  // queries over the second half of the keys, each half streams its own K/V,
-  // and the two partial softmaxes are merged at the end.
-  const bool split = nt <= ppi && n_tiles >= 2;
+  // positions fit tile A and the CTA's key range has >= 2 KV tiles): tile B
+  // takes the same queries over the second half of the range, each half
+  // streams its own K/V, and the two partial softmaxes are merged at the end.
+  const bool split = nt <= ppi && n_range >= 2;
   const int nt_a = min(nt, ppi);
-  const int n_a = split ? (n_tiles + 1) / 2 : (pos0 + nt_a + kKeys - 1) / kKeys;  // KV tiles of tile A
-  const int n_b = split ? n_tiles - n_a : (nt > ppi ? n_tiles : 0);              // KV tiles of tile B
-  const int b_tile0 = split ? n_a : 0;                                             // B's first KV tile
+  const int n_a = split ? (n_range + 1) / 2
+                        : (ranged ? n_range : (pos0 + nt_a + kKeys - 1) / kKeys);  // KV tiles of tile A
+  const int n_b = split ? n_range - n_a : (nt > ppi ? n_tiles : 0);              // KV tiles of tile B
+  const int a_tile0 = kt_lo;                                                       // A's first KV tile
+  const int b_tile0 = split ? kt_lo + n_a : 0;                                     // B's first KV tile
   const int n_steps = max(n_a, n_b);
   const bool two_q = n_b > 0 && !split;  // tile B has queries of its own
   // Index of tile x's step-j K (or V) tile in the order the MMAs consume them:
   // shared mode one per step; split mode A(0), B(0), A(1), B(1), ... then A's rest.
   auto use_idx = [&](int x, int j) { return split ? (x == 0 ? j + min(j, n_b) : 2 * j + 1) : j; };
-  const int n_loads = split ? n_a + n_b : n_tiles;
+  const int n_loads = split ? n_a + n_b : n_steps;
   auto load_tile = [&](int c) {  // KV tile of load c
-    if (!split) return c;
-    return c < 2 * n_b ? ((c & 1) ? b_tile0 + (c >> 1) : (c >> 1)) : c - n_b;
+    if (!split) return a_tile0 + c;
+    return c < 2 * n_b ? ((c & 1) ? b_tile0 + (c >> 1) : a_tile0 + (c >> 1)) : a_tile0 + c - n_b;
   };
 
   if (tid == 0) {
@@ -290,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         if (!wait_or_abort(&bars->p_full[x], j & 1, p, abort)) return false;
         if (!wait_or_abort(&bars->v_full[vst], (c / NV) & 1, p, abort)) return false;
         tc_fence_after_sync();
-        const int t = x == 0 ? j : b_tile0 + j;
+        const int t = x == 0 ? a_tile0 + j : b_tile0 + j;
         const int steps = (min(kKeys, kv_len - t * kKeys) + 15) / 16;
         const uint32_t vb = v_addr + vst * C::kTileBytes;
         for (int ks = 0; ks < steps; ++ks) {
@@ -355,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
           break;
         }
         tc_fence_after_sync();
-        const int t = x == 0 ? j : b_tile0 + j;            // KV tile
+        const int t = x == 0 ? a_tile0 + j : b_tile0 + j;  // KV tile
         const int key0 = t * kKeys;
         const bool masked = key0 + kKeys - 1 > pos_first;  // crosses the causal diagonal of this tile
         const int lim = pos_r - key0;                      // visible columns: c <= lim
@@ -419,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
         // The item's last KV tile: V rows past the sequence inside its last
         // page are zeroed (by the tile whose product reads it first) so that
         // their zero probabilities multiply finite values.
-        const bool zero_owner = split ? x == 1 : ((x == 0) == (n_a == n_tiles));
+        const bool zero_owner = split || n_b == 0 || ((x == 0) == (n_a == n_tiles));
         if (zero_owner && t == n_tiles - 1 && (kv_len & (kPageRows - 1)) != 0) {
           const int c = use_idx(x, j);
           if (!__all_sync(0xffffffffu, wait_or_abort(&bars->v_full[c % NV], (c / NV) & 1, p, abort))) {
@@ -470,41 +484,71 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
       if (split) done = done && __all_sync(0xffffffffu, wait_or_abort(&bars->o_done[1], 0, p, abort));
       if (done) {
         tc_fence_after_sync();
-        float wa = 1.f, wb = 0.f;
-        float inv_l;
+        // Merge weights: 2^(m_x - m) per tile, m = the larger row maximum
+        // (rows that saw no key in a key range have m_x = -inf, weight 0).
+        float m_b = -INFINITY, l_b = 0.f;
         if (split) {
-          const float m_b = xchg[r], l_b = xchg[kTileThreads + r];
-          const float m = fmaxf(m_run, m_b);
-          wa = ex2_approx(m_run - m);
-          wb = ex2_approx(m_b - m);
-          inv_l = 1.f / (l_run * wa + l_b * wb);
-        } else {
-          inv_l = 1.f / l_run;
+          m_b = xchg[r];
+          l_b = xchg[kTileThreads + r];
         }
-        wa *= inv_l;
-        wb *= inv_l;
-        T* dst = static_cast<T*>(p.out) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
-#pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          float v[32];
-          tmem_ld32(o_addr + cc * 32, v);
-          if (split) {
-            float vb[32];
-            tmem_ld32(o_addr + D + cc * 32, vb);  // O_B, same lanes
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = v[i] * wa + vb[i] * wb;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= wa;
-          }
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) pk[i >> 1] = MmaOp<T>::pack(v[i], v[i + 1]);
+        const float m = fmaxf(m_run, m_b);
+        const float wa = m == -INFINITY ? 0.f : ex2_approx(m_run - m);
+        const float wb = (split && m != -INFINITY) ? ex2_approx(m_b - m) : 0.f;
+        const float l = l_run * wa + l_b * wb;
+        if (slot >= 0) {
+          // Unnormalised partial of this key range: m, l and O in fp32.
+          float* part = p.partials + (int64_t)slot * (2 * kRows + kRows * D);
           if (r < rows_valid) {
+            part[r] = m;
+            part[kRows + r] = l;
+          }
+          float* orow = part + 2 * kRows + (int64_t)r * D;
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            float v[32];
+            tmem_ld32(o_addr + cc * 32, v);
+            if (split) {
+              float vb[32];
+              tmem_ld32(o_addr + D + cc * 32, vb);  // O_B, same lanes
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              reinterpret_cast<uint4*>(dst + cc * 32)[c] =
-                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              for (int i = 0; i < 32; ++i) v[i] = v[i] * wa + vb[i] * wb;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] *= wa;
+            }
+            if (r < rows_valid) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                reinterpret_cast<float4*>(orow + cc * 32)[c] =
+                    make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            }
+          }
+        } else {
+          const float inv_l = 1.f / l;
+          const float sa = wa * inv_l, sb = wb * inv_l;
+          T* dst = static_cast<T*>(p.out) + (qrow * p.hq + (int64_t)h * group + r % group) * D;
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            float v[32];
+            tmem_ld32(o_addr + cc * 32, v);
+            if (split) {
+              float vb[32];
+              tmem_ld32(o_addr + D + cc * 32, vb);  // O_B, same lanes
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = v[i] * sa + vb[i] * sb;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] *= sa;
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) pk[i >> 1] = MmaOp<T>::pack(v[i], v[i + 1]);
+            if (r < rows_valid) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                reinterpret_cast<uint4*>(dst + cc * 32)[c] =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            }
           }
         }
       }
@@ -519,8 +563,52 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   }
 }
 
+// Merge the key-range partials of one query tile: per row, m = max m_s,
+// O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s, written in the output dtype.
+// One block per combine entry, one thread per tile row.
 template <int D, typename T>
-cudaError_t launch_prefill(const PrefillParams& prm, cudaStream_t stream) {
+__global__ void __launch_bounds__(kRows) paged_prefill_combine_kernel(const __grid_constant__ PrefillParams p,
+                                                                     const int4* entries) {
+  const int4 e = entries[2 * blockIdx.x];  // records are two int4 apart
+  const int slot0 = e.x, ns = e.y, qrow0 = e.z, h = e.w >> 16, nt = e.w & 0xffff;
+  const int r = threadIdx.x;
+  const int group = p.group;
+  if (slot0 < 0 || ns < 1 || slot0 + ns > p.n_slots || nt < 1 || nt * group > kRows || qrow0 < 0 ||
+      (int64_t)qrow0 + nt > p.total_q || h < 0 || h >= p.hkv) {
+    if (r == 0) atomicExch(p.error, kDevBadItem);
+    return;
+  }
+  if (r >= nt * group) return;
+  constexpr int kSlotFloats = 2 * kRows + kRows * D;
+  const float* base = p.partials + (int64_t)slot0 * kSlotFloats;
+  float m = -INFINITY;
+  for (int s = 0; s < ns; ++s) m = fmaxf(m, base[(int64_t)s * kSlotFloats + r]);
+  float l = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float ms = base[(int64_t)s * kSlotFloats + r];
+    l += ms == -INFINITY ? 0.f : ex2_approx(ms - m) * base[(int64_t)s * kSlotFloats + kRows + r];
+  }
+  const float inv_l = 1.f / l;
+  T* dst = static_cast<T*>(p.out) + (((int64_t)qrow0 + r / group) * p.hq + (int64_t)h * group + r % group) * D;
+#pragma unroll 1
+  for (int d = 0; d < D; d += 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < ns; ++s) {
+      const float* ps = base + (int64_t)s * kSlotFloats;
+      const float ms = ps[r];
+      const float w = ms == -INFINITY ? 0.f : ex2_approx(ms - m) * inv_l;
+      const float4 a = *reinterpret_cast<const float4*>(ps + 2 * kRows + (int64_t)r * D + d);
+      const float4 b = *reinterpret_cast<const float4*>(ps + 2 * kRows + (int64_t)r * D + d + 4);
+      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+      acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
+    }
+    *reinterpret_cast<uint4*>(dst + d) = make_uint4(MmaOp<T>::pack(acc[0], acc[1]), MmaOp<T>::pack(acc[2], acc[3]),
+                                                    MmaOp<T>::pack(acc[4], acc[5]), MmaOp<T>::pack(acc[6], acc[7]));
+  }
+}
+
+template <int D, typename T>
+cudaError_t launch_prefill(const PrefillParams& prm, int32_t n_combine, cudaStream_t stream) {
   using C = PCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "prefill tile exceeds the shared memory of one CTA");
   static_assert(sizeof(Bars<C::kKStages, C::kVStages>) <= 256, "barrier block overflows its slot");
@@ -528,6 +616,9 @@ cudaError_t launch_prefill(const PrefillParams& prm, cudaStream_t stream) {
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (err != cudaSuccess) return err;
   kern<<<prm.n_items, kThreads, C::kSmemBytes, stream>>>(prm);
+  err = cudaGetLastError();
+  if (err != cudaSuccess || n_combine == 0) return err;
+  paged_prefill_combine_kernel<D, T><<<n_combine, kRows, 0, stream>>>(prm, prm.items + 2 * prm.n_items);
   return cudaGetLastError();
 }
 
@@ -543,24 +634,32 @@ extern "C" int32_t pkv_prefill_positions_per_item(int32_t num_q_heads, int32_t n
   return group > kRows ? 0 : 2 * (kRows / group);  // two query tiles of kRows / group positions
 }
 
+extern "C" int64_t pkv_prefill_workspace_bytes(int64_t n_slots, int32_t head_dim) {
+  if (n_slots <= 0) return 0;
+  return n_slots * (int64_t)(2 * kRows + kRows * head_dim) * (int64_t)sizeof(float);
+}
+
 extern "C" int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_lens, const int32_t* q_lens,
-                                    int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t* items_out,
-                                    int64_t items_capacity, int64_t* n_items_out) {
+                                    int32_t n_seqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t num_sms,
+                                    int32_t split_waves, int32_t* items_out, int64_t items_capacity,
+                                    int64_t* n_items_out, int64_t* n_combine_out, int64_t* n_slots_out) {
   pkv_clear_error();
-  const int ppi = pkv_prefill_positions_per_item(num_q_heads, num_kv_heads);
+  const int ppi = pkv_prefill_positions_per_item(num_q_heads, num_kv_heads);  // two query tiles
   if (ppi <= 0 || num_kv_heads > 0x7fff) {
     pkv_set_error("num_q_heads must be a positive multiple of num_kv_heads with at most 128 query heads per KV head");
     return PKV_ERR_UNSUPPORTED;
   }
-  if (n_seqs < 0 || !n_items_out || (n_seqs > 0 && (!rows || !past_lens || !q_lens))) {
+  if (n_seqs < 0 || num_sms < 0 || split_waves < 0 || !n_items_out || !n_combine_out || !n_slots_out ||
+      (n_seqs > 0 && (!rows || !past_lens || !q_lens))) {
     pkv_set_error("invalid plan arguments");
     return PKV_ERR_ARG;
   }
+  const int tile_positions = ppi / 2;
   struct Entry {
-    int64_t kv_len;
-    int32_t v[4];
+    int64_t work;  // KV tiles the CTA streams
+    int32_t v[8];
   };
-  std::vector<Entry> entries;
+  std::vector<Entry> base;
   int64_t qrow = 0;
   for (int32_t i = 0; i < n_seqs; ++i) {
     if (rows[i] < 0 || past_lens[i] < 0 || q_lens[i] < 0) {
@@ -573,31 +672,69 @@ extern "C" int32_t pkv_prefill_plan(const int32_t* rows, const int32_t* past_len
     }
     for (int32_t t0 = 0; t0 < q_lens[i]; t0 += ppi) {
       const int32_t n = std::min(ppi, q_lens[i] - t0);
+      const int64_t kv_len = (int64_t)past_lens[i] + t0 + n;
       for (int32_t hk = 0; hk < num_kv_heads; ++hk)
-        entries.push_back({(int64_t)past_lens[i] + t0 + n,
-                           {rows[i], past_lens[i] + t0, static_cast<int32_t>(qrow + t0), (hk << 16) | n}});
+        base.push_back({(kv_len + kKeys - 1) / kKeys,
+                        {rows[i], past_lens[i] + t0, static_cast<int32_t>(qrow + t0), (hk << 16) | n, 0, 0, -1, 0}});
     }
     qrow += q_lens[i];
   }
-  *n_items_out = static_cast<int64_t>(entries.size());
+  // Few items (a verify step): cut the keys of one-tile items into ranges of
+  // about `target` KV tiles so that about split_waves CTAs per SM share the
+  // work; each range writes a partial and a combine entry merges them.
+  std::vector<Entry> items, combine;
+  int32_t n_slots = 0;
+  const int64_t slots_wanted = (int64_t)split_waves * num_sms;
+  if (split_waves > 0 && num_sms > 0 && (int64_t)base.size() < slots_wanted) {
+    int64_t total = 0;
+    for (const Entry& e : base) total += e.work;
+    const int64_t target = std::max<int64_t>(2, (total + slots_wanted - 1) / slots_wanted);
+    for (const Entry& e : base) {
+      const int32_t nt = e.v[3] & 0xffff;
+      const int64_t ns = std::min<int64_t>(64, (e.work + target - 1) / target);
+      if (nt > tile_positions || ns < 2) {
+        items.push_back(e);
+        continue;
+      }
+      int32_t lo = 0;
+      for (int64_t s2 = 0; s2 < ns; ++s2) {
+        const int32_t hi = static_cast<int32_t>((e.work * (s2 + 1)) / ns);
+        Entry r = e;
+        r.work = hi - lo;
+        r.v[4] = lo;
+        r.v[5] = hi;
+        r.v[6] = n_slots + static_cast<int32_t>(s2);
+        items.push_back(r);
+        lo = hi;
+      }
+      combine.push_back({0, {n_slots, static_cast<int32_t>(ns), e.v[2], e.v[3], 0, 0, 0, 0}});
+      n_slots += static_cast<int32_t>(ns);
+    }
+  } else {
+    items = std::move(base);
+  }
+  *n_items_out = static_cast<int64_t>(items.size());
+  *n_combine_out = static_cast<int64_t>(combine.size());
+  *n_slots_out = n_slots;
   if (!items_out) return PKV_OK;
-  if ((int64_t)entries.size() > items_capacity) {
-    pkv_set_error("item buffer too small: need " + std::to_string(entries.size()) + " items");
+  if ((int64_t)(items.size() + combine.size()) > items_capacity) {
+    pkv_set_error("item buffer too small: need " + std::to_string(items.size() + combine.size()) + " records");
     return PKV_ERR_CAPACITY;
   }
-  // Longest key range first, so the grid's tail holds the short tiles.
-  std::stable_sort(entries.begin(), entries.end(),
-                   [](const Entry& a, const Entry& b) { return a.kv_len > b.kv_len; });
-  for (size_t i = 0; i < entries.size(); ++i)
-    for (int k = 0; k < 4; ++k) items_out[4 * i + k] = entries[i].v[k];
+  // Longest key range first, so the grid's tail holds the short ones.
+  std::stable_sort(items.begin(), items.end(), [](const Entry& a, const Entry& b) { return a.work > b.work; });
+  int32_t* o = items_out;
+  for (const Entry& e : items) o = std::copy(e.v, e.v + 8, o);
+  for (const Entry& e : combine) o = std::copy(e.v, e.v + 8, o);
   return PKV_OK;
 }
 
 extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* pool, int32_t layer, const void* q,
                                          const int32_t* block_tables, int32_t table_stride, int32_t table_rows,
-                                         const int32_t* work_items, int32_t n_items, int64_t total_q,
-                                         int32_t num_q_heads, float scale, void* out, int32_t* error_word,
-                                         void* stream) {
+                                         const int32_t* work_items, int32_t n_items, int32_t n_combine,
+                                         int64_t total_q, int32_t num_q_heads, float scale, void* out,
+                                         int32_t* error_word, void* workspace, int64_t workspace_bytes,
+                                         int64_t n_slots, void* stream) {
   pkv_clear_error();
   if (!g || g->block_size != kPageRows) {
     pkv_set_error("paged prefill attention needs block_size 16");
@@ -615,9 +752,16 @@ extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* poo
     pkv_set_error("num_q_heads must be a positive multiple of num_kv_heads with at most 128 query heads per KV head");
     return PKV_ERR_UNSUPPORTED;
   }
-  if (layer < 0 || layer >= g->num_layers || n_items < 0 || total_q < 0 || table_stride <= 0 || table_rows <= 0 ||
-      !(scale > 0.f)) {
-    pkv_set_error("invalid layer, item, query, table or scale arguments");
+  if (layer < 0 || layer >= g->num_layers || n_items < 0 || n_combine < 0 || n_slots < 0 || n_slots > INT32_MAX ||
+      total_q < 0 || table_stride <= 0 || table_rows <= 0 || !(scale > 0.f)) {
+    pkv_set_error("invalid layer, item, combine, query, table or scale arguments");
+    return PKV_ERR_ARG;
+  }
+  if ((n_combine > 0 || n_slots > 0) &&
+      (!workspace || (uintptr_t)workspace % 16 != 0 ||
+       workspace_bytes < pkv_prefill_workspace_bytes(n_slots, g->head_dim))) {
+    pkv_set_error("workspace too small or misaligned: need " +
+                  std::to_string(pkv_prefill_workspace_bytes(n_slots, g->head_dim)) + " bytes, 16-byte aligned");
     return PKV_ERR_ARG;
   }
   if (n_items == 0) return PKV_OK;
@@ -637,6 +781,8 @@ extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* poo
   prm.tables = block_tables;
   prm.items = reinterpret_cast<const int4*>(work_items);
   prm.error = error_word;
+  prm.partials = static_cast<float*>(workspace);
+  prm.n_slots = static_cast<int32_t>(n_slots);
   prm.total_q = total_q;
   prm.n_items = n_items;
   prm.table_stride = table_stride;
@@ -651,9 +797,9 @@ extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* poo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
   if (g->head_dim == 128)
-    err = g->dtype == PKV_BF16 ? launch_prefill<128, __nv_bfloat16>(prm, s) : launch_prefill<128, __half>(prm, s);
+    err = g->dtype == PKV_BF16 ? launch_prefill<128, __nv_bfloat16>(prm, n_combine, s) : launch_prefill<128, __half>(prm, n_combine, s);
   else
-    err = g->dtype == PKV_BF16 ? launch_prefill<64, __nv_bfloat16>(prm, s) : launch_prefill<64, __half>(prm, s);
+    err = g->dtype == PKV_BF16 ? launch_prefill<64, __nv_bfloat16>(prm, n_combine, s) : launch_prefill<64, __half>(prm, n_combine, s);
   if (err != cudaSuccess) {
     pkv_set_error(std::string("prefill launch failed: ") + cudaGetErrorString(err));
     return PKV_ERR_CUDA;

@@ -5,9 +5,10 @@
 // device upload and application of any pending block-table updates, the
 // split-K plan, and one staged upload of the step descriptor; one call per
 // layer then launches the fused decode kernels.  Host buffers are pinned and
-// recycled through a small ring guarded by CUDA events, device buffers are
-// recycled in stream order, so a step costs a few microseconds of host time
-// and never synchronises the host with the device.
+// recycled through a small ring (one CUDA event per trip round the ring guards
+// their reuse), device buffers are recycled in stream order, so a step costs
+// a few CUDA calls of host time and never synchronises the host with the
+// device.
 //
 // Everything a stepper launches goes to the stream passed to begin(); use one
 // stream per stepper.
@@ -31,8 +32,6 @@ struct Slot {
   int32_t* host = nullptr;
   int32_t* dev = nullptr;
   int64_t cap = 0;  // int32 elements
-  cudaEvent_t done = nullptr;
-  bool pending = false;
 };
 
 int32_t cuda_status(cudaError_t e, const char* what) {
@@ -55,8 +54,20 @@ struct pkv_stepper {
   int32_t* refs = nullptr;
   Slot slot[kRing];
   int next = 0;
+  int last_taken = -1;
+  // Recorded after the copy out of the ring's last slot; every copy of that
+  // trip round the ring is complete once it is, so it guards the reuse of
+  // all kRing slots (one event per kRing uploads instead of one per upload).
+  cudaEvent_t round_done = nullptr;
+  bool round_pending = false;
+  bool round_open = false;  // the ring's last slot was taken and not yet copied out
   std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
   std::vector<int32_t> last_copies;  // (src, dst) pairs applied by the last sync / upload
+  // Optional host array of per-block stored-token counts (the store's
+  // bookkeeping of which blocks hold data): copy-on-write copies carry the
+  // source's count, and each step sets the count of the block its token went to.
+  int32_t* fill = nullptr;
+  int64_t fill_n = 0;
   pkv_step_info info{};
   bool step_ready = false;
   void* ws = nullptr;
@@ -70,14 +81,14 @@ struct pkv_stepper {
   bool def_pending = false;
   // Optional per-launch timing of the decode kernels (events around them).
   std::vector<cudaEvent_t> t_start, t_stop;
-  int64_t t_cap = 0, t_count = 0;
+  int64_t t_cap = 0, t_count = 0, t_every = 1, t_seen = 0;
 
   ~pkv_stepper() {
+    if (round_done) {
+      cudaEventSynchronize(round_done);
+      cudaEventDestroy(round_done);
+    }
     for (auto& s : slot) {
-      if (s.done) {
-        cudaEventSynchronize(s.done);
-        cudaEventDestroy(s.done);
-      }
       if (s.host) cudaFreeHost(s.host);
       if (s.dev) cudaFree(s.dev);
     }
@@ -88,13 +99,20 @@ struct pkv_stepper {
 
   // A ring slot with room for `n` int32, its previous upload finished.
   int32_t take_slot(int64_t n, Slot** out) {
-    Slot& s = slot[next];
-    next = (next + 1) % kRing;
-    if (s.pending) {
-      int32_t st = cuda_status(cudaEventSynchronize(s.done), "stepper ring");
+    if (next == 0 && round_pending) {
+      int32_t st = cuda_status(cudaEventSynchronize(round_done), "stepper ring");
       if (st) return st;
-      s.pending = false;
+      round_pending = false;
+    } else if (next == 0 && round_open) {
+      // A failed call took the last slot without copying it out, so no event
+      // closes that round: wait for the device instead (error paths only).
+      int32_t st = cuda_status(cudaDeviceSynchronize(), "stepper ring");
+      if (st) return st;
     }
+    round_open = next == kRing - 1;
+    Slot& s = slot[next];
+    last_taken = next;
+    next = (next + 1) % kRing;
     if (s.cap < n) {
       const int64_t cap = std::max<int64_t>(n, 2 * s.cap);
       if (s.host) cudaFreeHost(s.host);
@@ -106,19 +124,26 @@ struct pkv_stepper {
       if (st) return st;
       s.cap = cap;
     }
-    if (!s.done) {
-      int32_t st = cuda_status(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "cudaEventCreate");
-      if (st) return st;
-    }
     *out = &s;
     return PKV_OK;
   }
 
+  // After the copy out of the slot last taken: close the trip round the ring.
+  int32_t copied(cudaStream_t stream) {
+    if (last_taken != kRing - 1) return PKV_OK;
+    round_open = false;
+    if (!round_done) {
+      int32_t st = cuda_status(cudaEventCreateWithFlags(&round_done, cudaEventDisableTiming), "cudaEventCreate");
+      if (st) return st;
+    }
+    int32_t st = cuda_status(cudaEventRecord(round_done, stream), "cudaEventRecord");
+    if (!st) round_pending = true;
+    return st;
+  }
+
   int32_t upload(Slot* s, int64_t n, cudaStream_t stream) {
     int32_t st = cuda_status(cudaMemcpyAsync(s->dev, s->host, n * 4, cudaMemcpyHostToDevice, stream), "H2D");
-    if (!st) st = cuda_status(cudaEventRecord(s->done, stream), "cudaEventRecord");
-    if (!st) s->pending = true;
-    return st;
+    return st ? st : copied(stream);
   }
 
   bool capacity_ok(pkv_step_info* out) {
@@ -165,13 +190,18 @@ struct pkv_stepper {
       }
     }
     *n_copies = s->host[3];
+    if (fill) {
+      for (size_t i = 0; i + 1 < last_copies.size(); i += 2) {
+        const int32_t src = last_copies[i], dst = last_copies[i + 1];
+        if (src >= 0 && src < fill_n && dst >= 0 && dst < fill_n) fill[dst] = fill[src];
+      }
+    }
     st = cuda_status(cudaMemcpyAsync(s->dev, s->host, written * 4, cudaMemcpyHostToDevice, stream), "H2D");
     if (st) return st;
     st = pkv_apply_updates(&geom, pool, tables, stride, rows, refs, lens, s->dev, s->host, stream);
-    // The host copy is read by pkv_apply_updates synchronously; the event only
-    // guards the pinned buffer against reuse before the H2D completes.
-    int32_t st2 = cuda_status(cudaEventRecord(s->done, stream), "cudaEventRecord");
-    s->pending = true;
+    // The host copy is read by pkv_apply_updates synchronously; the ring's
+    // event only guards the pinned buffer against reuse before the H2D completes.
+    int32_t st2 = copied(stream);
     launches += 1 + (s->host[3] > 0 ? 1 : 0);
     return st ? st : st2;
   }
@@ -207,6 +237,17 @@ int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t 
   st->rows = table_rows;
   st->lens = context_lens;
   st->refs = refcounts;
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_bind_fill(pkv_stepper* st, int32_t* block_fill, int64_t n_blocks) {
+  pkv_clear_error();
+  if (n_blocks < 0 || (n_blocks > 0 && !block_fill)) {
+    pkv_set_error("pkv_stepper_bind_fill: invalid arguments");
+    return PKV_ERR_ARG;
+  }
+  st->fill = n_blocks ? block_fill : nullptr;
+  st->fill_n = n_blocks;
   return PKV_OK;
 }
 
@@ -318,6 +359,13 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
     st->def_lens = h[def_off + 2];
     st->def_pending = true;
   }
+  if (st->fill) {
+    // After any copy-on-write copies (they carry the source block's count).
+    for (int i = 0; i < n; ++i) {
+      const int32_t b = st->tokb_h[i];
+      if (b >= 0 && b < st->fill_n) st->fill[b] = (st->lens_h[i] - 1) % bs + 1;
+    }
+  }
   info->pages_per_split = pps;
   info->n_items = (int32_t)n_items;
   info->n_combine = (int32_t)n_combine;
@@ -354,7 +402,7 @@ int32_t pkv_stepper_attention(pkv_stepper* st, int32_t layer, const void* q, con
     return PKV_ERR_ARG;
   }
   const pkv_step_info& in = st->info;
-  const bool timed = st->t_count < st->t_cap;
+  const bool timed = st->t_count < st->t_cap && (st->t_seen++ % st->t_every) == 0;
   const int32_t* def = st->def_pending ? st->def_dev : nullptr;
   if (timed) cudaEventRecord(st->t_start[st->t_count], static_cast<cudaStream_t>(stream));
   int32_t s = pkv_decode_attention_ex(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride, st->rows,
@@ -394,8 +442,14 @@ int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error) {
 
 int64_t pkv_stepper_launches(pkv_stepper* st) { return st->launches; }
 
-int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count) {
+int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every) {
   pkv_clear_error();
+  if (count < 0 || every < 1) {
+    pkv_set_error("pkv_stepper_time_launches: count must be >= 0 and every >= 1");
+    return PKV_ERR_ARG;
+  }
+  st->t_every = every;
+  st->t_seen = 0;
   for (auto e : st->t_start) cudaEventDestroy(e);
   for (auto e : st->t_stop) cudaEventDestroy(e);
   st->t_start.assign(count, nullptr);

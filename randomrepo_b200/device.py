@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import ctypes
 import weakref
+from dataclasses import dataclass
 
 import numpy as np
 import torch
@@ -75,6 +76,7 @@ class KVPool:
         self.context_lens = torch.zeros(64, dtype=torch.int32, device=self.device)
         # Error word of the prefill / verify kernel (0 = none).
         self.prefill_error = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._prefill_ws = torch.empty(0, dtype=torch.uint8, device=self.device)
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         # Kernel launches issued from Python through this pool (the stepper counts its own).
         self.launches = 0
@@ -135,9 +137,9 @@ class KVPool:
         _lib.raise_for_status(st)
         return copies[: n.value]
 
-    def time_launches(self, count: int) -> None:
-        """Time the next ``count`` decode-attention launches on the device (0 = off)."""
-        _lib.raise_for_status(lib.pkv_stepper_time_launches(self.stepper, int(count)))
+    def time_launches(self, count: int, every: int = 1) -> None:
+        """Time ``count`` of the next decode-attention launches, every ``every``-th one (0 = off)."""
+        _lib.raise_for_status(lib.pkv_stepper_time_launches(self.stepper, int(count), int(every)))
         self._timing_cap = int(count)
 
     def launch_times_ms(self) -> np.ndarray:
@@ -160,16 +162,24 @@ class KVPool:
         """Error word the prefill / verify kernel writes (0 = none); synchronises with the device."""
         return int(self.prefill_error.item())
 
-    def prefill(self, layer: int, q: torch.Tensor, items: torch.Tensor, n_items: int, num_q_heads: int,
+    def prefill(self, layer: int, q: torch.Tensor, plan: "PrefillPlan", records: torch.Tensor, num_q_heads: int,
                 scale: float, out: torch.Tensor) -> None:
-        """Launch paged prefill / verify attention (``pkv_prefill_attention``) on the current stream."""
+        """Launch paged prefill / verify attention (``pkv_prefill_attention``) on the current stream.
+
+        ``records`` is the device copy of ``plan.records``; key-range partials
+        go to a workspace the pool keeps (grown on demand, never shrunk).
+        """
+        need = int(lib.pkv_prefill_workspace_bytes(plan.n_slots, self.head_dim))
+        if need > self._prefill_ws.numel():
+            self._prefill_ws = torch.empty(_round_up(need, 1 << 20), dtype=torch.uint8, device=self.device)
         rows, cols = self.tables.shape
         st = lib.pkv_prefill_attention(self._geom_ref, self.pool.data_ptr(), int(layer), q.data_ptr(),
-                                       self.tables.data_ptr(), cols, rows, items.data_ptr(), int(n_items),
-                                       q.shape[0], int(num_q_heads), float(scale), out.data_ptr(),
-                                       self.prefill_error.data_ptr(), _stream_ptr())
+                                       self.tables.data_ptr(), cols, rows, records.data_ptr(), plan.n_items,
+                                       plan.n_combine, q.shape[0], int(num_q_heads), float(scale), out.data_ptr(),
+                                       self.prefill_error.data_ptr(), self._prefill_ws.data_ptr(),
+                                       self._prefill_ws.numel(), plan.n_slots, _stream_ptr())
         _lib.raise_for_status(st)
-        self.launches += 1
+        self.launches += 2 if plan.n_combine else 1
 
     # -- data movement --------------------------------------------------------
     def scatter(self, layer0: int, k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor | int,
@@ -225,17 +235,39 @@ def plan_decode(lens: np.ndarray, num_kv_heads: int, num_sms: int,
     return int(pps.value), items, int(n.value), int(nc.value)
 
 
+@dataclass
+class PrefillPlan:
+    """``pkv_prefill_plan`` output: int32 [n_items + n_combine, 8] records and their counts."""
+
+    records: np.ndarray
+    n_items: int
+    n_combine: int
+    n_slots: int
+
+
+PREFILL_SPLIT_WAVES = 0
+
+
 def plan_prefill(rows: np.ndarray, past_lens: np.ndarray, q_lens: np.ndarray, num_q_heads: int,
-                 num_kv_heads: int) -> np.ndarray:
-    """Plan one prefill / verify launch (``pkv_prefill_plan``): int32 [n_items, 4] work items."""
+                 num_kv_heads: int, num_sms: int = 0, split_waves: int | None = None) -> PrefillPlan:
+    """Plan one prefill / verify launch (``pkv_prefill_plan``).
+
+    With ``split_waves`` > 0 (default ``PREFILL_SPLIT_WAVES``) and ``num_sms``
+    > 0, a launch of few items (a verify step) cuts long key ranges across
+    about ``split_waves`` CTAs per SM and merges their partials; 0 keeps one
+    CTA per item.
+    """
+    waves = PREFILL_SPLIT_WAVES if split_waves is None else int(split_waves)
     rows = np.ascontiguousarray(rows, dtype=np.int32)
     past_lens = np.ascontiguousarray(past_lens, dtype=np.int32)
     q_lens = np.ascontiguousarray(q_lens, dtype=np.int32)
     if not rows.size == past_lens.size == q_lens.size:
         raise ValueError("rows, past_lens and q_lens must have one entry per sequence")
-    n = ctypes.c_int64()
-    args = (rows.ctypes.data, past_lens.ctypes.data, q_lens.ctypes.data, rows.size, num_q_heads, num_kv_heads)
-    _lib.raise_for_status(lib.pkv_prefill_plan(*args, None, 0, ctypes.byref(n)))
-    items = np.empty((n.value, 4), dtype=np.int32)
-    _lib.raise_for_status(lib.pkv_prefill_plan(*args, items.ctypes.data, items.shape[0], ctypes.byref(n)))
-    return items
+    n, nc, ns = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    args = (rows.ctypes.data, past_lens.ctypes.data, q_lens.ctypes.data, rows.size, num_q_heads, num_kv_heads,
+            int(num_sms), waves)
+    _lib.raise_for_status(lib.pkv_prefill_plan(*args, None, 0, ctypes.byref(n), ctypes.byref(nc), ctypes.byref(ns)))
+    records = np.empty((n.value + nc.value, 8), dtype=np.int32)
+    _lib.raise_for_status(lib.pkv_prefill_plan(*args, records.ctypes.data, records.shape[0], ctypes.byref(n),
+                                               ctypes.byref(nc), ctypes.byref(ns)))
+    return PrefillPlan(records, int(n.value), int(nc.value), int(ns.value))

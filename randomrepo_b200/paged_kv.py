@@ -274,8 +274,12 @@ class PagedKVCacheStore:
         # Tokens stored in each block's chunk (-1: the block holds no stored chunk).
         self._block_fill = np.full(allocator.total_blocks, -1, dtype=np.int32)
         self._pool: KVPool | None = None
+        # Host buffers of the decode fast path, reused from step to step.
+        self._host3: np.ndarray | None = None
+        self._host3_ptrs = (0, 0, 0)
+        self._io_checked: tuple = ()
         if None not in (num_layers, num_kv_heads, head_dim, dtype):
-            self._pool = KVPool(allocator, num_layers, num_kv_heads, head_dim, dtype, device)
+            self._pool = self._new_pool(num_layers, num_kv_heads, head_dim, dtype, device)
 
     # -- reference API (paged_kv.py:192-216) ------------------------------------
     @property
@@ -480,18 +484,27 @@ class PagedKVCacheStore:
         ``decode_attention(step, layer, q, k_new, v_new)``; the returned step
         serves the model's other layers.
         """
-        pool = self._require_pool()
-        ids = self._step_ids(sequence_ids)
+        pool = self._pool if self._pool is not None else self._require_pool()
+        ids = sequence_ids
+        if not (type(ids) is np.ndarray and ids.dtype == np.int64 and ids.ndim == 1 and ids.flags.c_contiguous
+                and ids.size):
+            ids = self._step_ids(sequence_ids)
         n = ids.size
-        out = self._check_decode_io(pool, n, q, k_new, v_new, out)
+        # The checks of q / k / v / out are skipped when the same tensor
+        # objects come back (a decode loop reusing its buffers).
+        chk = self._io_checked
+        if (out is None or not chk or chk[0] is not q or chk[1] is not k_new or chk[2] is not v_new
+                or chk[3] is not out or chk[4] != n):
+            out = self._check_decode_io(pool, n, q, k_new, v_new, out)
+            self._io_checked = (q, k_new, v_new, out, n)
+        host, (p_rows, p_lens, p_tokb) = self._host_buffers(n)
         info = _lib.StepInfo()
-        host = np.empty((3, n), dtype=np.int32)
         with _on_device(pool.device):
             stream = _current_stream(pool.device)
             sc = float(scale if scale is not None else pool.head_dim ** -0.5)
             st = lib.pkv_stepper_step(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(), k_new.data_ptr(),
                                       v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream, ctypes.byref(info),
-                                      host[0].ctypes.data, host[1].ctypes.data, host[2].ctypes.data, None, 0)
+                                      p_rows, p_lens, p_tokb, None, 0)
             if st == _lib.PKV_ERR_CAPACITY:
                 pool.grow(info.need_rows, info.need_cols)
                 st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
@@ -501,6 +514,16 @@ class PagedKVCacheStore:
         step = self._finish_step(pool, st, ids, info, host)
         step.committed = True
         return out, step
+
+    def _host_buffers(self, n: int):
+        """Rows / lengths / token blocks [3, n] for the stepper to fill, and their addresses (reused)."""
+        buf = self._host3
+        if buf is None or buf.shape[1] < n:
+            cap = max(n, 256)
+            buf = self._host3 = np.empty((3, cap), dtype=np.int32)
+            base = buf.ctypes.data
+            self._host3_ptrs = (base, base + 4 * cap, base + 8 * cap)
+        return buf[:, :n], self._host3_ptrs
 
     def decode_step(self, sequence_ids) -> DecodeStep:
         """Append one token to each sequence and upload the step for the decode kernels.
@@ -513,9 +536,8 @@ class PagedKVCacheStore:
         ids = self._step_ids(sequence_ids)
         n = ids.size
         info = _lib.StepInfo()
-        host = np.empty((3, n), dtype=np.int32)
-        st = lib.pkv_stepper_begin(pool.stepper, ids.ctypes.data, n, ctypes.byref(info), host[0].ctypes.data,
-                                   host[1].ctypes.data, host[2].ctypes.data)
+        host, (p_rows, p_lens, p_tokb) = self._host_buffers(n)
+        st = lib.pkv_stepper_begin(pool.stepper, ids.ctypes.data, n, ctypes.byref(info), p_rows, p_lens, p_tokb)
         if st == _lib.PKV_OK:
             with _on_device(pool.device):
                 stream = _current_stream(pool.device)
@@ -625,13 +647,13 @@ class PagedKVCacheStore:
         if total_q == 0:
             return out
         slots = np.concatenate(slot_parts)
-        items = plan_prefill(rows, past, q_lens, q.shape[1], pool.num_kv_heads)
+        plan = plan_prefill(rows, past, q_lens, q.shape[1], pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
             dev = pool.device
             slots_d = torch.from_numpy(slots).to(dev, non_blocking=True)
-            items_d = torch.from_numpy(items).to(dev, non_blocking=True)
+            records_d = torch.from_numpy(plan.records).to(dev, non_blocking=True)
             pool.scatter(layer, k.permute(1, 0, 2).unsqueeze(0), v.permute(1, 0, 2).unsqueeze(0), slots_d)
-            pool.prefill(layer, q, items_d, items.shape[0], q.shape[1],
+            pool.prefill(layer, q, plan, records_d, q.shape[1],
                          float(scale if scale is not None else pool.head_dim ** -0.5), out)
         return out
 
@@ -679,30 +701,26 @@ class PagedKVCacheStore:
 
     def _finish_step(self, pool: KVPool, st: int, ids, info, host) -> DecodeStep:
         rows, lens, tok_blocks = host[0], host[1], host[2]
-        bs = self.allocator.block_size_tokens
-        k = int(info.batch)
         if st != _lib.PKV_OK:
+            # The appends made before the failure stay (as with the reference's
+            # sequential append_tokens); their tokens have no stored K/V yet.
+            k = int(info.batch)
+            bs = self.allocator.block_size_tokens
             self._sync()
             self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
             _lib.raise_for_status(st)
-        if info.n_copies:
-            n = ctypes.c_int64()
-            pairs = np.empty((info.n_copies, 2), dtype=np.int32)
-            lib.pkv_stepper_copies(pool.stepper, pairs.ctypes.data, info.n_copies, ctypes.byref(n))
-            for src, dst in pairs.tolist():
-                self._block_fill[dst] = self._block_fill[src]
-        # Copy-on-write copies came first (they carry the source block's fill);
-        # then the fill of the blocks that receive this step's tokens.
-        self._block_fill[tok_blocks] = (lens - 1) % bs + 1
+        # Block fills of the step (and of its copy-on-write copies) were set by
+        # the native stepper.
         pool.step_serial += 1
-        return DecodeStep(sequence_ids=ids, info=info, serial=pool.step_serial, host_rows=rows, host_lens=lens)
+        return DecodeStep(sequence_ids=ids, info=info, serial=pool.step_serial, host_rows=rows.copy(),
+                          host_lens=lens.copy())
 
     # -- helpers -----------------------------------------------------------------
     def _ensure_pool(self, num_layers: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype,
                      device: torch.device) -> KVPool:
         if self._pool is None:
             dev = device if device.type == "cuda" else None
-            self._pool = KVPool(self.allocator, num_layers, num_kv_heads, head_dim, dtype, dev)
+            self._pool = self._new_pool(num_layers, num_kv_heads, head_dim, dtype, dev)
         p = self._pool
         if (p.num_layers, p.num_kv_heads, p.head_dim, p.dtype) != (num_layers, num_kv_heads, head_dim, dtype):
             raise ValueError(
@@ -712,17 +730,25 @@ class PagedKVCacheStore:
             )
         return p
 
+    def _new_pool(self, num_layers: int, num_kv_heads: int, head_dim: int, dtype: torch.dtype, device) -> KVPool:
+        pool = KVPool(self.allocator, num_layers, num_kv_heads, head_dim, dtype, device)
+        # The native stepper keeps the per-block stored-token counts of decode
+        # steps (and of copy-on-write copies) current in this array.
+        _lib.raise_for_status(lib.pkv_stepper_bind_fill(pool.stepper, self._block_fill.ctypes.data,
+                                                        self._block_fill.size))
+        return pool
+
     def _require_pool(self) -> KVPool:
         if self._pool is None:
             raise RuntimeError("the KV pool does not exist yet: write a cache first or pass its geometry")
         return self._pool
 
     def _sync(self) -> None:
+        """Bring the device tables up to date (the stepper carries block fills over copy-on-write copies)."""
         pool = self._pool
         if pool is None:
             return
-        for src, dst in pool.sync().tolist():
-            self._block_fill[dst] = self._block_fill[src]
+        pool.sync()
 
     def _slots(self, blocks, fills, bs: int) -> torch.Tensor:
         parts = [np.arange(f, dtype=np.int64) + int(b) * bs for b, f in zip(blocks, fills) if f > 0]

@@ -231,3 +231,34 @@ def test_prefill_rejects_unreserved_chunk(cuda_device):
     kv = torch.zeros((5, 2, 128), dtype=torch.bfloat16, device=cuda_device)
     with pytest.raises(ValueError):
         store.prefill_attention([0], q, kv, kv)
+
+
+@pytest.mark.parametrize("waves", [1, 2, 3])
+def test_key_split_verify_matches_oracle(cuda_device, monkeypatch, waves):
+    """Verify with each sequence's keys cut across CTAs (partials merged by the combine kernel)."""
+    import randomrepo_b200.device as devmod
+
+    monkeypatch.setattr(devmod, "PREFILL_SPLIT_WAVES", waves)
+    hq, hkv, d, kd = 12, 2, 128, 4
+    gen = torch.Generator().manual_seed(40 + waves)
+    prefixes = [128, 300, 700, 1024, 1280, 5, 17, 129, 555, 1111]
+    store = _make_store(hkv, d, torch.bfloat16, cuda_device)
+    ks, vs = [], []
+    for sid, pre in enumerate(prefixes):
+        k = torch.randn((pre + kd, hkv, d), generator=gen).to(torch.bfloat16)
+        v = torch.randn((pre + kd, hkv, d), generator=gen).to(torch.bfloat16)
+        _write(store, sid, k[: pre - 1].to(cuda_device), v[: pre - 1].to(cuda_device))
+        store.append_tokens(sid, kd + 1)
+        ks.append(k), vs.append(v)
+    b = len(prefixes)
+    q = torch.randn((b, kd + 1, hq, d), generator=gen).to(torch.bfloat16)
+    kn = torch.stack([k[p - 1:] for k, p in zip(ks, prefixes)])
+    vn = torch.stack([v[p - 1:] for v, p in zip(vs, prefixes)])
+    out = store.verify_attention(list(range(b)), q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
+    torch.cuda.synchronize()
+    got = _np32(out)
+    for sid, pre in enumerate(prefixes):
+        want = verify_attention(_np32(q[sid]), _np32(ks[sid]), _np32(vs[sid]), d ** -0.5, pre)
+        np.testing.assert_allclose(got[sid], want, rtol=RTOL, atol=ATOL, err_msg=f"prefix {pre}")
+    assert store.pool.prefill_error_flag() == 0
+
