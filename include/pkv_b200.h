@@ -375,6 +375,17 @@ void pkv_stepper_destroy(pkv_stepper* st);
  * refcounts the stepper keeps in sync; rebind after growing them. */
 int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
                                 int32_t* context_lens, int32_t* refcounts);
+/* Fixed-step mode, for decode steps recorded once in a CUDA graph and
+ * replayed: from now on every upload writes the step descriptor into one
+ * device block whose header carries the step's counts, the attention
+ * launches always have the same arguments (capacities, that block, a
+ * workspace sized now) and the kernels read the counts at run time.
+ * max_batch bounds the sequences of a step, max_items its work items (0: a
+ * default of KV-head groups x max_batch + 4 x the persistent grid's warps); a
+ * step beyond them fails with PKV_ERR_UNSUPPORTED.  The device tables must
+ * not be rebound while a graph holds such launches.  No counterpart in the
+ * reference (its decode loop is eager Python). */
+int32_t pkv_stepper_fix_steps(pkv_stepper* st, int32_t max_batch, int32_t max_items, void* stream);
 /* Optional: a host int32 array [n_blocks] of tokens stored per block that the
  * stepper keeps current -- a copy-on-write copy gives the new block its
  * source's count, an uploaded step sets the count of the block each step

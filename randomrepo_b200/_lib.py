@@ -153,6 +153,7 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_destroy": (None, [c_void_p]),
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "pkv_stepper_bind_fill": (c_int32, [c_void_p, c_void_p, c_int64]),
+    "pkv_stepper_fix_steps": (c_int32, [c_void_p, c_int32, c_int32, c_void_p]),
     "pkv_stepper_sync": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, I32P, I32P, I32P]),
     "pkv_stepper_begin": (c_int32, [c_void_p, c_void_p, c_int32, POINTER(StepInfo), c_void_p, c_void_p, c_void_p]),
     "pkv_stepper_upload": (c_int32, [c_void_p, c_void_p, POINTER(StepInfo), c_void_p, c_int64]),

@@ -91,6 +91,12 @@ struct DecodeParams {
   int32_t deferred_lens;
   int32_t* refcounts;
   int32_t* ws_error;
+  // Fixed-step mode (a launch recorded once in a CUDA graph and replayed for
+  // every step): when set, n_items, n_combine, batch, pages_per_split and the
+  // deferred-update counts are read from here at run time:
+  // {n_items, n_combine, batch, pages_per_split, deferred_refs, deferred_lens}.
+  const int32_t* step_header;
+  int32_t n_combine;
   int32_t n_items;
   int32_t batch;
   int32_t table_stride;
@@ -184,8 +190,24 @@ __device__ __forceinline__ Item next_item(const DecodeParams& p, int lane, int t
   return m;
 }
 
+// The launch's per-step values: from the parameters, or from the step header.
+__device__ __forceinline__ DecodeParams step_params(const DecodeParams& in) {
+  DecodeParams p = in;
+  if (in.step_header) {
+    const int32_t* h = in.step_header;
+    p.n_items = h[0];
+    p.n_combine = h[1];
+    p.batch = h[2];
+    p.pages_per_split = h[3];
+    p.deferred_refs = h[4];
+    p.deferred_lens = h[5];
+  }
+  return p;
+}
+
 template <int D, int HPC, typename T>
-__global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kernel(const DecodeParams launch_p) {
+  const DecodeParams p = step_params(launch_p);
   using C = Cfg<D, HPC>;
   constexpr int KK = D / 16;
   constexpr int S = C::kStages;
@@ -470,13 +492,7 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
 constexpr int kCombineThreads = 32;
 
 template <int D, int HPC, typename T>
-__global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(const DecodeParams p,
-                                                                               const int4* entries, int n_entries) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int e = blockIdx.x, pi = blockIdx.y;
-  const int hh = pi >> 3, gq = pi & 7;
-  if (e >= n_entries || gq >= p.group) return;
-  const int4 en = entries[e];
+__device__ __forceinline__ void combine_one(const DecodeParams& p, const int4 en, int hh, int gq) {
   const int b = en.x, hg = en.y, ns = en.z, slot0 = en.w;
   const int lane = threadIdx.x;
   if (b < 0 || b >= p.batch || (hg + 1) * HPC > p.hkv || ns < 2 || ns > kMaxSplitsPerSeq || slot0 < 0 ||
@@ -534,6 +550,19 @@ __global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(c
   dst[3] = MmaOp<T>::from_float(acc.w * inv);
 }
 
+template <int D, int HPC, typename T>
+__global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(const DecodeParams launch_p,
+                                                                               const int4* entries) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const DecodeParams p = step_params(launch_p);
+  const int pi = blockIdx.y;
+  const int hh = pi >> 3, gq = pi & 7;
+  if (gq >= p.group) return;
+  // One (entry, query head) per block; a fixed-step launch has a fixed grid
+  // and strides over however many entries the step has.
+  for (int e = blockIdx.x; e < p.n_combine; e += gridDim.x) combine_one<D, HPC, T>(p, entries[e], hh, gq);
+}
+
 // ---------------------------------------------------------------------------
 // Host side.
 
@@ -574,7 +603,7 @@ WsLayout ws_layout(int32_t batch, int32_t hkv, int32_t head_dim, int64_t n_items
 }
 
 template <int D, int HPC, typename T>
-int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entries, cudaStream_t s) {
+int32_t launch_decode(const DecodeParams& prm, const int4* entries, cudaStream_t s) {
   using C = Cfg<D, HPC>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -586,11 +615,19 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entrie
     }
     attr_set = true;
   }
-  const int grid = std::max(1, std::min((prm.n_items + C::kWarps - 1) / C::kWarps, num_sms_cached()));
+  // A fixed-step launch does not know its item count on the host: it always
+  // runs the persistent grid (idle warps fetch an out-of-range item and
+  // leave) and the combine kernel.
+  const bool fixed = prm.step_header != nullptr;
+  const int grid =
+      fixed ? num_sms_cached() : std::max(1, std::min((prm.n_items + C::kWarps - 1) / C::kWarps, num_sms_cached()));
   paged_decode_kernel<D, HPC, T><<<grid, C::kWarps * 32, C::kSmemBytes, s>>>(prm);
-  if (n_entries > 0) {
+  if (fixed || prm.n_combine > 0) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)n_entries, HPC * 8);
+    // One block per (entry, query head): n_combine is the step's count, or
+    // its capacity for a fixed-step launch (whose blocks past the step's
+    // count return at once).
+    cfg.gridDim = dim3((unsigned)std::max(1, prm.n_combine), HPC * 8);
     cfg.blockDim = dim3(kCombineThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
@@ -599,7 +636,7 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entrie
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t le = cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel<D, HPC, T>, prm, entries, n_entries);
+    cudaError_t le = cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel<D, HPC, T>, prm, entries);
     if (le != cudaSuccess) {
       pkv_set_error(std::string("pkv_decode_attention combine launch: ") + cudaGetErrorString(le));
       return PKV_ERR_CUDA;
@@ -614,9 +651,9 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, int n_entrie
 }
 
 template <int D, typename T>
-int32_t launch_for_heads(const DecodeParams& prm, const int4* entries, int n_entries, cudaStream_t s) {
-  return heads_per_item(prm.hkv) == 2 ? launch_decode<D, 2, T>(prm, entries, n_entries, s)
-                                      : launch_decode<D, 1, T>(prm, entries, n_entries, s);
+int32_t launch_for_heads(const DecodeParams& prm, const int4* entries, cudaStream_t s) {
+  return heads_per_item(prm.hkv) == 2 ? launch_decode<D, 2, T>(prm, entries, s)
+                                      : launch_decode<D, 1, T>(prm, entries, s);
 }
 
 }  // namespace
@@ -743,7 +780,7 @@ int32_t pkv_decode_attention(const pkv_pool_geom* g, void* pool, int32_t layer, 
   return pkv_decode_attention_ex(g, pool, layer, q, k_new, v_new, block_tables, table_stride, table_rows,
                                  context_lens, rows, seq_lens, new_blocks, work_items, n_items, n_combine, batch,
                                  num_q_heads, pages_per_split, scale, out, workspace, workspace_bytes, stream,
-                                 nullptr, 0, 0, nullptr);
+                                 nullptr, 0, 0, nullptr, nullptr, nullptr);
 }
 
 }  // extern "C"
@@ -755,7 +792,7 @@ int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t laye
                                 int32_t n_combine, int32_t batch, int32_t num_q_heads, int32_t pages_per_split,
                                 float scale, void* out, void* workspace, int64_t workspace_bytes, void* stream,
                                 const int32_t* deferred, int32_t deferred_refs, int32_t deferred_lens,
-                                int32_t* refcounts) {
+                                int32_t* refcounts, const int32_t* step_header, const int32_t* combine_entries) {
   pkv_clear_error();
   if (deferred && (!refcounts || !context_lens || deferred_refs < 0 || deferred_lens < 0)) {
     pkv_set_error("deferred updates need the refcount and length arrays");
@@ -819,6 +856,8 @@ int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t laye
   prm.refcounts = refcounts;
   prm.ws_ml = reinterpret_cast<float*>(ws + wl.ml);
   prm.ws_o = reinterpret_cast<float*>(ws + wl.o);
+  prm.step_header = step_header;
+  prm.n_combine = n_combine;
   prm.n_items = n_items;
   prm.batch = batch;
   prm.table_stride = table_stride;
@@ -831,12 +870,13 @@ int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t laye
   prm.pages_per_split = pages_per_split;
   prm.scale_log2 = scale * kLog2e;
   auto s = static_cast<cudaStream_t>(stream);
-  const int4* entries = reinterpret_cast<const int4*>(work_items) + n_items;
+  const int4* entries = combine_entries ? reinterpret_cast<const int4*>(combine_entries)
+                                        : reinterpret_cast<const int4*>(work_items) + n_items;
   if (g->head_dim == 128)
-    return g->dtype == PKV_BF16 ? launch_for_heads<128, __nv_bfloat16>(prm, entries, n_combine, s)
-                                : launch_for_heads<128, __half>(prm, entries, n_combine, s);
-  return g->dtype == PKV_BF16 ? launch_for_heads<64, __nv_bfloat16>(prm, entries, n_combine, s)
-                              : launch_for_heads<64, __half>(prm, entries, n_combine, s);
+    return g->dtype == PKV_BF16 ? launch_for_heads<128, __nv_bfloat16>(prm, entries, s)
+                                : launch_for_heads<128, __half>(prm, entries, s);
+  return g->dtype == PKV_BF16 ? launch_for_heads<64, __nv_bfloat16>(prm, entries, s)
+                              : launch_for_heads<64, __half>(prm, entries, s);
 }
 
 extern "C" {

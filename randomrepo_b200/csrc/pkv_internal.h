@@ -7,6 +7,11 @@
 // pkv_decode_attention plus length / refcount updates the decode does not
 // read, applied by the kernel itself: `deferred` holds deferred_refs
 // (block, refcount) pairs then deferred_lens (row, length) pairs.
+// Fixed-step mode (for launches recorded in a CUDA graph): with step_header
+// non-NULL the kernels read {n_items, n_combine, batch, pages_per_split,
+// deferred_refs, deferred_lens} from it at run time (the arguments then give
+// capacities), and the combine entries come from combine_entries (otherwise
+// they follow the n_items work items).
 int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t layer, const void* q, const void* k_new,
                                 const void* v_new, int32_t* block_tables, int32_t table_stride, int32_t table_rows,
                                 int32_t* context_lens, const int32_t* rows, const int32_t* seq_lens,
@@ -14,4 +19,4 @@ int32_t pkv_decode_attention_ex(const pkv_pool_geom* g, void* pool, int32_t laye
                                 int32_t n_combine, int32_t batch, int32_t num_q_heads, int32_t pages_per_split,
                                 float scale, void* out, void* workspace, int64_t workspace_bytes, void* stream,
                                 const int32_t* deferred, int32_t deferred_refs, int32_t deferred_lens,
-                                int32_t* refcounts);
+                                int32_t* refcounts, const int32_t* step_header, const int32_t* combine_entries);

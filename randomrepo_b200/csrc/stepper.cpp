@@ -79,6 +79,16 @@ struct pkv_stepper {
   const int32_t* def_dev = nullptr;
   int32_t def_refs = 0, def_lens = 0;
   bool def_pending = false;
+  // Fixed-step mode: every step's descriptor goes to the same device block,
+  // whose header gives the kernels the step's counts, so the attention
+  // launches of a step can be recorded once in a CUDA graph and replayed.
+  // Layout (int32): header[16] | deferred updates | slots (int64) | rows |
+  // lens | new blocks | combine entries (int4) | work items (int4).
+  bool fixed = false;
+  int32_t fx_batch = 0, fx_items = 0, fx_combine = 0;
+  int64_t fx_def_cap = 0, fx_off_def = 0, fx_off_slots = 0, fx_off_rows = 0, fx_off_comb = 0, fx_off_items = 0;
+  int32_t* fx_dev = nullptr;
+  std::vector<int32_t> fx_plan;
   // Optional per-launch timing of the decode kernels (events around them).
   std::vector<cudaEvent_t> t_start, t_stop;
   int64_t t_cap = 0, t_count = 0, t_every = 1, t_seen = 0;
@@ -93,6 +103,7 @@ struct pkv_stepper {
       if (s.dev) cudaFree(s.dev);
     }
     if (ws) cudaFree(ws);
+    if (fx_dev) cudaFree(fx_dev);
     for (auto e : t_start) cudaEventDestroy(e);
     for (auto e : t_stop) cudaEventDestroy(e);
   }
@@ -139,6 +150,73 @@ struct pkv_stepper {
     int32_t st = cuda_status(cudaEventRecord(round_done, stream), "cudaEventRecord");
     if (!st) round_pending = true;
     return st;
+  }
+
+  // The step descriptor into the fixed block (fixed-step mode).
+  int32_t upload_fixed(cudaStream_t cs, pkv_step_info* out_info, int32_t n, int32_t pps, int64_t n_items,
+                       int64_t n_combine, bool defer, int64_t pr, int64_t pl) {
+    if (n > fx_batch || n_items > fx_items || n_combine > fx_combine) {
+      pkv_set_error("decode step exceeds the fixed-step capacity (" + std::to_string(n) + " sequences, " +
+                    std::to_string(n_items) + " work items)");
+      return PKV_ERR_UNSUPPORTED;
+    }
+    if (defer && 4 + 2 * (pr + pl) > fx_def_cap) {
+      // Too many pending updates for the block: apply them with the table kernel.
+      int32_t n_copies = 0;
+      int32_t s = apply_pending(cs, nullptr, 0, &n_copies);
+      if (s) return s;
+      defer = false;
+    }
+    const int64_t used = fx_off_items + 4 * n_items;
+    Slot* sl;
+    int32_t s = take_slot(fx_off_items + 4 * (int64_t)fx_items, &sl);
+    if (s) return s;
+    int32_t* h = sl->host;
+    fx_plan.resize(4 * (n_items + n_combine));
+    s = pkv_decode_plan(lens_h.data(), n, geom.num_kv_heads, geom.head_dim, num_sms, &pps, fx_plan.data(),
+                        n_items + n_combine, &n_items, &n_combine);
+    if (s) return s;
+    std::memcpy(h + fx_off_items, fx_plan.data(), 4 * n_items * 4);
+    std::memcpy(h + fx_off_comb, fx_plan.data() + 4 * n_items, 4 * n_combine * 4);
+    int64_t written = 0;
+    if (defer) {
+      s = pkv_allocator_drain_updates(alloc, h + fx_off_def, fx_def_cap, &written);
+      if (s) return s;
+    }
+    std::memset(h, 0, 16 * 4);
+    h[0] = (int32_t)n_items;
+    h[1] = (int32_t)n_combine;
+    h[2] = n;
+    h[3] = pps;
+    h[4] = defer ? h[fx_off_def + 1] : 0;
+    h[5] = defer ? h[fx_off_def + 2] : 0;
+    int64_t* slots = reinterpret_cast<int64_t*>(h + fx_off_slots);
+    const int32_t bs = geom.block_size;
+    for (int i = 0; i < n; ++i) slots[i] = (int64_t)tokb_h[i] * bs + (lens_h[i] - 1) % bs;
+    std::memcpy(h + fx_off_rows, rows_h.data(), n * 4);
+    std::memcpy(h + fx_off_rows + fx_batch, lens_h.data(), n * 4);
+    std::memcpy(h + fx_off_rows + 2 * fx_batch, newb_h.data(), n * 4);
+    s = cuda_status(cudaMemcpyAsync(fx_dev, h, used * 4, cudaMemcpyHostToDevice, cs), "H2D");
+    if (!s) s = copied(cs);
+    if (s) return s;
+    if (fill) {
+      for (int i = 0; i < n; ++i) {
+        const int32_t b = tokb_h[i];
+        if (b >= 0 && b < fill_n) fill[b] = (lens_h[i] - 1) % bs + 1;
+      }
+    }
+    def_pending = false;
+    out_info->pages_per_split = pps;
+    out_info->n_items = (int32_t)n_items;
+    out_info->n_combine = (int32_t)n_combine;
+    out_info->items = fx_dev + fx_off_items;
+    out_info->slots = reinterpret_cast<const int64_t*>(fx_dev + fx_off_slots);
+    out_info->rows = fx_dev + fx_off_rows;
+    out_info->seq_lens = fx_dev + fx_off_rows + fx_batch;
+    out_info->new_blocks = fx_dev + fx_off_rows + 2 * fx_batch;
+    info = *out_info;
+    step_ready = true;
+    return PKV_OK;
   }
 
   int32_t upload(Slot* s, int64_t n, cudaStream_t stream) {
@@ -240,6 +318,57 @@ int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t 
   return PKV_OK;
 }
 
+int32_t pkv_stepper_fix_steps(pkv_stepper* st, int32_t max_batch, int32_t max_items, void* stream) {
+  pkv_clear_error();
+  if (max_batch <= 0 || max_items < 0) {
+    pkv_set_error("pkv_stepper_fix_steps: max_batch must be positive and max_items non-negative");
+    return PKV_ERR_ARG;
+  }
+  const int32_t hpc = pkv_decode_heads_per_item(st->geom.num_kv_heads);
+  const int32_t groups = st->geom.num_kv_heads / hpc;
+  const int32_t warps = st->num_sms * (2 * 16 * st->geom.head_dim * 2 * hpc >= 16384 ? 4 : 8);
+  if (max_items == 0) max_items = groups * max_batch + 4 * warps;
+  max_items = std::max(max_items, groups * max_batch);
+  auto cs = static_cast<cudaStream_t>(stream);
+  if (st->fx_dev) {
+    int32_t s0 = cuda_status(cudaStreamSynchronize(cs), "pkv_stepper_fix_steps");
+    if (s0) return s0;
+    cudaFree(st->fx_dev);
+    st->fx_dev = nullptr;
+  }
+  st->fixed = false;
+  st->fx_batch = max_batch;
+  st->fx_items = max_items;
+  st->fx_combine = groups * max_batch;
+  st->fx_def_cap = 4 + 4 * (int64_t)max_batch + 256;
+  st->fx_off_def = 16;
+  st->fx_off_slots = st->fx_off_def + st->fx_def_cap;        // even: int64-aligned
+  st->fx_off_rows = st->fx_off_slots + 2 * (int64_t)max_batch;
+  st->fx_off_comb = (st->fx_off_rows + 3 * (int64_t)max_batch + 3) & ~int64_t(3);  // int4-aligned
+  st->fx_off_items = st->fx_off_comb + 4 * (int64_t)st->fx_combine;
+  const int64_t total = st->fx_off_items + 4 * (int64_t)max_items;
+  int32_t s = cuda_status(cudaMalloc((void**)&st->fx_dev, total * 4), "cudaMalloc fixed step block");
+  if (!s) s = cuda_status(cudaMemsetAsync(st->fx_dev, 0, total * 4, cs), "cudaMemsetAsync fixed step block");
+  if (s) return s;
+  // The workspace for the capacities, allocated now so that no step allocates.
+  const int64_t need = pkv_decode_workspace_bytes(max_batch, st->geom.num_kv_heads, st->geom.head_dim, max_items);
+  if (need > st->ws_bytes) {
+    if (st->ws) {
+      s = cuda_status(cudaStreamSynchronize(cs), "stepper workspace");
+      if (s) return s;
+      cudaFree(st->ws);
+      st->ws = nullptr;
+    }
+    s = cuda_status(cudaMalloc(&st->ws, need), "cudaMalloc workspace");
+    if (!s) s = cuda_status(cudaMemsetAsync(st->ws, 0, need, cs), "cudaMemsetAsync workspace");
+    if (s) return s;
+    st->ws_bytes = need;
+  }
+  st->fixed = true;
+  st->step_ready = false;
+  return PKV_OK;
+}
+
 int32_t pkv_stepper_bind_fill(pkv_stepper* st, int32_t* block_fill, int64_t n_blocks) {
   pkv_clear_error();
   if (n_blocks < 0 || (n_blocks > 0 && !block_fill)) {
@@ -326,6 +455,7 @@ int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, i
   s = pkv_decode_plan(st->lens_h.data(), n, st->geom.num_kv_heads, st->geom.head_dim, st->num_sms, &pps, nullptr, 0,
                       &n_items, &n_combine);
   if (s) return s;
+  if (st->fixed) return st->upload_fixed(cs, info, n, pps, n_items, n_combine, defer, pr, pl);
   // Descriptor: [items + combine entries (int4) | slots (int64) | rows | lens | new_blocks]
   const int64_t n_quads = n_items + n_combine;
   const int64_t def_off = 4 * n_quads + 2 * n + 3 * n;
@@ -403,12 +533,25 @@ int32_t pkv_stepper_attention(pkv_stepper* st, int32_t layer, const void* q, con
   }
   const pkv_step_info& in = st->info;
   const bool timed = st->t_count < st->t_cap && (st->t_seen++ % st->t_every) == 0;
+  if (st->fixed) {
+    // Same arguments every step: capacities, the fixed block, its header.
+    if (timed) cudaEventRecord(st->t_start[st->t_count], static_cast<cudaStream_t>(stream));
+    int32_t s = pkv_decode_attention_ex(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride,
+                                        st->rows, st->lens, in.rows, in.seq_lens, in.new_blocks, in.items,
+                                        st->fx_items, st->fx_combine, st->fx_batch, num_q_heads, 1, scale, out,
+                                        st->ws, st->ws_bytes, stream, st->fx_dev + st->fx_off_def + 4, 0, 0,
+                                        st->refs, st->fx_dev, st->fx_dev + st->fx_off_comb);
+    if (timed) cudaEventRecord(st->t_stop[st->t_count++], static_cast<cudaStream_t>(stream));
+    if (s == PKV_OK) st->launches += 2;
+    return s;
+  }
   const int32_t* def = st->def_pending ? st->def_dev : nullptr;
   if (timed) cudaEventRecord(st->t_start[st->t_count], static_cast<cudaStream_t>(stream));
   int32_t s = pkv_decode_attention_ex(&st->geom, st->pool, layer, q, k_new, v_new, st->tables, st->stride, st->rows,
                                       st->lens, in.rows, in.seq_lens, in.new_blocks, in.items, in.n_items,
                                       in.n_combine, in.batch, num_q_heads, in.pages_per_split, scale, out, st->ws,
-                                      st->ws_bytes, stream, def, st->def_refs, st->def_lens, st->refs);
+                                      st->ws_bytes, stream, def, st->def_refs, st->def_lens, st->refs, nullptr,
+                                      nullptr);
   if (s == PKV_OK && def) st->def_pending = false;
   if (timed) cudaEventRecord(st->t_stop[st->t_count++], static_cast<cudaStream_t>(stream));
   if (s == PKV_OK) st->launches += 1 + (in.n_combine > 0 ? 1 : 0);

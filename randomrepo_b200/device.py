@@ -88,6 +88,7 @@ class KVPool:
             _lib.raise_for_status(status.value)
         weakref.finalize(self, lib.pkv_stepper_destroy, self.stepper)
         self.step_serial = 0
+        self.fixed_batch = 0  # fixed-step mode capacity (0: off)
         self._timing_cap = 0
         self._pending = [ctypes.pointer(ctypes.c_int64()) for _ in range(4)]
         self._bind()
@@ -112,6 +113,14 @@ class KVPool:
         lens[:rows] = self.context_lens
         self.tables, self.context_lens = tables, lens
         self._bind()
+
+    def fix_steps(self, max_batch: int, max_items: int = 0) -> None:
+        """Switch decode steps to fixed-step mode (``pkv_stepper_fix_steps``) so that their attention
+        launches can be recorded in a CUDA graph and replayed for later steps."""
+        with torch.cuda.device(self.device):
+            _lib.raise_for_status(lib.pkv_stepper_fix_steps(self.stepper, int(max_batch), int(max_items),
+                                                            _stream_ptr()))
+        self.fixed_batch = int(max_batch)
 
     def pending_copies(self) -> int:
         c = self._pending

@@ -19,10 +19,17 @@ every step.  Here the paged store is the cache:
   stacking), with greedy or temperature / top-p sampling as in
   agentrl/core/rollout.py:307-329.
 
+With ``cuda_graphs=True`` a decode step's whole forward (all layers, the
+attention launches and the LM head) is recorded once per batch size in a CUDA
+graph and replayed: the store runs in fixed-step mode (each step's descriptor
+goes to one device block whose header the kernels read), so a step costs the
+allocator step, one small upload and one graph launch on the host instead of
+a Python forward through every layer.
+
 Only ``last_hidden_state`` rows that need logits go through the LM head, so a
 long packed prefill never materialises [tokens, vocab] logits.  By default
-the head runs in fp32 on the model's final hidden state (an fp32 copy of its
-weight is kept): a bf16 head rounds logits to 8 bits of mantissa, which
+the head's logits come out in fp32 (a 16-bit GEMM accumulating and storing in
+fp32 on the GPU): a 16-bit head rounds logits to 8 bits of mantissa, which
 leaves exact ties in the argmax and coarse log-probabilities for the trainer.
 """
 
@@ -150,7 +157,7 @@ class PagedGenerator:
     """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches)."""
 
     def __init__(self, model, store, *, prefill_chunk_size: int = 512, eos_token_id: int | None = None,
-                 fp32_logits: bool = True) -> None:
+                 fp32_logits: bool = True, cuda_graphs: bool = False) -> None:
         use_paged_attention(model)
         self.model = model
         self.store = store
@@ -159,18 +166,23 @@ class PagedGenerator:
         self.device = next(model.parameters()).device
         self._base = model.get_decoder() if hasattr(model, "get_decoder") else model.model
         self._head = model.get_output_embeddings()
-        self._head32 = None
-        if fp32_logits:
-            w = self._head.weight.detach().float()
-            b = None if getattr(self._head, "bias", None) is None else self._head.bias.detach().float()
-            self._head32 = (w, b)
+        self.cuda_graphs = bool(cuda_graphs)
+        self._graphs: dict[int, tuple] = {}  # batch -> (graph, static tokens, static positions, static logits)
+        self._graph_tables = 0
+        self.fp32_logits = bool(fp32_logits)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """LM head on final hidden states [n, hidden] -> float32 logits [n, vocab]."""
         with torch.inference_mode():
-            if self._head32 is not None:
-                return torch.nn.functional.linear(hidden.float(), *self._head32)
-            return self._head(hidden).float()
+            if not self.fp32_logits:
+                return self._head(hidden).float()
+            w = self._head.weight
+            bias = getattr(self._head, "bias", None)
+            if hidden.is_cuda and hidden.dtype == w.dtype and w.dtype in (torch.bfloat16, torch.float16):
+                out = torch.mm(hidden, w.t(), out_dtype=torch.float32)
+            else:
+                out = torch.nn.functional.linear(hidden.float(), w.float())
+            return out if bias is None else out + bias.float()
 
     # -- forwards -------------------------------------------------------------
     def _forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor, ph: _Phase) -> torch.Tensor:
@@ -214,11 +226,58 @@ class PagedGenerator:
 
     def decode_step(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
         """Feed one token per sequence; returns next-token logits [n, vocab] (float32)."""
+        if self.cuda_graphs:
+            return self._decode_step_graph(sequence_ids, tokens)
         step = self.store.decode_step(sequence_ids)
         pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
         h = self._forward(tokens.reshape(-1, 1).to(self.device), pos.reshape(-1, 1),
                           _Phase("decode", self.store, step=step))
         return self.logits(h[:, -1])
+
+    def _decode_step_graph(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
+        pool = self.store.pool
+        n = len(sequence_ids)
+        if pool.fixed_batch < n:
+            pool.fix_steps(max(n, 2 * pool.fixed_batch))
+            self._graphs.clear()
+        step = self.store.decode_step(sequence_ids)
+        if pool.tables.data_ptr() != self._graph_tables:
+            # Graphs hold the tables' address: a grown (moved) table voids them.
+            self._graphs.clear()
+            self._graph_tables = pool.tables.data_ptr()
+        pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
+        tok = tokens.reshape(-1, 1).to(self.device)
+        entry = self._graphs.get(n)
+        if entry is None:
+            return self._capture(n, step, tok, pos.reshape(-1, 1))
+        graph, tok_s, pos_s, logits_s = entry
+        tok_s.copy_(tok)
+        pos_s.copy_(pos.reshape(-1, 1))
+        graph.replay()
+        return logits_s.clone()
+
+    def _capture(self, n: int, step, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Run this step eagerly (on a side stream, as capture requires a warm-up), then record it."""
+        tok_s, pos_s = tok.clone(), pos.clone()
+        ph = _Phase("decode", self.store, step=step)
+        cur = torch.cuda.current_stream(self.device)
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            logits = self.logits(self._forward(tok_s, pos_s, ph)[:, -1])
+        cur.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits_s = self.logits(self._forward(tok_s, pos_s, ph)[:, -1])
+        self._graphs[n] = (graph, tok_s, pos_s, logits_s)
+        return logits
+
+    def reserve_tables(self, max_tokens: int) -> None:
+        """Grow the device tables now for sequences of up to ``max_tokens`` (graph mode keeps their address)."""
+        pool = self.store.pool
+        stats = self.store.allocator._stats()
+        bs = self.store.allocator.block_size_tokens
+        pool.grow(int(stats.row_capacity) + 1, -(-int(max_tokens) // bs) + 1)
 
     # -- sampling ---------------------------------------------------------------
     @staticmethod
@@ -258,6 +317,8 @@ class PagedGenerator:
                 next_logits.append(logits[g])
         cur = torch.stack(next_logits)
         n = len(seq_ids)
+        if self.cuda_graphs:
+            self.reserve_tables(max(int(torch.as_tensor(p).numel()) for p in prompts) + max_new_tokens)
         tokens = [[] for _ in range(n)]
         logprobs = [[] for _ in range(n)]
         argmax = [[] for _ in range(n)]

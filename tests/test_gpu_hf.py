@@ -138,3 +138,23 @@ def test_group_fork_rollout_members_share_prompt(cuda_device):
         for m in range(4):
             assert grp["tokens"][4 * gi + m] == solo["tokens"][gi]
     assert store.allocator.used_block_count == 0
+
+
+def test_cuda_graph_decode_matches_eager(cuda_device):
+    """Decode steps replayed from CUDA graphs (fixed-step mode) give the eager path's tokens and logprobs."""
+    from randomrepo_b200.hf import PagedGenerator, make_store
+
+    model = _model(cuda_device, 128, 2, 12, 2)
+    gen = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 512, (n,), generator=gen) for n in (30, 77, 12)]
+    eager = PagedGenerator(model, make_store(model, total_blocks=1024), prefill_chunk_size=64)
+    graphs = PagedGenerator(model, make_store(model, total_blocks=1024), prefill_chunk_size=64, cuda_graphs=True)
+    for group in (1, 2):  # two batch sizes: a graph each
+        a = eager.generate(prompts, group_size=group, max_new_tokens=40)
+        b = graphs.generate(prompts, group_size=group, max_new_tokens=40)
+        assert a["tokens"] == b["tokens"]
+        np.testing.assert_allclose(np.concatenate(b["logprobs"]), np.concatenate(a["logprobs"]), atol=1e-4)
+    # Batch 6 outgrew the fixed-step capacity set for batch 3: capacity grew and the graphs were re-recorded.
+    assert set(graphs._graphs) == {6}
+    pool = graphs.store.pool
+    assert pool.decode_error_flag() == 0 and graphs.store.allocator.used_block_count == 0
