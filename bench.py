@@ -24,6 +24,11 @@ every 512-token chunk in one launch) against the measured bf16 tensor peak, and
 the speculative-verify read (1.5B target shape, 64 sequences, k = 4) against
 the measured HBM bandwidth, each timed alone with CUDA events and L2 flushed.
 
+It also carries ``rollout``: a GRPO rollout of the Qwen2.5-1.5B architecture
+(random-init bf16, 4 prompts x group 8, 128 new tokens) through
+PagedGenerator with CUDA-graph decode steps, next to stock HF generate on the
+same model and batch.
+
 Multi-GPU (torchrun): every rank owns its own 256 sequences and KV pool (weak
 scaling, no data-path collective); the timed region is bracketed by NCCL
 barriers and the elapsed time is the max over ranks.
@@ -354,6 +359,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         del store, q, kn, vn, out, q_d, kn_d, vn_d
         torch.cuda.empty_cache()
         result["tensor_tiles"] = run_tensor_tiles(device, args.seed, args.steps, args.warmup)
+    if world == 1 and not args.no_rollout:
+        result["rollout"] = run_rollout(device, args.seed)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
     return result
@@ -461,6 +468,84 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
     return res
 
 
+ROLLOUT_SHAPE = {"prompts": 4, "group": 8, "len_lo": 64, "len_hi": 256, "new_tokens": 128, "temperature": 1.0}
+
+
+def run_rollout(device: torch.device, seed: int, iters: int = 2) -> dict:
+    """GRPO rollout at the Qwen2.5-1.5B architecture, random-init bf16: PagedGenerator (CUDA-graph
+    decode steps, packed prefill, forked group prompts) against stock HF generate on the same batch."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
+
+    rs = ROLLOUT_SHAPE
+    torch.manual_seed(seed)
+    cfg = Qwen2Config(vocab_size=151936, hidden_size=1536, intermediate_size=8960, num_hidden_layers=28,
+                      num_attention_heads=12, num_key_value_heads=2, max_position_embeddings=32768,
+                      rope_theta=1000000.0, tie_word_embeddings=True, attn_implementation="sdpa")
+    with torch.device(device):
+        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16).eval()
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(rs["len_lo"], rs["len_hi"] + 1, size=rs["prompts"])
+    prompts = [torch.from_numpy(rng.integers(0, cfg.vocab_size, size=int(n))) for n in lens]
+    group, new = rs["group"], rs["new_tokens"]
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record()
+        n = fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return n, e0.elapsed_time(e1) / 1e3
+
+    ids = torch.zeros((len(prompts) * group, int(lens.max())), dtype=torch.long)
+    mask = torch.zeros_like(ids)
+    for g, p in enumerate(prompts):
+        ids[g * group:(g + 1) * group, -p.numel():] = p
+        mask[g * group:(g + 1) * group, -p.numel():] = 1
+    ids, mask = ids.to(device), mask.to(device)
+
+    def hf():
+        with torch.inference_mode():
+            out = model.generate(ids, attention_mask=mask, max_new_tokens=new, do_sample=True,
+                                 temperature=rs["temperature"], top_p=1.0, top_k=0, pad_token_id=0)
+        return (out.shape[1] - ids.shape[1]) * out.shape[0]
+
+    # Stock HF first: PagedGenerator switches the model's attention implementation.
+    hf()
+    hf_runs = [timed(hf) for _ in range(iters)]
+    store = make_store(model, total_blocks=4096)
+    gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
+
+    def ours(it):
+        r = gen.generate(prompts, group_size=group, max_new_tokens=new, first_id=it * 10000,
+                         sampling=SamplingConfig(do_sample=True, temperature=rs["temperature"], seed=it))
+        return sum(len(t) for t in r["tokens"])
+
+    ours(0)  # records the decode-step graph
+    ours_runs = [timed(lambda it=it: ours(it)) for it in range(1, iters + 1)]
+    if store.pool.decode_error_flag() or store.pool.prefill_error_flag():
+        raise RuntimeError("rollout kernels reported a device error")
+    ours_tps = sum(n for n, _ in ours_runs) / sum(t for _, t in ours_runs)
+    hf_tps = sum(n for n, _ in hf_runs) / sum(t for _, t in hf_runs)
+    del gen, store, model
+    torch.cuda.empty_cache()
+    return {
+        "workload": f"GRPO rollout, Qwen2.5-1.5B architecture (28 layers, 12q/2kv heads, head_dim 128, vocab "
+                    f"151936), random-init bf16, {rs['prompts']} prompts x group {group}, prompts "
+                    f"U[{rs['len_lo']},{rs['len_hi']}] random ids, {new} new tokens, temperature "
+                    f"{rs['temperature']}, seed {seed}",
+        "tokens_per_s": ours_tps,
+        "path": "PagedGenerator: packed prefill kernel, one prefill per group + copy-on-write forks, CUDA-graph "
+                "decode steps (fused append + paged decode per layer), fp32 logits",
+        "hf_generate_tokens_per_s": hf_tps,
+        "hf_generate_path": "stock HF generate on the same model and batch (SDPA + DynamicCache, left-padded)",
+        "speedup_vs_hf_generate": ours_tps / hf_tps,
+        "timing": f"CUDA events around whole rollouts, mean of {iters} after one warm-up each",
+    }
+
+
 def cpu_baseline(lengths: np.ndarray, seconds: float, sample: int = 32, steps: int | None = None) -> dict:
     """The reference's resident-cache decode step (oracle restatement) on a bounded sample."""
     from oracle.decode_step import ResidentDecodeBatch
@@ -555,6 +640,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tiles", action="store_true", help="skip the prefill / verify kernel lines (N=1 only)")
+    ap.add_argument("--no-rollout", action="store_true", help="skip the end-to-end rollout line (N=1 only)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
