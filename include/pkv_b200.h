@@ -433,6 +433,74 @@ int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every)
 /* Device milliseconds of the timed launches so far (waits for the last). */
 int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacity, int64_t* n_out);
 
+/* ---------------------------------------------------------------------------
+ * Vocabulary rows: token log-probabilities, token selection, speculative
+ * accept / reject.  Logits are fp32 rows of `vocab` columns, row r at
+ * logits + r * ld (ld >= vocab).  Each launch streams the rows once.  The
+ * workspace is device scratch of at least the size the matching
+ * *_workspace_bytes call returns.  `tickets` is an int32 device array
+ * (n_rows entries for the row entry points, pkv_spec_tickets for
+ * pkv_spec_accept) that is zero-filled once before its first use: the
+ * kernels leave it zero again, so one array serves every later launch.
+ * Launches sharing a workspace or a ticket array must run in stream order.
+ * ------------------------------------------------------------------------- */
+
+/* Workspace bytes for pkv_token_logprobs / pkv_sample_tokens over n_rows rows
+ * (-1 for invalid arguments). */
+int64_t pkv_sampling_workspace_bytes(int64_t n_rows, int32_t vocab);
+
+/* Replaces torch.log_softmax(logits, -1).gather(-1, tokens) of the
+ * old-policy pass (agentrl/core/rollout.py:462-465): logprobs_out[r] =
+ * logits[r][tokens[r]] - logsumexp(logits[r]) (NaN for a token outside
+ * [0, vocab)), lse_out[r] = logsumexp(logits[r]).  Either output may be NULL
+ * (logprobs_out needs tokens). */
+int32_t pkv_token_logprobs(const float* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* tokens,
+                           float* logprobs_out, float* lse_out, int32_t* tickets, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+
+/* Replaces the rollout's next-token choice (agentrl/core/rollout.py:307-315)
+ * and the log-probability recorded for it: with do_sample = 0, tokens_out[r]
+ * = argmax of row r (first index of the maximum); otherwise a draw from
+ * softmax(race_logits[r] / temperature) (race_logits NULL = logits; pass
+ * top-p filtered logits there, -inf for dropped columns), made with the
+ * Gumbel-max trick from a counter-based hash of (seed, offset, r, column).
+ * logprobs_out[r] = log_softmax(logits[r])[tokens_out[r]] (temperature 1);
+ * argmax_out[r] = argmax of logits[r].  logprobs_out and argmax_out may be
+ * NULL. */
+int32_t pkv_sample_tokens(const float* logits, const float* race_logits, int64_t ld, int32_t n_rows, int32_t vocab,
+                          float temperature, int32_t do_sample, uint64_t seed, uint64_t offset, int64_t* tokens_out,
+                          float* logprobs_out, int64_t* argmax_out, int32_t* tickets, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes and ticket count for pkv_spec_accept (-1 for invalid
+ * arguments). */
+int64_t pkv_spec_workspace_bytes(int32_t batch, int32_t k, int32_t vocab);
+int64_t pkv_spec_tickets(int32_t batch, int32_t k);
+
+/* Replaces SpeculativeRolloutOrchestrator._verify_draft
+ * (agentrl/generation/speculative.py:217-274) for a batch of sequences.
+ * target_logits [batch][k + 1][ld]: row i is the target's prediction after
+ * the sequence's last accepted token and drafts 0..i-1 (row k is the bonus
+ * row); draft_logits [batch][k][ld]: the draft's logits that proposed draft
+ * i; draft_tokens [batch][k]; n_draft[b] <= k drafts are valid (the draft
+ * stops after eos, speculative.py:210-211).  Draft i is accepted when u <=
+ * min(1, exp(lp_target - log(p_draft + 1e-12))), p_draft from softmax(draft
+ * logits / draft_temperature) and u = uniforms[b][i] (NULL: hashed from
+ * seed / offset); the first rejection draws a correction from
+ * max(p_target - p_draft, 0) (p_target itself if that is all zero), and
+ * accepting all n_draft drafts draws a bonus token from p_target of row
+ * n_draft; both draws are argmax when do_sample = 0.  An accepted
+ * eos_token_id (< 0: none) ends the round without a draw.  Outputs:
+ * tokens_out / logprobs_out [batch][k + 1] (the emitted tokens and their
+ * target log-probabilities, -1 / 0 past n_out), n_out[b] (tokens emitted;
+ * -1 when a draft token lies outside the vocabulary) and n_accepted[b]. */
+int32_t pkv_spec_accept(const float* target_logits, const float* draft_logits, int64_t ld,
+                        const int64_t* draft_tokens, const int32_t* n_draft, const float* uniforms, int32_t batch,
+                        int32_t k, int32_t vocab, float draft_temperature, int32_t do_sample, int64_t eos_token_id,
+                        uint64_t seed, uint64_t offset, int64_t* tokens_out, float* logprobs_out, int32_t* n_out,
+                        int32_t* n_accepted, int32_t* tickets, void* workspace, int64_t workspace_bytes,
+                        void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

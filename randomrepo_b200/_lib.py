@@ -9,7 +9,7 @@ runs on it.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpkv_b200.so"
@@ -170,6 +170,24 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_launches": (c_int64, [c_void_p]),
     "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64, c_int64]),
     "pkv_stepper_launch_times": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
+    "pkv_sampling_workspace_bytes": (c_int64, [c_int64, c_int32]),
+    "pkv_token_logprobs": (
+        c_int32,
+        [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
+    ),
+    "pkv_sample_tokens": (
+        c_int32,
+        [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_float, c_int32, c_uint64, c_uint64, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
+    ),
+    "pkv_spec_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
+    "pkv_spec_tickets": (c_int64, [c_int32, c_int32]),
+    "pkv_spec_accept": (
+        c_int32,
+        [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_float, c_int32,
+         c_int64, c_uint64, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+         c_void_p],
+    ),
 }
 
 # Entry points added after the first build; bound when present.

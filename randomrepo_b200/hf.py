@@ -42,6 +42,8 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from .sampling import SamplingConfig, top_p_filter
+
 ATTN_IMPLEMENTATION = "paged_b200"
 
 _local = threading.local()
@@ -51,7 +53,7 @@ _local = threading.local()
 class _Phase:
     kind: str                    # "decode" or "prefill"
     store: object
-    step: object = None          # DecodeStep for a decode phase
+    step: object = None          # DecodeStep (decode) or PrefillStep (prefill, laid out by the first layer)
     sequence_ids: list = field(default_factory=list)
     q_lens: np.ndarray | None = None
 
@@ -86,9 +88,11 @@ def paged_attention_forward(module, query, key, value, attention_mask=None, scal
         return out.view(b, 1, hq, d), None
     if b != 1:
         raise ValueError("prefill runs packed: batch 1, the chunks of all sequences along the token axis")
+    if ph.step is None and hasattr(ph.store, "prefill_step"):
+        ph.step = ph.store.prefill_step(ph.sequence_ids, ph.q_lens, hq)
     out = ph.store.prefill_attention(ph.sequence_ids, q.reshape(t, hq, d).contiguous(),
                                      k.reshape(t, hkv, d).contiguous(), v.reshape(t, hkv, d).contiguous(),
-                                     q_lens=ph.q_lens, layer=layer, scale=scaling)
+                                     q_lens=ph.q_lens, layer=layer, scale=scaling, step=ph.step)
     return out.view(1, t, hq, d), None
 
 
@@ -132,32 +136,18 @@ def make_store(model, total_blocks: int, block_size: int = 16, device=None):
                              head_dim=head_dim, dtype=dtype, device=dev)
 
 
-@dataclass
-class SamplingConfig:
-    """agentrl/core/rollout.py:307-329: greedy unless do_sample with temperature > 0 (then top-p)."""
-
-    do_sample: bool = False
-    temperature: float = 1.0
-    top_p: float = 1.0
-    seed: int = 0
-
-
-def _top_p(logits: torch.Tensor, top_p: float) -> torch.Tensor:
-    if top_p >= 1.0:
-        return logits
-    sorted_logits, idx = torch.sort(logits, descending=True, dim=-1)
-    probs = torch.softmax(sorted_logits, dim=-1)
-    cum = probs.cumsum(dim=-1)
-    drop = cum - probs > top_p
-    sorted_logits = sorted_logits.masked_fill(drop, float("-inf"))
-    return torch.full_like(logits, float("-inf")).scatter(-1, idx, sorted_logits)
+_top_p = top_p_filter
 
 
 class PagedGenerator:
-    """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches)."""
+    """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches).
+
+    Token selection and log-probabilities go through ``sampler`` (by default
+    the library's ``DeviceSampler`` kernels, created on first use).
+    """
 
     def __init__(self, model, store, *, prefill_chunk_size: int = 512, eos_token_id: int | None = None,
-                 fp32_logits: bool = True, cuda_graphs: bool = False) -> None:
+                 fp32_logits: bool = True, cuda_graphs: bool = False, sampler=None) -> None:
         use_paged_attention(model)
         self.model = model
         self.store = store
@@ -170,6 +160,15 @@ class PagedGenerator:
         self._graphs: dict[int, tuple] = {}  # batch -> (graph, static tokens, static positions, static logits)
         self._graph_tables = 0
         self.fp32_logits = bool(fp32_logits)
+        self._sampler = sampler
+
+    @property
+    def sampler(self):
+        if self._sampler is None:
+            from .sampling import DeviceSampler
+
+            self._sampler = DeviceSampler(self.device)
+        return self._sampler
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """LM head on final hidden states [n, hidden] -> float32 logits [n, vocab]."""
@@ -189,6 +188,35 @@ class PagedGenerator:
         with _phase(ph), torch.inference_mode():
             out = self._base(input_ids=input_ids, position_ids=position_ids, use_cache=False)
         return out.last_hidden_state
+
+    def _token_count(self, sid: int) -> int:
+        return int(self.store.token_count(sid))
+
+    def extend_hidden(self, sequence_ids, chunks) -> tuple[torch.Tensor, np.ndarray]:
+        """Append one chunk of tokens to each (existing) sequence and run one packed forward
+        over all chunks: returns (final hidden states [sum of chunk lengths, hidden], chunk
+        lengths).  Each chunk attends to its sequence's cached tokens and causally to itself."""
+        ids = [int(s) for s in sequence_ids]
+        toks = [torch.as_tensor(c, dtype=torch.long).reshape(-1) for c in chunks]
+        if len(ids) != len(toks):
+            raise ValueError("one chunk per sequence id")
+        q_lens = np.array([t.numel() for t in toks], dtype=np.int64)
+        past = [self._token_count(sid) for sid in ids]
+        for sid, t in zip(ids, toks):
+            self.store.append_tokens(sid, t.numel())
+        input_ids = torch.cat(toks).to(self.device).unsqueeze(0)
+        pos = torch.cat([torch.arange(p0, p0 + t.numel()) for p0, t in zip(past, toks)]).to(self.device)
+        h = self._forward(input_ids, pos.unsqueeze(0), _Phase("prefill", self.store, sequence_ids=ids, q_lens=q_lens))
+        return h[0], q_lens
+
+    def extend(self, sequence_ids, chunks, *, all_logits: bool = False) -> torch.Tensor:
+        """``extend_hidden`` then the LM head: float32 logits of each chunk's last token
+        [n, vocab], or of every token [sum of chunk lengths, vocab] with ``all_logits``."""
+        h, q_lens = self.extend_hidden(sequence_ids, chunks)
+        if all_logits:
+            return self.logits(h)
+        ends = torch.from_numpy(np.cumsum(q_lens) - 1).to(h.device)
+        return self.logits(h.index_select(0, ends))
 
     def prefill(self, sequence_ids, prompts) -> torch.Tensor:
         """Reserve each prompt, write its K/V, return next-token logits [n, vocab] (float32).
@@ -210,18 +238,11 @@ class PagedGenerator:
         rounds = max((t.numel() + cs - 1) // cs for t in toks)
         for c in range(rounds):
             members = [i for i, t in enumerate(toks) if t.numel() > c * cs]
-            chunks = [toks[i][c * cs:(c + 1) * cs] for i in members]
-            q_lens = np.array([ch.numel() for ch in chunks], dtype=np.int64)
-            for i, ch in zip(members, chunks):
-                self.store.append_tokens(ids[i], ch.numel())
-            input_ids = torch.cat(chunks).to(self.device).unsqueeze(0)
-            pos = torch.cat([torch.arange(c * cs, c * cs + ch.numel()) for ch in chunks]).to(self.device)
-            h = self._forward(input_ids, pos.unsqueeze(0),
-                              _Phase("prefill", self.store, sequence_ids=[ids[i] for i in members], q_lens=q_lens))
+            h, q_lens = self.extend_hidden([ids[i] for i in members], [toks[i][c * cs:(c + 1) * cs] for i in members])
             ends = np.cumsum(q_lens) - 1
             for j, i in enumerate(members):
                 if (c + 1) * cs >= toks[i].numel():
-                    last_hidden[i] = h[0, int(ends[j])]
+                    last_hidden[i] = h[int(ends[j])]
         return self.logits(torch.stack(last_hidden))
 
     def decode_step(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
@@ -279,14 +300,6 @@ class PagedGenerator:
         bs = self.store.allocator.block_size_tokens
         pool.grow(int(stats.row_capacity) + 1, -(-int(max_tokens) // bs) + 1)
 
-    # -- sampling ---------------------------------------------------------------
-    @staticmethod
-    def sample(logits: torch.Tensor, cfg: SamplingConfig, gen: torch.Generator | None) -> torch.Tensor:
-        if cfg.do_sample and cfg.temperature > 0:
-            probs = torch.softmax(_top_p(logits / cfg.temperature, cfg.top_p), dim=-1)
-            return torch.multinomial(probs, 1, generator=gen).reshape(-1)
-        return torch.argmax(logits, dim=-1)
-
     # -- rollout ----------------------------------------------------------------
     def generate(self, prompts, *, group_size: int = 1, max_new_tokens: int = 16,
                  sampling: SamplingConfig | None = None, force_tokens=None, first_id: int = 0,
@@ -296,14 +309,15 @@ class PagedGenerator:
         Each prompt is prefilled once; the other members of its group fork the
         prompt's pages (copy-on-write) and start from the same next-token
         logits.  Returns ``{"sequence_ids", "tokens" (list per sequence),
-        "logprobs" (list per sequence), "argmax" (per step, the greedy token
-        of each sequence's logits)}``.  ``force_tokens[i]`` (optional) feeds
-        sequence i those tokens instead of sampled ones (teacher forcing).
+        "logprobs" (list per sequence: the temperature-1 log-probability of
+        each emitted token, the old-policy value of rollout.py:456-472),
+        "argmax" (per step, the greedy token of each sequence's logits)}``.
+        ``force_tokens[i]`` (optional) feeds sequence i those tokens instead
+        of sampled ones (teacher forcing).
         """
         cfg = sampling or SamplingConfig()
-        gen = None
-        if cfg.do_sample:
-            gen = torch.Generator(device=self.device).manual_seed(cfg.seed)
+        sampler = self.sampler
+        sampler.reseed(cfg.seed)
         n_groups = len(prompts)
         heads = [first_id + g * group_size for g in range(n_groups)]
         logits = self.prefill(heads, prompts)
@@ -326,13 +340,12 @@ class PagedGenerator:
         for step in range(max_new_tokens):
             if not active:
                 break
-            lp = torch.log_softmax(cur, dim=-1)
-            am = torch.argmax(cur, dim=-1)
             if force_tokens is not None:
                 nxt = torch.tensor([int(force_tokens[i][step]) for i in active], device=cur.device)
+                _, _, am = sampler.sample(cur)
+                chosen_lp = sampler.token_logprobs(cur, nxt)
             else:
-                nxt = self.sample(cur, cfg, gen)
-            chosen_lp = lp.gather(1, nxt.reshape(-1, 1)).reshape(-1)
+                nxt, chosen_lp, am = sampler.sample(cur, cfg)
             nxt_h, lp_h, am_h = nxt.tolist(), chosen_lp.tolist(), am.tolist()
             still = []
             for j, i in enumerate(active):

@@ -29,7 +29,7 @@ import torch
 
 from . import _lib
 from ._lib import lib
-from .device import KVPool, plan_prefill
+from .device import KVPool, PrefillPlan, plan_prefill
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -255,6 +255,24 @@ class DecodeStep:
         return int(self.info.pages_per_split)
 
 
+@dataclass
+class PrefillStep:
+    """One prefill / verify forward's layout on the device, shared by every layer.
+
+    Sequence i's chunk is its last ``q_lens[i]`` tokens; ``slots`` are the pool
+    slots of the chunks' tokens (packed in ``sequence_ids`` order) and
+    ``records`` the uploaded work items of ``plan``.
+    """
+
+    sequence_ids: np.ndarray
+    q_lens: np.ndarray
+    num_q_heads: int
+    total_q: int
+    plan: PrefillPlan | None
+    slots: torch.Tensor | None
+    records: torch.Tensor | None
+
+
 class PagedKVCacheStore:
     """Block-backed KV store (paged_kv.py:178-360) on a device KV pool.
 
@@ -298,6 +316,10 @@ class PagedKVCacheStore:
 
     def has_sequence(self, sequence_id: int) -> bool:
         return self.allocator.has_sequence(sequence_id)
+
+    def token_count(self, sequence_id: int) -> int:
+        """Tokens the sequence holds (KeyError if unknown)."""
+        return self.allocator.view(sequence_id).token_count
 
     def release(self, sequence_id: int) -> None:
         """paged_kv.py:205-213: drop the resident cache, the stored blocks and the table."""
@@ -589,42 +611,19 @@ class PagedKVCacheStore:
                      int(step.info.slots), step.batch)
 
     # -- device chunked-prefill / speculative-verify path (extension) -----------
-    def prefill_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
-                          q_lens=None, layer: int = 0, scale: float | None = None,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
-        """Causal attention of chunks of queries over the paged cache, one layer.
-
-        Sequence i's chunk is its last ``q_lens[i]`` tokens (already reserved /
-        appended in the allocator): ``k``/``v`` ``[total_q, Hkv, D]`` are
-        written into those slots, then each query ``[total_q, Hq, D]`` (packed in
-        ``sequence_ids`` order) attends to its sequence's earlier tokens and the
-        chunk up to itself -- the attention of one HF forward over a prefill
-        chunk with a past cache (agentrl/generation/prefill.py:96-104).
-        ``q_lens`` defaults to an equal split of ``total_q``.
-        """
+    def prefill_step(self, sequence_ids, q_lens, num_q_heads: int) -> PrefillStep:
+        """Lay out one prefill / verify forward: each sequence's chunk is its last ``q_lens[i]``
+        tokens (already reserved / appended in the allocator).  Records the chunks' block fills,
+        plans the attention launch and uploads slots and work items once for all layers."""
         pool = self._require_pool()
         ids = self._step_ids(sequence_ids)
         n = ids.size
-        total_q = q.shape[0] if q.dim() == 3 else -1
-        if q_lens is None:
-            if total_q % n:
-                raise ValueError("q_lens is required when the queries do not split evenly over the sequences")
-            q_lens = np.full(n, total_q // n, dtype=np.int64)
         q_lens = np.asarray(q_lens, dtype=np.int64).reshape(-1)
-        if q_lens.size != n or (q_lens < 0).any() or int(q_lens.sum()) != total_q:
-            raise ValueError("q_lens must give one non-negative chunk length per sequence summing to q.shape[0]")
-        if q.dim() != 3 or q.shape[2] != pool.head_dim or q.shape[1] % pool.num_kv_heads:
-            raise ValueError("q must be [total_q, num_q_heads, head_dim] with num_q_heads a multiple of num_kv_heads")
-        if q.dtype != pool.dtype or q.device != pool.device or not q.is_contiguous():
-            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
-        shape = (total_q, pool.num_kv_heads, pool.head_dim)
-        for t in (k, v):
-            if t.shape != shape or t.dtype != pool.dtype or t.device != pool.device or not t.is_contiguous():
-                raise ValueError("k/v must be contiguous [total_q, num_kv_heads, head_dim] pool-dtype tensors")
-        if out is None:
-            out = torch.empty_like(q)
-        elif out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or not out.is_contiguous():
-            raise ValueError("out must be a contiguous tensor shaped and typed like q")
+        if q_lens.size != n or (q_lens < 0).any():
+            raise ValueError("q_lens must give one non-negative chunk length per sequence")
+        hq = int(num_q_heads)
+        if hq <= 0 or hq % pool.num_kv_heads:
+            raise ValueError("num_q_heads must be a positive multiple of the pool's KV heads")
         bs = self.allocator.block_size_tokens
         # Device tables up to date and copy-on-write copies applied (they carry
         # their source block's fill) before the chunk's fills are recorded.
@@ -644,35 +643,84 @@ class PagedKVCacheStore:
                 blocks = np.asarray(view.physical_blocks, dtype=np.int64)[pos // bs]
                 slot_parts.append(blocks * bs + pos % bs)
                 np.maximum.at(self._block_fill, blocks, (pos % bs + 1).astype(np.int32))
+        total_q = int(q_lens.sum())
+        if total_q == 0:
+            return PrefillStep(ids, q_lens, hq, 0, None, None, None)
+        slots = np.concatenate(slot_parts)
+        plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
+        with _on_device(pool.device):
+            slots_d = torch.from_numpy(slots).to(pool.device, non_blocking=True)
+            records_d = torch.from_numpy(plan.records).to(pool.device, non_blocking=True)
+        return PrefillStep(ids, q_lens, hq, total_q, plan, slots_d, records_d)
+
+    def prefill_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                          q_lens=None, layer: int = 0, scale: float | None = None,
+                          out: torch.Tensor | None = None, step: PrefillStep | None = None) -> torch.Tensor:
+        """Causal attention of chunks of queries over the paged cache, one layer.
+
+        Sequence i's chunk is its last ``q_lens[i]`` tokens (already reserved /
+        appended in the allocator): ``k``/``v`` ``[total_q, Hkv, D]`` are
+        written into those slots, then each query ``[total_q, Hq, D]`` (packed in
+        ``sequence_ids`` order) attends to its sequence's earlier tokens and the
+        chunk up to itself -- the attention of one HF forward over a prefill
+        chunk with a past cache (agentrl/generation/prefill.py:96-104).
+        ``q_lens`` defaults to an equal split of ``total_q``.  ``step`` (from
+        ``prefill_step`` for the same sequences and chunk lengths) skips the
+        per-call layout work, for the layers after the first of a forward.
+        """
+        pool = self._require_pool()
+        total_q = q.shape[0] if q.dim() == 3 else -1
+        if step is None:
+            ids = self._step_ids(sequence_ids)
+            n = ids.size
+            if q_lens is None:
+                if n == 0 or total_q % n:
+                    raise ValueError("q_lens is required when the queries do not split evenly over the sequences")
+                q_lens = np.full(n, total_q // n, dtype=np.int64)
+            q_lens = np.asarray(q_lens, dtype=np.int64).reshape(-1)
+            if q_lens.size != n or (q_lens < 0).any() or int(q_lens.sum()) != total_q:
+                raise ValueError("q_lens must give one non-negative chunk length per sequence summing to q.shape[0]")
+        if q.dim() != 3 or q.shape[2] != pool.head_dim or q.shape[1] % pool.num_kv_heads:
+            raise ValueError("q must be [total_q, num_q_heads, head_dim] with num_q_heads a multiple of num_kv_heads")
+        if q.dtype != pool.dtype or q.device != pool.device or not q.is_contiguous():
+            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
+        shape = (total_q, pool.num_kv_heads, pool.head_dim)
+        for t in (k, v):
+            if t.shape != shape or t.dtype != pool.dtype or t.device != pool.device or not t.is_contiguous():
+                raise ValueError("k/v must be contiguous [total_q, num_kv_heads, head_dim] pool-dtype tensors")
+        if out is None:
+            out = torch.empty_like(q)
+        elif out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or not out.is_contiguous():
+            raise ValueError("out must be a contiguous tensor shaped and typed like q")
+        if step is None:
+            step = self.prefill_step(sequence_ids, q_lens, q.shape[1])
+        elif step.total_q != total_q or step.num_q_heads != q.shape[1]:
+            raise ValueError("the prefill step was laid out for other chunk lengths or query heads")
         if total_q == 0:
             return out
-        slots = np.concatenate(slot_parts)
-        plan = plan_prefill(rows, past, q_lens, q.shape[1], pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
-            dev = pool.device
-            slots_d = torch.from_numpy(slots).to(dev, non_blocking=True)
-            records_d = torch.from_numpy(plan.records).to(dev, non_blocking=True)
-            pool.scatter(layer, k.permute(1, 0, 2).unsqueeze(0), v.permute(1, 0, 2).unsqueeze(0), slots_d)
-            pool.prefill(layer, q, plan, records_d, q.shape[1],
+            pool.scatter(layer, k.permute(1, 0, 2).unsqueeze(0), v.permute(1, 0, 2).unsqueeze(0), step.slots)
+            pool.prefill(layer, q, step.plan, step.records, q.shape[1],
                          float(scale if scale is not None else pool.head_dim ** -0.5), out)
         return out
 
     def verify_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
-                         layer: int = 0, scale: float | None = None) -> torch.Tensor:
+                         layer: int = 0, scale: float | None = None, step: PrefillStep | None = None) -> torch.Tensor:
         """The k+1-query speculative-verify read, one layer: ``q [B, k+1, Hq, D]`` -> same shape.
 
         Each sequence already holds its last accepted token and k draft tokens
         (appended in the allocator); ``k``/``v`` ``[B, k+1, Hkv, D]`` are their
         K/V.  The rows equal rows ``prefix_len-1 .. prefix_len-1+k`` of the
         reference's full causal verify forward (agentrl/generation/speculative.py:229-264).
-        Rejected drafts are dropped afterwards with ``truncate``.
+        Rejected drafts are dropped afterwards with ``truncate``.  ``step``:
+        ``prefill_step(sequence_ids, [k+1] * B, Hq)``, shared by the layers.
         """
         if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
             raise ValueError("verify inputs are q [B, k+1, Hq, D] and k/v [B, k+1, Hkv, D]")
         b, t = q.shape[0], q.shape[1]
         out = self.prefill_attention(sequence_ids, q.reshape(b * t, q.shape[2], q.shape[3]),
                                      k.reshape(b * t, k.shape[2], k.shape[3]), v.reshape(b * t, v.shape[2], v.shape[3]),
-                                     q_lens=np.full(b, t, dtype=np.int64), layer=layer, scale=scale)
+                                     q_lens=np.full(b, t, dtype=np.int64), layer=layer, scale=scale, step=step)
         return out.view(q.shape)
 
     @staticmethod

@@ -1,0 +1,162 @@
+"""Paged speculative decoding on the GPU: device caches, device verify read, device accept / reject.
+
+Random-init bf16 Qwen2 target and draft models (seeded) roll out through
+``PagedSpeculativeGenerator`` on two device KV pools.  The rounds are then
+checked one by one against the reference algorithm (oracle/speculative.py,
+agentrl/generation/speculative.py:188-274) run on HF's own forward (SDPA,
+full prefix, fp32 logits from the final hidden state) over the same prefix
+and the same acceptance draws, teacher-forced: every round starts from the
+prefix our rollout reached, so one near-tie does not cascade.  A round may
+differ only at a near-tie of the reference itself (its draw u within 0.05 of
+the acceptance probability, or a top-2 gap under 0.02 in logits / 2e-3 in
+probability); bf16 attention in two implementations differs by about that
+much, as HF's own eager and SDPA backends do.
+
+A draft identical to the target must have nearly every draft accepted: a
+wrong page, position, truncation or pending token in either cache shows up
+as rejected drafts.
+"""
+
+from __future__ import annotations
+
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import speculative as ospec
+
+pytestmark = pytest.mark.gpu
+
+VOCAB = 512
+U_TABLE = torch.rand((64, 128, 8), generator=torch.Generator().manual_seed(17))
+
+
+def _uniform(seq: int, rnd: int):
+    return U_TABLE[seq, rnd].tolist()
+
+
+def _model(device, seed: int, layers: int, head_dim: int = 64, hq: int = 4, hkv: int = 2):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(seed)
+    cfg = Qwen2Config(vocab_size=VOCAB, hidden_size=hq * head_dim, intermediate_size=2 * hq * head_dim,
+                      num_hidden_layers=layers, num_attention_heads=hq, num_key_value_heads=hkv,
+                      max_position_embeddings=4096, rope_theta=10000.0, attn_implementation="sdpa")
+    return Qwen2ForCausalLM(cfg).to(device=device, dtype=torch.bfloat16).eval()
+
+
+def _hf_logits(model):
+    w = model.get_output_embeddings().weight.detach().float()
+
+    def full(ids):
+        with torch.inference_mode():
+            h = model.model(input_ids=torch.tensor([ids], device=model.device)).last_hidden_state[0]
+            return torch.nn.functional.linear(h.float(), w).cpu()
+    return full
+
+
+def _spec(target, draft, k, *, graphs=False, eos=None):
+    from randomrepo_b200.hf import PagedGenerator, make_store
+    from randomrepo_b200.speculative import PagedSpeculativeGenerator
+
+    t = PagedGenerator(target, make_store(target, total_blocks=2048), prefill_chunk_size=32)
+    d = PagedGenerator(draft, make_store(draft, total_blocks=2048), prefill_chunk_size=32, cuda_graphs=graphs,
+                       sampler=t.sampler)
+    return PagedSpeculativeGenerator(t, d, k=k, eos_token_id=eos)
+
+
+def _prompts(n=8, seed=11):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, VOCAB, (int(m),), generator=g) for m in torch.randint(8, 41, (n,), generator=g)]
+
+
+def _check_rounds(res, prompts, target, draft, k):
+    t_full, d_full = _hf_logits(target), _hf_logits(draft)
+    n_rounds, exact = 0, 0
+    for i, p in enumerate(prompts):
+        prompt = p.tolist()
+        for rnd, (plen, drafts, nd, na, emitted) in enumerate(res["trace"][i]):
+            n_rounds += 1
+            prefix = prompt + res["tokens"][i][:plen - len(prompt)]
+            drafts = drafts[:nd]
+            # Draft proposals: greedy under the draft model, teacher-forced on our drafts.
+            dl = d_full(prefix + drafts[:-1])[plen - 1:]
+            probs = [torch.softmax(dl[j], -1) for j in range(len(drafts))]
+            draft_ok = all(int(torch.argmax(dl[j])) == drafts[j] for j in range(len(drafts)))
+            rows = t_full(prefix + drafts)[plen - 1:]
+            dlps = [float(torch.log(probs[j][drafts[j]] + 1e-12)) for j in range(len(drafts))]
+            ref = ospec.verify_draft(rows, drafts, dlps, probs, _uniform(i, rnd)[:k])
+            got = (na, emitted)
+            want = (ref.n_accepted, [t for t, _ in ref.steps][:len(emitted)])
+            if got == want and draft_ok:
+                exact += 1
+                continue
+            top2 = [float(torch.topk(dl[j], 2).values[0] - torch.topk(dl[j], 2).values[1])
+                    for j in range(len(drafts))]
+            near = (not draft_ok and min(top2, default=1.0) < 0.02) or ref.u_margin < 0.05 or ref.draw_gap < 2e-3
+            assert near, (i, plen, got, want, ref.u_margin, ref.draw_gap, top2)
+    return n_rounds, exact
+
+
+def test_rounds_match_the_reference_algorithm_on_hf(cuda_device):
+    target, draft = _model(cuda_device, 0, 2), _model(cuda_device, 1, 1)
+    prompts = _prompts()
+    sg = _spec(copy.deepcopy(target), copy.deepcopy(draft), 4)
+    res = sg.generate(prompts, max_new_tokens=40, uniforms=_uniform, trace=True)
+    assert all(len(t) == 40 for t in res["tokens"])
+    n_rounds, exact = _check_rounds(res, prompts, target, draft, 4)
+    assert n_rounds >= 8 * 8 and exact >= 0.9 * n_rounds, (exact, n_rounds)
+    assert 0 < res["accepted"] < res["proposed"]
+    for gen in (sg.target, sg.draft):
+        assert gen.store.pool.decode_error_flag() == 0 and gen.store.pool.prefill_error_flag() == 0
+        assert gen.store.allocator.used_block_count == 0
+
+
+def test_draft_equal_to_target_accepts_nearly_everything(cuda_device):
+    target = _model(cuda_device, 0, 2)
+    sg = _spec(copy.deepcopy(target), copy.deepcopy(target), 4)
+    u = lambda s, r: [0.98] * 4  # noqa: E731 - accept unless p_target < 0.98 p_draft
+    res = sg.generate(_prompts(), group_size=2, max_new_tokens=48, uniforms=u)
+    rate = res["accepted"] / res["proposed"]
+    assert rate > 0.9, rate
+    # Every round emitted k + 1 tokens when all drafts were accepted: far fewer rounds than tokens.
+    assert res["rounds"] <= 48 // 5 + 4
+
+
+def test_graphed_draft_matches_eager_draft(cuda_device):
+    target, draft = _model(cuda_device, 0, 2), _model(cuda_device, 1, 1)
+    prompts = _prompts(6, seed=3)
+    a = _spec(copy.deepcopy(target), copy.deepcopy(draft), 3).generate(prompts, max_new_tokens=24,
+                                                                       uniforms=_uniform)
+    sg = _spec(copy.deepcopy(target), copy.deepcopy(draft), 3, graphs=True)
+    b = sg.generate(prompts, max_new_tokens=24, uniforms=_uniform)
+    assert a["tokens"] == b["tokens"]
+    np.testing.assert_allclose(np.concatenate(b["logprobs"]), np.concatenate(a["logprobs"]), atol=1e-4)
+    assert sg.draft._graphs  # the draft's decode steps ran as graphs
+    assert sg.draft.store.allocator.used_block_count == 0
+
+
+def test_groups_eos_and_sampling(cuda_device):
+    from randomrepo_b200.sampling import SamplingConfig
+
+    target, draft = _model(cuda_device, 0, 2), _model(cuda_device, 1, 1)
+    prompts = _prompts(3, seed=5)
+    solo = _spec(copy.deepcopy(target), copy.deepcopy(draft), 4).generate(
+        prompts, max_new_tokens=20, uniforms=lambda s, r: _uniform(s, r))
+    eos = solo["tokens"][0][7]
+    sg = _spec(copy.deepcopy(target), copy.deepcopy(draft), 4, eos=eos)
+    grp = sg.generate(prompts, group_size=4, max_new_tokens=20, uniforms=lambda s, r: _uniform(s // 4, r))
+    for gi in range(3):
+        want = solo["tokens"][gi]
+        if eos in want:
+            want = want[:want.index(eos) + 1]
+        for m in range(4):
+            assert grp["tokens"][4 * gi + m] == want
+    cfg = SamplingConfig(do_sample=True, temperature=0.9, seed=2)
+    s1 = sg.generate(prompts, group_size=2, max_new_tokens=16, sampling=cfg, first_id=100)
+    s2 = sg.generate(prompts, group_size=2, max_new_tokens=16, sampling=cfg, first_id=200)
+    assert s1["tokens"] == s2["tokens"]
+    assert all(0 <= t < VOCAB for seq in s1["tokens"] for t in seq)
+    assert sg.target.store.allocator.used_block_count == 0 and sg.draft.store.allocator.used_block_count == 0

@@ -1,6 +1,6 @@
 """HF integration plumbing on CPU: PagedGenerator over a fake store equals HF's own greedy generate.
 
-The fake store below is test infrastructure: it keeps every sequence's K/V
+The fake store (tests/fakes.py) is test infrastructure: it keeps every sequence's K/V
 per layer in plain fp32 tensors (with copy-on-write forks, releases and the
 decode-step descriptor the real store returns) and attends with the oracle's
 arithmetic (oracle/attention.py).  Running a tiny fp32 Qwen2 through
@@ -8,81 +8,19 @@ arithmetic (oracle/attention.py).  Running a tiny fp32 Qwen2 through
 adds around the kernels: the attention-interface layouts, packed and chunked
 prefill positions, decode positions, group forks and sampling bookkeeping.
 The result must equal HF ``generate`` (SDPA, DynamicCache, greedy) token for
-token.  The same generator runs on the device store in tests/test_gpu_hf.py.
+token.  Token selection goes through the oracle's sampler (the reference's
+torch ops); the device store and the device sampler run the same generator
+in tests/test_gpu_hf.py.
 """
 
 from __future__ import annotations
-
-from dataclasses import dataclass
 
 import numpy as np
 import pytest
 import torch
 
-from oracle.attention import gqa_attention
-
-
-@dataclass
-class _FakeStep:
-    host_lens: np.ndarray
-    ids: list
-
-
-class FakeStore:
-    def __init__(self, layers: int):
-        self.layers = layers
-        self.kv = {}    # sid -> list per layer of [k [T,Hkv,D], v]
-        self.count = {}
-
-    def reserve(self, sid, n):
-        assert sid not in self.count
-        self.count[sid] = n
-        self.kv[sid] = [[None, None] for _ in range(self.layers)]
-
-    def append_tokens(self, sid, n):
-        self.count[sid] += n
-
-    def fork(self, parent, child):
-        self.count[child] = self.count[parent]
-        self.kv[child] = [[k.clone(), v.clone()] for k, v in self.kv[parent]]
-
-    def has_sequence(self, sid):
-        return sid in self.count
-
-    def release(self, sid):
-        del self.count[sid], self.kv[sid]
-
-    def decode_step(self, ids):
-        for s in ids:
-            self.count[s] += 1
-        return _FakeStep(np.array([self.count[s] for s in ids]), list(ids))
-
-    def _append(self, sid, layer, k, v):
-        ent = self.kv[sid][layer]
-        ent[0] = k if ent[0] is None else torch.cat([ent[0], k])
-        ent[1] = v if ent[1] is None else torch.cat([ent[1], v])
-        assert ent[0].shape[0] == self.count[sid]
-
-    def decode_attention(self, step, layer, q, k, v, scale=None):
-        outs = []
-        for i, sid in enumerate(step.ids):
-            self._append(sid, layer, k[i:i + 1], v[i:i + 1])
-            kk, vv = self.kv[sid][layer]
-            o = gqa_attention(q[i:i + 1].numpy(), kk.numpy(), vv.numpy(), scale, past=kk.shape[0] - 1)
-            outs.append(torch.from_numpy(o))
-        return torch.cat(outs).to(q.dtype)
-
-    def prefill_attention(self, ids, q, k, v, q_lens=None, layer=0, scale=None):
-        outs, off = [], 0
-        for sid, n in zip(ids, q_lens):
-            n = int(n)
-            self._append(sid, layer, k[off:off + n], v[off:off + n])
-            kk, vv = self.kv[sid][layer]
-            past = kk.shape[0] - n
-            o = gqa_attention(q[off:off + n].numpy(), kk.numpy(), vv.numpy(), scale, past=past)
-            outs.append(torch.from_numpy(o))
-            off += n
-        return torch.cat(outs).to(q.dtype)
+from oracle.sampling import OracleSampler
+from tests.fakes import FakeStore
 
 
 def _tiny_model():
@@ -110,7 +48,7 @@ def test_paged_generator_equals_hf_greedy_generate_on_cpu():
         out = ref.generate(p.unsqueeze(0), attention_mask=torch.ones(1, p.numel(), dtype=torch.long),
                            max_new_tokens=new, do_sample=False, pad_token_id=0)
         want.append(out[0, p.numel():].tolist())
-    g = PagedGenerator(ours, FakeStore(2), prefill_chunk_size=16)  # prompts of 23 / 40 tokens take 2-3 chunks
+    g = PagedGenerator(ours, FakeStore(2), prefill_chunk_size=16, sampler=OracleSampler())  # prompts of 23 / 40 tokens take 2-3 chunks
     res = g.generate(prompts, group_size=2, max_new_tokens=new)
     assert res["sequence_ids"] == [0, 1, 2, 3, 4, 5]
     for gi in range(3):
@@ -124,7 +62,7 @@ def test_teacher_forcing_and_sampling_bookkeeping():
     from randomrepo_b200.hf import PagedGenerator, SamplingConfig
 
     model = _tiny_model()
-    g = PagedGenerator(model, FakeStore(2), prefill_chunk_size=64, eos_token_id=None)
+    g = PagedGenerator(model, FakeStore(2), prefill_chunk_size=64, eos_token_id=None, sampler=OracleSampler())
     prompts = [torch.arange(5), torch.arange(7)]
     forced = [[3, 4, 5, 6], [7, 8, 9, 10]]
     res = g.generate(prompts, max_new_tokens=4, force_tokens=forced)
@@ -143,9 +81,9 @@ def test_eos_stops_and_releases():
 
     model = _tiny_model()
     store = FakeStore(2)
-    g = PagedGenerator(model, store, eos_token_id=None)
+    g = PagedGenerator(model, store, eos_token_id=None, sampler=OracleSampler())
     first = g.generate([torch.arange(6)], max_new_tokens=3)["tokens"][0]
-    g2 = PagedGenerator(model, store, eos_token_id=first[1])
+    g2 = PagedGenerator(model, store, eos_token_id=first[1], sampler=OracleSampler())
     res = g2.generate([torch.arange(6)], max_new_tokens=8, first_id=10)
     assert res["tokens"][0] == first[:2]  # stops right after emitting eos
     assert not store.count
