@@ -24,10 +24,16 @@ every 512-token chunk in one launch) against the measured bf16 tensor peak, and
 the speculative-verify read (1.5B target shape, 64 sequences, k = 4) against
 the measured HBM bandwidth, each timed alone with CUDA events and L2 flushed.
 
-It also carries ``rollout``: a GRPO rollout of the Qwen2.5-1.5B architecture
-(random-init bf16, 4 prompts x group 8, 128 new tokens) through
+It also carries ``vocab_rows``: the fused log-softmax + gather, sampling and
+speculative accept kernels over Qwen2's 151 936-column logits rows against
+the measured HBM bandwidth; ``rollout``: a GRPO rollout of the Qwen2.5-1.5B
+architecture (random-init bf16, 4 prompts x group 8, 128 new tokens) through
 PagedGenerator with CUDA-graph decode steps, next to stock HF generate on the
-same model and batch.
+same model and batch; ``old_policy``: that rollout's old-policy
+log-probabilities through PagedGenerator.score next to the reference's own
+padded-forward pass; and ``speculative``: a speculative rollout (1.5B target,
+0.5B draft, k = 4, 64 sequences) through PagedSpeculativeGenerator, next to
+the plain paged rollout and HF's stock assisted generation.
 
 Multi-GPU (torchrun): every rank owns its own 256 sequences and KV pool (weak
 scaling, no data-path collective); the timed region is bracketed by NCCL
@@ -359,8 +365,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         del store, q, kn, vn, out, q_d, kn_d, vn_d
         torch.cuda.empty_cache()
         result["tensor_tiles"] = run_tensor_tiles(device, args.seed, args.steps, args.warmup)
+    if world == 1 and not args.no_tiles:
+        result["vocab_rows"] = run_vocab_rows(device, args.seed, args.steps, args.warmup)
     if world == 1 and not args.no_rollout:
-        result["rollout"] = run_rollout(device, args.seed)
+        result["rollout"], result["old_policy"] = run_rollout(device, args.seed)
+        result["speculative"] = run_speculative(device, args.seed)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
     return result
@@ -469,35 +478,53 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
 
 
 ROLLOUT_SHAPE = {"prompts": 4, "group": 8, "len_lo": 64, "len_hi": 256, "new_tokens": 128, "temperature": 1.0}
+SPEC_SHAPE = {"prompts": 8, "group": 8, "len_lo": 64, "len_hi": 256, "new_tokens": 64, "k": 4, "temperature": 1.0}
+QWEN_1P5B = dict(vocab_size=151936, hidden_size=1536, intermediate_size=8960, num_hidden_layers=28,
+                 num_attention_heads=12, num_key_value_heads=2, max_position_embeddings=32768,
+                 rope_theta=1000000.0, tie_word_embeddings=True)
+QWEN_0P5B = dict(vocab_size=151936, hidden_size=896, intermediate_size=4864, num_hidden_layers=24,
+                 num_attention_heads=14, num_key_value_heads=2, max_position_embeddings=32768,
+                 rope_theta=1000000.0, tie_word_embeddings=True)
 
 
-def run_rollout(device: torch.device, seed: int, iters: int = 2) -> dict:
-    """GRPO rollout at the Qwen2.5-1.5B architecture, random-init bf16: PagedGenerator (CUDA-graph
-    decode steps, packed prefill, forked group prompts) against stock HF generate on the same batch."""
+def _qwen(device: torch.device, arch: dict, seed: int):
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
+    torch.manual_seed(seed)
+    with torch.device(device):
+        return Qwen2ForCausalLM(Qwen2Config(**arch, attn_implementation="sdpa")).to(torch.bfloat16).eval()
+
+
+def _set_attention(model, name: str) -> None:
+    model.config._attn_implementation = name
+    for sub in model.modules():
+        cfg = getattr(sub, "config", None)
+        if cfg is not None:
+            cfg._attn_implementation = name
+
+
+def _timed(device: torch.device, fn):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record()
+    n = fn()
+    e1.record()
+    torch.cuda.synchronize(device)
+    return n, e0.elapsed_time(e1) / 1e3
+
+
+def run_rollout(device: torch.device, seed: int, iters: int = 2) -> tuple[dict, dict]:
+    """GRPO rollout at the Qwen2.5-1.5B architecture, random-init bf16: PagedGenerator (CUDA-graph
+    decode steps, packed prefill, forked group prompts) against stock HF generate on the same batch;
+    then the old-policy log-probabilities of that rollout (score) against the reference's own pass."""
     from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
 
     rs = ROLLOUT_SHAPE
-    torch.manual_seed(seed)
-    cfg = Qwen2Config(vocab_size=151936, hidden_size=1536, intermediate_size=8960, num_hidden_layers=28,
-                      num_attention_heads=12, num_key_value_heads=2, max_position_embeddings=32768,
-                      rope_theta=1000000.0, tie_word_embeddings=True, attn_implementation="sdpa")
-    with torch.device(device):
-        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16).eval()
+    model = _qwen(device, QWEN_1P5B, seed)
     rng = np.random.default_rng(seed)
     lens = rng.integers(rs["len_lo"], rs["len_hi"] + 1, size=rs["prompts"])
-    prompts = [torch.from_numpy(rng.integers(0, cfg.vocab_size, size=int(n))) for n in lens]
+    prompts = [torch.from_numpy(rng.integers(0, QWEN_1P5B["vocab_size"], size=int(n))) for n in lens]
     group, new = rs["group"], rs["new_tokens"]
-
-    def timed(fn):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(device)
-        e0.record()
-        n = fn()
-        e1.record()
-        torch.cuda.synchronize(device)
-        return n, e0.elapsed_time(e1) / 1e3
 
     ids = torch.zeros((len(prompts) * group, int(lens.max())), dtype=torch.long)
     mask = torch.zeros_like(ids)
@@ -514,35 +541,279 @@ def run_rollout(device: torch.device, seed: int, iters: int = 2) -> dict:
 
     # Stock HF first: PagedGenerator switches the model's attention implementation.
     hf()
-    hf_runs = [timed(hf) for _ in range(iters)]
+    hf_runs = [_timed(device, hf) for _ in range(iters)]
     store = make_store(model, total_blocks=4096)
     gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
+    last = {}
 
     def ours(it):
         r = gen.generate(prompts, group_size=group, max_new_tokens=new, first_id=it * 10000,
                          sampling=SamplingConfig(do_sample=True, temperature=rs["temperature"], seed=it))
+        last["r"] = r
         return sum(len(t) for t in r["tokens"])
 
     ours(0)  # records the decode-step graph
-    ours_runs = [timed(lambda it=it: ours(it)) for it in range(1, iters + 1)]
+    ours_runs = [_timed(device, lambda it=it: ours(it)) for it in range(1, iters + 1)]
     if store.pool.decode_error_flag() or store.pool.prefill_error_flag():
         raise RuntimeError("rollout kernels reported a device error")
     ours_tps = sum(n for n, _ in ours_runs) / sum(t for _, t in ours_runs)
     hf_tps = sum(n for n, _ in hf_runs) / sum(t for _, t in hf_runs)
-    del gen, store, model
-    torch.cuda.empty_cache()
-    return {
+    rollout = {
         "workload": f"GRPO rollout, Qwen2.5-1.5B architecture (28 layers, 12q/2kv heads, head_dim 128, vocab "
                     f"151936), random-init bf16, {rs['prompts']} prompts x group {group}, prompts "
                     f"U[{rs['len_lo']},{rs['len_hi']}] random ids, {new} new tokens, temperature "
                     f"{rs['temperature']}, seed {seed}",
         "tokens_per_s": ours_tps,
         "path": "PagedGenerator: packed prefill kernel, one prefill per group + copy-on-write forks, CUDA-graph "
-                "decode steps (fused append + paged decode per layer), fp32 logits",
+                "decode steps (fused append + paged decode per layer), fp32 logits, device sampling kernel",
         "hf_generate_tokens_per_s": hf_tps,
         "hf_generate_path": "stock HF generate on the same model and batch (SDPA + DynamicCache, left-padded)",
         "speedup_vs_hf_generate": ours_tps / hf_tps,
         "timing": f"CUDA events around whole rollouts, mean of {iters} after one warm-up each",
+    }
+    old = run_old_policy(device, model, gen, prompts, last["r"], group, iters)
+    del gen, store, model
+    torch.cuda.empty_cache()
+    return rollout, old
+
+
+def run_old_policy(device: torch.device, model, gen, prompts, roll: dict, group: int, iters: int) -> dict:
+    """Old-policy log-probabilities of a finished rollout (agentrl/core/rollout.py:456-472).
+
+    Reference: its own pass -- one HF forward over the right-padded [B, L]
+    batch, log_softmax over [B, L-1, vocab], gather, completion mask.  Ours:
+    PagedGenerator.score (group prompt prefilled once + forks, packed prefill,
+    logits only for scored rows, fused log-softmax + gather kernel)."""
+    rows = [torch.cat([prompts[i // group], torch.tensor(t, dtype=torch.long)]) for i, t in enumerate(roll["tokens"])]
+    width = max(r.numel() for r in rows)
+    ids = torch.zeros(len(rows), width, dtype=torch.long)
+    am = torch.zeros_like(ids)
+    cm = torch.zeros(len(rows), width, dtype=torch.bool)
+    for i, r in enumerate(rows):
+        ids[i, :r.numel()] = r
+        am[i, :r.numel()] = 1
+        cm[i, prompts[i // group].numel():r.numel()] = True
+    ids_d, am_d, cm_d = ids.to(device), am.to(device), cm.to(device)
+    scored = int(cm[:, 1:].sum())
+
+    def reference():
+        with torch.inference_mode():
+            logits = model(input_ids=ids_d, attention_mask=am_d).logits
+            token_logprobs = torch.log_softmax(logits[:, :-1, :], dim=-1)
+            gathered = token_logprobs.gather(dim=-1, index=ids_d[:, 1:].unsqueeze(-1)).squeeze(-1)
+            aligned = torch.zeros_like(ids_d, dtype=logits.dtype)
+            aligned[:, 1:] = gathered * cm_d[:, 1:].to(dtype=logits.dtype)
+        return aligned
+
+    def ours():
+        return gen.score(ids, am, cm, group_size=group)
+
+    _set_attention(model, "sdpa")
+    torch.cuda.reset_peak_memory_stats(device)
+    base_mem = torch.cuda.memory_allocated(device)
+    want = reference()
+    ref_runs = [_timed(device, reference) for _ in range(iters)]
+    ref_peak = torch.cuda.max_memory_allocated(device) - base_mem
+    _set_attention(model, "paged_b200")
+    torch.cuda.reset_peak_memory_stats(device)
+    got = ours()
+    our_runs = [_timed(device, ours) for _ in range(iters)]
+    our_peak = torch.cuda.max_memory_allocated(device) - base_mem
+    diff = (got.float() - want.float())[cm_d].abs()
+    ref_s = statistics.mean(t for _, t in ref_runs)
+    our_s = statistics.mean(t for _, t in our_runs)
+    return {
+        "workload": f"old-policy log-probabilities of that rollout: {len(rows)} sequences (prompt + completion, "
+                    f"up to {width} tokens), {scored} scored completion tokens, vocab 151936",
+        "scored_tokens_per_s": scored / our_s,
+        "ms": our_s * 1e3,
+        "path": "PagedGenerator.score: group prompt prefilled once + copy-on-write forks, packed prefill "
+                "kernel, LM head only on scored rows (<= 2048 at a time, fp32), fused log-softmax + gather kernel",
+        "reference_scored_tokens_per_s": scored / ref_s,
+        "reference_ms": ref_s * 1e3,
+        "reference_path": "agentrl/core/rollout.py:456-472 as written: HF forward (SDPA) over the right-padded "
+                          "batch, log_softmax over [B, L-1, vocab], gather, mask",
+        "speedup_vs_reference": ref_s / our_s,
+        "peak_extra_bytes": {"ours": int(our_peak), "reference": int(ref_peak)},
+        "max_abs_logprob_diff": float(diff.max()),
+        "mean_abs_logprob_diff": float(diff.mean()),
+        "timing": f"CUDA events around whole passes, mean of {iters} after one warm-up each",
+    }
+
+
+def run_speculative(device: torch.device, seed: int, iters: int = 2) -> dict:
+    """Speculative GRPO rollout at the speculative configuration: target Qwen2.5-1.5B architecture,
+    draft Qwen2.5-0.5B architecture, k = 4, 64 sequences; random-init bf16 weights."""
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
+    from randomrepo_b200.speculative import PagedSpeculativeGenerator
+
+    ss = SPEC_SHAPE
+    target = _qwen(device, QWEN_1P5B, seed)
+    draft = _qwen(device, QWEN_0P5B, seed + 1)
+    rng = np.random.default_rng(seed + 7)
+    lens = rng.integers(ss["len_lo"], ss["len_hi"] + 1, size=ss["prompts"])
+    prompts = [torch.from_numpy(rng.integers(0, QWEN_1P5B["vocab_size"], size=int(n))) for n in lens]
+    group, new, k = ss["group"], ss["new_tokens"], ss["k"]
+    cfg = SamplingConfig(do_sample=True, temperature=ss["temperature"], seed=0)
+
+    # Stock HF assisted generation (speculative sampling, batch 1 only) on the same models.
+    hf_note = None
+    hf_tps = None
+    try:
+        def hf():
+            with torch.inference_mode():
+                n = 0
+                for p in prompts[:2]:
+                    x = p.unsqueeze(0).to(device)
+                    out = target.generate(x, attention_mask=torch.ones_like(x), assistant_model=draft,
+                                          max_new_tokens=new, do_sample=True, temperature=ss["temperature"],
+                                          top_p=1.0, top_k=0, pad_token_id=0)
+                    n += out.shape[1] - x.shape[1]
+            return n
+        hf()
+        hf_runs = [_timed(device, hf) for _ in range(iters)]
+        hf_tps = sum(n for n, _ in hf_runs) / sum(t for _, t in hf_runs)
+    except Exception as e:  # noqa: BLE001 - recorded in the line
+        hf_note = f"HF assisted generation unavailable: {type(e).__name__}: {str(e)[:160]}"
+
+    t_store = make_store(target, total_blocks=16384)
+    d_store = make_store(draft, total_blocks=16384)
+    tgen = PagedGenerator(target, t_store, prefill_chunk_size=512)
+    dgen = PagedGenerator(draft, d_store, prefill_chunk_size=512, cuda_graphs=True, sampler=tgen.sampler)
+    spec = PagedSpeculativeGenerator(tgen, dgen, k=k)
+    stats = {}
+
+    def ours(it):
+        r = spec.generate(prompts, group_size=group, max_new_tokens=new, first_id=it * 10000,
+                          sampling=SamplingConfig(do_sample=True, temperature=ss["temperature"], seed=it))
+        stats.update(rounds=r["rounds"], proposed=r["proposed"], accepted=r["accepted"])
+        return sum(len(t) for t in r["tokens"])
+
+    ours(0)
+    runs = [_timed(device, lambda it=it: ours(it)) for it in range(1, iters + 1)]
+    spec_tps = sum(n for n, _ in runs) / sum(t for _, t in runs)
+    for st in (t_store, d_store):
+        if st.pool.decode_error_flag() or st.pool.prefill_error_flag():
+            raise RuntimeError("speculative kernels reported a device error")
+    # The same target without a draft, for context.
+    pstore = make_store(target, total_blocks=16384)
+    plain = PagedGenerator(target, pstore, prefill_chunk_size=512, cuda_graphs=True)
+
+    def plain_run(it):
+        r = plain.generate(prompts, group_size=group, max_new_tokens=new, first_id=it * 10000, sampling=cfg)
+        return sum(len(t) for t in r["tokens"])
+
+    plain_run(0)
+    pruns = [_timed(device, lambda it=it: plain_run(it)) for it in range(1, iters + 1)]
+    plain_tps = sum(n for n, _ in pruns) / sum(t for _, t in pruns)
+    rate = stats["accepted"] / max(stats["proposed"], 1)
+    del spec, tgen, dgen, plain, t_store, d_store, pstore, target, draft
+    torch.cuda.empty_cache()
+    out = {
+        "workload": f"speculative GRPO rollout: target Qwen2.5-1.5B architecture, draft Qwen2.5-0.5B architecture "
+                    f"(24 layers, 14q/2kv heads, head_dim 64), random-init bf16, k={k}, {ss['prompts']} prompts x "
+                    f"group {group} = {ss['prompts'] * group} sequences, prompts U[{ss['len_lo']},{ss['len_hi']}], "
+                    f"{new} new tokens, temperature {ss['temperature']}",
+        "tokens_per_s": spec_tps,
+        "path": "PagedSpeculativeGenerator: paged caches for both models (group prompts prefilled once + forks), "
+                "CUDA-graph draft decode steps, paged verify read (prefill kernel, k+1 queries per sequence), "
+                "device accept / reject (pkv_spec_accept), truncate of rejected drafts",
+        "acceptance_rate": rate,
+        "rounds": stats["rounds"],
+        "acceptance_note": "random-init draft and target are unrelated models, so few drafts are accepted; the "
+                           "round cost is the measured machinery, the acceptance rate is the weights'",
+        "plain_paged_tokens_per_s": plain_tps,
+        "plain_paged_path": "PagedGenerator on the same target and batch, CUDA-graph decode steps",
+        "timing": f"CUDA events around whole rollouts, mean of {iters} after one warm-up each",
+    }
+    if hf_tps is not None:
+        out["hf_assisted_tokens_per_s"] = hf_tps
+        out["hf_assisted_path"] = "stock HF generate(assistant_model=draft), batch 1 (its only mode), 2 prompts"
+        out["speedup_vs_hf_assisted"] = spec_tps / hf_tps
+    else:
+        out["hf_assisted"] = hf_note
+    return out
+
+
+def run_vocab_rows(device: torch.device, seed: int, steps: int, warmup: int) -> dict:
+    """The vocabulary-row kernels at Qwen2's vocabulary against the measured HBM bandwidth."""
+    from randomrepo_b200.sampling import DeviceSampler
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    vocab, rows = 151936, 4096
+    logits = torch.randn(rows, vocab, device=device, generator=g) * 2.0  # 2.49 GB > L2
+    tokens = torch.randint(0, vocab, (rows,), device=device, generator=g)
+    s = DeviceSampler(device, seed=seed)
+    peak, peak_kind = measured_peaks()
+
+    def time_it(fn, n):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            ts.append(e0.elapsed_time(e1))
+        return statistics.mean(ts)
+
+    n = max(3, min(steps, 20))
+    lp_ms = time_it(lambda: s.token_logprobs(logits, tokens), n)
+    torch_ms = time_it(lambda: torch.log_softmax(logits, -1).gather(-1, tokens.unsqueeze(-1)), n)
+    lp_bytes = rows * vocab * 4 + rows * 12
+    sm_ms = time_it(lambda: s.sample(logits[:512], temperature=1.0), n)
+    sm_bytes = 512 * vocab * 4 + 512 * 20
+    # Speculative accept at the speculative configuration: 64 sequences, k = 4.
+    b, k = 64, 4
+    tl = torch.randn(b, k + 1, vocab, device=device, generator=g) * 2.0
+    dl = tl[:, :k] + 0.7 * torch.randn(b, k, vocab, device=device, generator=g)
+    dtok = torch.argmax(dl, dim=-1)
+    nd = torch.full((b,), k, dtype=torch.int32, device=device)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+
+    ts = []
+    for i in range(warmup + n):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _, _, n_out, n_acc = s.spec_accept(tl, dl, dtok, nd, do_sample=True)
+        e1.record()
+        torch.cuda.synchronize(device)
+        if i >= warmup:
+            ts.append(e0.elapsed_time(e1))
+    acc_ms = statistics.mean(ts)
+    rejects = int((n_acc < nd).sum())
+    acc_bytes = (b * (k + 1) + b * k) * vocab * 4 + (rejects * 2 + (b - rejects)) * vocab * 4
+    del logits, tl, dl, flush
+    torch.cuda.empty_cache()
+
+    def line(ms, nbytes):
+        ach = nbytes / (ms * 1e-3) / 1e9
+        return {"ms": ms, "bytes_per_launch": nbytes, "achieved": ach, "peak": peak, "unit": "GB/s",
+                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs"}
+
+    return {
+        "token_logprobs": {
+            "workload": f"fused log-softmax + gather, {rows} rows x vocab {vocab} fp32 (2.49 GB, > L2)",
+            "roofline": line(lp_ms, lp_bytes),
+            "torch_log_softmax_gather_ms": torch_ms,
+            "speedup_vs_torch": torch_ms / lp_ms,
+        },
+        "sample_tokens": {
+            "workload": f"Gumbel-max draw at temperature 1 + temperature-1 log-prob + argmax, 512 rows x {vocab}",
+            "roofline": line(sm_ms, sm_bytes),
+        },
+        "spec_accept": {
+            "workload": f"speculative accept / reject, {b} sequences, k={k}, vocab {vocab}, sampled corrections "
+                        f"({rejects} rejections); L2 flushed before each launch",
+            "roofline": line(acc_ms, acc_bytes),
+            "bytes_rule": "target rows (k+1) + draft rows k per sequence once, then the drawn row (+ its draft "
+                          "row on a rejection) again",
+        },
+        "timing": f"CUDA events per launch, mean of {n} after {warmup} warm-up launches",
+        "gpu_launches_per_call": {"token_logprobs": 1, "sample_tokens": 1, "spec_accept": 3},
     }
 
 

@@ -11,11 +11,14 @@
 //    (agentrl/generation/speculative.py:217-274), for a whole batch at once.
 //
 // All of it streams rows of `vocab` fp32 logits (151 936 for Qwen2: 594 KB a
-// row) from HBM once.  A row is cut into chunks of kChunk columns, one CTA
-// each (grid = rows x chunks, so a handful of rows already covers the 148
-// SMs).  Each CTA reduces its chunk in registers and writes one partial
-// record; the CTA that takes the row's last ticket (an atomic after a release
-// fence -- nothing ever waits) merges the row's partials, writes the row's
+// row) from HBM once.  Each CTA streams a span of one row with kUnroll
+// float4 loads in flight per thread (coalesced, evict-first), folding them
+// into per-thread state, then reduces the state across the CTA.  The host
+// cuts rows into as many spans as it takes to put about four CTAs on every
+// SM (none for a batch of thousands of rows, a few for a handful).  A row of
+// one span is finished by its CTA; otherwise each CTA writes one partial
+// record and the CTA that takes the row's last ticket (an atomic after a
+// release fence -- nothing ever waits) merges the partials, writes the row's
 // results and re-arms the ticket for the next launch, so the tickets stay
 // zero between launches (and across CUDA-graph replays).
 //
@@ -30,6 +33,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <string>
 
 #include "pkv_b200.h"
@@ -40,8 +44,11 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarpsPerCta = kThreads / 32;
-constexpr int kChunk = 8192;               // columns of one row per CTA
-constexpr int kPer = kChunk / kThreads;    // 32 per thread
+constexpr int kUnroll = 4;                   // float4 loads in flight per thread
+constexpr int kGroup = 4 * kUnroll;          // columns a thread folds in per iteration
+constexpr int kSpanQuantum = 4 * kThreads;   // spans are multiples of this many columns
+constexpr int kMinSpan = 4096;               // columns below which a row is not split further
+constexpr int kCtasPerSm = 4;                // split target: resident CTAs per SM (<= 64 registers)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kMaxDrafts = 16;
@@ -68,9 +75,12 @@ __device__ __forceinline__ float uniform_open(uint64_t h) {
 // u in [0, 1) (the range torch.rand draws from).
 __device__ __forceinline__ float uniform_co(uint64_t h) { return (float)(uint32_t)(h >> 40) * 0x1p-24f; }
 
+// g = -log(-log u).  The inner log is the accurate one: u near 1 gives the
+// small -log u that wins races, so it needs relative accuracy there; the
+// outer log only shifts keys by its absolute error (~1e-7).
 __device__ __forceinline__ float gumbel(uint64_t key, int v) {
   const float u = uniform_open(mix64(key + (uint64_t)(uint32_t)v * 0xd1b54a32d192ed03ull));
-  return -logf(-logf(u));
+  return -__logf(-logf(u));
 }
 
 // ---------------------------------------------------------------------------
@@ -116,39 +126,48 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-// Column of register q of this thread in the chunk starting at v0.  With
-// float4 loads a thread holds 4 adjacent columns per load; either way the
-// columns of one thread rise with q, so strict comparisons keep the first
-// index of a tie inside the thread.
+// Load iteration `i0` of a thread's stream over columns [.., v_end) of a
+// row: kGroup columns, x[q] at column col[q] (rising with q), -inf past v_end.
+// VEC: kUnroll float4 loads (v_end a multiple of 4); else kGroup scalar loads.
 template <bool VEC>
-__device__ __forceinline__ int col_of(int v0, int q) {
-  if (VEC) return v0 + 4 * ((q >> 2) * kThreads + (int)threadIdx.x) + (q & 3);
-  return v0 + q * kThreads + (int)threadIdx.x;
-}
-
-// Load this thread's kPer columns of a row chunk; columns >= vocab read -inf.
-template <bool VEC>
-__device__ __forceinline__ void load_chunk(const float* __restrict__ row, int v0, int vocab, float (&x)[kPer]) {
+__device__ __forceinline__ void load_group(const float* __restrict__ row, int i0, int v_end, float (&x)[kGroup],
+                                           int (&col)[kGroup]) {
   if (VEC) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int f_end = v_end >> 2;
 #pragma unroll
-    for (int j = 0; j < kPer / 4; ++j) {
-      const int c = col_of<true>(v0, 4 * j);
-      float4 t = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (c < vocab) t = __ldcs(r4 + (c >> 2));
-      x[4 * j + 0] = t.x;
-      x[4 * j + 1] = c + 1 < vocab ? t.y : -INFINITY;
-      x[4 * j + 2] = c + 2 < vocab ? t.z : -INFINITY;
-      x[4 * j + 3] = c + 3 < vocab ? t.w : -INFINITY;
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = i0 + u * kThreads;
+      const float4 t = j < f_end ? __ldcs(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      x[4 * u + 0] = t.x;
+      x[4 * u + 1] = t.y;
+      x[4 * u + 2] = t.z;
+      x[4 * u + 3] = t.w;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) col[4 * u + e] = 4 * j + e;
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      const int c = col_of<false>(v0, q);
-      x[q] = c < vocab ? __ldcs(row + c) : -INFINITY;
+    for (int q = 0; q < kGroup; ++q) {
+      const int j = i0 + q * kThreads;
+      x[q] = j < v_end ? __ldcs(row + j) : -INFINITY;
+      col[q] = j;
     }
   }
 }
+
+// A thread's first load index and the stride between its iterations over a
+// span [v_begin, v_end) (in float4s for VEC, in floats otherwise).
+template <bool VEC>
+__device__ __forceinline__ int first_index(int v_begin) {
+  return (VEC ? (v_begin >> 2) : v_begin) + (int)threadIdx.x;
+}
+template <bool VEC>
+__device__ __forceinline__ int end_index(int v_end) {
+  return VEC ? (v_end >> 2) : v_end;
+}
+constexpr int kIterStride = kThreads * kUnroll;    // float4s per iteration of the CTA (VEC)
+constexpr int kIterStrideScalar = kThreads * kGroup;
 
 // Release this CTA's partial and take a ticket; true in the row's last CTA
 // (which then sees every partial of the row).
@@ -180,7 +199,8 @@ struct RowArgs {
   const float* x;          // row r at x + r * ld
   const float* race_x;     // race logits (same layout), or null for x
   int64_t ld;
-  int32_t rows, vocab, nchunks;
+  int32_t rows, vocab;
+  int32_t splits, span;    // CTAs per row and columns per CTA (a multiple of kSpanQuantum)
   float lse_scale;         // statistics of x * lse_scale (> 0)
   float race_scale;        // race key = race_x * race_scale + gumbel
   int32_t race;            // 0: token = argmax; 1: token = race winner
@@ -189,7 +209,7 @@ struct RowArgs {
   // r % rpg < tpg, else none.
   const int64_t* tokens;
   int32_t rpg, tpg;
-  RowPart* parts;          // [rows][nchunks]
+  RowPart* parts;          // [rows][splits] (splits > 1)
   int32_t* tickets;        // [rows], zero between launches
   float* lse_out;          // [rows] natural-log log-sum-exp of x * lse_scale
   float* lp_out;           // [rows] x[token] * lse_scale - lse (NaN for a token outside the vocabulary)
@@ -198,79 +218,94 @@ struct RowArgs {
   int64_t* amax_out;       // [rows] argmax of x
 };
 
-template <bool VEC>
-__global__ void __launch_bounds__(kThreads) row_stats_kernel(const RowArgs a) {
-  const int r = blockIdx.x / a.nchunks, c = blockIdx.x - r * a.nchunks;
-  const int v0 = c * kChunk;
-  const float* row = a.x + (int64_t)r * a.ld;
-  float x[kPer];
-  load_chunk<VEC>(row, v0, a.vocab, x);
-
-  float amax = -INFINITY;
-  int aidx = -1;
-#pragma unroll
-  for (int q = 0; q < kPer; ++q)
-    if (x[q] > amax) {
-      amax = x[q];
-      aidx = col_of<VEC>(v0, q);
-    }
-  const float k2 = a.lse_scale * kLog2e;
-  float m = amax == -INFINITY ? -INFINITY : amax * k2;
-  float s = 0.f;
-  if (amax != -INFINITY) {
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) s += exp2f(fmaf(x[q], k2, -m));
-  }
-  float rkey = -INFINITY;
-  int ridx = -1;
-  if (a.race) {
-    const uint64_t key = row_key(a.seed, a.offset, 0, (uint64_t)r);
-    if (a.race_x) load_chunk<VEC>(a.race_x + (int64_t)r * a.ld, v0, a.vocab, x);
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      if (x[q] == -INFINITY) continue;
-      const int v = col_of<VEC>(v0, q);
-      const float kk = fmaf(x[q], a.race_scale, gumbel(key, v));
-      if (kk > rkey) {
-        rkey = kk;
-        ridx = v;
-      }
-    }
-  }
-
-  warp_lse(m, s);
-  warp_arg(amax, aidx);
-  warp_arg(rkey, ridx);
+// Merge of the per-thread states of a CTA into thread 0's (smem + warp shuffles).
+__device__ __forceinline__ RowPart cta_reduce(RowPart t) {
+  warp_lse(t.m, t.s);
+  warp_arg(t.amax, t.aidx);
+  warp_arg(t.rkey, t.ridx);
   __shared__ RowPart sp[kWarpsPerCta];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) sp[warp] = RowPart{m, s, amax, aidx, rkey, ridx, {0, 0}};
+  if (lane == 0) sp[warp] = t;
   __syncthreads();
   if (threadIdx.x == 0) {
-    RowPart t = sp[0];
     for (int w = 1; w < kWarpsPerCta; ++w) {
       lse_merge(t.m, t.s, sp[w].m, sp[w].s);
       arg_merge(t.amax, t.aidx, sp[w].amax, sp[w].aidx);
       arg_merge(t.rkey, t.ridx, sp[w].rkey, sp[w].ridx);
     }
-    a.parts[(int64_t)r * a.nchunks + c] = t;
   }
-  if (!last_of_row(a.tickets + r, a.nchunks)) return;
+  return t;
+}
 
-  // The row's last CTA: merge the partials (warp 0), write the results.
-  if (warp != 0) return;
+// RACE: 0 none, 1 race over x, 2 race over race_x.
+template <bool VEC, int RACE>
+__global__ void __launch_bounds__(kThreads) row_stats_kernel(const RowArgs a) {
+  const int r = blockIdx.x / a.splits, c = blockIdx.x - r * a.splits;
+  const int v_begin = c * a.span, v_end = min(a.vocab, v_begin + a.span);
+  const float* row = a.x + (int64_t)r * a.ld;
+  const float* rrow = RACE == 2 ? a.race_x + (int64_t)r * a.ld : row;
+  const float k2 = a.lse_scale * kLog2e;
+  const uint64_t key = RACE ? row_key(a.seed, a.offset, 0, (uint64_t)r) : 0;
   RowPart t{-INFINITY, 0.f, -INFINITY, -1, -INFINITY, -1, {0, 0}};
-  for (int i = lane; i < a.nchunks; i += 32) {
-    const RowPart* p = a.parts + (int64_t)r * a.nchunks + i;
-    const float pm = __ldcg(&p->m), ps = __ldcg(&p->s), pa = __ldcg(&p->amax), pk = __ldcg(&p->rkey);
-    const int pai = __ldcg(&p->aidx), pri = __ldcg(&p->ridx);
-    lse_merge(t.m, t.s, pm, ps);
-    arg_merge(t.amax, t.aidx, pa, pai);
-    arg_merge(t.rkey, t.ridx, pk, pri);
+  const int i_end = end_index<VEC>(v_end);
+  for (int i = first_index<VEC>(v_begin); i < i_end; i += VEC ? kIterStride : kIterStrideScalar) {
+    float x[kGroup];
+    int col[kGroup];
+    load_group<VEC>(row, i, v_end, x, col);
+    float rx[kGroup];
+    if (RACE == 2) load_group<VEC>(rrow, i, v_end, rx, col);
+    float gm = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kGroup; ++q) gm = fmaxf(gm, x[q]);
+    if (gm == -INFINITY) continue;
+    // Rescale the running sum once per group, then one 2^y per column.
+    const float gy = gm * k2;
+    if (gy > t.m) {
+      t.s *= exp2f(t.m - gy);
+      t.m = gy;
+    }
+#pragma unroll
+    for (int q = 0; q < kGroup; ++q) {
+      t.s += exp2f(fmaf(x[q], k2, -t.m));
+      if (x[q] > t.amax) {
+        t.amax = x[q];
+        t.aidx = col[q];
+      }
+    }
+    if (RACE) {
+#pragma unroll
+      for (int q = 0; q < kGroup; ++q) {
+        const float v = RACE == 2 ? rx[q] : x[q];
+        if (v == -INFINITY) continue;
+        const float kk = fmaf(v, a.race_scale, gumbel(key, col[q]));
+        if (kk > t.rkey) {
+          t.rkey = kk;
+          t.ridx = col[q];
+        }
+      }
+    }
   }
-  warp_lse(t.m, t.s);
-  warp_arg(t.amax, t.aidx);
-  warp_arg(t.rkey, t.ridx);
-  if (lane != 0) return;
+  t = cta_reduce(t);
+  const int lane = threadIdx.x & 31;
+  if (a.splits > 1) {
+    if (threadIdx.x == 0) a.parts[(int64_t)r * a.splits + c] = t;
+    if (!last_of_row(a.tickets + r, a.splits)) return;
+    // The row's last CTA: merge the partials (warp 0), write the results.
+    if (threadIdx.x >= 32) return;
+    RowPart u{-INFINITY, 0.f, -INFINITY, -1, -INFINITY, -1, {0, 0}};
+    for (int i = lane; i < a.splits; i += 32) {
+      const RowPart* p = a.parts + (int64_t)r * a.splits + i;
+      lse_merge(u.m, u.s, __ldcg(&p->m), __ldcg(&p->s));
+      arg_merge(u.amax, u.aidx, __ldcg(&p->amax), __ldcg(&p->aidx));
+      arg_merge(u.rkey, u.ridx, __ldcg(&p->rkey), __ldcg(&p->ridx));
+    }
+    warp_lse(u.m, u.s);
+    warp_arg(u.amax, u.aidx);
+    warp_arg(u.rkey, u.ridx);
+    t = u;
+    if (lane == 0) a.tickets[r] = 0;
+  }
+  if (threadIdx.x != 0) return;
   const float lse = (t.m + log2f(t.s)) * kLn2;
   if (a.lse_out) a.lse_out[r] = lse;
   if (a.lp_out && a.tokens) {
@@ -280,11 +315,10 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(const RowArgs a) {
       a.lp_out[r] = (tok >= 0 && tok < a.vocab) ? row[tok] * a.lse_scale - lse : NAN;
     }
   }
-  const int tok = (a.race && t.ridx >= 0) ? t.ridx : t.aidx;
+  const int tok = (RACE && t.ridx >= 0) ? t.ridx : t.aidx;
   if (a.tok_out) a.tok_out[r] = tok;
   if (a.tok_lp_out) a.tok_lp_out[r] = tok >= 0 ? row[tok] * a.lse_scale - lse : NAN;
   if (a.amax_out) a.amax_out[r] = t.aidx;
-  a.tickets[r] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -303,7 +337,8 @@ struct AccArgs {
   const float* xt;         // target logits [batch][k + 1][ld]
   const float* xd;         // draft logits [batch][k][ld]
   int64_t ld;
-  int32_t batch, k, vocab, nchunks;
+  int32_t batch, k, vocab;
+  int32_t splits, span;    // CTAs per sequence and columns per CTA
   const int64_t* dtok;     // [batch][k]
   const int32_t* n_draft;  // [batch]
   const float* uniforms;   // [batch][k], or null: hashed from (seed, offset)
@@ -315,7 +350,7 @@ struct AccArgs {
   const float* lp_t;       // [batch][k + 1]: target log-prob of draft i at row i
   const float* lp_d;       // [batch][k]: draft log-prob (at its temperature) of draft i
   const float* lse_d;      // [batch][k]
-  AccPart* parts;          // [batch][nchunks]
+  AccPart* parts;          // [batch][splits] (splits > 1)
   int32_t* tickets;        // [batch]
   int64_t* tok_out;        // [batch][k + 1]
   float* lp_out;           // [batch][k + 1]
@@ -366,7 +401,7 @@ __device__ Decision decide(const AccArgs& a, int b) {
 
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads) spec_accept_kernel(const AccArgs a) {
-  const int b = blockIdx.x / a.nchunks, c = blockIdx.x - b * a.nchunks;
+  const int b = blockIdx.x / a.splits, c = blockIdx.x - b * a.splits;
   __shared__ Decision sd;
   if (threadIdx.x == 0) sd = decide(a, b);
   __syncthreads();
@@ -391,83 +426,81 @@ __global__ void __launch_bounds__(kThreads) spec_accept_kernel(const AccArgs a) 
     return;
   }
 
-  const int v0 = c * kChunk;
+  const int v_begin = c * a.span, v_end = min(a.vocab, v_begin + a.span);
   const int64_t trow = (int64_t)b * K1 + d.m;
+  const int64_t drow = (int64_t)b * a.k + d.m;  // read only on a rejection (d.m < n_draft <= k)
   const float* xt = a.xt + trow * a.ld;
-  float x[kPer];
-  load_chunk<VEC>(xt, v0, a.vocab, x);
+  const float* xd = a.xd + drow * a.ld;
   const bool sample = a.do_sample != 0;
   const uint64_t key = row_key(a.seed, a.offset, 2, (uint64_t)b);
-  float sum_w = 0.f, key_w = -INFINITY, key_p = -INFINITY;
-  int idx_w = -1, idx_p = -1;
-  if (d.reject) {
-    const int64_t drow = (int64_t)b * a.k + d.m;
-    float y[kPer];
-    load_chunk<VEC>(a.xd + drow * a.ld, v0, a.vocab, y);
-    const float lt2 = a.lse_t[trow] * kLog2e;
-    const float ld2 = a.lse_d[drow] * kLog2e;
-    const float kd = a.inv_t_draft * kLog2e;
+  const float lt2 = a.lse_t[trow] * kLog2e;
+  const float ld2 = d.reject ? a.lse_d[drow] * kLog2e : 0.f;
+  const float kd = a.inv_t_draft * kLog2e;
+  AccPart t{0.f, -INFINITY, -1, -INFINITY, -1, {0, 0, 0}};
+  const int i_end = end_index<VEC>(v_end);
+  for (int i = first_index<VEC>(v_begin); i < i_end; i += VEC ? kIterStride : kIterStrideScalar) {
+    float x[kGroup], y[kGroup];
+    int col[kGroup];
+    load_group<VEC>(xt, i, v_end, x, col);
+    if (d.reject) load_group<VEC>(xd, i, v_end, y, col);
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
+    for (int q = 0; q < kGroup; ++q) {
       if (x[q] == -INFINITY) continue;
-      const int v = col_of<VEC>(v0, q);
-      // correction_probs = clamp(p_target - p_draft, 0) (speculative.py:251)
-      const float w = fmaxf(exp2f(fmaf(x[q], kLog2e, -lt2)) - exp2f(fmaf(y[q], kd, -ld2)), 0.f);
-      sum_w += w;
-      float g = 0.f;
-      if (sample) g = gumbel(key, v);
-      const float kw = sample ? (w > 0.f ? logf(w) + g : -INFINITY) : w;
-      if (kw > key_w) {
-        key_w = kw;
-        idx_w = v;
+      const float g = sample ? gumbel(key, col[q]) : 0.f;
+      if (d.reject) {
+        // correction_probs = clamp(p_target - p_draft, 0) (speculative.py:251)
+        const float w = fmaxf(exp2f(fmaf(x[q], kLog2e, -lt2)) - exp2f(fmaf(y[q], kd, -ld2)), 0.f);
+        t.sum_w += w;
+        const float kw = sample ? (w > 0.f ? __logf(w) + g : -INFINITY) : w;
+        if (kw > t.key_w) {
+          t.key_w = kw;
+          t.idx_w = col[q];
+        }
       }
-      const float kp = sample ? x[q] + g : x[q];
-      if (kp > key_p) {
-        key_p = kp;
-        idx_p = v;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      if (x[q] == -INFINITY) continue;
-      const int v = col_of<VEC>(v0, q);
-      const float kp = sample ? x[q] + gumbel(key, v) : x[q];
-      if (kp > key_p) {
-        key_p = kp;
-        idx_p = v;
+      const float kp = x[q] + g;
+      if (kp > t.key_p) {
+        t.key_p = kp;
+        t.idx_p = col[q];
       }
     }
   }
-  sum_w = warp_sum(sum_w);
-  warp_arg(key_w, idx_w);
-  warp_arg(key_p, idx_p);
+  t.sum_w = warp_sum(t.sum_w);
+  warp_arg(t.key_w, t.idx_w);
+  warp_arg(t.key_p, t.idx_p);
   __shared__ AccPart sp[kWarpsPerCta];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) sp[warp] = AccPart{sum_w, key_w, idx_w, key_p, idx_p, {0, 0, 0}};
+  if (lane == 0) sp[warp] = t;
   __syncthreads();
   if (threadIdx.x == 0) {
-    AccPart t = sp[0];
     for (int w = 1; w < kWarpsPerCta; ++w) {
       t.sum_w += sp[w].sum_w;
       arg_merge(t.key_w, t.idx_w, sp[w].key_w, sp[w].idx_w);
       arg_merge(t.key_p, t.idx_p, sp[w].key_p, sp[w].idx_p);
     }
-    a.parts[(int64_t)b * a.nchunks + c] = t;
   }
-  if (!last_of_row(a.tickets + b, a.nchunks)) return;
-  if (warp != 0) return;
-
-  AccPart t{0.f, -INFINITY, -1, -INFINITY, -1, {0, 0, 0}};
-  for (int i = lane; i < a.nchunks; i += 32) {
-    const AccPart* p = a.parts + (int64_t)b * a.nchunks + i;
-    t.sum_w += __ldcg(&p->sum_w);
-    arg_merge(t.key_w, t.idx_w, __ldcg(&p->key_w), __ldcg(&p->idx_w));
-    arg_merge(t.key_p, t.idx_p, __ldcg(&p->key_p), __ldcg(&p->idx_p));
+  if (a.splits > 1) {
+    if (threadIdx.x == 0) a.parts[(int64_t)b * a.splits + c] = t;
+    if (!last_of_row(a.tickets + b, a.splits)) return;
+    if (warp != 0) return;
+    AccPart u{0.f, -INFINITY, -1, -INFINITY, -1, {0, 0, 0}};
+    for (int i = lane; i < a.splits; i += 32) {
+      const AccPart* p = a.parts + (int64_t)b * a.splits + i;
+      u.sum_w += __ldcg(&p->sum_w);
+      arg_merge(u.key_w, u.idx_w, __ldcg(&p->key_w), __ldcg(&p->idx_w));
+      arg_merge(u.key_p, u.idx_p, __ldcg(&p->key_p), __ldcg(&p->idx_p));
+    }
+    u.sum_w = warp_sum(u.sum_w);
+    warp_arg(u.key_w, u.idx_w);
+    warp_arg(u.key_p, u.idx_p);
+    t = u;
+    if (lane == 0) a.tickets[b] = 0;
+  } else if (warp != 0) {
+    return;
   }
-  t.sum_w = warp_sum(t.sum_w);
-  warp_arg(t.key_w, t.idx_w);
-  warp_arg(t.key_p, t.idx_p);
+  // Warp 0 of the finishing CTA; lane 0 holds the merged record (broadcast).
+  t.sum_w = __shfl_sync(0xffffffffu, t.sum_w, 0);
+  t.idx_w = __shfl_sync(0xffffffffu, t.idx_w, 0);
+  t.idx_p = __shfl_sync(0xffffffffu, t.idx_p, 0);
   // An all-zero correction falls back to the target distribution itself
   // (speculative.py:252-253).
   const int tok = (d.reject && t.sum_w > 0.f && t.idx_w >= 0) ? t.idx_w : t.idx_p;
@@ -487,7 +520,6 @@ __global__ void __launch_bounds__(kThreads) spec_accept_kernel(const AccArgs a) 
   if (lane == 0) {
     a.n_out[b] = d.m + 1;
     a.n_acc[b] = d.m;
-    a.tickets[b] = 0;
   }
 }
 
@@ -496,11 +528,30 @@ __global__ void __launch_bounds__(kThreads) spec_accept_kernel(const AccArgs a) 
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-int32_t nchunks_of(int32_t vocab) { return (vocab + kChunk - 1) / kChunk; }
+int num_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
 
-// Row workspace: RowPart x rows x nchunks (scratch: written before it is read).
+// Most CTAs one row is ever cut into.
+int32_t max_splits(int32_t vocab) { return (vocab + kMinSpan - 1) / kMinSpan; }
+
+// Cut each of `rows` rows into spans so that the launch has about
+// kCtasPerSm CTAs per SM, never spans under kMinSpan columns.
+void plan_split(int64_t rows, int32_t vocab, int32_t* splits, int32_t* span) {
+  const int64_t target = (int64_t)num_sms() * kCtasPerSm;
+  int64_t sp = rows > 0 ? (target + rows - 1) / rows : 1;
+  sp = std::max<int64_t>(1, std::min<int64_t>(sp, max_splits(vocab)));
+  const int64_t per = (vocab + sp - 1) / sp;
+  *span = (int32_t)((per + kSpanQuantum - 1) / kSpanQuantum * kSpanQuantum);
+  *splits = (int32_t)((vocab + *span - 1) / *span);
+}
+
+// Row workspace: RowPart x rows x splits (scratch: written before it is read).
 int64_t row_ws_bytes(int64_t rows, int32_t vocab) {
-  return align256(rows * nchunks_of(vocab) * (int64_t)sizeof(RowPart));
+  return align256(rows * max_splits(vocab) * (int64_t)sizeof(RowPart));
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -514,20 +565,31 @@ int32_t check_rows(const float* x, int64_t ld, int64_t rows, int32_t vocab, cons
     pkv_set_error(std::string(who) + ": logits must be non-null with rows >= 0, vocab >= 1 and ld >= vocab");
     return PKV_ERR_ARG;
   }
-  if (rows * (int64_t)nchunks_of(vocab) > INT32_MAX) {
+  if (rows * (int64_t)max_splits(vocab) > INT32_MAX) {
     pkv_set_error(std::string(who) + ": too many rows for one launch");
     return PKV_ERR_ARG;
   }
   return PKV_OK;
 }
 
+template <bool VEC>
+void launch_rows_t(const RowArgs& a, unsigned grid, cudaStream_t s) {
+  if (!a.race)
+    row_stats_kernel<VEC, 0><<<grid, kThreads, 0, s>>>(a);
+  else if (!a.race_x)
+    row_stats_kernel<VEC, 1><<<grid, kThreads, 0, s>>>(a);
+  else
+    row_stats_kernel<VEC, 2><<<grid, kThreads, 0, s>>>(a);
+}
+
 int32_t launch_rows(RowArgs a, bool vec, cudaStream_t s, const char* who) {
   if (a.rows == 0) return PKV_OK;
-  const unsigned grid = (unsigned)((int64_t)a.rows * a.nchunks);
+  plan_split(a.rows, a.vocab, &a.splits, &a.span);
+  const unsigned grid = (unsigned)((int64_t)a.rows * a.splits);
   if (vec)
-    row_stats_kernel<true><<<grid, kThreads, 0, s>>>(a);
+    launch_rows_t<true>(a, grid, s);
   else
-    row_stats_kernel<false><<<grid, kThreads, 0, s>>>(a);
+    launch_rows_t<false>(a, grid, s);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     pkv_set_error(std::string(who) + ": " + cudaGetErrorString(e));
@@ -537,7 +599,7 @@ int32_t launch_rows(RowArgs a, bool vec, cudaStream_t s, const char* who) {
 }
 
 // Speculative workspace (scratch): [lse_t, lp_t: batch (k+1)][lse_d, lp_d:
-// batch k][RowPart: batch (2k+1) x nchunks][AccPart: batch x nchunks].
+// batch k][RowPart: batch (2k+1) x splits][AccPart: batch x splits].
 // Tickets: batch (2k+1) row tickets, then batch accept tickets.
 struct SpecWs {
   int64_t lse_t, lp_t, lse_d, lp_d, row_parts, acc_parts, total;
@@ -545,7 +607,7 @@ struct SpecWs {
 
 SpecWs spec_ws(int64_t batch, int32_t k, int32_t vocab) {
   SpecWs w;
-  const int64_t nt = batch * (k + 1), nd = batch * k, nc = nchunks_of(vocab);
+  const int64_t nt = batch * (k + 1), nd = batch * k, nc = max_splits(vocab);
   w.lse_t = 0;
   w.lp_t = w.lse_t + align256(nt * 4);
   w.lse_d = w.lp_t + align256(nt * 4);
@@ -584,7 +646,6 @@ extern "C" int32_t pkv_token_logprobs(const float* logits, int64_t ld, int32_t n
   a.ld = ld;
   a.rows = n_rows;
   a.vocab = vocab;
-  a.nchunks = nchunks_of(vocab);
   a.lse_scale = 1.f;
   a.race_scale = 1.f;
   a.tokens = tokens;
@@ -622,7 +683,6 @@ extern "C" int32_t pkv_sample_tokens(const float* logits, const float* race_logi
   a.ld = ld;
   a.rows = n_rows;
   a.vocab = vocab;
-  a.nchunks = nchunks_of(vocab);
   a.lse_scale = 1.f;
   a.race = do_sample ? 1 : 0;
   a.race_scale = do_sample ? 1.f / temperature : 1.f;
@@ -677,7 +737,7 @@ extern "C" int32_t pkv_spec_accept(const float* target_logits, const float* draf
   if (batch == 0) return PKV_OK;
   char* base = static_cast<char*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int32_t nc = nchunks_of(vocab);
+  const int32_t nc = max_splits(vocab);
   const bool vec = vec_ok(ld, vocab, target_logits) && aligned16(draft_logits);
   RowPart* parts = reinterpret_cast<RowPart*>(base + w.row_parts);
   const int64_t nt = (int64_t)batch * (k + 1), nd = (int64_t)batch * k;
@@ -690,7 +750,6 @@ extern "C" int32_t pkv_spec_accept(const float* target_logits, const float* draf
   t.ld = ld;
   t.rows = (int32_t)nt;
   t.vocab = vocab;
-  t.nchunks = nc;
   t.lse_scale = 1.f;
   t.race_scale = 1.f;
   t.tokens = draft_tokens;
@@ -721,7 +780,7 @@ extern "C" int32_t pkv_spec_accept(const float* target_logits, const float* draf
   a.batch = batch;
   a.k = k;
   a.vocab = vocab;
-  a.nchunks = nc;
+  plan_split(batch, vocab, &a.splits, &a.span);
   a.dtok = draft_tokens;
   a.n_draft = n_draft;
   a.uniforms = uniforms;
@@ -740,7 +799,7 @@ extern "C" int32_t pkv_spec_accept(const float* target_logits, const float* draf
   a.lp_out = logprobs_out;
   a.n_out = n_out;
   a.n_acc = n_accepted;
-  const unsigned grid = (unsigned)((int64_t)batch * nc);
+  const unsigned grid = (unsigned)((int64_t)batch * a.splits);
   if (vec)
     spec_accept_kernel<true><<<grid, kThreads, 0, s>>>(a);
   else

@@ -300,6 +300,106 @@ class PagedGenerator:
         bs = self.store.allocator.block_size_tokens
         pool.grow(int(stats.row_capacity) + 1, -(-int(max_tokens) // bs) + 1)
 
+    # -- old-policy log-probabilities ---------------------------------------------
+    _score_ids = 1 << 62   # sequence ids of the scoring pass's temporary sequences
+
+    def score(self, input_ids, attention_mask=None, completion_mask=None, *, group_size: int = 1,
+              max_logit_rows: int = 2048) -> torch.Tensor:
+        """Per-token log-probabilities of packed sequences (rollout.py:456-472).
+
+        ``input_ids`` / ``attention_mask`` / ``completion_mask`` are [B, L]
+        (right padding: each mask row is ones then zeros).  Returns float32
+        [B, L] on the model's device: ``out[b, p] = log_softmax(logits[b, p-1])[input_ids[b, p]]``
+        where ``completion_mask[b, p]`` is set (p >= 1), else 0 -- the
+        reference's aligned ``old_policy_logprobs``.
+
+        The reference runs one full forward over the padded [B, L] batch and a
+        log_softmax over [B, L-1, vocab].  Here each group of ``group_size``
+        consecutive rows prefills its common prefix once (the members fork
+        its pages), the rest of every row goes through packed chunked
+        prefill, and logits exist only for rows that are scored, at most
+        ``max_logit_rows`` at a time, reduced to one number each by the fused
+        log-softmax + gather kernel.
+        """
+        ids = torch.as_tensor(input_ids).to("cpu", torch.int64)
+        if ids.dim() != 2:
+            raise ValueError("input_ids must be [B, L]")
+        b_rows, width = ids.shape
+        am = (torch.ones_like(ids) if attention_mask is None else torch.as_tensor(attention_mask).to("cpu")).bool()
+        cm = (torch.ones_like(ids) if completion_mask is None else torch.as_tensor(completion_mask).to("cpu")).bool()
+        if am.shape != ids.shape or cm.shape != ids.shape:
+            raise ValueError("masks must match input_ids")
+        if group_size < 1 or b_rows % group_size:
+            raise ValueError("the batch must hold whole groups")
+        lens = am.sum(dim=1)
+        if not torch.equal(am, torch.arange(width).unsqueeze(0) < lens.unsqueeze(1)):
+            raise ValueError("attention_mask must be right padding (ones, then zeros)")
+        out = torch.zeros((b_rows, width), dtype=torch.float32, device=self.device)
+        rows = [ids[b, :int(lens[b])].tolist() for b in range(b_rows)]
+        # Positions p - 1 whose logits are needed (p scored).
+        need = [[p - 1 for p in range(1, int(lens[b])) if cm[b, p]] for b in range(b_rows)]
+        base = PagedGenerator._score_ids
+        PagedGenerator._score_ids += b_rows
+        seq = [base + b for b in range(b_rows)]
+        try:
+            heads = list(range(0, b_rows, group_size))
+            shared = {}
+            for g0 in heads:
+                members = range(g0, g0 + group_size)
+                n = min(len(rows[b]) for b in members)
+                for b in members:
+                    n = next((i for i in range(n) if rows[b][i] != rows[g0][i]), n)
+                    if need[b]:
+                        n = min(n, need[b][0])
+                shared[g0] = n
+                self.store.reserve(seq[g0], 0)
+            # Every group's common prefix once, all groups packed per round.
+            cs = self.prefill_chunk_size
+            for c in range(0, max(shared.values()), cs):
+                members = [g0 for g0 in heads if shared[g0] > c]
+                self.extend_hidden([seq[g0] for g0 in members],
+                                   [rows[g0][c:min(c + cs, shared[g0])] for g0 in members])
+            for g0 in heads:
+                for b in range(g0 + 1, g0 + group_size):
+                    self.store.fork(seq[g0], seq[b])
+            # Every row's remainder, packed, in rounds of at most prefill_chunk_size tokens per row.
+            self._score_rest(seq, rows, need, out, ids, max_logit_rows)
+        finally:
+            for sid in seq:
+                if self.store.has_sequence(sid):
+                    self.store.release(sid)
+        return out
+
+    def _score_rest(self, seq, rows, need, out, ids, max_logit_rows: int) -> None:
+        cs = self.prefill_chunk_size
+        pos = [self._token_count(s) for s in seq]
+        need_sets = [set(n) for n in need]
+        while True:
+            members = [b for b in range(len(seq)) if pos[b] < len(rows[b])]
+            if not members:
+                return
+            chunks = [rows[b][pos[b]:pos[b] + cs] for b in members]
+            h, q_lens = self.extend_hidden([seq[b] for b in members], chunks)
+            # Rows of h whose logits are needed, with their (row, target position).
+            pick, where = [], []
+            off = 0
+            for b, n in zip(members, q_lens.tolist()):
+                for j in range(n):
+                    p = pos[b] + j
+                    if p in need_sets[b]:
+                        pick.append(off + j)
+                        where.append((b, p + 1))
+                off += n
+                pos[b] += n
+            for s0 in range(0, len(pick), max_logit_rows):
+                sel = torch.tensor(pick[s0:s0 + max_logit_rows], device=h.device)
+                tgt = [where[i] for i in range(s0, min(s0 + max_logit_rows, len(pick)))]
+                bi = torch.tensor([t[0] for t in tgt])
+                pi = torch.tensor([t[1] for t in tgt])
+                nxt = ids[bi, pi].to(h.device)
+                lp = self.sampler.token_logprobs(self.logits(h.index_select(0, sel)), nxt)
+                out[bi.to(out.device), pi.to(out.device)] = lp.to(out.device)
+
     # -- rollout ----------------------------------------------------------------
     def generate(self, prompts, *, group_size: int = 1, max_new_tokens: int = 16,
                  sampling: SamplingConfig | None = None, force_tokens=None, first_id: int = 0,

@@ -158,3 +158,48 @@ def test_cuda_graph_decode_matches_eager(cuda_device):
     assert set(graphs._graphs) == {6}
     pool = graphs.store.pool
     assert pool.decode_error_flag() == 0 and graphs.store.allocator.used_block_count == 0
+
+
+def test_score_matches_the_reference_old_policy_pass(cuda_device):
+    """PagedGenerator.score vs agentrl/core/rollout.py:456-472 run on HF (SDPA, padded batch, fp32 head).
+
+    The rows are a sampled GRPO rollout of 3 prompts x 4 members, so the
+    groups share their prompt pages; bf16 attention in the two
+    implementations bounds the agreement (same scale as the greedy near-ties).
+    The rollout's own recorded log-probabilities are the same quantity and
+    must agree as well.
+    """
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
+
+    model = _model(cuda_device, 64, 2)
+    store = make_store(model, total_blocks=1024)
+    g = PagedGenerator(copy.deepcopy(model), store, prefill_chunk_size=16)
+    gen = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, 512, (int(n),), generator=gen) for n in (9, 21, 34)]
+    roll = g.generate(prompts, group_size=4, max_new_tokens=24,
+                      sampling=SamplingConfig(do_sample=True, temperature=1.0, seed=3))
+    rows = [torch.cat([prompts[i // 4], torch.tensor(t)]) for i, t in enumerate(roll["tokens"])]
+    width = max(r.numel() for r in rows)
+    ids = torch.zeros(len(rows), width, dtype=torch.long)
+    am = torch.zeros_like(ids)
+    cm = torch.zeros(len(rows), width, dtype=torch.bool)
+    for i, r in enumerate(rows):
+        ids[i, :r.numel()] = r
+        am[i, :r.numel()] = 1
+        cm[i, prompts[i // 4].numel():r.numel()] = True
+    got = g.score(ids, am, cm, group_size=4, max_logit_rows=37).cpu()
+    w = model.get_output_embeddings().weight.detach().float()
+    with torch.inference_mode():
+        h = model.model(input_ids=ids.to(cuda_device), attention_mask=am.to(cuda_device)).last_hidden_state
+        logits = torch.nn.functional.linear(h.float(), w)
+    want = torch.zeros_like(got)
+    want[:, 1:] = (torch.log_softmax(logits[:, :-1], -1).gather(-1, ids[:, 1:].to(cuda_device).unsqueeze(-1))
+                   .squeeze(-1).cpu() * cm[:, 1:])
+    diff = (got - want)[cm].abs()
+    assert float(diff.max()) < 0.1 and float(diff.mean()) < 0.02, (float(diff.max()), float(diff.mean()))
+    assert (got[~cm] == 0).all()
+    rolled = torch.tensor([lp for seq in roll["logprobs"] for lp in seq])
+    scored = torch.cat([got[i, prompts[i // 4].numel():rows[i].numel()] for i in range(len(rows))])
+    d2 = (rolled - scored).abs()
+    assert float(d2.max()) < 0.1 and float(d2.mean()) < 0.02, (float(d2.max()), float(d2.mean()))
+    assert store.allocator.used_block_count == 0

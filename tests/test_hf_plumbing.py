@@ -15,6 +15,8 @@ in tests/test_gpu_hf.py.
 
 from __future__ import annotations
 
+import copy
+
 import numpy as np
 import pytest
 import torch
@@ -111,3 +113,48 @@ def test_kv_geometry_follows_the_reference_rule():
                                        hidden_size=64, head_dim=None)) == (2, 4, 16)
     assert kv_geometry(SimpleNamespace(num_hidden_layers=24, num_key_value_heads=2, num_attention_heads=14,
                                        hidden_size=896, head_dim=64)) == (24, 2, 64)
+
+
+def _reference_compute_logprobs(model, input_ids, attention_mask, completion_mask):
+    """agentrl/core/rollout.py:456-472 on an HF model (full padded forward, log_softmax, gather, mask)."""
+    with torch.no_grad():
+        logits = model(input_ids=input_ids, attention_mask=attention_mask).logits.float()
+    token_logprobs = torch.log_softmax(logits[:, :-1, :], dim=-1)
+    gathered = token_logprobs.gather(dim=-1, index=input_ids[:, 1:].unsqueeze(-1)).squeeze(-1)
+    aligned = torch.zeros_like(input_ids, dtype=logits.dtype)
+    aligned[:, 1:] = gathered * completion_mask[:, 1:].to(dtype=logits.dtype)
+    return aligned
+
+
+@pytest.mark.parametrize("group_size", [1, 2])
+def test_score_equals_reference_compute_logprobs(group_size):
+    from randomrepo_b200.hf import PagedGenerator
+
+    model = _tiny_model()
+    gen = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 128, (n,), generator=gen) for n in (6, 13)]
+    rows, comp = [], []
+    for gi, p in enumerate(prompts):
+        for m in range(group_size):
+            c = torch.randint(0, 128, (5 + 7 * m + 3 * gi,), generator=gen)
+            rows.append(torch.cat([p, c]))
+            mask = torch.cat([torch.zeros(p.numel(), dtype=torch.bool), torch.ones(c.numel(), dtype=torch.bool)])
+            mask[p.numel() + 2] = False  # a masked hole inside the completion
+            comp.append(mask)
+    width = max(r.numel() for r in rows)
+    ids = torch.zeros(len(rows), width, dtype=torch.long)
+    am = torch.zeros_like(ids)
+    cm = torch.zeros(len(rows), width, dtype=torch.bool)
+    for i, (r, c) in enumerate(zip(rows, comp)):
+        ids[i, :r.numel()] = r
+        am[i, :r.numel()] = 1
+        cm[i, :r.numel()] = c
+    want = _reference_compute_logprobs(model, ids, am, cm)
+    store = FakeStore(2)
+    g = PagedGenerator(copy.deepcopy(model), store, prefill_chunk_size=8, sampler=OracleSampler())
+    got = g.score(ids, am, cm, group_size=group_size, max_logit_rows=5)
+    torch.testing.assert_close(got, want, atol=1e-4, rtol=1e-4)
+    assert (got[~cm] == 0).all()
+    assert not store.count  # temporary sequences released
+    with pytest.raises(ValueError):
+        g.score(ids, 1 - am, cm)
