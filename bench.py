@@ -678,7 +678,7 @@ def run_speculative(device: torch.device, seed: int, iters: int = 2) -> dict:
 
     t_store = make_store(target, total_blocks=16384)
     d_store = make_store(draft, total_blocks=16384)
-    tgen = PagedGenerator(target, t_store, prefill_chunk_size=512)
+    tgen = PagedGenerator(target, t_store, prefill_chunk_size=512, cuda_graphs=True)
     dgen = PagedGenerator(draft, d_store, prefill_chunk_size=512, cuda_graphs=True, sampler=tgen.sampler)
     spec = PagedSpeculativeGenerator(tgen, dgen, k=k)
     stats = {}
@@ -716,8 +716,9 @@ def run_speculative(device: torch.device, seed: int, iters: int = 2) -> dict:
                     f"{new} new tokens, temperature {ss['temperature']}",
         "tokens_per_s": spec_tps,
         "path": "PagedSpeculativeGenerator: paged caches for both models (group prompts prefilled once + forks), "
-                "CUDA-graph draft decode steps, paged verify read (prefill kernel, k+1 queries per sequence), "
-                "device accept / reject (pkv_spec_accept), truncate of rejected drafts",
+                "CUDA-graph draft decode steps, CUDA-graph target verify forward through the paged verify read "
+                "(prefill kernel, k+1 queries per sequence), device accept / reject (pkv_spec_accept), truncate "
+                "of rejected drafts",
         "acceptance_rate": rate,
         "rounds": stats["rounds"],
         "acceptance_note": "random-init draft and target are unrelated models, so few drafts are accepted; the "

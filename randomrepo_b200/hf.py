@@ -24,7 +24,10 @@ attention launches and the LM head) is recorded once per batch size in a CUDA
 graph and replayed: the store runs in fixed-step mode (each step's descriptor
 goes to one device block whose header the kernels read), so a step costs the
 allocator step, one small upload and one graph launch on the host instead of
-a Python forward through every layer.
+a Python forward through every layer.  Graphs exist for a fixed ladder of
+batch sizes (``GRAPH_BATCHES``); a step of fewer sequences is padded with
+placeholder sequences (each holding at most one block, rolled back when it
+fills), so a batch that shrinks as sequences finish reuses its graphs.
 
 Only ``last_hidden_state`` rows that need logits go through the LM head, so a
 long packed prefill never materialises [tokens, vocab] logits.  By default
@@ -138,6 +141,17 @@ def make_store(model, total_blocks: int, block_size: int = 16, device=None):
 
 _top_p = top_p_filter
 
+# Batch sizes decode-step graphs are recorded for (multiples of 64 above).
+GRAPH_BATCHES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
+
+
+def graph_batch(n: int) -> int:
+    """The recorded batch size a decode step of ``n`` sequences is padded to."""
+    for b in GRAPH_BATCHES:
+        if n <= b:
+            return b
+    return -(-n // 64) * 64
+
 
 class PagedGenerator:
     """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches).
@@ -159,6 +173,10 @@ class PagedGenerator:
         self.cuda_graphs = bool(cuda_graphs)
         self._graphs: dict[int, tuple] = {}  # batch -> (graph, static tokens, static positions, static logits)
         self._graph_tables = 0
+        self._pads: list[int] = []           # placeholder sequences that pad graphed steps
+        self._pad_len: dict[int, int] = {}
+        # (padded batch, chunk length) -> (graph, static ids, static positions, static logits, upload buffers)
+        self._ext_graphs: dict[tuple[int, int], tuple] = {}
         self.fp32_logits = bool(fp32_logits)
         self._sampler = sampler
 
@@ -218,6 +236,75 @@ class PagedGenerator:
         ends = torch.from_numpy(np.cumsum(q_lens) - 1).to(h.device)
         return self.logits(h.index_select(0, ends))
 
+    def verify_logits(self, sequence_ids, chunks) -> torch.Tensor:
+        """Logits of every token of equal-length chunks appended to existing sequences,
+        [n * L, vocab] (the speculative verify forward).  With ``cuda_graphs`` the forward is
+        replayed from a CUDA graph recorded per (padded batch, L): the step's slots and work
+        items go to fixed device buffers, placeholders pad the batch to a recorded size."""
+        lens = {len(c) for c in chunks}
+        if not self.cuda_graphs or len(lens) != 1:
+            return self.extend(sequence_ids, chunks, all_logits=True)
+        return self._extend_graph([int(s) for s in sequence_ids], chunks, lens.pop())
+
+    def _extend_graph(self, ids, chunks, L: int) -> torch.Tensor:
+        store = self.store
+        n = len(ids)
+        nb = graph_batch(n)
+        pads = self._placeholders(nb - n) if nb > n else []
+        # _placeholders counted one decode token per placeholder: these take L instead.
+        for p in pads:
+            self._pad_len[p] -= 1
+        past = [self._token_count(s) for s in ids] + [self._pad_len[p] for p in pads]
+        all_ids = ids + pads
+        for sid in all_ids:
+            store.append_tokens(sid, L)
+        toks = torch.tensor([t for c in chunks for t in c] + [0] * (L * len(pads)), dtype=torch.long)
+        pos = torch.tensor([p0 + j for p0 in past for j in range(L)], dtype=torch.long)
+        q_lens = np.full(nb, L, dtype=np.int64)
+        hq = int(self.model.config.num_attention_heads)
+        pool = store.pool
+        key = (nb, L)
+        entry = self._ext_graphs.get(key)
+        try:
+            bufs = entry[4] if entry is not None else None
+            step = store.prefill_step(all_ids, q_lens, hq, buffers=bufs)
+            if pool.tables.data_ptr() != self._graph_tables:
+                # The step grew (moved) the device tables: every graph holds the old address.
+                self._graphs.clear()
+                self._ext_graphs.clear()
+                self._graph_tables = pool.tables.data_ptr()
+                entry = None
+            if entry is None:
+                if bufs is None:
+                    bufs = {"slots": step.slots.clone(), "records": step.records.clone(),
+                            "n_items": step.plan.n_items}
+                    step = store.prefill_step(all_ids, q_lens, hq, buffers=bufs)
+                tok_s = toks.to(self.device).unsqueeze(0)
+                pos_s = pos.to(self.device).unsqueeze(0)
+                ph = _Phase("prefill", store, step=step, sequence_ids=all_ids, q_lens=q_lens)
+                cur = torch.cuda.current_stream(self.device)
+                side = torch.cuda.Stream(device=self.device)
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    out = self.logits(self._forward(tok_s, pos_s, ph)[0])
+                cur.wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    logits_s = self.logits(self._forward(tok_s, pos_s, ph)[0])
+                self._ext_graphs[key] = (graph, tok_s, pos_s, logits_s, bufs)
+            else:
+                graph, tok_s, pos_s, logits_s, _ = entry
+                tok_s.copy_(toks.unsqueeze(0), non_blocking=True)
+                pos_s.copy_(pos.unsqueeze(0), non_blocking=True)
+                graph.replay()
+                out = logits_s.clone()
+        finally:
+            if pads:
+                store.truncate(pads, [0] * len(pads))
+                for p in pads:
+                    self._pad_len[p] = 0
+        return out[:n * L]
+
     def prefill(self, sequence_ids, prompts) -> torch.Tensor:
         """Reserve each prompt, write its K/V, return next-token logits [n, vocab] (float32).
 
@@ -255,27 +342,61 @@ class PagedGenerator:
                           _Phase("decode", self.store, step=step))
         return self.logits(h[:, -1])
 
+    _pad_ids = 1 << 61   # sequence ids of placeholder sequences
+
+    def _placeholders(self, count: int) -> list[int]:
+        """``count`` placeholder sequences for padding a graphed step, each with room for one token."""
+        while len(self._pads) < count:
+            sid = PagedGenerator._pad_ids
+            PagedGenerator._pad_ids += 1
+            self.store.reserve(sid, 0)
+            self._pads.append(sid)
+            self._pad_len[sid] = 0
+        pads = self._pads[:count]
+        bs = self.store.allocator.block_size_tokens
+        full = [p for p in pads if self._pad_len[p] >= bs]
+        if full:
+            self.store.truncate(full, [0] * len(full))
+            for p in full:
+                self._pad_len[p] = 0
+        for p in pads:
+            self._pad_len[p] += 1
+        return pads
+
+    def release_placeholders(self) -> None:
+        """Return the placeholder sequences' rows and blocks to the store."""
+        for sid in self._pads:
+            if self.store.has_sequence(sid):
+                self.store.release(sid)
+        self._pads, self._pad_len = [], {}
+
     def _decode_step_graph(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
         pool = self.store.pool
         n = len(sequence_ids)
-        if pool.fixed_batch < n:
-            pool.fix_steps(max(n, 2 * pool.fixed_batch))
+        nb = graph_batch(n)
+        pads = self._placeholders(nb - n) if nb > n else []
+        if pool.fixed_batch < nb:
+            pool.fix_steps(max(nb, 2 * pool.fixed_batch))
             self._graphs.clear()
-        step = self.store.decode_step(sequence_ids)
+        step = self.store.decode_step(list(sequence_ids) + pads)
         if pool.tables.data_ptr() != self._graph_tables:
             # Graphs hold the tables' address: a grown (moved) table voids them.
             self._graphs.clear()
+            self._ext_graphs.clear()
             self._graph_tables = pool.tables.data_ptr()
         pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
-        tok = tokens.reshape(-1, 1).to(self.device)
-        entry = self._graphs.get(n)
+        tok = tokens.reshape(-1).to(self.device)
+        if pads:
+            tok = torch.cat([tok, tok.new_zeros(len(pads))])
+        tok = tok.reshape(-1, 1)
+        entry = self._graphs.get(nb)
         if entry is None:
-            return self._capture(n, step, tok, pos.reshape(-1, 1))
+            return self._capture(nb, step, tok, pos.reshape(-1, 1))[:n]
         graph, tok_s, pos_s, logits_s = entry
         tok_s.copy_(tok)
         pos_s.copy_(pos.reshape(-1, 1))
         graph.replay()
-        return logits_s.clone()
+        return logits_s[:n].clone()
 
     def _capture(self, n: int, step, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """Run this step eagerly (on a side stream, as capture requires a warm-up), then record it."""
@@ -467,4 +588,5 @@ class PagedGenerator:
             for sid in seq_ids:
                 if self.store.has_sequence(sid):
                     self.store.release(sid)
+            self.release_placeholders()
         return {"sequence_ids": seq_ids, "tokens": tokens, "logprobs": logprobs, "argmax": argmax}

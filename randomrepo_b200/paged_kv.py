@@ -611,10 +611,15 @@ class PagedKVCacheStore:
                      int(step.info.slots), step.batch)
 
     # -- device chunked-prefill / speculative-verify path (extension) -----------
-    def prefill_step(self, sequence_ids, q_lens, num_q_heads: int) -> PrefillStep:
+    def prefill_step(self, sequence_ids, q_lens, num_q_heads: int, buffers: dict | None = None) -> PrefillStep:
         """Lay out one prefill / verify forward: each sequence's chunk is its last ``q_lens[i]``
         tokens (already reserved / appended in the allocator).  Records the chunks' block fills,
-        plans the attention launch and uploads slots and work items once for all layers."""
+        plans the attention launch and uploads slots and work items once for all layers.
+
+        ``buffers`` (``{"slots": int64, "records": int32 [n, 8]}`` device tensors) makes the
+        upload go into those fixed addresses -- a forward recorded in a CUDA graph reads them
+        there -- and requires the plan to have exactly ``buffers["n_items"]`` work items and
+        no split-key combine entries (ValueError otherwise)."""
         pool = self._require_pool()
         ids = self._step_ids(sequence_ids)
         n = ids.size
@@ -649,8 +654,16 @@ class PagedKVCacheStore:
         slots = np.concatenate(slot_parts)
         plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
-            slots_d = torch.from_numpy(slots).to(pool.device, non_blocking=True)
-            records_d = torch.from_numpy(plan.records).to(pool.device, non_blocking=True)
+            if buffers is None:
+                slots_d = torch.from_numpy(slots).to(pool.device, non_blocking=True)
+                records_d = torch.from_numpy(plan.records).to(pool.device, non_blocking=True)
+            else:
+                if plan.n_combine or plan.n_items != buffers["n_items"] or slots.size > buffers["slots"].numel():
+                    raise ValueError("the prefill plan does not fit the recorded launch")
+                slots_d = buffers["slots"][:slots.size]
+                records_d = buffers["records"][:plan.n_items]
+                slots_d.copy_(torch.from_numpy(slots), non_blocking=True)
+                records_d.copy_(torch.from_numpy(plan.records), non_blocking=True)
         return PrefillStep(ids, q_lens, hq, total_q, plan, slots_d, records_d)
 
     def prefill_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,

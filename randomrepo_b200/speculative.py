@@ -10,10 +10,12 @@ stores:
   opens the first round) and the other members of its GRPO group fork the
   prompt's pages (copy-on-write);
 * a round over all active sequences is k draft forwards -- the first feeds
-  the draft the one or two tokens it has not seen yet (packed), the rest are
-  decode steps (CUDA-graphed with ``cuda_graphs=True`` on the draft) -- then
+  the draft the one or two tokens it has not seen yet, the rest are decode
+  steps; with ``cuda_graphs=True`` on the draft all of them are graphed decode
+  steps (sequences two tokens behind take one extra step first) -- then
   one target forward of k + 1 tokens per sequence, the paged verify read
-  (``verify`` rows = positions prefix_len - 1 .. prefix_len - 1 + k);
+  (``verify`` rows = positions prefix_len - 1 .. prefix_len - 1 + k),
+  replayed from a CUDA graph with ``cuda_graphs=True`` on the target;
 * ``pkv_spec_accept`` decides every sequence's round in one launch group;
 * rejected drafts leave both caches through ``truncate`` (blocks past the
   kept tokens return to the pool, shared prompt blocks stay shared).
@@ -30,7 +32,6 @@ draws).
 
 from __future__ import annotations
 
-import numpy as np
 import torch
 
 from .sampling import SamplingConfig
@@ -80,7 +81,14 @@ class PagedSpeculativeGenerator:
         """k draft proposals per sequence: (tokens [n, k] int64, logits [n, k, vocab] float32)."""
         draft, sampler = self.draft, self.sampler
         dev = draft.device
-        if all(len(p) == 1 for p in pending):
+        if draft.cuda_graphs:
+            # Graphed decode steps only: sequences two tokens behind take one
+            # step on their own first (its logits are not needed).
+            two = [j for j, p in enumerate(pending) if len(p) == 2]
+            if two:
+                draft.decode_step([ids[j] for j in two], torch.tensor([pending[j][0] for j in two], device=dev))
+            first = draft.decode_step(ids, torch.tensor([p[-1] for p in pending], device=dev))
+        elif all(len(p) == 1 for p in pending):
             first = draft.decode_step(ids, torch.tensor([p[0] for p in pending], device=dev))
         else:
             first = draft.extend(ids, pending)
@@ -164,7 +172,7 @@ class PagedSpeculativeGenerator:
             # Target verify: the last accepted token and the k drafts of every sequence.
             dtok_h = dtok.cpu()
             chunks = [[prefix[j][-1]] + dtok_h[j].tolist() for j in range(len(active))]
-            tlogits = self.target.extend(ids, chunks, all_logits=True).view(len(active), k + 1, -1)
+            tlogits = self.target.verify_logits(ids, chunks).view(len(active), k + 1, -1)
             u = None
             if uniforms is not None:
                 u = torch.tensor([list(uniforms(i, rnd))[:k] for i in active], dtype=torch.float32, device=dev)
@@ -215,4 +223,6 @@ class PagedSpeculativeGenerator:
                 for gen in (self.target, self.draft):
                     if gen.store.has_sequence(sid):
                         gen.store.release(sid)
+            for gen in (self.target, self.draft):
+                gen.release_placeholders()
         return result

@@ -154,10 +154,37 @@ def test_cuda_graph_decode_matches_eager(cuda_device):
         b = graphs.generate(prompts, group_size=group, max_new_tokens=40)
         assert a["tokens"] == b["tokens"]
         np.testing.assert_allclose(np.concatenate(b["logprobs"]), np.concatenate(a["logprobs"]), atol=1e-4)
-    # Batch 6 outgrew the fixed-step capacity set for batch 3: capacity grew and the graphs were re-recorded.
-    assert set(graphs._graphs) == {6}
+    # Batches 3 and 6 run padded to the recorded sizes 4 and 8; batch 8 outgrew the
+    # fixed-step capacity set for 4, so capacity grew and the graphs were re-recorded.
+    assert set(graphs._graphs) == {8}
     pool = graphs.store.pool
     assert pool.decode_error_flag() == 0 and graphs.store.allocator.used_block_count == 0
+
+
+def test_cuda_graphs_shrinking_batch_reuses_padded_graphs(cuda_device):
+    """Sequences that stop at eos shrink the batch step by step: the graphed path pads each step to a
+    recorded size (placeholder sequences) instead of recording a graph per size, with the eager tokens."""
+    from randomrepo_b200.hf import PagedGenerator, graph_batch, make_store
+
+    model = _model(cuda_device, 64, 2)
+    gen = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, 512, (int(n),), generator=gen) for n in torch.randint(5, 60, (12,), generator=gen)]
+    probe = PagedGenerator(model, make_store(model, total_blocks=2048), prefill_chunk_size=64)
+    free = probe.generate(prompts, group_size=2, max_new_tokens=48)["tokens"]
+    # As eos the token found in the most sequences: several stop early, at different steps.
+    eos = int(np.bincount(np.concatenate([np.unique(t) for t in free])).argmax())
+    eager = PagedGenerator(model, make_store(model, total_blocks=2048), prefill_chunk_size=64, eos_token_id=eos)
+    graphs = PagedGenerator(model, make_store(model, total_blocks=2048), prefill_chunk_size=64, eos_token_id=eos,
+                            cuda_graphs=True)
+    a = eager.generate(prompts, group_size=2, max_new_tokens=48)
+    b = graphs.generate(prompts, group_size=2, max_new_tokens=48)
+    assert a["tokens"] == b["tokens"]
+    # Sequences still decoding at each step after the first (the first comes from prefill).
+    active = {sum(len(t) > s for t in a["tokens"]) for s in range(1, 48)} - {0}
+    buckets = {graph_batch(c) for c in active}
+    assert len(active) >= 3 and len(buckets) < len(active)  # the batch shrank, sizes shared a graph
+    assert set(graphs._graphs) == buckets
+    assert graphs.store.allocator.used_block_count == 0 and graphs.store.resident_sequence_count == 0
 
 
 def test_score_matches_the_reference_old_policy_pass(cuda_device):

@@ -61,7 +61,7 @@ def _spec(target, draft, k, *, graphs=False, eos=None):
     from randomrepo_b200.hf import PagedGenerator, make_store
     from randomrepo_b200.speculative import PagedSpeculativeGenerator
 
-    t = PagedGenerator(target, make_store(target, total_blocks=2048), prefill_chunk_size=32)
+    t = PagedGenerator(target, make_store(target, total_blocks=2048), prefill_chunk_size=32, cuda_graphs=graphs)
     d = PagedGenerator(draft, make_store(draft, total_blocks=2048), prefill_chunk_size=32, cuda_graphs=graphs,
                        sampler=t.sampler)
     return PagedSpeculativeGenerator(t, d, k=k, eos_token_id=eos)
@@ -125,7 +125,9 @@ def test_draft_equal_to_target_accepts_nearly_everything(cuda_device):
     assert res["rounds"] <= 48 // 5 + 4
 
 
-def test_graphed_draft_matches_eager_draft(cuda_device):
+def test_graphed_rounds_match_eager_rounds(cuda_device):
+    """Draft decode steps and target verify forwards replayed from CUDA graphs (padded batches,
+    fixed upload buffers) give the eager rounds' tokens."""
     target, draft = _model(cuda_device, 0, 2), _model(cuda_device, 1, 1)
     prompts = _prompts(6, seed=3)
     a = _spec(copy.deepcopy(target), copy.deepcopy(draft), 3).generate(prompts, max_new_tokens=24,
@@ -134,8 +136,8 @@ def test_graphed_draft_matches_eager_draft(cuda_device):
     b = sg.generate(prompts, max_new_tokens=24, uniforms=_uniform)
     assert a["tokens"] == b["tokens"]
     np.testing.assert_allclose(np.concatenate(b["logprobs"]), np.concatenate(a["logprobs"]), atol=1e-4)
-    assert sg.draft._graphs  # the draft's decode steps ran as graphs
-    assert sg.draft.store.allocator.used_block_count == 0
+    assert sg.draft._graphs and sg.target._ext_graphs  # draft steps and verify forwards ran as graphs
+    assert sg.draft.store.allocator.used_block_count == 0 and sg.target.store.allocator.used_block_count == 0
 
 
 def test_groups_eos_and_sampling(cuda_device):
