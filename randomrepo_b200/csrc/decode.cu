@@ -255,6 +255,9 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
   int issued = 0, consumed = 0;
   bool iss_next = false;
   int iss_pg = cur.pg0;
+  // Pages are read once per step: evict them first, so the split partials
+  // this kernel writes are still in L2 when the combine kernel reads them.
+  const uint64_t kv_policy = l2_evict_first_policy();
 
   // Keep kStages copies in flight along the stream cur -> nxt.
   auto issue_ahead = [&]() {
@@ -271,8 +274,9 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
       if (lane == 0) {
         const int st = issued % S;
         mbar_arrive_expect_tx(&full[st], C::kStageBytes);
-        bulk_copy_g2s(ring + st * C::kStageBytes,
-                      layer_base + ((int64_t)blk * p.hkv + m.hg * HPC) * C::kHeadBytes, C::kStageBytes, &full[st]);
+        bulk_copy_g2s_hint(ring + st * C::kStageBytes,
+                           layer_base + ((int64_t)blk * p.hkv + m.hg * HPC) * C::kHeadBytes, C::kStageBytes,
+                           &full[st], kv_policy);
       }
       ++issued;
       ++iss_pg;

@@ -98,6 +98,24 @@ __device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gsrc, 
                : "memory");
 }
 
+// L2 policy for data read exactly once: its lines are the first evicted, so
+// what the same kernel writes for a later reader (split-K partials) stays.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_copy_g2s with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar,
+                                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // ---- tcgen05 (5th-generation tensor cores, accumulators in tensor memory) ----
 
 __device__ __forceinline__ void tc_fence_before_sync() {
