@@ -12,7 +12,9 @@
 // from an atomic counter (dynamic, largest-first scheduling) and owns it
 // entirely, so no barrier ever couples warps.
 //
-// Per warp: a private ring of kStages shared-memory stages.  One stage holds
+// Per warp: a private ring of kStages shared-memory stages (5 warps x 2
+// stages of 16 KB at D = 128 with two KV heads per item; 8 warps x 3 stages
+// of 8 KB otherwise: PKV_DECODE_* in pkv_internal.h).  One stage holds
 // one block's K and V pages of the item's HPC heads -- adjacent in the pool
 // and stored pre-swizzled (pkv_device.cuh) -- filled by one cp.async.bulk
 // (no tensor map, no multicast) whose completion is counted on the stage's
@@ -59,8 +61,10 @@ struct Cfg {
   static constexpr int kPageBytes = 16 * D * 2;         // one K (or V) page of one head
   static constexpr int kHeadBytes = 2 * kPageBytes;     // K + V of one head in one block
   static constexpr int kStageBytes = HPC * kHeadBytes;  // one ring stage = one block, HPC heads
-  static constexpr int kWarps = kStageBytes >= 16384 ? 4 : 8;
-  static constexpr int kStages = (192 * 1024) / (kWarps * kStageBytes) > 8 ? 8 : (192 * 1024) / (kWarps * kStageBytes);
+  static constexpr int kWarps = kStageBytes >= 16384 ? PKV_DECODE_WARPS_BIG : 8;
+  static constexpr int kStages = PKV_DECODE_RING_BYTES / (kWarps * kStageBytes) > 8
+                                     ? 8
+                                     : PKV_DECODE_RING_BYTES / (kWarps * kStageBytes);
   static constexpr int kSmemBytes = kWarps * kStages * kStageBytes + 1024;
   static constexpr int kVecsPerRow = D * 2 / 16;        // 16-byte chunks per token row
 };
@@ -587,7 +591,7 @@ int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
 int warps_per_cta(int head_dim, int hpc) {
   const int stage = hpc * 2 * 16 * head_dim * 2;
-  return stage >= 16384 ? 4 : 8;
+  return stage >= 16384 ? PKV_DECODE_WARPS_BIG : 8;
 }
 
 struct WsLayout {
@@ -696,13 +700,14 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
                   " tokens");
     return PKV_ERR_UNSUPPORTED;
   }
-  // About 3 items per warp of the persistent grid (dynamic scheduling evens
+  // About PKV_DECODE_ITEMS_PER_WARP (3) items per warp of the persistent grid (dynamic scheduling evens
   // out the rest), 4..32 pages per item, at most kMaxSplitsPerSeq items per
   // sequence and head group.
   const int64_t work = total_pages * groups;
   const int64_t warps = (int64_t)num_sms * warps_per_cta(head_dim, hpc);
   int32_t pps = (int32_t)std::min<int64_t>(kMaxPagesPerItem,
-                                           std::max<int64_t>(4, (work + warps * 3 - 1) / (warps * 3)));
+                                           std::max<int64_t>(4, (work + warps * PKV_DECODE_ITEMS_PER_WARP - 1) /
+                                                                    (warps * PKV_DECODE_ITEMS_PER_WARP)));
   pps = std::max(pps, (max_pages + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq);
   int64_t n = 0, nc = 0;
   for (int b = 0; b < batch; ++b) {

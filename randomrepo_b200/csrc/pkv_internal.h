@@ -4,6 +4,26 @@
 
 #include "pkv_b200.h"
 
+// Decode launch shape.  A warp owns a ring of bulk-copy stages totalling
+// PKV_DECODE_RING_BYTES / warps; stages of 16 KB or more (D = 128, two KV
+// heads) run PKV_DECODE_WARPS_BIG warps per CTA, smaller stages 8.  The
+// planner sizes work items for about PKV_DECODE_ITEMS_PER_WARP items per warp
+// of the persistent grid.
+#ifndef PKV_DECODE_WARPS_BIG
+#define PKV_DECODE_WARPS_BIG 5
+#endif
+#ifndef PKV_DECODE_RING_BYTES
+#define PKV_DECODE_RING_BYTES (200 * 1024)
+#endif
+#ifndef PKV_DECODE_ITEMS_PER_WARP
+#define PKV_DECODE_ITEMS_PER_WARP 3
+#endif
+// Decode-step descriptors uploaded on a separate copy stream (1) or on the
+// caller's stream (0).
+#ifndef PKV_STEPPER_COPY_STREAM
+#define PKV_STEPPER_COPY_STREAM 1
+#endif
+
 // pkv_decode_attention plus length / refcount updates the decode does not
 // read, applied by the kernel itself: `deferred` holds deferred_refs
 // (block, refcount) pairs then deferred_lens (row, length) pairs.

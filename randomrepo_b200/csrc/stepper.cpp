@@ -60,6 +60,14 @@ struct pkv_stepper {
   // all kRing slots (one event per kRing uploads instead of one per upload).
   cudaEvent_t round_done = nullptr;
   bool round_pending = false;
+#if PKV_STEPPER_COPY_STREAM
+  // Descriptor uploads on their own stream: the copy for step i+1 runs while
+  // step i's kernels do; the step's kernels wait for it through copy_ev, and
+  // the first copy of each trip round the ring waits (on the device) for the
+  // kernels enqueued before it, which read the slots it is about to reuse.
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t copy_ev = nullptr, reuse_ev = nullptr;
+#endif
   bool round_open = false;  // the ring's last slot was taken and not yet copied out
   std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
   std::vector<int32_t> last_copies;  // (src, dst) pairs applied by the last sync / upload
@@ -98,6 +106,14 @@ struct pkv_stepper {
       cudaEventSynchronize(round_done);
       cudaEventDestroy(round_done);
     }
+#if PKV_STEPPER_COPY_STREAM
+    if (copy_stream) {
+      cudaStreamSynchronize(copy_stream);
+      cudaStreamDestroy(copy_stream);
+      cudaEventDestroy(copy_ev);
+      cudaEventDestroy(reuse_ev);
+    }
+#endif
     for (auto& s : slot) {
       if (s.host) cudaFreeHost(s.host);
       if (s.dev) cudaFree(s.dev);
@@ -220,8 +236,26 @@ struct pkv_stepper {
   }
 
   int32_t upload(Slot* s, int64_t n, cudaStream_t stream) {
+#if PKV_STEPPER_COPY_STREAM
+    if (!copy_stream) {
+      int32_t st = cuda_status(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      if (!st) st = cuda_status(cudaEventCreateWithFlags(&copy_ev, cudaEventDisableTiming), "cudaEventCreate");
+      if (!st) st = cuda_status(cudaEventCreateWithFlags(&reuse_ev, cudaEventDisableTiming), "cudaEventCreate");
+      if (st) return st;
+    }
+    if (last_taken == 0) {
+      int32_t st = cuda_status(cudaEventRecord(reuse_ev, stream), "cudaEventRecord");
+      if (!st) st = cuda_status(cudaStreamWaitEvent(copy_stream, reuse_ev, 0), "cudaStreamWaitEvent");
+      if (st) return st;
+    }
+    int32_t st = cuda_status(cudaMemcpyAsync(s->dev, s->host, n * 4, cudaMemcpyHostToDevice, copy_stream), "H2D");
+    if (!st) st = cuda_status(cudaEventRecord(copy_ev, copy_stream), "cudaEventRecord");
+    if (!st) st = cuda_status(cudaStreamWaitEvent(stream, copy_ev, 0), "cudaStreamWaitEvent");
+    return st ? st : copied(copy_stream);
+#else
     int32_t st = cuda_status(cudaMemcpyAsync(s->dev, s->host, n * 4, cudaMemcpyHostToDevice, stream), "H2D");
     return st ? st : copied(stream);
+#endif
   }
 
   bool capacity_ok(pkv_step_info* out) {
@@ -326,7 +360,7 @@ int32_t pkv_stepper_fix_steps(pkv_stepper* st, int32_t max_batch, int32_t max_it
   }
   const int32_t hpc = pkv_decode_heads_per_item(st->geom.num_kv_heads);
   const int32_t groups = st->geom.num_kv_heads / hpc;
-  const int32_t warps = st->num_sms * (2 * 16 * st->geom.head_dim * 2 * hpc >= 16384 ? 4 : 8);
+  const int32_t warps = st->num_sms * (2 * 16 * st->geom.head_dim * 2 * hpc >= 16384 ? PKV_DECODE_WARPS_BIG : 8);
   if (max_items == 0) max_items = groups * max_batch + 4 * warps;
   max_items = std::max(max_items, groups * max_batch);
   auto cs = static_cast<cudaStream_t>(stream);
