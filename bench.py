@@ -946,10 +946,15 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     sys.path.insert(0, str(ROOT))
+    # stdout carries the one JSON line; anything else written to it (library
+    # banners such as NCCL's version line, HF messages) goes to stderr.
+    line_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            print(json.dumps(run_reference(args)), file=line_out, flush=True)
         return
 
     if world != args.gpus:
@@ -963,7 +968,7 @@ def main() -> None:
     try:
         result = run_ours(args, rank, world, device)
         if result is not None:
-            print(json.dumps(result), flush=True)
+            print(json.dumps(result), file=line_out, flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist
