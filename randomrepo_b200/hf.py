@@ -179,6 +179,9 @@ class PagedGenerator:
         self._ext_graphs: dict[tuple[int, int], tuple] = {}
         self.fp32_logits = bool(fp32_logits)
         self._sampler = sampler
+        # Device times of the last generate on a CUDA device: prefill_ms (prompts
+        # + forks), decode_ms (the decode loop), token counts.
+        self.last_timings: dict = {}
 
     @property
     def sampler(self):
@@ -541,7 +544,13 @@ class PagedGenerator:
         sampler.reseed(cfg.seed)
         n_groups = len(prompts)
         heads = [first_id + g * group_size for g in range(n_groups)]
+        marks = None
+        if self.device.type == "cuda":
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            marks[0].record()
         logits = self.prefill(heads, prompts)
+        if marks is not None:
+            marks[1].record()
         seq_ids, next_logits = [], []
         for g in range(n_groups):
             for m in range(group_size):
@@ -552,6 +561,9 @@ class PagedGenerator:
                 next_logits.append(logits[g])
         cur = torch.stack(next_logits)
         n = len(seq_ids)
+        # Prompt blocks the group members share (copy-on-write) right after the forks.
+        alloc = getattr(self.store, "allocator", None)
+        shared_after_prefill = (alloc.shared_block_count, alloc.used_block_count) if alloc is not None else (0, 0)
         if self.cuda_graphs:
             self.reserve_tables(max(int(torch.as_tensor(p).numel()) for p in prompts) + max_new_tokens)
         tokens = [[] for _ in range(n)]
@@ -584,6 +596,15 @@ class PagedGenerator:
             keep = torch.tensor(still, device=cur.device)
             active = [active[j] for j in still]
             cur = self.decode_step([seq_ids[i] for i in active], nxt[keep])
+        if marks is not None:
+            marks[2].record()
+            marks[2].synchronize()
+            self.last_timings = {
+                "prefill_ms": marks[0].elapsed_time(marks[1]), "decode_ms": marks[1].elapsed_time(marks[2]),
+                "prefill_tokens": sum(int(torch.as_tensor(p).numel()) for p in prompts),
+                "decode_tokens": sum(len(t) for t in tokens),
+                "shared_blocks_after_prefill": shared_after_prefill,
+            }
         if release:
             for sid in seq_ids:
                 if self.store.has_sequence(sid):
