@@ -324,7 +324,8 @@ def run_mode(mode: str, model, prompts, *, group: int, new_tokens: int, steps: i
                 timings = dict(gen.last_timings)
             tokens = res["tokens"]
             clock.mark(1)
-            pressure = gen.store.allocator.allocator_pressure
+            alloc = gen.store.allocator
+            pressure = alloc.max_blocks_in_use / alloc.total_blocks  # the pool's high watermark
             sids, sam, scm = _score_inputs(prompts, tokens, group)
             gen.score(sids, sam, scm, group_size=group)
             clock.mark(2)
