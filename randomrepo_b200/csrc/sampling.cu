@@ -528,11 +528,19 @@ __global__ void __launch_bounds__(kThreads) spec_accept_kernel(const AccArgs a) 
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// SM count of the current device (queried once per device).
 int num_sms() {
-  int dev = 0, sms = 0;
+  constexpr int kMaxDevices = 64;
+  static int cache[kMaxDevices] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms > 0 ? sms : 148;
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (cache[dev] == 0) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = sms > 0 ? sms : 148;
+  }
+  return cache[dev];
 }
 
 // Most CTAs one row is ever cut into.

@@ -244,8 +244,18 @@ class PagedGenerator:
         [n * L, vocab] (the speculative verify forward).  With ``cuda_graphs`` the forward is
         replayed from a CUDA graph recorded per (padded batch, L): the step's slots and work
         items go to fixed device buffers, placeholders pad the batch to a recorded size."""
+        from . import device as _device
+        from ._lib import lib as _lib
+
         lens = {len(c) for c in chunks}
-        if not self.cuda_graphs or len(lens) != 1:
+        cfg = self.model.config
+        hq, hkv = int(cfg.num_attention_heads), int(getattr(cfg, "num_key_value_heads", None) or
+                                                     cfg.num_attention_heads)
+        # The recorded launch needs a fixed shape: every chunk fits one work
+        # item per KV head and the plan does not cut keys across CTAs.
+        fixed_shape = (len(lens) == 1 and _device.PREFILL_SPLIT_WAVES == 0 and
+                       next(iter(lens)) <= _lib.pkv_prefill_positions_per_item(hq, hkv))
+        if not self.cuda_graphs or not fixed_shape:
             return self.extend(sequence_ids, chunks, all_logits=True)
         return self._extend_graph([int(s) for s in sequence_ids], chunks, lens.pop())
 

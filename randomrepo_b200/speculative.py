@@ -118,12 +118,10 @@ class PagedSpeculativeGenerator:
         acceptance draws.
         """
         cfg = sampling or SamplingConfig()
-        sampler = self.sampler
-        sampler.reseed(cfg.seed)
+        self.sampler.reseed(cfg.seed)
         do_sample = bool(cfg.do_sample) and cfg.temperature > 0
         eff_t = cfg.temperature if cfg.temperature > 0 else 1.0
         draft_t = eff_t if do_sample else None
-        eos = self.eos_token_id
         k = min(self.k, int(max_new_tokens))
         n_groups = len(prompts)
         heads = [first_id + g * group_size for g in range(n_groups)]
@@ -139,6 +137,21 @@ class PagedSpeculativeGenerator:
         if max_new_tokens <= 0 or n == 0:
             return result
 
+        try:
+            return self._rounds(toks, heads, seq_ids, group_size, max_new_tokens, k, do_sample, eff_t, draft_t,
+                                uniforms, trace, release, result)
+        except BaseException:
+            if release:
+                self._release(seq_ids)
+            raise
+
+    def _rounds(self, toks, heads, seq_ids, group_size, max_new_tokens, k, do_sample, eff_t, draft_t, uniforms,
+                trace, release, result) -> dict:
+        """Prefill both caches, then speculative rounds until every sequence is done."""
+        sampler = self.sampler
+        eos = self.eos_token_id
+        n_groups = len(toks)
+        n = len(seq_ids)
         # Prompts minus their last token into both caches, once per group.
         for gen in (self.target, self.draft):
             self._prefill_prefixes(gen, heads, [t[:-1] for t in toks])
@@ -219,10 +232,13 @@ class PagedSpeculativeGenerator:
                 self.draft.store.truncate(keep_ids, d_keep)
             active = still
         if release:
-            for sid in seq_ids:
-                for gen in (self.target, self.draft):
-                    if gen.store.has_sequence(sid):
-                        gen.store.release(sid)
-            for gen in (self.target, self.draft):
-                gen.release_placeholders()
+            self._release(seq_ids)
         return result
+
+    def _release(self, seq_ids) -> None:
+        for sid in seq_ids:
+            for gen in (self.target, self.draft):
+                if gen.store.has_sequence(sid):
+                    gen.store.release(sid)
+        for gen in (self.target, self.draft):
+            gen.release_placeholders()
