@@ -1,6 +1,6 @@
 """GPU parity of paged GQA decode attention (fused with the step's K/V append).
 
-Floating-point bar (BASELINE tolerance): |out - oracle| <= 2e-2 + 1e-2 * |oracle|
+Floating-point bar (the attention tolerance): |out - oracle| <= 2e-2 + 1e-2 * |oracle|
 elementwise, bf16/f16 inputs, fp32 accumulation.  The oracle is the fp32
 restatement of HF ``sdpa_attention_forward`` (pinned to the reference's
 attention by tests/test_oracle_golden.py); the golden HF outputs themselves are
