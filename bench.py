@@ -281,51 +281,33 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         raise RuntimeError(f"decode kernel reported device error {err}")
 
     # ---- end to end through the public API with host buffers ---------------
-    # Every step copies its own q/k/v in from pinned host memory (one packed
-    # buffer) and its output back out.  The input copy runs on a copy stream
-    # into one of two device buffers, so step i+1's inputs cross PCIe while
-    # step i computes; the output copy follows the step on its stream.
+    # Every step hands the store pinned host q/k/v (one packed buffer) and a
+    # pinned host output: the native stepper copies the inputs in on its copy
+    # stream ahead of the step descriptor and the output back out on a second
+    # stream, so step i+1's input copy and step i-1's output copy run while
+    # step i's kernels do.  The region ends after the last output copy.
     nq, nk = q.numel(), kn.numel()
     inp_h = torch.empty(nq + 2 * nk, dtype=q.dtype).pin_memory()
     inp_h[:nq].copy_(q.reshape(-1).cpu())
     inp_h[nq:nq + nk].copy_(kn.reshape(-1).cpu())
     inp_h[nq + nk:].copy_(vn.reshape(-1).cpu())
+    q_h, k_h, v_h = inp_h[:nq].view(q.shape), inp_h[nq:nq + nk].view(kn.shape), inp_h[nq + nk:].view(vn.shape)
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    inp_d = [torch.empty_like(inp_h, device=device) for _ in range(2)]
-    views = [(d[:nq].view(q.shape), d[nq:nq + nk].view(kn.shape), d[nq + nk:].view(vn.shape)) for d in inp_d]
-    copy = torch.cuda.Stream(device=device)
-    main = torch.cuda.current_stream(device)
-    loaded = [torch.cuda.Event() for _ in range(2)]
-    consumed = [torch.cuda.Event() for _ in range(2)]
-    for e in consumed:
-        e.record(main)
-    e2e_i = [0]
-
-    def load(i):
-        with torch.cuda.stream(copy):
-            copy.wait_event(consumed[i])   # the step that read this buffer has finished
-            inp_d[i].copy_(inp_h, non_blocking=True)
-            loaded[i].record(copy)
 
     def e2e_step():
-        i = e2e_i[0] % 2
-        e2e_i[0] += 1
-        load(1 - i)                        # the next step's inputs, during this step
-        main.wait_event(loaded[i])
-        step(*views[i], out)
-        consumed[i].record(main)
-        out_h.copy_(out, non_blocking=True)
+        store.decode(ids, q_h, k_h, v_h, layer=0, out=out_h)
+        alloc.truncate(ids, lengths)
 
-    load(0)
     for _ in range(args.warmup):
         e2e_step()
+    store.wait_host_outputs()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         e2e_step()
-    main.wait_stream(copy)  # every input copy issued in the region ends inside it
+    store.fence_host_outputs()  # every output copy issued in the region ends inside it
     e1.record()
     torch.cuda.synchronize(device)
     e2e_ms = e0.elapsed_time(e1)
@@ -380,9 +362,10 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             "unit": "tokens/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "path": "PagedKVCacheStore.decode with q/k/v copied in from one pinned host buffer (on a copy stream, "
-                    "into two device buffers: the next step's copy overlaps this step) and the output copied out "
-                    "to pinned host memory every step",
+            "path": "PagedKVCacheStore.decode given pinned host q/k/v (one packed buffer) and a pinned host "
+                    "output: pkv_stepper_step_host copies the inputs in on the stepper's copy stream with the step "
+                    "descriptor and the output out on a second stream, every step; the region ends after the last "
+                    "output copy",
         },
         "gpu_launches": launches,
         "clocks": clocks.summary(),

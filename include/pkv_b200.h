@@ -418,6 +418,33 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
                          const void* k_new, const void* v_new, int32_t num_q_heads, float scale, void* out,
                          void* stream, pkv_step_info* info, int32_t* rows_out, int32_t* lens_out,
                          int32_t* token_blocks_out, int32_t* copies_out, int64_t copies_cap);
+/* pkv_stepper_step with q / k_new / v_new and out in HOST memory (pinned for
+ * the copies to overlap; q and out [n][num_q_heads][head_dim], k_new and
+ * v_new [n][num_kv_heads][head_dim], the pool's dtype; k_new / v_new both
+ * NULL for attention without the append).  The stepper stages the inputs in
+ * device buffers of its own: they cross on its copy stream ahead of the step
+ * descriptor (one copy when q, k_new and v_new lie back to back), the
+ * output crosses on a second stream of the stepper after the step's
+ * kernels, so a step's input copy and the previous step's output copy run
+ * while the kernels of the step between them do.  Host pointers are read and
+ * written asynchronously: q / k_new / v_new must stay unchanged and out must
+ * not be read until `stream` has passed pkv_stepper_host_fence.  This is the
+ * host-facing form of the reference's decode step, whose q / k / v come from
+ * the model on the same device (agentrl/generation/continuous.py:407-497).
+ * On PKV_ERR_CAPACITY the step is begun and its inputs staged: grow and
+ * rebind the tables, then call pkv_stepper_upload and
+ * pkv_stepper_attention_host. */
+int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer,
+                              const void* q_host, const void* k_new_host, const void* v_new_host,
+                              int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
+                              int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out);
+/* The attention + output copy of a host step whose inputs were staged by
+ * pkv_stepper_step_host and whose descriptor is uploaded (the capacity retry). */
+int32_t pkv_stepper_attention_host(pkv_stepper* st, int32_t layer, int32_t num_q_heads, float scale, void* out_host,
+                                   void* stream);
+/* Make `stream` wait for every output copy of the host steps issued so far;
+ * once `stream` has run past this point their out buffers hold the results. */
+int32_t pkv_stepper_host_fence(pkv_stepper* st, void* stream);
 /* The copy-on-write (src, dst) block pairs the last sync / upload applied
  * (*n_pairs gets their count; up to `capacity` pairs are written). */
 int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs);

@@ -18,11 +18,6 @@
 #ifndef PKV_DECODE_ITEMS_PER_WARP
 #define PKV_DECODE_ITEMS_PER_WARP 3
 #endif
-// Decode-step descriptors uploaded on a separate copy stream (1) or on the
-// caller's stream (0).
-#ifndef PKV_STEPPER_COPY_STREAM
-#define PKV_STEPPER_COPY_STREAM 1
-#endif
 
 // pkv_decode_attention plus length / refcount updates the decode does not
 // read, applied by the kernel itself: `deferred` holds deferred_refs

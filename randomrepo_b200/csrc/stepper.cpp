@@ -60,14 +60,33 @@ struct pkv_stepper {
   // all kRing slots (one event per kRing uploads instead of one per upload).
   cudaEvent_t round_done = nullptr;
   bool round_pending = false;
-#if PKV_STEPPER_COPY_STREAM
   // Descriptor uploads on their own stream: the copy for step i+1 runs while
   // step i's kernels do; the step's kernels wait for it through copy_ev, and
   // the first copy of each trip round the ring waits (on the device) for the
   // kernels enqueued before it, which read the slots it is about to reuse.
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t copy_ev = nullptr, reuse_ev = nullptr;
-#endif
+  // Host-buffer steps (pkv_stepper_step_host): device staging of q / k / v
+  // and of the output in kIo entries used in turn.  A step's inputs cross on
+  // copy_stream ahead of its descriptor (so the one wait on copy_ev covers
+  // both), its output crosses on d2h_stream after its kernels; `used` marks
+  // the kernels that read an entry's inputs and wrote its output, `read` the
+  // copy of that output to the host.
+  static constexpr int kIo = 2;
+  struct Io {
+    char* in = nullptr;
+    char* out = nullptr;
+    int64_t in_cap = 0, out_cap = 0;
+    cudaEvent_t used = nullptr, read = nullptr;
+    bool used_set = false, read_set = false;
+  };
+  Io io[kIo];
+  int io_next = 0;
+  int io_cur = -1;        // entry of the step whose inputs were staged last
+  int io_last_read = -1;  // entry of the last output copy issued
+  int64_t io_q_bytes = 0, io_kv_bytes = 0;
+  int32_t io_batch = 0;
+  cudaStream_t d2h_stream = nullptr;
   bool round_open = false;  // the ring's last slot was taken and not yet copied out
   std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
   std::vector<int32_t> last_copies;  // (src, dst) pairs applied by the last sync / upload
@@ -106,14 +125,22 @@ struct pkv_stepper {
       cudaEventSynchronize(round_done);
       cudaEventDestroy(round_done);
     }
-#if PKV_STEPPER_COPY_STREAM
     if (copy_stream) {
       cudaStreamSynchronize(copy_stream);
       cudaStreamDestroy(copy_stream);
       cudaEventDestroy(copy_ev);
       cudaEventDestroy(reuse_ev);
     }
-#endif
+    if (d2h_stream) {
+      cudaStreamSynchronize(d2h_stream);
+      cudaStreamDestroy(d2h_stream);
+    }
+    for (auto& e : io) {
+      if (e.used) cudaEventDestroy(e.used);
+      if (e.read) cudaEventDestroy(e.read);
+      if (e.in) cudaFree(e.in);
+      if (e.out) cudaFree(e.out);
+    }
     for (auto& s : slot) {
       if (s.host) cudaFreeHost(s.host);
       if (s.dev) cudaFree(s.dev);
@@ -235,14 +262,16 @@ struct pkv_stepper {
     return PKV_OK;
   }
 
+  int32_t ensure_copy_stream() {
+    if (copy_stream) return PKV_OK;
+    int32_t st = cuda_status(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (!st) st = cuda_status(cudaEventCreateWithFlags(&copy_ev, cudaEventDisableTiming), "cudaEventCreate");
+    if (!st) st = cuda_status(cudaEventCreateWithFlags(&reuse_ev, cudaEventDisableTiming), "cudaEventCreate");
+    return st;
+  }
+
   int32_t upload(Slot* s, int64_t n, cudaStream_t stream) {
-#if PKV_STEPPER_COPY_STREAM
-    if (!copy_stream) {
-      int32_t st = cuda_status(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "cudaStreamCreate");
-      if (!st) st = cuda_status(cudaEventCreateWithFlags(&copy_ev, cudaEventDisableTiming), "cudaEventCreate");
-      if (!st) st = cuda_status(cudaEventCreateWithFlags(&reuse_ev, cudaEventDisableTiming), "cudaEventCreate");
-      if (st) return st;
-    }
+    if (int32_t e = ensure_copy_stream()) return e;
     if (last_taken == 0) {
       int32_t st = cuda_status(cudaEventRecord(reuse_ev, stream), "cudaEventRecord");
       if (!st) st = cuda_status(cudaStreamWaitEvent(copy_stream, reuse_ev, 0), "cudaStreamWaitEvent");
@@ -252,10 +281,58 @@ struct pkv_stepper {
     if (!st) st = cuda_status(cudaEventRecord(copy_ev, copy_stream), "cudaEventRecord");
     if (!st) st = cuda_status(cudaStreamWaitEvent(stream, copy_ev, 0), "cudaStreamWaitEvent");
     return st ? st : copied(copy_stream);
-#else
-    int32_t st = cuda_status(cudaMemcpyAsync(s->dev, s->host, n * 4, cudaMemcpyHostToDevice, stream), "H2D");
-    return st ? st : copied(stream);
-#endif
+  }
+
+  // Copy a step's host q / k / v into the next staging entry on copy_stream
+  // (one copy when the three lie back to back in host memory).
+  int32_t stage_inputs(int32_t n, int32_t num_q_heads, const void* q, const void* k, const void* v) {
+    if (int32_t e = ensure_copy_stream()) return e;
+    const int64_t eb = geom.dtype == PKV_F32 ? 4 : 2;
+    const int64_t qb = (int64_t)n * num_q_heads * geom.head_dim * eb;
+    const int64_t kb = k ? (int64_t)n * geom.num_kv_heads * geom.head_dim * eb : 0;
+    const int64_t in_need = qb + 2 * kb;
+    Io& e = io[io_next];
+    if (e.in_cap < in_need || e.out_cap < qb) {
+      // Grow (rare): after the device has finished with the old buffers.
+      if (e.in || e.out) {
+        if (int32_t st = cuda_status(cudaDeviceSynchronize(), "host-step staging")) return st;
+      }
+      if (e.in) cudaFree(e.in);
+      if (e.out) cudaFree(e.out);
+      e.in = e.out = nullptr;
+      e.in_cap = e.out_cap = 0;
+      const int64_t in_cap = std::max<int64_t>(in_need, 1 << 20), out_cap = std::max<int64_t>(qb, 1 << 20);
+      int32_t st = cuda_status(cudaMalloc((void**)&e.in, in_cap), "cudaMalloc host-step staging");
+      if (!st) st = cuda_status(cudaMalloc((void**)&e.out, out_cap), "cudaMalloc host-step staging");
+      if (st) return st;
+      e.in_cap = in_cap;
+      e.out_cap = out_cap;
+    }
+    if (!e.used) {
+      int32_t st = cuda_status(cudaEventCreateWithFlags(&e.used, cudaEventDisableTiming), "cudaEventCreate");
+      if (!st) st = cuda_status(cudaEventCreateWithFlags(&e.read, cudaEventDisableTiming), "cudaEventCreate");
+      if (st) return st;
+    }
+    // The kernels that last read this entry's inputs have finished.
+    if (e.used_set) {
+      if (int32_t st = cuda_status(cudaStreamWaitEvent(copy_stream, e.used, 0), "cudaStreamWaitEvent")) return st;
+    }
+    const char* qc = static_cast<const char*>(q);
+    int32_t st;
+    if (!k || (static_cast<const char*>(k) == qc + qb && static_cast<const char*>(v) == qc + qb + kb)) {
+      st = cuda_status(cudaMemcpyAsync(e.in, q, in_need, cudaMemcpyHostToDevice, copy_stream), "H2D q/k/v");
+    } else {
+      st = cuda_status(cudaMemcpyAsync(e.in, q, qb, cudaMemcpyHostToDevice, copy_stream), "H2D q");
+      if (!st) st = cuda_status(cudaMemcpyAsync(e.in + qb, k, kb, cudaMemcpyHostToDevice, copy_stream), "H2D k");
+      if (!st) st = cuda_status(cudaMemcpyAsync(e.in + qb + kb, v, kb, cudaMemcpyHostToDevice, copy_stream), "H2D v");
+    }
+    if (st) return st;
+    io_cur = io_next;
+    io_next = (io_next + 1) % kIo;
+    io_q_bytes = qb;
+    io_kv_bytes = kb;
+    io_batch = n;
+    return PKV_OK;
   }
 
   bool capacity_ok(pkv_step_info* out) {
@@ -601,6 +678,74 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
   s = pkv_stepper_upload(st, stream, info, copies_out, copies_cap);
   if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention
   return pkv_stepper_attention(st, layer, q, k_new, v_new, num_q_heads, scale, out, stream);
+}
+
+int32_t pkv_stepper_attention_host(pkv_stepper* st, int32_t layer, int32_t num_q_heads, float scale, void* out_host,
+                                   void* stream) {
+  if (st->io_cur < 0 || !st->step_ready || st->io_batch != st->info.batch) {
+    pkv_clear_error();
+    pkv_set_error("pkv_stepper_attention_host: no host step staged and uploaded");
+    return PKV_ERR_ARG;
+  }
+  if (!out_host || num_q_heads <= 0 ||
+      (int64_t)st->io_batch * num_q_heads * st->geom.head_dim * (st->geom.dtype == PKV_F32 ? 4 : 2) !=
+          st->io_q_bytes) {
+    pkv_clear_error();
+    pkv_set_error("pkv_stepper_attention_host: output / head count does not match the staged step");
+    return PKV_ERR_ARG;
+  }
+  auto cs = static_cast<cudaStream_t>(stream);
+  auto& e = st->io[st->io_cur];
+  st->io_cur = -1;
+  if (!st->d2h_stream) {
+    int32_t s = cuda_status(cudaStreamCreateWithFlags(&st->d2h_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (s) return s;
+  }
+  // The copy of this entry's previous output to the host has finished.
+  if (e.read_set) {
+    if (int32_t s = cuda_status(cudaStreamWaitEvent(cs, e.read, 0), "cudaStreamWaitEvent")) return s;
+  }
+  const char* k = st->io_kv_bytes ? e.in + st->io_q_bytes : nullptr;
+  const char* v = st->io_kv_bytes ? e.in + st->io_q_bytes + st->io_kv_bytes : nullptr;
+  int32_t s = pkv_stepper_attention(st, layer, e.in, k, v, num_q_heads, scale, e.out, stream);
+  if (s) return s;
+  s = cuda_status(cudaEventRecord(e.used, cs), "cudaEventRecord");
+  if (!s) s = cuda_status(cudaStreamWaitEvent(st->d2h_stream, e.used, 0), "cudaStreamWaitEvent");
+  if (!s)
+    s = cuda_status(cudaMemcpyAsync(out_host, e.out, st->io_q_bytes, cudaMemcpyDeviceToHost, st->d2h_stream),
+                    "D2H out");
+  if (!s) s = cuda_status(cudaEventRecord(e.read, st->d2h_stream), "cudaEventRecord");
+  if (s) return s;
+  e.used_set = e.read_set = true;
+  st->io_last_read = (int)(&e - st->io);
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer,
+                              const void* q_host, const void* k_new_host, const void* v_new_host,
+                              int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
+                              int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out) {
+  if (!q_host || !out_host || num_q_heads <= 0 || num_q_heads % st->geom.num_kv_heads != 0 ||
+      (!k_new_host) != (!v_new_host)) {
+    pkv_clear_error();
+    pkv_set_error("pkv_stepper_step_host: q and out are required, num_q_heads must be a positive multiple of the "
+                  "KV heads, and k_new / v_new come together");
+    return PKV_ERR_ARG;
+  }
+  int32_t s = pkv_stepper_begin(st, sequence_ids, n, info, rows_out, lens_out, token_blocks_out);
+  if (s) return s;
+  s = st->stage_inputs(n, num_q_heads, q_host, k_new_host, v_new_host);
+  if (s) return s;
+  s = pkv_stepper_upload(st, stream, info, nullptr, 0);
+  if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention_host
+  return pkv_stepper_attention_host(st, layer, num_q_heads, scale, out_host, stream);
+}
+
+int32_t pkv_stepper_host_fence(pkv_stepper* st, void* stream) {
+  pkv_clear_error();
+  if (st->io_last_read < 0) return PKV_OK;
+  return cuda_status(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), st->io[st->io_last_read].read, 0),
+                     "cudaStreamWaitEvent");
 }
 
 int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs) {

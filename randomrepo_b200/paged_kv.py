@@ -505,6 +505,13 @@ class PagedKVCacheStore:
         Equivalent to ``decode_step(sequence_ids)`` followed by
         ``decode_attention(step, layer, q, k_new, v_new)``; the returned step
         serves the model's other layers.
+
+        With q / k_new / v_new (and ``out``, if given) in host memory the step
+        runs through ``pkv_stepper_step_host``: the stepper copies the inputs
+        in and the output back out on streams of its own, overlapped with the
+        neighbouring steps' kernels (pinned tensors for the copies to be
+        asynchronous).  ``out`` is then complete only after
+        ``wait_host_outputs()``; the inputs must not change until then.
         """
         pool = self._pool if self._pool is not None else self._require_pool()
         ids = sequence_ids
@@ -512,6 +519,8 @@ class PagedKVCacheStore:
                 and ids.size):
             ids = self._step_ids(sequence_ids)
         n = ids.size
+        if q.device.type == "cpu":
+            return self._decode_host(pool, ids, n, q, k_new, v_new, layer, scale, out)
         # The checks of q / k / v / out are skipped when the same tensor
         # objects come back (a decode loop reusing its buffers).
         chk = self._io_checked
@@ -536,6 +545,46 @@ class PagedKVCacheStore:
         step = self._finish_step(pool, st, ids, info, host)
         step.committed = True
         return out, step
+
+    def _decode_host(self, pool: KVPool, ids, n: int, q, k_new, v_new, layer: int, scale, out):
+        """``decode`` with host tensors: inputs staged and output returned by the native stepper."""
+        chk = self._io_checked
+        if (out is None or not chk or chk[0] is not q or chk[1] is not k_new or chk[2] is not v_new
+                or chk[3] is not out or chk[4] != n):
+            if k_new is None or v_new is None:
+                raise ValueError("a host-tensor decode step needs k_new and v_new")
+            out = self._check_decode_io(pool, n, q, k_new, v_new, out, device=torch.device("cpu"))
+            self._io_checked = (q, k_new, v_new, out, n)
+        host, (p_rows, p_lens, p_tokb) = self._host_buffers(n)
+        info = _lib.StepInfo()
+        with _on_device(pool.device):
+            stream = _current_stream(pool.device)
+            sc = float(scale if scale is not None else pool.head_dim ** -0.5)
+            st = lib.pkv_stepper_step_host(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(),
+                                           k_new.data_ptr(), v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream,
+                                           ctypes.byref(info), p_rows, p_lens, p_tokb)
+            if st == _lib.PKV_ERR_CAPACITY:
+                pool.grow(info.need_rows, info.need_cols)
+                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+                if st == _lib.PKV_OK:
+                    st = lib.pkv_stepper_attention_host(pool.stepper, int(layer), q.shape[1], sc, out.data_ptr(),
+                                                        stream)
+        step = self._finish_step(pool, st, ids, info, host)
+        step.committed = True
+        return out, step
+
+    def wait_host_outputs(self) -> None:
+        """Block until the outputs of every host-tensor ``decode`` issued so far are in host memory."""
+        pool = self._require_pool()
+        with _on_device(pool.device):
+            _lib.raise_for_status(lib.pkv_stepper_host_fence(pool.stepper, _current_stream(pool.device)))
+            torch.cuda.current_stream(pool.device).synchronize()
+
+    def fence_host_outputs(self) -> None:
+        """Make the current stream wait for the output copies of the host-tensor steps issued so far."""
+        pool = self._require_pool()
+        with _on_device(pool.device):
+            _lib.raise_for_status(lib.pkv_stepper_host_fence(pool.stepper, _current_stream(pool.device)))
 
     def _host_buffers(self, n: int):
         """Rows / lengths / token blocks [3, n] for the stepper to fill, and their addresses (reused)."""
@@ -744,18 +793,23 @@ class PagedKVCacheStore:
         return ids
 
     @staticmethod
-    def _check_decode_io(pool: KVPool, n: int, q, k_new, v_new, out):
+    def _check_decode_io(pool: KVPool, n: int, q, k_new, v_new, out, device: torch.device | None = None):
+        dev = pool.device if device is None else device
         if q.dim() != 3 or q.shape[0] != n or q.shape[2] != pool.head_dim:
             raise ValueError("q must be [batch, num_q_heads, head_dim]")
-        if q.dtype != pool.dtype or q.device != pool.device or not q.is_contiguous():
-            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device")
+        if q.shape[1] <= 0 or q.shape[1] % pool.num_kv_heads:
+            raise ValueError("num_q_heads must be a positive multiple of the pool's KV heads")
+        if q.dtype != pool.dtype or q.device != dev or not q.is_contiguous():
+            raise ValueError("q must be a contiguous tensor of the pool's dtype on the pool's device "
+                             "(or all in host memory)")
         shape = (n, pool.num_kv_heads, pool.head_dim)
         for t in (k_new, v_new):
-            if t is not None and (t.shape != shape or t.dtype != pool.dtype or t.device != pool.device
+            if t is not None and (t.shape != shape or t.dtype != pool.dtype or t.device != dev
                                   or not t.is_contiguous()):
-                raise ValueError("k_new/v_new must be contiguous [batch, num_kv_heads, head_dim] pool-dtype tensors")
+                raise ValueError("k_new/v_new must be contiguous [batch, num_kv_heads, head_dim] pool-dtype tensors "
+                                 "on q's device")
         if out is None:
-            return torch.empty_like(q)
+            return torch.empty(q.shape, dtype=q.dtype, pin_memory=True) if dev.type == "cpu" else torch.empty_like(q)
         if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device or not out.is_contiguous():
             raise ValueError("out must be a contiguous tensor shaped and typed like q")
         return out

@@ -212,3 +212,72 @@ def test_decode_rejects_bad_inputs(cuda_device):
         odd.decode_attention(st, 0, q[:1].to(cuda_device))
     with pytest.raises(KeyError):
         store.decode_step([0, 42])
+
+
+@pytest.mark.parametrize("n_seqs", [6, 256])
+def test_host_buffer_decode_equals_device_decode(cuda_device, n_seqs):
+    """``decode`` with pinned host q / k / v / out (the stepper stages them) equals the device-tensor call.
+
+    Steps alternate between one packed host buffer (a single input copy) and
+    three separate tensors (three copies); every step keeps its own inputs and
+    output until ``wait_host_outputs``, so the staging entries are reused while
+    earlier output copies are still in flight.
+    """
+    gen = torch.Generator().manual_seed(11)
+    lengths = torch.randint(64, 2049, (n_seqs,), generator=gen).tolist() if n_seqs > 6 else [1, 15, 16, 17, 300, 2049]
+    hq, hkv, d = 12, 2, 128
+    dev_store, _, _, _, ks, vs = _batch_case(cuda_device, lengths, hq, hkv, d, torch.bfloat16, seed=5)
+    host_store, _, _, _, _, _ = _batch_case(cuda_device, lengths, hq, hkv, d, torch.bfloat16, seed=5)
+    ks, vs = [k[:-1] for k in ks], [v[:-1] for v in vs]  # the cases' own step tokens are not used here
+    ids = np.arange(n_seqs, dtype=np.int64)
+    nq, nk = n_seqs * hq * d, n_seqs * hkv * d
+    want, got, keep = [], [], []
+    for s in range(5):
+        q = torch.randn((n_seqs, hq, d), generator=gen).to(torch.bfloat16)
+        kn = torch.randn((n_seqs, hkv, d), generator=gen).to(torch.bfloat16)
+        vn = torch.randn((n_seqs, hkv, d), generator=gen).to(torch.bfloat16)
+        for b in range(n_seqs):
+            ks[b] = torch.cat([ks[b], kn[b : b + 1]])
+            vs[b] = torch.cat([vs[b], vn[b : b + 1]])
+        out_d, _ = dev_store.decode(ids, q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
+        want.append(out_d)
+        if s % 2 == 0:
+            packed = torch.empty(nq + 2 * nk, dtype=torch.bfloat16).pin_memory()
+            packed[:nq].copy_(q.reshape(-1))
+            packed[nq : nq + nk].copy_(kn.reshape(-1))
+            packed[nq + nk :].copy_(vn.reshape(-1))
+            hq_t, hk_t, hv_t = (packed[:nq].view(q.shape), packed[nq : nq + nk].view(kn.shape),
+                                packed[nq + nk :].view(vn.shape))
+        else:
+            hq_t, hk_t, hv_t = q.pin_memory(), kn.pin_memory(), vn.pin_memory()
+        out_h = torch.full(q.shape, float("nan"), dtype=torch.bfloat16).pin_memory()
+        res, step = host_store.decode(ids, hq_t, hk_t, hv_t, out=out_h)
+        assert res is out_h and step.batch == n_seqs
+        got.append(out_h)
+        keep.append((hq_t, hk_t, hv_t))
+    host_store.wait_host_outputs()
+    torch.cuda.synchronize()
+    for s in range(5):
+        assert torch.equal(got[s], want[s].cpu()), f"step {s}"
+    _close(got[-1], _oracle(q, ks, vs, d ** -0.5))
+    for sid in (0, n_seqs // 2, n_seqs - 1):
+        a = host_store.read_sequence_legacy_cache(sid)
+        assert torch.equal(a[0][0][0].permute(1, 0, 2).cpu(), ks[sid])
+        assert torch.equal(a[0][1][0].permute(1, 0, 2).cpu(), vs[sid])
+    assert host_store.pool.decode_error_flag() == 0
+
+
+def test_host_buffer_decode_rejects_bad_inputs(cuda_device):
+    store, q, kn, vn, _, _ = _batch_case(cuda_device, [4, 5], 12, 2, 128, torch.bfloat16, seed=2)
+    ids = np.arange(2, dtype=np.int64)
+    with pytest.raises(ValueError):
+        store.decode(ids, q, kn, None)
+    with pytest.raises(ValueError):
+        store.decode(ids, q, kn.to(cuda_device), vn)  # mixed host / device
+    with pytest.raises(ValueError):
+        store.decode(ids, q.float(), kn, vn)
+    with pytest.raises(ValueError):
+        store.decode(ids, q, kn, vn, out=torch.empty((2, 12, 64), dtype=torch.bfloat16))
+    out, _ = store.decode(ids, q, kn, vn)  # a pinned output is made
+    store.wait_host_outputs()
+    assert out.device.type == "cpu" and out.is_pinned() and torch.isfinite(out.float()).all()
