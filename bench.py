@@ -62,6 +62,7 @@ L2_BYTES = 126 * 2**20
 FALLBACK_HBM_GBS = 6650.0
 TIMING_EVERY = 4
 FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 
 
 def workload_config(n_gpus: int) -> dict:
@@ -97,15 +98,16 @@ def measured_peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def measured_tensor_peak() -> tuple[float, str]:
-    """Dense bf16 TFLOP/s for a kernel timed on its own (the burst figure)."""
+def measured_tensor_peak(sustained: bool = False) -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst figure for a kernel timed on its own, the sustained one for a long run."""
     p = ROOT / "MEASURED_PEAKS.json"
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["bf16_tflops"]), "measured bf16_tflops (MEASURED_PEAKS.json)"
+            return float(json.loads(p.read_text())[key]), f"measured {key} (MEASURED_PEAKS.json)"
         except (KeyError, ValueError):
             pass
-    return FALLBACK_BF16_TFLOPS, "fallback bf16 TFLOP/s"
+    return (FALLBACK_BF16_TFLOPS_SUSTAINED if sustained else FALLBACK_BF16_TFLOPS), "fallback bf16 TFLOP/s"
 
 
 def tiles_traffic(which: str) -> float | None:
@@ -379,6 +381,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if world == 1 and not args.no_rollout:
         result["rollout"], result["old_policy"] = run_rollout(device, args.seed)
         result["speculative"] = run_speculative(device, args.seed)
+        result["decode_7b"] = run_decode_7b(device, args.seed)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
     return result
@@ -584,6 +587,107 @@ def run_rollout(device: torch.device, seed: int, iters: int = 2) -> tuple[dict, 
     del gen, store, model
     torch.cuda.empty_cache()
     return rollout, old
+
+
+QWEN_7B = dict(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+               num_attention_heads=28, num_key_value_heads=4, max_position_embeddings=32768,
+               rope_theta=1000000.0, tie_word_embeddings=False)
+DECODE_7B_SHAPE = {"seqs": 512, "prompt_lo": 256, "prompt_hi": 4096, "generated": 512, "steps": 16, "warmup": 3,
+                   "temperature": 1.0}
+
+
+def run_decode_7b(device: torch.device, seed: int) -> dict:
+    """Decode steps of a 7B-shape rollout in its KV-bound middle: Qwen2.5-7B architecture (28 layers,
+    28q/4kv heads, head_dim 128, vocab 152064), random-init bf16, 512 sequences each holding a prompt
+    of U[256, 4096] tokens plus 512 generated ones (random K/V in the pages: the step's cost does not
+    depend on their values).  One step = the whole forward for one token per sequence (CUDA graph:
+    fused append + paged decode per layer), fp32 logits and the device sampling kernel.  Reported
+    against the step's HBM bound: weights (all but the input embedding, of which 512 rows are read)
+    + every sequence's K/V + the appended K/V + the fp32 logits, and against the bf16 tensor time of
+    its FLOPs."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from randomrepo_b200.hf import PagedGenerator, kv_geometry, make_store
+
+    sh = DECODE_7B_SHAPE
+    rng = np.random.default_rng(seed)
+    n = sh["seqs"]
+    ctx = rng.integers(sh["prompt_lo"], sh["prompt_hi"] + 1, size=n) + sh["generated"]
+    total_steps = sh["warmup"] + sh["steps"] + 1
+    bs = 16
+    blocks = int(sum(-(-(int(c) + total_steps) // bs) for c in ctx)) + 256
+    torch.cuda.synchronize(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen2ForCausalLM._from_config(Qwen2Config(**QWEN_7B, attn_implementation="sdpa"),
+                                              dtype=torch.bfloat16).eval()
+    store = make_store(model, total_blocks=blocks)
+    for sid, c in enumerate(ctx.tolist()):
+        store.reserve(sid, int(c))
+    store.pool.pool.normal_(generator=torch.Generator(device=device).manual_seed(seed))
+    gen = PagedGenerator(model, store, cuda_graphs=True)
+    gen.reserve_tables(int(ctx.max()) + total_steps + bs)
+    sampler = gen.sampler
+    ids = list(range(n))
+    tok = torch.from_numpy(rng.integers(0, QWEN_7B["vocab_size"], size=n)).to(device)
+
+    def step(t):
+        logits = gen.decode_step(ids, t)
+        return sampler.sample(logits, temperature=sh["temperature"])[0]
+
+    for _ in range(sh["warmup"]):
+        tok = step(tok)
+    lens0 = ctx + sh["warmup"]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record()
+    for _ in range(sh["steps"]):
+        tok = step(tok)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / sh["steps"]
+    if store.pool.decode_error_flag():
+        raise RuntimeError("decode kernels reported a device error")
+
+    layers, hkv, d = kv_geometry(model.config)
+    kv_token = layers * hkv * d * 2 * 2
+    embed = model.get_input_embeddings().weight
+    w_bytes = sum(p.numel() * p.element_size() for p in model.parameters()) - embed.numel() * embed.element_size()
+    w_bytes += n * embed.shape[1] * embed.element_size()
+    kv_bytes = float(np.mean([(lens0 + i + 1).sum() for i in range(sh["steps"])])) * kv_token
+    logit_bytes = n * QWEN_7B["vocab_size"] * 4
+    step_bytes = w_bytes + kv_bytes + n * kv_token + logit_bytes
+    matmul_params = sum(p.numel() for nm, p in model.named_parameters() if p.dim() == 2 and "embed" not in nm)
+    flops = 2.0 * n * matmul_params + 4.0 * QWEN_7B["num_attention_heads"] * d * layers * (kv_bytes / kv_token)
+    hbm, hbm_kind = measured_peaks()
+    tf, tf_kind = measured_tensor_peak(sustained=True)
+    t_hbm = step_bytes / (hbm * 1e9) * 1e3
+    t_tensor = flops / (tf * 1e12) * 1e3
+    res = {
+        "workload": f"decode steps at the Qwen2.5-7B architecture, random-init bf16, {n} sequences of "
+                    f"U[{sh['prompt_lo']},{sh['prompt_hi']}] prompt + {sh['generated']} generated tokens "
+                    f"(mean context {float(ctx.mean()):.0f}), temperature {sh['temperature']}, seed {seed}",
+        "tokens_per_s": n * 1e3 / ms,
+        "ms_per_step": ms,
+        "path": "PagedGenerator.decode_step (CUDA graph: 28 x fused append + paged decode, HF projections / "
+                "MLPs through cuBLAS, fp32 LM head) + DeviceSampler.sample",
+        "bytes_per_step": step_bytes,
+        "bytes_rule": "weights except the input embedding (+ the 512 embedding rows read) + K/V of every "
+                      "sequence's context + the appended K/V + fp32 logits",
+        "kv_bytes_per_step": kv_bytes,
+        "flops_per_step": flops,
+        "hbm_bound_ms": t_hbm,
+        "tensor_bound_ms": t_tensor,
+        "frac_of_hbm_bound": t_hbm / ms,
+        "peaks": f"{hbm_kind} hbm_gbs {hbm}; {tf_kind} {tf}",
+        "timing": f"CUDA events around {sh['steps']} steps after {sh['warmup']} warm-up steps (the first "
+                  f"records the graph); ~{kv_bytes / 1e9:.0f} GB of K/V per step, far above L2",
+        "gpu_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+    }
+    del gen, store, model
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_old_policy(device: torch.device, model, gen, prompts, roll: dict, group: int, iters: int) -> dict:

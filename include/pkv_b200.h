@@ -354,7 +354,7 @@ typedef struct pkv_step_info {
   int32_t n_copies;         /* copy-on-write block copies applied before the step */
   int32_t need_rows;        /* device table rows / columns the step needs */
   int32_t need_cols;
-  int32_t reserved;
+  int32_t need_items;       /* fixed-step mode: the work items a step needs beyond the capacity (else 0) */
   const int32_t* rows;      /* device [batch] */
   const int32_t* seq_lens;  /* device [batch] (tokens incl. the step's token) */
   const int32_t* new_blocks;/* device [batch] */
@@ -386,6 +386,8 @@ int32_t pkv_stepper_bind_tables(pkv_stepper* st, int32_t* block_tables, int32_t 
  * not be rebound while a graph holds such launches.  No counterpart in the
  * reference (its decode loop is eager Python). */
 int32_t pkv_stepper_fix_steps(pkv_stepper* st, int32_t max_batch, int32_t max_items, void* stream);
+/* The fixed-step capacities in force (0, 0 when the mode is off). */
+int32_t pkv_stepper_fixed_capacity(pkv_stepper* st, int32_t* max_batch, int32_t* max_items);
 /* Optional: a host int32 array [n_blocks] of tokens stored per block that the
  * stepper keeps current -- a copy-on-write copy gives the new block its
  * source's count, an uploaded step sets the count of the block each step
@@ -403,7 +405,11 @@ int32_t pkv_stepper_begin(pkv_stepper* st, const int64_t* sequence_ids, int32_t 
                           int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out);
 /* Step phase 2: apply pending updates, plan, upload the descriptor on
  * `stream`.  PKV_ERR_CAPACITY (info->need_rows / need_cols set, nothing
- * launched) asks the caller to grow and rebind the tables and call again. */
+ * launched) asks the caller to grow and rebind the tables and call again.
+ * In fixed-step mode a step with more work items than the capacity fails
+ * with PKV_ERR_UNSUPPORTED and info->need_items set: fix the steps again
+ * with room for them (graphs recorded before hold the old block) and call
+ * again. */
 int32_t pkv_stepper_upload(pkv_stepper* st, void* stream, pkv_step_info* info, int32_t* copies_out,
                            int64_t copies_cap);
 /* Fused append + paged decode attention of the uploaded step for one layer

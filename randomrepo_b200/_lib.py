@@ -70,7 +70,7 @@ class StepInfo(ctypes.Structure):
         ("n_copies", c_int32),
         ("need_rows", c_int32),
         ("need_cols", c_int32),
-        ("reserved", c_int32),
+        ("need_items", c_int32),
         ("rows", c_void_p),
         ("seq_lens", c_void_p),
         ("new_blocks", c_void_p),
@@ -154,6 +154,7 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "pkv_stepper_bind_fill": (c_int32, [c_void_p, c_void_p, c_int64]),
     "pkv_stepper_fix_steps": (c_int32, [c_void_p, c_int32, c_int32, c_void_p]),
+    "pkv_stepper_fixed_capacity": (c_int32, [c_void_p, I32P, I32P]),
     "pkv_stepper_sync": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, I32P, I32P, I32P]),
     "pkv_stepper_begin": (c_int32, [c_void_p, c_void_p, c_int32, POINTER(StepInfo), c_void_p, c_void_p, c_void_p]),
     "pkv_stepper_upload": (c_int32, [c_void_p, c_void_p, POINTER(StepInfo), c_void_p, c_int64]),
@@ -237,11 +238,12 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
-def raise_for_status(status: int, *, key: object | None = None) -> None:
-    """Translate a status into the exception the reference raises for it."""
+def raise_for_status(status: int, *, key: object | None = None, message: str | None = None) -> None:
+    """Translate a status into the exception the reference raises for it (``message``: the
+    failure's text when it was read before later library calls replaced it)."""
     if status == PKV_OK:
         return
-    msg = last_error()
+    msg = last_error() if message is None else message
     if status == PKV_ERR_VALUE:
         raise ValueError(msg)
     if status == PKV_ERR_KEY:

@@ -200,7 +200,9 @@ struct pkv_stepper {
                        int64_t n_combine, bool defer, int64_t pr, int64_t pl) {
     if (n > fx_batch || n_items > fx_items || n_combine > fx_combine) {
       pkv_set_error("decode step exceeds the fixed-step capacity (" + std::to_string(n) + " sequences, " +
-                    std::to_string(n_items) + " work items)");
+                    std::to_string(n_items) + " work items; capacity " + std::to_string(fx_batch) + ", " +
+                    std::to_string(fx_items) + ")");
+      if (n <= fx_batch) out_info->need_items = (int32_t)n_items;
       return PKV_ERR_UNSUPPORTED;
     }
     if (defer && 4 + 2 * (pr + pl) > fx_def_cap) {
@@ -477,6 +479,12 @@ int32_t pkv_stepper_fix_steps(pkv_stepper* st, int32_t max_batch, int32_t max_it
   }
   st->fixed = true;
   st->step_ready = false;
+  return PKV_OK;
+}
+
+int32_t pkv_stepper_fixed_capacity(pkv_stepper* st, int32_t* max_batch, int32_t* max_items) {
+  *max_batch = st->fixed ? st->fx_batch : 0;
+  *max_items = st->fixed ? st->fx_items : 0;
   return PKV_OK;
 }
 

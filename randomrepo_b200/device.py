@@ -89,6 +89,8 @@ class KVPool:
         weakref.finalize(self, lib.pkv_stepper_destroy, self.stepper)
         self.step_serial = 0
         self.fixed_batch = 0  # fixed-step mode capacity (0: off)
+        self.fixed_items = 0
+        self.fixed_serial = 0  # bumped by every fix_steps (graphs hold the fixed block's address)
         self._timing_cap = 0
         self._pending = [ctypes.pointer(ctypes.c_int64()) for _ in range(4)]
         self._bind()
@@ -120,7 +122,10 @@ class KVPool:
         with torch.cuda.device(self.device):
             _lib.raise_for_status(lib.pkv_stepper_fix_steps(self.stepper, int(max_batch), int(max_items),
                                                             _stream_ptr()))
-        self.fixed_batch = int(max_batch)
+        b, i = ctypes.c_int32(), ctypes.c_int32()
+        lib.pkv_stepper_fixed_capacity(self.stepper, ctypes.byref(b), ctypes.byref(i))
+        self.fixed_batch, self.fixed_items = int(b.value), int(i.value)
+        self.fixed_serial += 1
 
     def pending_copies(self) -> int:
         c = self._pending

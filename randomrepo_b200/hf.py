@@ -173,6 +173,7 @@ class PagedGenerator:
         self.cuda_graphs = bool(cuda_graphs)
         self._graphs: dict[int, tuple] = {}  # batch -> (graph, static tokens, static positions, static logits)
         self._graph_tables = 0
+        self._graph_fixed = 0
         self._pads: list[int] = []           # placeholder sequences that pad graphed steps
         self._pad_len: dict[int, int] = {}
         # (padded batch, chunk length) -> (graph, static ids, static positions, static logits, upload buffers)
@@ -390,13 +391,16 @@ class PagedGenerator:
         pads = self._placeholders(nb - n) if nb > n else []
         if pool.fixed_batch < nb:
             pool.fix_steps(max(nb, 2 * pool.fixed_batch))
-            self._graphs.clear()
         step = self.store.decode_step(list(sequence_ids) + pads)
         if pool.tables.data_ptr() != self._graph_tables:
             # Graphs hold the tables' address: a grown (moved) table voids them.
             self._graphs.clear()
             self._ext_graphs.clear()
             self._graph_tables = pool.tables.data_ptr()
+        if pool.fixed_serial != self._graph_fixed:
+            # Decode graphs hold the fixed step block, which a new capacity replaces.
+            self._graphs.clear()
+            self._graph_fixed = pool.fixed_serial
         pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
         tok = tokens.reshape(-1).to(self.device)
         if pads:

@@ -536,15 +536,35 @@ class PagedKVCacheStore:
             st = lib.pkv_stepper_step(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(), k_new.data_ptr(),
                                       v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream, ctypes.byref(info),
                                       p_rows, p_lens, p_tokb, None, 0)
-            if st == _lib.PKV_ERR_CAPACITY:
-                pool.grow(info.need_rows, info.need_cols)
-                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+            if st != _lib.PKV_OK and self._needs_retry(pool, st, info):
+                st = self._upload_retry(pool, stream, info, st)
                 if st == _lib.PKV_OK:
                     st = lib.pkv_stepper_attention(pool.stepper, int(layer), q.data_ptr(), k_new.data_ptr(),
                                                    v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream)
         step = self._finish_step(pool, st, ids, info, host)
         step.committed = True
         return out, step
+
+    @staticmethod
+    def _needs_retry(pool: KVPool, st: int, info) -> bool:
+        """A step that failed only for want of table room or of fixed-step work-item capacity."""
+        return st == _lib.PKV_ERR_CAPACITY or (st == _lib.PKV_ERR_UNSUPPORTED and info.need_items > 0)
+
+    @staticmethod
+    def _upload_retry(pool: KVPool, stream: int, info, st: int) -> int:
+        """Make the room a begun step asked for, then upload it again (until it fits or fails otherwise)."""
+        for _ in range(4):
+            if st == _lib.PKV_ERR_CAPACITY:
+                pool.grow(info.need_rows, info.need_cols)
+            elif st == _lib.PKV_ERR_UNSUPPORTED and info.need_items > 0:
+                # Fixed-step mode: a new block with room for the step (graphs
+                # recorded on the old one are dropped by their owners).
+                pool.fix_steps(pool.fixed_batch, max_items=int(info.need_items * 5 // 4 + 64))
+            else:
+                return st
+            info.need_items = 0
+            st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+        return st
 
     def _decode_host(self, pool: KVPool, ids, n: int, q, k_new, v_new, layer: int, scale, out):
         """``decode`` with host tensors: inputs staged and output returned by the native stepper."""
@@ -563,9 +583,8 @@ class PagedKVCacheStore:
             st = lib.pkv_stepper_step_host(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(),
                                            k_new.data_ptr(), v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream,
                                            ctypes.byref(info), p_rows, p_lens, p_tokb)
-            if st == _lib.PKV_ERR_CAPACITY:
-                pool.grow(info.need_rows, info.need_cols)
-                st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+            if st != _lib.PKV_OK and self._needs_retry(pool, st, info):
+                st = self._upload_retry(pool, stream, info, st)
                 if st == _lib.PKV_OK:
                     st = lib.pkv_stepper_attention_host(pool.stepper, int(layer), q.shape[1], sc, out.data_ptr(),
                                                         stream)
@@ -613,9 +632,8 @@ class PagedKVCacheStore:
             with _on_device(pool.device):
                 stream = _current_stream(pool.device)
                 st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
-                if st == _lib.PKV_ERR_CAPACITY:
-                    pool.grow(info.need_rows, info.need_cols)
-                    st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
+                if st != _lib.PKV_OK and self._needs_retry(pool, st, info):
+                    st = self._upload_retry(pool, stream, info, st)
         return self._finish_step(pool, st, ids, info, host)
 
     def decode_attention(self, step: DecodeStep, layer: int, q: torch.Tensor, k_new: torch.Tensor | None = None,
@@ -819,11 +837,13 @@ class PagedKVCacheStore:
         if st != _lib.PKV_OK:
             # The appends made before the failure stay (as with the reference's
             # sequential append_tokens); their tokens have no stored K/V yet.
+            # (The message is read first: the sync below makes library calls.)
+            msg = _lib.last_error()
             k = int(info.batch)
             bs = self.allocator.block_size_tokens
             self._sync()
             self._block_fill[tok_blocks[:k]] = (lens[:k] - 1) % bs + 1
-            _lib.raise_for_status(st)
+            _lib.raise_for_status(st, message=msg)
         # Block fills of the step (and of its copy-on-write copies) were set by
         # the native stepper.
         pool.step_serial += 1

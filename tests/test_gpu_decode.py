@@ -281,3 +281,20 @@ def test_host_buffer_decode_rejects_bad_inputs(cuda_device):
     out, _ = store.decode(ids, q, kn, vn)  # a pinned output is made
     store.wait_host_outputs()
     assert out.device.type == "cpu" and out.is_pinned() and torch.isfinite(out.float()).all()
+
+
+def test_fixed_step_mode_grows_its_work_item_capacity(cuda_device):
+    """Fixed-step mode (the descriptor block CUDA graphs replay) with too small a work-item capacity:
+    the step reports the items it needs, the store fixes the steps again and the results are unchanged."""
+    lengths = [3000, 2049, 700, 64, 17, 1]
+    store, q, kn, vn, ks, vs = _batch_case(cuda_device, lengths, 12, 2, 128, torch.bfloat16, seed=8)
+    pool = store.pool
+    pool.fix_steps(len(lengths), max_items=len(lengths))  # one item per sequence: far too few
+    serial, cap = pool.fixed_serial, pool.fixed_items
+    assert cap == len(lengths)
+    step = store.decode_step(list(range(len(lengths))))
+    assert step.n_items > cap and pool.fixed_items >= step.n_items and pool.fixed_serial == serial + 1
+    out = store.decode_attention(step, 0, q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
+    torch.cuda.synchronize()
+    _close(out, _oracle(q, ks, vs, 128 ** -0.5))
+    assert pool.decode_error_flag() == 0
