@@ -373,7 +373,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_tiles:
-        del store, q, kn, vn, out, inp_d
+        del store, q, kn, vn, out, q_h, k_h, v_h, inp_h, out_h
         torch.cuda.empty_cache()
         result["tensor_tiles"] = run_tensor_tiles(device, args.seed, args.steps, args.warmup)
     if world == 1 and not args.no_tiles:
