@@ -420,6 +420,21 @@ def _tile_workload(device: torch.device, hq: int, hkv: int, d: int, seqs, seed: 
     return store, q, plan, torch.from_numpy(plan.records).to(device), flops, kv_bytes
 
 
+class _L2Flush:
+    """Empties L2 between timed launches: writes a buffer twice the size of L2, then reads a second
+    one of that size, so that the written lines have gone back to HBM before the timed launch
+    starts (otherwise their write-back would land on the timed kernel's HBM traffic)."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.w = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+        self.r = torch.zeros(2 * L2_BYTES // 4, dtype=torch.int32, device=device)
+        self.sink = torch.empty(1, dtype=torch.int64, device=device)
+
+    def __call__(self) -> None:
+        self.w.zero_()
+        torch.sum(self.r, dim=0, keepdim=True, out=self.sink)
+
+
 def _time_prefill(store, q, plan, records, steps: int, warmup: int) -> tuple[float, int]:
     """Mean device ms of one pkv_prefill_attention launch (L2 flushed before each) and launches timed."""
     pool = store.pool
@@ -427,11 +442,11 @@ def _time_prefill(store, q, plan, records, steps: int, warmup: int) -> tuple[flo
     scale = q.shape[2] ** -0.5
     for _ in range(warmup):
         pool.prefill(0, q, plan, records, q.shape[1], scale, out)
-    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=q.device)
+    flush = _L2Flush(q.device)
     launches0 = pool.launch_count()
     times = []
     for _ in range(steps):
-        flush.zero_()
+        flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         pool.prefill(0, q, plan, records, q.shape[1], scale, out)
@@ -885,11 +900,11 @@ def run_vocab_rows(device: torch.device, seed: int, steps: int, warmup: int) -> 
     dl = tl[:, :k] + 0.7 * torch.randn(b, k, vocab, device=device, generator=g)
     dtok = torch.argmax(dl, dim=-1)
     nd = torch.full((b,), k, dtype=torch.int32, device=device)
-    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+    flush = _L2Flush(device)
 
     ts = []
     for i in range(warmup + n):
-        flush.zero_()
+        flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         _, _, n_out, n_acc = s.spec_accept(tl, dl, dtok, nd, do_sample=True)
