@@ -13,8 +13,11 @@ Arms:
   ours (default)     ``value``: device-timed steps through PagedKVCacheStore
                      (host allocator step + one descriptor upload + the fused
                      sm_100a decode kernel) with inputs resident in HBM;
-                     ``e2e``: the same steps with q/k/v copied from pinned host
-                     memory and the output copied back inside the timed region.
+                     ``e2e``: the same steps given host q/k/v (page-locked,
+                     write-combined) and a page-locked host output, every
+                     step's copies inside the timed region (the stepper's host
+                     path overlaps them with the neighbouring steps' kernels);
+                     median of three timed regions.
   --impl reference   the reference's CPU path (the oracle's restatement of the
                      resident-cache decode step) on the host cores, rank 0 only.
 
@@ -26,7 +29,9 @@ the measured HBM bandwidth, each timed alone with CUDA events and L2 flushed.
 
 It also carries ``vocab_rows``: the fused log-softmax + gather, sampling and
 speculative accept kernels over Qwen2's 151 936-column logits rows against
-the measured HBM bandwidth; ``rollout``: a GRPO rollout of the Qwen2.5-1.5B
+the measured HBM bandwidth; ``decode_7b``: whole decode steps of the
+Qwen2.5-7B architecture for 512 sequences of ~2.8k tokens against the step's
+HBM bound; ``rollout``: a GRPO rollout of the Qwen2.5-1.5B
 architecture (random-init bf16, 4 prompts x group 8, 128 new tokens) through
 PagedGenerator with CUDA-graph decode steps, next to stock HF generate on the
 same model and batch; ``old_policy``: that rollout's old-policy
@@ -62,6 +67,7 @@ L2_BYTES = 126 * 2**20
 FALLBACK_HBM_GBS = 6650.0
 TIMING_EVERY = 4
 FALLBACK_BF16_TFLOPS = 1590.0
+E2E_REPEATS = 3
 FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 
 
@@ -288,8 +294,10 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     # stream ahead of the step descriptor and the output back out on a second
     # stream, so step i+1's input copy and step i-1's output copy run while
     # step i's kernels do.  The region ends after the last output copy.
+    from randomrepo_b200 import host_input_tensor
+
     nq, nk = q.numel(), kn.numel()
-    inp_h = torch.empty(nq + 2 * nk, dtype=q.dtype).pin_memory()
+    inp_h = host_input_tensor((nq + 2 * nk,), q.dtype)  # page-locked, write-combined
     inp_h[:nq].copy_(q.reshape(-1).cpu())
     inp_h[nq:nq + nk].copy_(kn.reshape(-1).cpu())
     inp_h[nq + nk:].copy_(vn.reshape(-1).cpu())
@@ -303,20 +311,27 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     for _ in range(args.warmup):
         e2e_step()
     store.wait_host_outputs()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    store.fence_host_outputs()  # every output copy issued in the region ends inside it
-    e1.record()
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    # Three timed regions of K steps each: PCIe and host time on these shared
+    # hosts vary from run to run (other tenants), so the median is reported
+    # and all three are listed.
+    e2e_runs = []
+    for _ in range(E2E_REPEATS):
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        store.fence_host_outputs()  # every output copy issued in the region ends inside it
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        e2e_runs.append(ms)
+    e2e_ms = statistics.median(e2e_runs)
     barrier()
     h2d = inp_h.numel() * inp_h.element_size() + (6 * SEQS + 1) * 4
     d2h = out_h.numel() * out_h.element_size()
@@ -361,13 +376,15 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         },
         "e2e": {
             "value": world * SEQS * 1000.0 / (e2e_ms / args.steps),
+            "runs_tokens_per_s": [world * SEQS * 1000.0 / (ms / args.steps) for ms in e2e_runs],
+            "timing": f"median of {E2E_REPEATS} timed regions of {args.steps} steps (max over ranks each)",
             "unit": "tokens/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "path": "PagedKVCacheStore.decode given pinned host q/k/v (one packed buffer) and a pinned host "
-                    "output: pkv_stepper_step_host copies the inputs in on the stepper's copy stream with the step "
-                    "descriptor and the output out on a second stream, every step; the region ends after the last "
-                    "output copy",
+            "path": "PagedKVCacheStore.decode given host q/k/v (one packed page-locked write-combined buffer "
+                    "from host_input_tensor) and a page-locked host output: pkv_stepper_step_host copies the "
+                    "inputs in on the stepper's copy stream with the step descriptor and the output out on a "
+                    "second stream, every step; the region ends after the last output copy",
         },
         "gpu_launches": launches,
         "clocks": clocks.summary(),

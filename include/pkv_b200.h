@@ -451,6 +451,15 @@ int32_t pkv_stepper_attention_host(pkv_stepper* st, int32_t layer, int32_t num_q
 /* Make `stream` wait for every output copy of the host steps issued so far;
  * once `stream` has run past this point their out buffers hold the results. */
 int32_t pkv_stepper_host_fence(pkv_stepper* st, void* stream);
+/* Page-locked host memory for a host step's inputs (q / k_new / v_new):
+ * write-combined unless write_combined is 0.  The GPU reads write-combined
+ * memory over PCIe without snooping the host's caches, which on the hosts
+ * measured here doubled host-to-device bandwidth for 1-16 MB copies (about
+ * 50 GB/s against 16-38 GB/s from cacheable page-locked memory); host reads
+ * of it are slow, so use it only for data the host writes and the GPU reads,
+ * and default page-locked memory for outputs.  Free with pkv_host_free. */
+int32_t pkv_host_alloc(int64_t bytes, int32_t write_combined, void** ptr_out);
+int32_t pkv_host_free(void* ptr);
 /* The copy-on-write (src, dst) block pairs the last sync / upload applied
  * (*n_pairs gets their count; up to `capacity` pairs are written). */
 int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs);

@@ -25,6 +25,7 @@ _EXPORTS = {
     "PagedKVAllocator": "paged_kv",
     "PagedKVCacheStore": "paged_kv",
     "PagedKVSequenceView": "paged_kv",
+    "host_input_tensor": "paged_kv",
     "PagedGenerator": "hf",
     "SamplingConfig": "hf",
     "StepGather": "sharding",

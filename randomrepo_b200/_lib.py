@@ -173,6 +173,8 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "pkv_stepper_attention_host": (c_int32, [c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "pkv_stepper_host_fence": (c_int32, [c_void_p, c_void_p]),
+    "pkv_host_alloc": (c_int32, [c_int64, c_int32, POINTER(c_void_p)]),
+    "pkv_host_free": (c_int32, [c_void_p]),
     "pkv_stepper_copies": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
     "pkv_stepper_error": (c_int32, [c_void_p, I32P]),
     "pkv_stepper_launches": (c_int64, [c_void_p]),

@@ -67,26 +67,33 @@ struct pkv_stepper {
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t copy_ev = nullptr, reuse_ev = nullptr;
   // Host-buffer steps (pkv_stepper_step_host): device staging of q / k / v
-  // and of the output in kIo entries used in turn.  A step's inputs cross on
-  // copy_stream ahead of its descriptor (so the one wait on copy_ev covers
-  // both), its output crosses on d2h_stream after its kernels; `used` marks
-  // the kernels that read an entry's inputs and wrote its output, `read` the
-  // copy of that output to the host.
-  static constexpr int kIo = 2;
+  // and of the output in kIo entries used in turn, in rounds of kIoRound.  A
+  // step's inputs cross on copy_stream ahead of its descriptor (so the one
+  // wait on copy_ev covers both), its output crosses on d2h_stream after its
+  // kernels (k_done).  Reuse is guarded once per round, a round behind: the
+  // first step of round r records the kernels and output copies enqueued so
+  // far (in_ev / out_ev [r % 2]) and waits for those recorded at the start
+  // of round r - 1, i.e. for round r - 2, the last one that used these
+  // entries -- long finished, so the guard never stalls the pipeline.  A step
+  // costs three CUDA calls beyond a device-buffer step.
+  static constexpr int kIoRound = kRing;
+  static constexpr int kIo = 2 * kIoRound;
   struct Io {
     char* in = nullptr;
     char* out = nullptr;
     int64_t in_cap = 0, out_cap = 0;
-    cudaEvent_t used = nullptr, read = nullptr;
-    bool used_set = false, read_set = false;
   };
   Io io[kIo];
   int io_next = 0;
   int io_cur = -1;        // entry of the step whose inputs were staged last
-  int io_last_read = -1;  // entry of the last output copy issued
+  int64_t io_in_round = 0;   // rounds begun on the staging side
+  int64_t io_cur_round = 0;  // round of the entry staged last
+  int64_t out_ev_round[2] = {-1, -1};  // round whose start each out_ev records
+  bool io_out_issued = false;
   int64_t io_q_bytes = 0, io_kv_bytes = 0;
   int32_t io_batch = 0;
   cudaStream_t d2h_stream = nullptr;
+  cudaEvent_t in_ev[2] = {}, out_ev[2] = {}, k_done = nullptr, fence_ev = nullptr;
   bool round_open = false;  // the ring's last slot was taken and not yet copied out
   std::vector<int32_t> rows_h, lens_h, newb_h, tokb_h, plan_h, upd_h;
   std::vector<int32_t> last_copies;  // (src, dst) pairs applied by the last sync / upload
@@ -136,11 +143,11 @@ struct pkv_stepper {
       cudaStreamDestroy(d2h_stream);
     }
     for (auto& e : io) {
-      if (e.used) cudaEventDestroy(e.used);
-      if (e.read) cudaEventDestroy(e.read);
       if (e.in) cudaFree(e.in);
       if (e.out) cudaFree(e.out);
     }
+    for (auto ev : {in_ev[0], in_ev[1], out_ev[0], out_ev[1], k_done, fence_ev})
+      if (ev) cudaEventDestroy(ev);
     for (auto& s : slot) {
       if (s.host) cudaFreeHost(s.host);
       if (s.dev) cudaFree(s.dev);
@@ -287,8 +294,18 @@ struct pkv_stepper {
 
   // Copy a step's host q / k / v into the next staging entry on copy_stream
   // (one copy when the three lie back to back in host memory).
-  int32_t stage_inputs(int32_t n, int32_t num_q_heads, const void* q, const void* k, const void* v) {
+  int32_t ensure_host_io() {
+    if (d2h_stream) return PKV_OK;
+    int32_t st = cuda_status(cudaStreamCreateWithFlags(&d2h_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (cudaEvent_t* ev : {&in_ev[0], &in_ev[1], &out_ev[0], &out_ev[1], &k_done, &fence_ev})
+      if (!st) st = cuda_status(cudaEventCreateWithFlags(ev, cudaEventDisableTiming), "cudaEventCreate");
+    return st;
+  }
+
+  int32_t stage_inputs(int32_t n, int32_t num_q_heads, const void* q, const void* k, const void* v,
+                       cudaStream_t stream) {
     if (int32_t e = ensure_copy_stream()) return e;
+    if (int32_t e = ensure_host_io()) return e;
     const int64_t eb = geom.dtype == PKV_F32 ? 4 : 2;
     const int64_t qb = (int64_t)n * num_q_heads * geom.head_dim * eb;
     const int64_t kb = k ? (int64_t)n * geom.num_kv_heads * geom.head_dim * eb : 0;
@@ -310,14 +327,14 @@ struct pkv_stepper {
       e.in_cap = in_cap;
       e.out_cap = out_cap;
     }
-    if (!e.used) {
-      int32_t st = cuda_status(cudaEventCreateWithFlags(&e.used, cudaEventDisableTiming), "cudaEventCreate");
-      if (!st) st = cuda_status(cudaEventCreateWithFlags(&e.read, cudaEventDisableTiming), "cudaEventCreate");
+    // First entry of a round r: record the kernels enqueued so far (through
+    // round r - 1) and let this round's copies wait for round r - 2's.
+    if (io_next % kIoRound == 0) {
+      const int64_t r = io_in_round++;
+      int32_t st = PKV_OK;
+      if (r >= 1) st = cuda_status(cudaEventRecord(in_ev[r % 2], stream), "cudaEventRecord");
+      if (!st && r >= 2) st = cuda_status(cudaStreamWaitEvent(copy_stream, in_ev[(r - 1) % 2], 0), "cudaStreamWaitEvent");
       if (st) return st;
-    }
-    // The kernels that last read this entry's inputs have finished.
-    if (e.used_set) {
-      if (int32_t st = cuda_status(cudaStreamWaitEvent(copy_stream, e.used, 0), "cudaStreamWaitEvent")) return st;
     }
     const char* qc = static_cast<const char*>(q);
     int32_t st;
@@ -330,6 +347,7 @@ struct pkv_stepper {
     }
     if (st) return st;
     io_cur = io_next;
+    io_cur_round = io_in_round - 1;
     io_next = (io_next + 1) % kIo;
     io_q_bytes = qb;
     io_kv_bytes = kb;
@@ -703,29 +721,34 @@ int32_t pkv_stepper_attention_host(pkv_stepper* st, int32_t layer, int32_t num_q
     return PKV_ERR_ARG;
   }
   auto cs = static_cast<cudaStream_t>(stream);
-  auto& e = st->io[st->io_cur];
+  const int ei = st->io_cur;
+  auto& e = st->io[ei];
   st->io_cur = -1;
-  if (!st->d2h_stream) {
-    int32_t s = cuda_status(cudaStreamCreateWithFlags(&st->d2h_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  // First entry of a round r: record the output copies enqueued so far
+  // (through round r - 1) and let this round's kernels wait for round r - 2's
+  // (recorded at the start of round r - 1; if that start was never reached --
+  // a step abandoned after staging -- wait for every copy enqueued so far).
+  if (ei % pkv_stepper::kIoRound == 0 && st->io_out_issued) {
+    const int64_t r = st->io_cur_round;
+    const int slot = (int)(r % 2), prev = 1 - slot;
+    int32_t s = cuda_status(cudaEventRecord(st->out_ev[slot], st->d2h_stream), "cudaEventRecord");
+    const bool have_prev = st->out_ev_round[prev] == r - 1;
+    if (!s) s = cuda_status(cudaStreamWaitEvent(cs, have_prev ? st->out_ev[prev] : st->out_ev[slot], 0),
+                            "cudaStreamWaitEvent");
     if (s) return s;
-  }
-  // The copy of this entry's previous output to the host has finished.
-  if (e.read_set) {
-    if (int32_t s = cuda_status(cudaStreamWaitEvent(cs, e.read, 0), "cudaStreamWaitEvent")) return s;
+    st->out_ev_round[slot] = r;
   }
   const char* k = st->io_kv_bytes ? e.in + st->io_q_bytes : nullptr;
   const char* v = st->io_kv_bytes ? e.in + st->io_q_bytes + st->io_kv_bytes : nullptr;
   int32_t s = pkv_stepper_attention(st, layer, e.in, k, v, num_q_heads, scale, e.out, stream);
   if (s) return s;
-  s = cuda_status(cudaEventRecord(e.used, cs), "cudaEventRecord");
-  if (!s) s = cuda_status(cudaStreamWaitEvent(st->d2h_stream, e.used, 0), "cudaStreamWaitEvent");
+  s = cuda_status(cudaEventRecord(st->k_done, cs), "cudaEventRecord");
+  if (!s) s = cuda_status(cudaStreamWaitEvent(st->d2h_stream, st->k_done, 0), "cudaStreamWaitEvent");
   if (!s)
     s = cuda_status(cudaMemcpyAsync(out_host, e.out, st->io_q_bytes, cudaMemcpyDeviceToHost, st->d2h_stream),
                     "D2H out");
-  if (!s) s = cuda_status(cudaEventRecord(e.read, st->d2h_stream), "cudaEventRecord");
   if (s) return s;
-  e.used_set = e.read_set = true;
-  st->io_last_read = (int)(&e - st->io);
+  st->io_out_issued = true;
   return PKV_OK;
 }
 
@@ -742,18 +765,36 @@ int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int3
   }
   int32_t s = pkv_stepper_begin(st, sequence_ids, n, info, rows_out, lens_out, token_blocks_out);
   if (s) return s;
-  s = st->stage_inputs(n, num_q_heads, q_host, k_new_host, v_new_host);
+  s = st->stage_inputs(n, num_q_heads, q_host, k_new_host, v_new_host, static_cast<cudaStream_t>(stream));
   if (s) return s;
   s = pkv_stepper_upload(st, stream, info, nullptr, 0);
   if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention_host
   return pkv_stepper_attention_host(st, layer, num_q_heads, scale, out_host, stream);
 }
 
+int32_t pkv_host_alloc(int64_t bytes, int32_t write_combined, void** ptr_out) {
+  pkv_clear_error();
+  if (bytes <= 0 || !ptr_out) {
+    pkv_set_error("pkv_host_alloc: bytes must be positive and ptr_out non-NULL");
+    return PKV_ERR_ARG;
+  }
+  *ptr_out = nullptr;
+  return cuda_status(cudaHostAlloc(ptr_out, (size_t)bytes,
+                                   write_combined ? cudaHostAllocWriteCombined : cudaHostAllocDefault),
+                     "cudaHostAlloc");
+}
+
+int32_t pkv_host_free(void* ptr) {
+  pkv_clear_error();
+  return ptr ? cuda_status(cudaFreeHost(ptr), "cudaFreeHost") : PKV_OK;
+}
+
 int32_t pkv_stepper_host_fence(pkv_stepper* st, void* stream) {
   pkv_clear_error();
-  if (st->io_last_read < 0) return PKV_OK;
-  return cuda_status(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), st->io[st->io_last_read].read, 0),
-                     "cudaStreamWaitEvent");
+  if (!st->io_out_issued) return PKV_OK;
+  int32_t s = cuda_status(cudaEventRecord(st->fence_ev, st->d2h_stream), "cudaEventRecord");
+  return s ? s : cuda_status(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), st->fence_ev, 0),
+                             "cudaStreamWaitEvent");
 }
 
 int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity, int64_t* n_pairs) {

@@ -63,6 +63,31 @@ class _on_device:
             torch.cuda.set_device(self._prev)
 
 
+def _is_i64_vector(a) -> bool:
+    return type(a) is np.ndarray and a.dtype == np.int64 and a.ndim == 1 and a.flags.c_contiguous
+
+
+class _PointerCache:
+    """Data addresses of the int64 index arrays a decode loop hands over every step (usually the
+    same array objects): ``ndarray.ctypes.data`` costs about a microsecond per call.  Entries keep
+    their array alive, so an address stays valid while it is cached; at most 16 are kept."""
+
+    __slots__ = ("_entries",)
+
+    def __init__(self) -> None:
+        self._entries: dict[int, tuple[np.ndarray, int]] = {}
+
+    def __call__(self, a: np.ndarray) -> int:
+        e = self._entries.get(id(a))
+        if e is not None and e[0] is a:
+            return e[1]
+        if len(self._entries) >= 16:
+            self._entries.clear()
+        ptr = a.ctypes.data
+        self._entries[id(a)] = (a, ptr)
+        return ptr
+
+
 @dataclass(frozen=True, slots=True)
 class PagedKVSequenceView:
     """Read-only sequence mapping inside the paged-KV allocator (paged_kv.py:11-22)."""
@@ -93,6 +118,7 @@ class PagedKVAllocator:
         self.total_blocks = int(total_blocks)
         self.block_size_tokens = int(block_size_tokens)
         self._view_buf = np.zeros(64, dtype=np.int32)
+        self._ptr = _PointerCache()
         weakref.finalize(self, lib.pkv_allocator_destroy, handle)
 
     def _stats(self) -> _lib.AllocatorStats:
@@ -203,11 +229,16 @@ class PagedKVAllocator:
 
         No reference counterpart: it rolls back rejected speculative drafts.
         """
-        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
-        counts = np.ascontiguousarray(np.atleast_1d(np.asarray(token_counts, dtype=np.int64)))
+        if _is_i64_vector(sequence_ids) and _is_i64_vector(token_counts):
+            ids, counts = sequence_ids, token_counts
+            p_ids, p_counts = self._ptr(ids), self._ptr(counts)
+        else:
+            ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
+            counts = np.ascontiguousarray(np.atleast_1d(np.asarray(token_counts, dtype=np.int64)))
+            p_ids, p_counts = ids.ctypes.data, counts.ctypes.data
         if ids.shape != counts.shape:
             raise ValueError("sequence_ids and token_counts must have the same length")
-        _lib.raise_for_status(lib.pkv_allocator_truncate(self._handle, ids.ctypes.data, counts.ctypes.data, ids.size))
+        _lib.raise_for_status(lib.pkv_allocator_truncate(self._handle, p_ids, p_counts, ids.size))
 
     def refcount(self, block_id: int) -> int:
         out = ctypes.c_int32()
@@ -271,6 +302,25 @@ class PrefillStep:
     plan: PrefillPlan | None
     slots: torch.Tensor | None
     records: torch.Tensor | None
+
+
+def host_input_tensor(shape, dtype: torch.dtype, *, write_combined: bool = True) -> torch.Tensor:
+    """A CPU tensor in page-locked host memory from ``pkv_host_alloc``, for the q / k / v a host
+    hands to ``PagedKVCacheStore.decode``: write-combined by default, which the GPU reads over
+    PCIe without snooping the host's caches (about twice the host-to-device bandwidth of
+    cacheable page-locked memory on the hosts measured here).  Reading it back on the host is
+    slow; keep outputs in ordinary page-locked memory.  Freed when the tensor is collected."""
+    n = 1
+    for x in shape:
+        n *= int(x)
+    itemsize = torch.empty((), dtype=dtype).element_size()
+    nbytes = max(1, n * itemsize)
+    ptr = ctypes.c_void_p()
+    _lib.raise_for_status(lib.pkv_host_alloc(nbytes, 1 if write_combined else 0, ctypes.byref(ptr)))
+    raw = (ctypes.c_char * nbytes).from_address(ptr.value)
+    t = torch.frombuffer(raw, dtype=torch.uint8)[: n * itemsize].view(dtype).view(*shape)
+    weakref.finalize(raw, lib.pkv_host_free, ptr.value)  # runs once no tensor over ``raw`` is left
+    return t
 
 
 class PagedKVCacheStore:
@@ -515,12 +565,14 @@ class PagedKVCacheStore:
         """
         pool = self._pool if self._pool is not None else self._require_pool()
         ids = sequence_ids
-        if not (type(ids) is np.ndarray and ids.dtype == np.int64 and ids.ndim == 1 and ids.flags.c_contiguous
-                and ids.size):
+        if _is_i64_vector(ids) and ids.size:
+            p_ids = self.allocator._ptr(ids)
+        else:
             ids = self._step_ids(sequence_ids)
+            p_ids = ids.ctypes.data
         n = ids.size
         if q.device.type == "cpu":
-            return self._decode_host(pool, ids, n, q, k_new, v_new, layer, scale, out)
+            return self._decode_host(pool, ids, p_ids, n, q, k_new, v_new, layer, scale, out)
         # The checks of q / k / v / out are skipped when the same tensor
         # objects come back (a decode loop reusing its buffers).
         chk = self._io_checked
@@ -533,7 +585,7 @@ class PagedKVCacheStore:
         with _on_device(pool.device):
             stream = _current_stream(pool.device)
             sc = float(scale if scale is not None else pool.head_dim ** -0.5)
-            st = lib.pkv_stepper_step(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(), k_new.data_ptr(),
+            st = lib.pkv_stepper_step(pool.stepper, p_ids, n, int(layer), q.data_ptr(), k_new.data_ptr(),
                                       v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream, ctypes.byref(info),
                                       p_rows, p_lens, p_tokb, None, 0)
             if st != _lib.PKV_OK and self._needs_retry(pool, st, info):
@@ -566,7 +618,7 @@ class PagedKVCacheStore:
             st = lib.pkv_stepper_upload(pool.stepper, stream, ctypes.byref(info), None, 0)
         return st
 
-    def _decode_host(self, pool: KVPool, ids, n: int, q, k_new, v_new, layer: int, scale, out):
+    def _decode_host(self, pool: KVPool, ids, p_ids: int, n: int, q, k_new, v_new, layer: int, scale, out):
         """``decode`` with host tensors: inputs staged and output returned by the native stepper."""
         chk = self._io_checked
         if (out is None or not chk or chk[0] is not q or chk[1] is not k_new or chk[2] is not v_new
@@ -580,7 +632,7 @@ class PagedKVCacheStore:
         with _on_device(pool.device):
             stream = _current_stream(pool.device)
             sc = float(scale if scale is not None else pool.head_dim ** -0.5)
-            st = lib.pkv_stepper_step_host(pool.stepper, ids.ctypes.data, n, int(layer), q.data_ptr(),
+            st = lib.pkv_stepper_step_host(pool.stepper, p_ids, n, int(layer), q.data_ptr(),
                                            k_new.data_ptr(), v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream,
                                            ctypes.byref(info), p_rows, p_lens, p_tokb)
             if st != _lib.PKV_OK and self._needs_retry(pool, st, info):

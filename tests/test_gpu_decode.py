@@ -218,11 +218,16 @@ def test_decode_rejects_bad_inputs(cuda_device):
 def test_host_buffer_decode_equals_device_decode(cuda_device, n_seqs):
     """``decode`` with pinned host q / k / v / out (the stepper stages them) equals the device-tensor call.
 
-    Steps alternate between one packed host buffer (a single input copy) and
-    three separate tensors (three copies); every step keeps its own inputs and
-    output until ``wait_host_outputs``, so the staging entries are reused while
-    earlier output copies are still in flight.
+    Steps alternate between one packed host buffer (a single input copy; from
+    ``host_input_tensor``, write-combined or not) and three separate tensors
+    (three copies); every step keeps its own inputs and
+    output until ``wait_host_outputs``.  Twenty steps go one and a quarter times
+    round the stepper's sixteen staging entries (guarded in rounds of eight),
+    so entries are reused while earlier output copies may still be in flight.
     """
+    STEPS = 20
+    from randomrepo_b200 import host_input_tensor
+
     gen = torch.Generator().manual_seed(11)
     lengths = torch.randint(64, 2049, (n_seqs,), generator=gen).tolist() if n_seqs > 6 else [1, 15, 16, 17, 300, 2049]
     hq, hkv, d = 12, 2, 128
@@ -232,7 +237,7 @@ def test_host_buffer_decode_equals_device_decode(cuda_device, n_seqs):
     ids = np.arange(n_seqs, dtype=np.int64)
     nq, nk = n_seqs * hq * d, n_seqs * hkv * d
     want, got, keep = [], [], []
-    for s in range(5):
+    for s in range(STEPS):
         q = torch.randn((n_seqs, hq, d), generator=gen).to(torch.bfloat16)
         kn = torch.randn((n_seqs, hkv, d), generator=gen).to(torch.bfloat16)
         vn = torch.randn((n_seqs, hkv, d), generator=gen).to(torch.bfloat16)
@@ -242,7 +247,7 @@ def test_host_buffer_decode_equals_device_decode(cuda_device, n_seqs):
         out_d, _ = dev_store.decode(ids, q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
         want.append(out_d)
         if s % 2 == 0:
-            packed = torch.empty(nq + 2 * nk, dtype=torch.bfloat16).pin_memory()
+            packed = host_input_tensor((nq + 2 * nk,), torch.bfloat16, write_combined=s % 4 == 0)
             packed[:nq].copy_(q.reshape(-1))
             packed[nq : nq + nk].copy_(kn.reshape(-1))
             packed[nq + nk :].copy_(vn.reshape(-1))
@@ -257,7 +262,7 @@ def test_host_buffer_decode_equals_device_decode(cuda_device, n_seqs):
         keep.append((hq_t, hk_t, hv_t))
     host_store.wait_host_outputs()
     torch.cuda.synchronize()
-    for s in range(5):
+    for s in range(STEPS):
         assert torch.equal(got[s], want[s].cpu()), f"step {s}"
     _close(got[-1], _oracle(q, ks, vs, d ** -0.5))
     for sid in (0, n_seqs // 2, n_seqs - 1):
