@@ -429,7 +429,8 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
  * v_new [n][num_kv_heads][head_dim], the pool's dtype; k_new / v_new both
  * NULL for attention without the append).  The stepper stages the inputs in
  * device buffers of its own: they cross on its copy stream ahead of the step
- * descriptor (one copy when q, k_new and v_new lie back to back), the
+ * descriptor (one copy when inputs_packed is 1: q, k_new and v_new are
+ * consecutive parts of ONE host allocation, back to back; else three), the
  * output crosses on a second stream of the stepper after the step's
  * kernels, so a step's input copy and the previous step's output copy run
  * while the kernels of the step between them do.  Host pointers are read and
@@ -442,7 +443,7 @@ int32_t pkv_stepper_step(pkv_stepper* st, const int64_t* sequence_ids, int32_t n
  * pkv_stepper_attention_host. */
 int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer,
                               const void* q_host, const void* k_new_host, const void* v_new_host,
-                              int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
+                              int32_t inputs_packed, int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
                               int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out);
 /* The attention + output copy of a host step whose inputs were staged by
  * pkv_stepper_step_host and whose descriptor is uploaded (the capacity retry). */

@@ -168,8 +168,8 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "pkv_stepper_step_host": (
         c_int32,
-        [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_float, c_void_p, c_void_p,
-         POINTER(StepInfo), c_void_p, c_void_p, c_void_p],
+        [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p,
+         c_void_p, POINTER(StepInfo), c_void_p, c_void_p, c_void_p],
     ),
     "pkv_stepper_attention_host": (c_int32, [c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "pkv_stepper_host_fence": (c_int32, [c_void_p, c_void_p]),

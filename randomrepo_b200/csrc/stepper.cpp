@@ -292,8 +292,7 @@ struct pkv_stepper {
     return st ? st : copied(copy_stream);
   }
 
-  // Copy a step's host q / k / v into the next staging entry on copy_stream
-  // (one copy when the three lie back to back in host memory).
+  // The output stream and the staging guards' events (on first use).
   int32_t ensure_host_io() {
     if (d2h_stream) return PKV_OK;
     int32_t st = cuda_status(cudaStreamCreateWithFlags(&d2h_stream, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -302,7 +301,10 @@ struct pkv_stepper {
     return st;
   }
 
-  int32_t stage_inputs(int32_t n, int32_t num_q_heads, const void* q, const void* k, const void* v,
+  // Copy a step's host q / k / v into the next staging entry on copy_stream
+  // (one copy when the caller says the three are consecutive parts of one
+  // allocation: adjacent addresses alone do not make one copyable range).
+  int32_t stage_inputs(int32_t n, int32_t num_q_heads, const void* q, const void* k, const void* v, bool packed,
                        cudaStream_t stream) {
     if (int32_t e = ensure_copy_stream()) return e;
     if (int32_t e = ensure_host_io()) return e;
@@ -338,7 +340,7 @@ struct pkv_stepper {
     }
     const char* qc = static_cast<const char*>(q);
     int32_t st;
-    if (!k || (static_cast<const char*>(k) == qc + qb && static_cast<const char*>(v) == qc + qb + kb)) {
+    if (!k || (packed && static_cast<const char*>(k) == qc + qb && static_cast<const char*>(v) == qc + qb + kb)) {
       st = cuda_status(cudaMemcpyAsync(e.in, q, in_need, cudaMemcpyHostToDevice, copy_stream), "H2D q/k/v");
     } else {
       st = cuda_status(cudaMemcpyAsync(e.in, q, qb, cudaMemcpyHostToDevice, copy_stream), "H2D q");
@@ -754,7 +756,7 @@ int32_t pkv_stepper_attention_host(pkv_stepper* st, int32_t layer, int32_t num_q
 
 int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int32_t n, int32_t layer,
                               const void* q_host, const void* k_new_host, const void* v_new_host,
-                              int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
+                              int32_t inputs_packed, int32_t num_q_heads, float scale, void* out_host, void* stream, pkv_step_info* info,
                               int32_t* rows_out, int32_t* lens_out, int32_t* token_blocks_out) {
   if (!q_host || !out_host || num_q_heads <= 0 || num_q_heads % st->geom.num_kv_heads != 0 ||
       (!k_new_host) != (!v_new_host)) {
@@ -765,7 +767,8 @@ int32_t pkv_stepper_step_host(pkv_stepper* st, const int64_t* sequence_ids, int3
   }
   int32_t s = pkv_stepper_begin(st, sequence_ids, n, info, rows_out, lens_out, token_blocks_out);
   if (s) return s;
-  s = st->stage_inputs(n, num_q_heads, q_host, k_new_host, v_new_host, static_cast<cudaStream_t>(stream));
+  s = st->stage_inputs(n, num_q_heads, q_host, k_new_host, v_new_host, inputs_packed != 0,
+                       static_cast<cudaStream_t>(stream));
   if (s) return s;
   s = pkv_stepper_upload(st, stream, info, nullptr, 0);
   if (s) return s;  // PKV_ERR_CAPACITY: grow, rebind, then upload + attention_host

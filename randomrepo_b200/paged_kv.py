@@ -579,7 +579,7 @@ class PagedKVCacheStore:
         if (out is None or not chk or chk[0] is not q or chk[1] is not k_new or chk[2] is not v_new
                 or chk[3] is not out or chk[4] != n):
             out = self._check_decode_io(pool, n, q, k_new, v_new, out)
-            self._io_checked = (q, k_new, v_new, out, n)
+            self._io_checked = (q, k_new, v_new, out, n, False)
         host, (p_rows, p_lens, p_tokb) = self._host_buffers(n)
         info = _lib.StepInfo()
         with _on_device(pool.device):
@@ -626,15 +626,20 @@ class PagedKVCacheStore:
             if k_new is None or v_new is None:
                 raise ValueError("a host-tensor decode step needs k_new and v_new")
             out = self._check_decode_io(pool, n, q, k_new, v_new, out, device=torch.device("cpu"))
-            self._io_checked = (q, k_new, v_new, out, n)
+            # One copy moves q, k and v only when they are consecutive parts of one allocation.
+            base = q.untyped_storage().data_ptr()
+            packed = (k_new.untyped_storage().data_ptr() == base and v_new.untyped_storage().data_ptr() == base
+                      and k_new.data_ptr() == q.data_ptr() + q.nbytes
+                      and v_new.data_ptr() == k_new.data_ptr() + k_new.nbytes)
+            self._io_checked = (q, k_new, v_new, out, n, packed)
         host, (p_rows, p_lens, p_tokb) = self._host_buffers(n)
         info = _lib.StepInfo()
         with _on_device(pool.device):
             stream = _current_stream(pool.device)
             sc = float(scale if scale is not None else pool.head_dim ** -0.5)
-            st = lib.pkv_stepper_step_host(pool.stepper, p_ids, n, int(layer), q.data_ptr(),
-                                           k_new.data_ptr(), v_new.data_ptr(), q.shape[1], sc, out.data_ptr(), stream,
-                                           ctypes.byref(info), p_rows, p_lens, p_tokb)
+            st = lib.pkv_stepper_step_host(pool.stepper, p_ids, n, int(layer), q.data_ptr(), k_new.data_ptr(),
+                                           v_new.data_ptr(), int(self._io_checked[5]), q.shape[1], sc,
+                                           out.data_ptr(), stream, ctypes.byref(info), p_rows, p_lens, p_tokb)
             if st != _lib.PKV_OK and self._needs_retry(pool, st, info):
                 st = self._upload_retry(pool, stream, info, st)
                 if st == _lib.PKV_OK:

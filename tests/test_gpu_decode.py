@@ -303,3 +303,21 @@ def test_fixed_step_mode_grows_its_work_item_capacity(cuda_device):
     torch.cuda.synchronize()
     _close(out, _oracle(q, ks, vs, 128 ** -0.5))
     assert pool.decode_error_flag() == 0
+
+
+def test_host_buffer_decode_separate_allocations(cuda_device):
+    """Three separately allocated host inputs -- which the host allocator may place back to back --
+    are copied one by one (a single copy across two allocations is an invalid range)."""
+    from randomrepo_b200 import host_input_tensor
+
+    for trial in range(4):
+        store, q, kn, vn, ks, vs = _batch_case(cuda_device, [37, 5], 12, 2, 128, torch.bfloat16, seed=30 + trial)
+        ids = np.arange(2, dtype=np.int64)
+        qh = host_input_tensor(q.shape, torch.bfloat16)
+        kh = host_input_tensor(kn.shape, torch.bfloat16)
+        vh = host_input_tensor(vn.shape, torch.bfloat16)
+        qh.copy_(q), kh.copy_(kn), vh.copy_(vn)
+        out, _ = store.decode(ids, qh, kh, vh)
+        store.wait_host_outputs()
+        _close(out, _oracle(q, ks, vs, 128 ** -0.5))
+        assert store.pool.decode_error_flag() == 0
