@@ -158,3 +158,44 @@ def test_score_equals_reference_compute_logprobs(group_size):
     assert not store.count  # temporary sequences released
     with pytest.raises(ValueError):
         g.score(ids, 1 - am, cm)
+
+
+def test_paged_generator_reproduces_the_reference_orchestrator_c1():
+    """Greedy tokens of the reference's own continuous-batching loop, pinned.
+
+    tests/golden/continuous_c1_trace.json holds what AgentRL's
+    ``ContinuousBatchingOrchestrator._generate_active_batch_with_cache``
+    (agentrl/generation/continuous.py:363-504, paged-KV mode) generated on
+    CPU for a random-init fp32 Qwen2 (2 layers, 4/2 heads, head_dim 16, vocab
+    512, seed 0): two prompts x group 4, greedy, 16 new tokens.  The same
+    model and prompts through ``PagedGenerator`` (the paged attention
+    interface over the fake store, one prefill per group plus forks) must give
+    the same tokens (bar: >= 99 % of positions; here every one).
+    """
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from randomrepo_b200.hf import PagedGenerator
+    from tests.conftest import load_json
+
+    trace = load_json("continuous_c1_trace.json")
+    m = trace["model"]
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=m["vocab"], hidden_size=m["hidden"], intermediate_size=128,
+                      num_hidden_layers=m["layers"], num_attention_heads=m["heads"],
+                      num_key_value_heads=m["kv_heads"], head_dim=m["head_dim"], rope_theta=1e4,
+                      max_position_embeddings=256, tie_word_embeddings=False)
+    model = Qwen2ForCausalLM(cfg).eval()
+    prompts = [torch.tensor(p) for p in trace["prompts"]]
+    group = 4
+    heads = prompts[::group]
+    assert all(torch.equal(prompts[i], heads[i // group]) for i in range(len(prompts)))
+    g = PagedGenerator(model, FakeStore(m["layers"]), prefill_chunk_size=512, eos_token_id=3,
+                       sampler=OracleSampler())
+    res = g.generate(heads, group_size=group, max_new_tokens=16)
+    want = trace["generated"]
+    got = res["tokens"]
+    total = sum(len(w) for w in want)
+    same = sum(a == b for w, t in zip(want, got) for a, b in zip(w, t))
+    assert [len(t) for t in got] == [len(w) for w in want]
+    assert same / total >= 0.99, (same, total)
+    assert got == want
