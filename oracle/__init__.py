@@ -27,5 +27,7 @@ attention restatement is pinned against HF ``sdpa_attention_forward`` outputs
 committed as fixtures by the same script.  The fork/refcount extension has no
 reference counterpart: its parity is unpinned by the reference and is checked
 semantically (every fork member gathers exactly what an independent prefill
-would have stored).
+would have stored).  The speculative loop (``speculative.py``) is pinned
+against a recorded run of the reference's own orchestrator, acceptance draws
+included (``speculative_c1_trace.json``, made by the same script).
 """

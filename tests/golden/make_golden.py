@@ -22,7 +22,15 @@ unchanged from that tree, and HF transformers' ``sdpa_attention_forward``
   block sizes 2 and 16, ragged lengths);
 * ``attention_sdpa.npz`` -- fp32 ``sdpa_attention_forward`` outputs for GQA
   decode, chunked prefill after a cached past, and the k+1-query verify rows
-  of a full causal forward, on bf16-representable inputs.
+  of a full causal forward, on bf16-representable inputs;
+* ``speculative_c1_trace.json`` -- ``SpeculativeRolloutOrchestrator.
+  _generate_speculative_tokens`` (agentrl/generation/speculative.py) on CPU
+  with the C1 target above and a draft (an unrelated 1-layer model, seed 1,
+  or a copy of the target), k = 4, greedy, 16 new tokens, eos 3: every
+  prompt's tokens and target log-probabilities, and the acceptance draws
+  ``torch.rand`` returned in each verify round (recorded, in order).
+
+``--only NAME`` (a fixture file's stem) rewrites just that fixture.
 
 The fixtures are small (about 1 MB together) and are committed; tests never run
 this script.
@@ -191,6 +199,78 @@ def continuous_c1_trace(ref_root: Path) -> dict:
     }
 
 
+def speculative_c1_trace(ref_root: Path) -> dict:
+    import copy
+
+    from agentrl.core.config import GRPOConfig
+    from agentrl.generation.speculative import SpeculativeRolloutOrchestrator
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    def model(layers: int, seed: int):
+        torch.manual_seed(seed)
+        cfg = Qwen2Config(
+            vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=layers,
+            num_attention_heads=4, num_key_value_heads=2, head_dim=16, rope_theta=1e4,
+            max_position_embeddings=256, tie_word_embeddings=False,
+        )
+        return Qwen2ForCausalLM(cfg).eval()
+
+    class Tokenizer(_IdTokenizer):
+        def __call__(self, text, return_tensors=None, add_special_tokens=False):
+            ids = torch.tensor([[int(t) for t in text.split()]], dtype=torch.long)
+            return {"input_ids": ids, "attention_mask": torch.ones_like(ids)}
+
+    target = model(2, 0)
+    gen = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(4, 512, (int(torch.randint(8, 33, (1,), generator=gen)),), generator=gen).tolist()
+               for _ in range(3)]
+    cases = {}
+    for name, draft in (("unrelated_draft", model(1, 1)), ("draft_equals_target", copy.deepcopy(target))):
+
+        class Layout:
+            def policy_forward(self, input_ids, attention_mask):
+                return target(input_ids=input_ids, attention_mask=attention_mask).logits
+
+        config = GRPOConfig(
+            model_name="fake/model", use_speculative_decoding=True, draft_model_name="fake/draft",
+            speculative_k=4, max_new_tokens=16, do_sample=False, dtype="float32",
+        )
+        orch = SpeculativeRolloutOrchestrator(
+            config=config, environment=SimpleNamespace(), verifier=SimpleNamespace(), tokenizer=Tokenizer(),
+            layout=Layout(), device=torch.device("cpu"), rng=torch.Generator().manual_seed(7), draft_model=draft,
+        )
+        rounds: list[list[float]] = []
+        orig_verify, orig_rand = orch._verify_draft, torch.rand
+
+        def verify(*args, **kwargs):
+            rounds.append([])
+            return orig_verify(*args, **kwargs)
+
+        def rand(*args, **kwargs):
+            out = orig_rand(*args, **kwargs)
+            rounds[-1].append(float(out.item()))
+            return out
+
+        orch._verify_draft = verify
+        runs = []
+        torch.rand = rand
+        try:
+            with torch.no_grad():
+                for p in prompts:
+                    rounds.clear()
+                    toks, lps = orch._generate_speculative_tokens(" ".join(str(t) for t in p))
+                    runs.append({"tokens": toks.tolist(), "logprobs": lps.tolist(), "round_draws": [list(r) for r in rounds]})
+        finally:
+            torch.rand = orig_rand
+        cases[name] = runs
+    return {
+        "target": {"layers": 2, "seed": 0}, "drafts": {"unrelated_draft": {"layers": 1, "seed": 1},
+                                                       "draft_equals_target": "copy of the target"},
+        "model": {"vocab": 512, "hidden": 64, "intermediate": 128, "heads": 4, "kv_heads": 2, "head_dim": 16},
+        "k": 4, "max_new_tokens": 16, "eos_token_id": 3, "prompts": prompts, "cases": cases,
+    }
+
+
 def store_roundtrips(PagedKVAllocator, PagedKVCacheStore) -> dict[str, np.ndarray]:
     out: dict[str, np.ndarray] = {}
     g = torch.Generator().manual_seed(1)
@@ -266,14 +346,29 @@ def attention_fixtures() -> dict[str, np.ndarray]:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    args = sys.argv[1:]
+    only = None
+    if "--only" in args:
+        i = args.index("--only")
+        only = args[i + 1]
+        del args[i:i + 2]
+    ref_root = Path(args[0] if args else "/root/reference").resolve()
     sys.path.insert(0, str(ref_root))
     from agentrl.generation.paged_kv import PagedKVAllocator, PagedKVCacheStore
 
-    (HERE / "allocator_traces.json").write_text(json.dumps(allocator_traces(PagedKVAllocator)))
-    (HERE / "continuous_c1_trace.json").write_text(json.dumps(continuous_c1_trace(ref_root), indent=0))
-    np.savez_compressed(HERE / "store_roundtrip.npz", **store_roundtrips(PagedKVAllocator, PagedKVCacheStore))
-    np.savez_compressed(HERE / "attention_sdpa.npz", **attention_fixtures())
+    def want(name: str) -> bool:
+        return only is None or only == name
+
+    if want("allocator_traces"):
+        (HERE / "allocator_traces.json").write_text(json.dumps(allocator_traces(PagedKVAllocator)))
+    if want("continuous_c1_trace"):
+        (HERE / "continuous_c1_trace.json").write_text(json.dumps(continuous_c1_trace(ref_root), indent=0))
+    if want("store_roundtrip"):
+        np.savez_compressed(HERE / "store_roundtrip.npz", **store_roundtrips(PagedKVAllocator, PagedKVCacheStore))
+    if want("attention_sdpa"):
+        np.savez_compressed(HERE / "attention_sdpa.npz", **attention_fixtures())
+    if want("speculative_c1_trace"):
+        (HERE / "speculative_c1_trace.json").write_text(json.dumps(speculative_c1_trace(ref_root), indent=0))
     print("fixtures written to", HERE)
 
 

@@ -157,3 +157,59 @@ def test_oracle_verify_draft_known_answers():
     p1 = t[1].softmax(-1)
     r = ospec.verify_draft(t[1:], [3], [float(torch.log(p1[3])) + 0.01], [p1 * 1.0001], [1.0])
     assert r.n_accepted == 0 and r.steps[0][0] == 0
+
+
+def _c1_model(trace: dict, layers: int, seed: int):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    m = trace["model"]
+    torch.manual_seed(seed)
+    cfg = Qwen2Config(vocab_size=m["vocab"], hidden_size=m["hidden"], intermediate_size=m["intermediate"],
+                      num_hidden_layers=layers, num_attention_heads=m["heads"], num_key_value_heads=m["kv_heads"],
+                      head_dim=m["head_dim"], rope_theta=1e4, max_position_embeddings=256, tie_word_embeddings=False)
+    return Qwen2ForCausalLM(cfg).eval()
+
+
+@pytest.mark.parametrize("case", ["unrelated_draft", "draft_equals_target"])
+def test_reference_orchestrator_run_is_reproduced(case):
+    """The reference's own speculative loop, pinned.
+
+    tests/golden/speculative_c1_trace.json records what AgentRL's
+    ``SpeculativeRolloutOrchestrator._generate_speculative_tokens``
+    (agentrl/generation/speculative.py:148-274) produced on CPU for a
+    random-init fp32 Qwen2 target (2 layers, head_dim 16, vocab 512, seed 0)
+    with an unrelated 1-layer draft (rejections and corrections) or a copy of
+    the target (every draft accepted, bonus tokens), k = 4, greedy, 16 new
+    tokens, eos 3 -- including the acceptance draws its ``torch.rand`` returned
+    in every verify round.  Given those draws, the oracle's loop and the
+    batched paged loop (PagedSpeculativeGenerator over fake stores, all three
+    prompts at once) emit the same tokens and the same target log-probabilities.
+    """
+    from tests.conftest import load_json
+
+    trace = load_json("speculative_c1_trace.json")
+    target = _c1_model(trace, trace["target"]["layers"], trace["target"]["seed"])
+    if case == "draft_equals_target":
+        draft = copy.deepcopy(target)
+    else:
+        draft = _c1_model(trace, trace["drafts"][case]["layers"], trace["drafts"][case]["seed"])
+    runs = trace["cases"][case]
+    k, new, eos = trace["k"], trace["max_new_tokens"], trace["eos_token_id"]
+
+    def draws(seq: int, rnd: int) -> list[float]:
+        got = runs[seq]["round_draws"][rnd]
+        return got + [0.5] * (k - len(got))  # draws after a rejection are never read
+
+    for i, p in enumerate(trace["prompts"]):
+        toks, lps, rounds = ospec.generate(p, _full_logits(target), _last_logits(draft), k=k, max_new_tokens=new,
+                                           eos_token_id=eos, uniform_fn=lambda r, j, i=i: draws(i, r)[j])
+        assert toks == runs[i]["tokens"]
+        np.testing.assert_allclose(lps, runs[i]["logprobs"], rtol=1e-5, atol=1e-5)
+        assert len(rounds) == len(runs[i]["round_draws"])
+
+    sg = _spec(copy.deepcopy(target), copy.deepcopy(draft), k, eos=eos)
+    res = sg.generate([torch.tensor(p) for p in trace["prompts"]], max_new_tokens=new, uniforms=draws)
+    for i in range(len(trace["prompts"])):
+        assert res["tokens"][i] == runs[i]["tokens"]
+        np.testing.assert_allclose(res["logprobs"][i], runs[i]["logprobs"], rtol=1e-4, atol=1e-4)
+    assert not sg.target.store.count and not sg.draft.store.count
