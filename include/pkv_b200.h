@@ -477,6 +477,31 @@ int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every)
 int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacity, int64_t* n_out);
 
 /* ---------------------------------------------------------------------------
+ * Fused elementwise layers of a Qwen2-family decoder (bf16 / f16), each one
+ * launch doing what the HF modules do in several, with the same roundings
+ * (transformers models/qwen2/modeling_qwen2.py).  No reference counterpart:
+ * AgentRL runs those modules eagerly inside its HF forwards
+ * (agentrl/generation/continuous.py:407-497).
+ * ------------------------------------------------------------------------- */
+
+/* Qwen2RMSNorm: out = w * to_dtype(x * rsqrt(mean(x^2) + eps)), x in fp32,
+ * rows x hidden (hidden <= 8192).  With residual (and sum_out) non-NULL, x is
+ * first to_dtype(x + residual) -- Qwen2DecoderLayer's residual add -- and that
+ * sum is written to sum_out. */
+int32_t pkv_rms_norm(const void* x, const void* residual, void* sum_out, const void* weight, void* out, int64_t rows,
+                     int32_t hidden, float eps, int32_t dtype, void* stream);
+/* apply_rotary_pos_emb for the q and k of `rows` tokens: q [rows][q_heads *
+ * head_dim], k [rows][kv_heads * head_dim] (the projections' outputs), cos /
+ * sin [rows][head_dim]; out = to_dtype(to_dtype(x * cos) +
+ * to_dtype(rotate_half(x) * sin)) into q_out / k_out of the same layouts. */
+int32_t pkv_rope(const void* q, const void* k, const void* cos, const void* sin, void* q_out, void* k_out,
+                 int64_t rows, int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t dtype, void* stream);
+/* Qwen2MLP's act_fn(gate) * up with SiLU: out[r][c] = to_dtype(to_dtype(
+ * silu(gate)) * up) for rows x cols, gate / up rows ld_in elements apart. */
+int32_t pkv_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t cols, int64_t ld_in,
+                     int32_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Vocabulary rows: token log-probabilities, token selection, speculative
  * accept / reject.  Logits are fp32 rows of `vocab` columns, row r at
  * logits + r * ld (ld >= vocab).  Each launch streams the rows once.  The

@@ -180,6 +180,15 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_launches": (c_int64, [c_void_p]),
     "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64, c_int64]),
     "pkv_stepper_launch_times": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
+    "pkv_rms_norm": (
+        c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p]
+    ),
+    "pkv_rope": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
+         c_void_p],
+    ),
+    "pkv_silu_mul": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "pkv_sampling_workspace_bytes": (c_int64, [c_int64, c_int32]),
     "pkv_token_logprobs": (
         c_int32,

@@ -71,32 +71,171 @@ def _phase(ph: _Phase):
         _local.phase = prev
 
 
+def _paged_rows(ph: _Phase, layer: int, q, k, v, b: int, t: int, scaling):
+    """The store's attention for q [b*t, Hq, D], k/v [b*t, Hkv, D] (contiguous) -> [b*t, Hq, D]."""
+    hq = q.shape[1]
+    if ph.kind == "decode":
+        if t != 1:
+            raise ValueError("a decode step feeds one token per sequence")
+        return ph.store.decode_attention(ph.step, layer, q, k, v, scale=scaling)
+    if b != 1:
+        raise ValueError("prefill runs packed: batch 1, the chunks of all sequences along the token axis")
+    if ph.step is None and hasattr(ph.store, "prefill_step"):
+        ph.step = ph.store.prefill_step(ph.sequence_ids, ph.q_lens, hq)
+    return ph.store.prefill_attention(ph.sequence_ids, q, k, v, q_lens=ph.q_lens, layer=layer, scale=scaling,
+                                      step=ph.step)
+
+
 def paged_attention_forward(module, query, key, value, attention_mask=None, scaling=None, dropout=0.0, **kwargs):
     """HF attention-interface entry: q [B, Hq, T, D], k/v [B, Hkv, T, D] -> ([B, T, Hq, D], None)."""
     ph = getattr(_local, "phase", None)
     if ph is None:
         raise RuntimeError("paged_b200 attention ran outside a PagedGenerator forward")
-    layer = int(module.layer_idx)
     b, hq, t, d = query.shape
     hkv = key.shape[1]
-    q = query.transpose(1, 2)
-    k = key.transpose(1, 2)
-    v = value.transpose(1, 2)
-    if ph.kind == "decode":
-        if t != 1:
-            raise ValueError("a decode step feeds one token per sequence")
-        out = ph.store.decode_attention(ph.step, layer, q.reshape(b, hq, d).contiguous(),
-                                        k.reshape(b, hkv, d).contiguous(), v.reshape(b, hkv, d).contiguous(),
-                                        scale=scaling)
-        return out.view(b, 1, hq, d), None
-    if b != 1:
-        raise ValueError("prefill runs packed: batch 1, the chunks of all sequences along the token axis")
-    if ph.step is None and hasattr(ph.store, "prefill_step"):
-        ph.step = ph.store.prefill_step(ph.sequence_ids, ph.q_lens, hq)
-    out = ph.store.prefill_attention(ph.sequence_ids, q.reshape(t, hq, d).contiguous(),
-                                     k.reshape(t, hkv, d).contiguous(), v.reshape(t, hkv, d).contiguous(),
-                                     q_lens=ph.q_lens, layer=layer, scale=scaling, step=ph.step)
-    return out.view(1, t, hq, d), None
+    out = _paged_rows(ph, int(module.layer_idx), query.transpose(1, 2).reshape(b * t, hq, d).contiguous(),
+                      key.transpose(1, 2).reshape(b * t, hkv, d).contiguous(),
+                      value.transpose(1, 2).reshape(b * t, hkv, d).contiguous(), b, t, scaling)
+    return out.view(b, t, hq, d), None
+
+
+# -- fused elementwise layers -------------------------------------------------
+# Inside a PagedGenerator forward, the decoder layers of a Qwen2-family model
+# on the GPU (bf16 / f16, SiLU MLP) run their RMSNorms (with the residual add
+# folded into the second), rotary embedding and SiLU product as single
+# launches of the library (pkv_rms_norm, pkv_rope, pkv_silu_mul) instead of
+# HF's eager op chains, and hand the rotated q / k to the store without the
+# HF layout transposes.  Outside such a forward every module runs its own HF
+# code unchanged.
+
+def _dtype_code(t: torch.Tensor) -> int:
+    from ._lib import PKV_BF16, PKV_F16
+
+    return PKV_BF16 if t.dtype == torch.bfloat16 else PKV_F16
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def fused_rms_norm(x: torch.Tensor, norm, residual: torch.Tensor | None = None):
+    """``norm(x)`` (a Qwen2RMSNorm) in one launch; with ``residual``, of ``residual + x``, which is returned too."""
+    from ._lib import lib, raise_for_status
+
+    x = x.contiguous()
+    hidden = x.shape[-1]
+    out = torch.empty_like(x)
+    total = None
+    if residual is not None:
+        residual = residual.contiguous()
+        total = torch.empty_like(x)
+    raise_for_status(lib.pkv_rms_norm(x.data_ptr(), residual.data_ptr() if residual is not None else None,
+                                      total.data_ptr() if total is not None else None, norm.weight.data_ptr(),
+                                      out.data_ptr(), x.numel() // hidden, hidden, float(norm.variance_epsilon),
+                                      _dtype_code(x), _stream()))
+    return out if residual is None else (out, total)
+
+
+def fused_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, head_dim: int):
+    """apply_rotary_pos_emb on the projections' outputs q [..., Hq*D], k [..., Hkv*D] -> [rows, H, D] each."""
+    from ._lib import lib, raise_for_status
+
+    rows = q.numel() // q.shape[-1]
+    hq, hkv = q.shape[-1] // head_dim, k.shape[-1] // head_dim
+    q = q.contiguous()
+    k = k.contiguous()
+    cos = cos.contiguous()
+    sin = sin.contiguous()
+    qo = torch.empty((rows, hq, head_dim), dtype=q.dtype, device=q.device)
+    ko = torch.empty((rows, hkv, head_dim), dtype=k.dtype, device=k.device)
+    raise_for_status(lib.pkv_rope(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
+                                  ko.data_ptr(), rows, hq, hkv, head_dim, _dtype_code(q), _stream()))
+    return qo, ko
+
+
+def fused_silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """SiLU(gate) * up in one launch (both [..., cols], contiguous)."""
+    from ._lib import lib, raise_for_status
+
+    gate = gate.contiguous()
+    up = up.contiguous()
+    cols = gate.shape[-1]
+    out = torch.empty_like(gate)
+    raise_for_status(lib.pkv_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel() // cols, cols,
+                                      cols, _dtype_code(gate), _stream()))
+    return out
+
+
+def _fused_norm_forward(self, hidden_states):
+    if getattr(_local, "phase", None) is None:
+        return type(self).forward(self, hidden_states)
+    return fused_rms_norm(hidden_states, self)
+
+
+def _fused_mlp_forward(self, x):
+    if getattr(_local, "phase", None) is None:
+        return type(self).forward(self, x)
+    return self.down_proj(fused_silu_mul(self.gate_proj(x), self.up_proj(x)))
+
+
+def _fused_attention_forward(self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
+                             **kwargs):
+    ph = getattr(_local, "phase", None)
+    if ph is None:
+        return type(self).forward(self, hidden_states, position_embeddings, attention_mask,
+                                  past_key_values=past_key_values, **kwargs)
+    input_shape = hidden_states.shape[:-1]
+    b, t = int(input_shape[0]), int(input_shape[1])
+    d = int(self.head_dim)
+    cos, sin = position_embeddings
+    q, k = fused_rope(self.q_proj(hidden_states), self.k_proj(hidden_states), cos, sin, d)
+    v = self.v_proj(hidden_states)
+    v = v.reshape(b * t, v.shape[-1] // d, d)
+    out = _paged_rows(ph, int(self.layer_idx), q, k, v, b, t, self.scaling)
+    return self.o_proj(out.reshape(*input_shape, -1)), None
+
+
+def _fused_layer_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
+                         use_cache=False, position_embeddings=None, **kwargs):
+    if getattr(_local, "phase", None) is None:
+        return type(self).forward(self, hidden_states, attention_mask=attention_mask, position_ids=position_ids,
+                                  past_key_values=past_key_values, use_cache=use_cache,
+                                  position_embeddings=position_embeddings, **kwargs)
+    h = fused_rms_norm(hidden_states, self.input_layernorm)
+    a, _ = self.self_attn(hidden_states=h, attention_mask=attention_mask, position_ids=position_ids,
+                          past_key_values=past_key_values, use_cache=use_cache,
+                          position_embeddings=position_embeddings, **kwargs)
+    h2, hidden = fused_rms_norm(a, self.post_attention_layernorm, residual=hidden_states)
+    return hidden + self.mlp(h2)
+
+
+def install_fused_layers(model) -> bool:
+    """Give the decoder layers of a Qwen2-family model on the GPU (bf16 / f16) the fused forwards above
+    (per instance; the classes are untouched).  Returns whether they were installed."""
+    import types
+
+    base = model.get_decoder() if hasattr(model, "get_decoder") else getattr(model, "model", None)
+    layers = getattr(base, "layers", None)
+    p = next(model.parameters())
+    cfg = model.config
+    if (layers is None or not p.is_cuda or p.dtype not in (torch.bfloat16, torch.float16)
+            or getattr(cfg, "hidden_act", None) != "silu"):
+        return False
+    for layer in layers:
+        attn, mlp = getattr(layer, "self_attn", None), getattr(layer, "mlp", None)
+        parts = (getattr(layer, "input_layernorm", None), getattr(layer, "post_attention_layernorm", None))
+        if (attn is None or mlp is None or None in parts or not all(hasattr(n, "variance_epsilon") for n in parts)
+                or not all(hasattr(attn, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj", "head_dim"))
+                or not all(hasattr(mlp, a) for a in ("gate_proj", "up_proj", "down_proj"))):
+            return False
+    for layer in layers:
+        layer.forward = types.MethodType(_fused_layer_forward, layer)
+        layer.self_attn.forward = types.MethodType(_fused_attention_forward, layer.self_attn)
+        layer.mlp.forward = types.MethodType(_fused_mlp_forward, layer.mlp)
+    norm = getattr(base, "norm", None)
+    if norm is not None and hasattr(norm, "variance_epsilon"):
+        norm.forward = types.MethodType(_fused_norm_forward, norm)
+    return True
 
 
 def register() -> None:
@@ -161,8 +300,10 @@ class PagedGenerator:
     """
 
     def __init__(self, model, store, *, prefill_chunk_size: int = 512, eos_token_id: int | None = None,
-                 fp32_logits: bool = True, cuda_graphs: bool = False, sampler=None) -> None:
+                 fp32_logits: bool = True, cuda_graphs: bool = False, sampler=None, fused_layers: bool = True) -> None:
         use_paged_attention(model)
+        # Fused norm / rotary / SiLU launches inside this generator's forwards (Qwen2-family models on the GPU).
+        self.fused_layers = bool(fused_layers) and install_fused_layers(model)
         self.model = model
         self.store = store
         self.prefill_chunk_size = int(prefill_chunk_size)

@@ -236,8 +236,9 @@ def test_greedy_tokens_at_the_qwen2p5_1p5b_architecture(cuda_device):
     """The same teacher-forced check at the full Qwen2.5-1.5B architecture (28 layers, 12/2 heads,
     head_dim 128, vocab 151 936, random-init bf16; prompts of 64-256 tokens in one 512-token prefill
     chunk).  Random-init logits this deep are flat (median top-2 gap ~0.13), so bf16 near-ties are
-    frequent: measured 92.6 % agreement against 91.4 % for HF's own eager vs SDPA backends, every
-    mismatch below a gap of 0.05."""
+    frequent.  Bars: agreement at least HF's own eager-vs-SDPA agreement minus 0.01 (and >= 0.88), and
+    every mismatch a near-tie: top-2 gap below max(0.05, twice the largest gap at which HF's two
+    backends disagree on the same positions)."""
     from transformers import Qwen2Config, Qwen2ForCausalLM
 
     from randomrepo_b200.hf import PagedGenerator, make_store
@@ -262,9 +263,44 @@ def test_greedy_tokens_at_the_qwen2p5_1p5b_architecture(cuda_device):
     forced = g.generate(prompts, max_new_tokens=new, force_tokens=want)
     pairs = [(a == w, gp) for am, ws, gs in zip(forced["argmax"], want, gaps) for a, w, gp in zip(am, ws, gs)]
     agree = float(np.mean([ok for ok, _ in pairs]))
-    floor = _agreement(_teacher_forced_argmax(eager, prompts, want, new),
-                       _teacher_forced_argmax(ref, prompts, want, new))
-    assert all(gp < 0.05 for ok, gp in pairs if not ok), [gp for ok, gp in pairs if not ok]
+    eager_am = _teacher_forced_argmax(eager, prompts, want, new)
+    floor = _agreement(eager_am, _teacher_forced_argmax(ref, prompts, want, new))
+    hf_noise = [gp for ea, ws, gs in zip(eager_am, want, gaps) for e, w, gp in zip(ea, ws, gs) if e != w]
+    gap_bar = max([0.05] + [2 * gp for gp in hf_noise])
+    ours_gaps = [gp for ok, gp in pairs if not ok]
+    assert all(gp < gap_bar for gp in ours_gaps), (gap_bar, sorted(ours_gaps)[-5:], sorted(hf_noise)[-5:])
     assert agree >= floor - 0.01 and agree >= 0.88, f"agreement {agree:.4f}, HF eager vs SDPA {floor:.4f}"
     assert store.pool.decode_error_flag() == 0 and store.pool.prefill_error_flag() == 0
     assert store.allocator.used_block_count == 0
+
+
+def test_fused_layers_match_hf_modules(cuda_device):
+    """Fused norm / rotary / SiLU launches (installed by PagedGenerator) against the same generator running HF's
+    own module code: teacher-forced on the same tokens, greedy selections agree on >= 99 % of positions (every
+    disagreement a near-tie under 0.02) and the chosen tokens' log-probabilities within 0.05."""
+    from randomrepo_b200.hf import PagedGenerator, make_store
+
+    base = _model(cuda_device, 128, 3, 12, 2)
+    fused_m, plain_m = copy.deepcopy(base), copy.deepcopy(base)
+    gen = torch.Generator().manual_seed(19)
+    prompts = [torch.randint(0, 512, (int(n),), generator=gen) for n in torch.randint(8, 60, (6,), generator=gen)]
+    new = 24
+    want, gaps = _hf_greedy(base, prompts, new)
+    fused = PagedGenerator(fused_m, make_store(fused_m, total_blocks=1024), prefill_chunk_size=32)
+    plain = PagedGenerator(plain_m, make_store(plain_m, total_blocks=1024), prefill_chunk_size=32,
+                           fused_layers=False)
+    assert fused.fused_layers and not plain.fused_layers
+    a = fused.generate(prompts, max_new_tokens=new, force_tokens=want)
+    b = plain.generate(prompts, max_new_tokens=new, force_tokens=want)
+    pairs = [(x == y, gp) for u, v, gs in zip(a["argmax"], b["argmax"], gaps) for x, y, gp in zip(u, v, gs)]
+    assert float(np.mean([ok for ok, _ in pairs])) >= 0.99
+    assert all(gp < 0.02 for ok, gp in pairs if not ok)
+    np.testing.assert_allclose(np.concatenate(a["logprobs"]), np.concatenate(b["logprobs"]), atol=0.05)
+    # Outside a generator forward the model runs HF's own code again (here with SDPA attention).
+    for m in (fused_m, plain_m):
+        for mod in m.modules():
+            if hasattr(mod, "config"):
+                mod.config._attn_implementation = "sdpa"
+    with torch.inference_mode():
+        ids = prompts[0].unsqueeze(0).to(cuda_device)
+        assert torch.equal(fused_m(input_ids=ids).logits, plain_m(input_ids=ids).logits)
