@@ -490,12 +490,15 @@ int32_t pkv_stepper_launch_times(pkv_stepper* st, float* ms_out, int64_t capacit
  * sum is written to sum_out. */
 int32_t pkv_rms_norm(const void* x, const void* residual, void* sum_out, const void* weight, void* out, int64_t rows,
                      int32_t hidden, float eps, int32_t dtype, void* stream);
-/* apply_rotary_pos_emb for the q and k of `rows` tokens: q [rows][q_heads *
- * head_dim], k [rows][kv_heads * head_dim] (the projections' outputs), cos /
- * sin [rows][head_dim]; out = to_dtype(to_dtype(x * cos) +
- * to_dtype(rotate_half(x) * sin)) into q_out / k_out of the same layouts. */
-int32_t pkv_rope(const void* q, const void* k, const void* cos, const void* sin, void* q_out, void* k_out,
-                 int64_t rows, int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t dtype, void* stream);
+/* apply_rotary_pos_emb for the q and k of `rows` tokens: q rows of q_heads *
+ * head_dim, k rows of kv_heads * head_dim, q_ld / k_ld elements apart (three
+ * tensors, or one packed q|k|v projection row), cos / sin [rows][head_dim];
+ * out = to_dtype(to_dtype(x * cos) + to_dtype(rotate_half(x) * sin)) into
+ * contiguous q_out [rows][q_heads][head_dim] / k_out.  With v and v_out
+ * non-NULL the v rows (v_ld apart) are copied to contiguous v_out too. */
+int32_t pkv_rope(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
+                 void* k_out, void* v_out, int64_t rows, int64_t q_ld, int64_t k_ld, int64_t v_ld, int32_t q_heads,
+                 int32_t kv_heads, int32_t head_dim, int32_t dtype, void* stream);
 /* Qwen2MLP's act_fn(gate) * up with SiLU: out[r][c] = to_dtype(to_dtype(
  * silu(gate)) * up) for rows x cols, gate / up rows ld_in elements apart. */
 int32_t pkv_silu_mul(const void* gate, const void* up, void* out, int64_t rows, int64_t cols, int64_t ld_in,

@@ -185,8 +185,8 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "pkv_rope": (
         c_int32,
-        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
-         c_void_p],
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+         c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p],
     ),
     "pkv_silu_mul": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "pkv_sampling_workspace_bytes": (c_int64, [c_int64, c_int32]),

@@ -98,11 +98,14 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
   }
 }
 
-// One CTA per token row: q heads then k heads, D columns each.
+// One CTA per token row: q heads, then k heads (rotated), then v heads
+// (copied, when given); inputs rows q_ld / k_ld / v_ld elements apart (one
+// packed q|k|v projection row, or three tensors), outputs contiguous.
 template <typename T>
-__global__ void rope_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ cosv,
-                            const T* __restrict__ sinv, T* __restrict__ q_out, T* __restrict__ k_out, int hq, int hkv,
-                            int d) {
+__global__ void rope_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                            const T* __restrict__ cosv, const T* __restrict__ sinv, T* __restrict__ q_out,
+                            T* __restrict__ k_out, T* __restrict__ v_out, int64_t q_ld, int64_t k_ld, int64_t v_ld,
+                            int hq, int hkv, int d) {
   const int64_t row = blockIdx.x;
   const int half = d >> 1;
   const T* c = cosv + row * d;
@@ -111,11 +114,14 @@ __global__ void rope_kernel(const T* __restrict__ q, const T* __restrict__ k, co
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int h = i / d, e = i - h * d;
     const bool is_q = h < hq;
-    const T* x = is_q ? q + (row * hq + h) * d : k + (row * hkv + (h - hq)) * d;
+    const T* x = is_q ? q + row * q_ld + h * d : k + row * k_ld + (h - hq) * d;
     T* o = is_q ? q_out + (row * hq + h) * d : k_out + (row * hkv + (h - hq)) * d;
     const float xv = Cvt<T>::f(x[e]);
     const float rot = e < half ? -Cvt<T>::f(x[e + half]) : Cvt<T>::f(x[e - half]);
     o[e] = Cvt<T>::t(rnd<T>(xv * Cvt<T>::f(c[e])) + rnd<T>(rot * Cvt<T>::f(s[e])));
+  }
+  if (v) {
+    for (int i = threadIdx.x; i < hkv * d; i += blockDim.x) v_out[row * hkv * d + i] = v[row * v_ld + i];
   }
 }
 
@@ -180,11 +186,13 @@ int32_t pkv_rms_norm(const void* x, const void* residual, void* sum_out, const v
   return cuda_status(cudaGetLastError(), "pkv_rms_norm launch");
 }
 
-int32_t pkv_rope(const void* q, const void* k, const void* cos, const void* sin, void* q_out, void* k_out,
-                 int64_t rows, int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t dtype, void* stream) {
+int32_t pkv_rope(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
+                 void* k_out, void* v_out, int64_t rows, int64_t q_ld, int64_t k_ld, int64_t v_ld, int32_t q_heads,
+                 int32_t kv_heads, int32_t head_dim, int32_t dtype, void* stream) {
   pkv_clear_error();
-  if (!q || !k || !cos || !sin || !q_out || !k_out || rows < 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 ||
-      head_dim % 2) {
+  if (!q || !k || !cos || !sin || !q_out || !k_out || (v != nullptr) != (v_out != nullptr) || rows < 0 ||
+      q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 2 || q_ld < (int64_t)q_heads * head_dim ||
+      k_ld < (int64_t)kv_heads * head_dim || (v && v_ld < (int64_t)kv_heads * head_dim)) {
     pkv_set_error("pkv_rope: invalid arguments");
     return PKV_ERR_ARG;
   }
@@ -197,16 +205,16 @@ int32_t pkv_rope(const void* q, const void* k, const void* cos, const void* sin,
   const int threads = 256;
   if (dtype == PKV_BF16) {
     using T = __nv_bfloat16;
-    rope_kernel<T><<<(unsigned)rows, threads, 0, s>>>(static_cast<const T*>(q), static_cast<const T*>(k),
-                                                     static_cast<const T*>(cos), static_cast<const T*>(sin),
-                                                     static_cast<T*>(q_out), static_cast<T*>(k_out), q_heads,
-                                                     kv_heads, head_dim);
+    rope_kernel<T><<<(unsigned)rows, threads, 0, s>>>(
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(cos),
+        static_cast<const T*>(sin), static_cast<T*>(q_out), static_cast<T*>(k_out), static_cast<T*>(v_out), q_ld,
+        k_ld, v_ld, q_heads, kv_heads, head_dim);
   } else {
     using T = __half;
-    rope_kernel<T><<<(unsigned)rows, threads, 0, s>>>(static_cast<const T*>(q), static_cast<const T*>(k),
-                                                     static_cast<const T*>(cos), static_cast<const T*>(sin),
-                                                     static_cast<T*>(q_out), static_cast<T*>(k_out), q_heads,
-                                                     kv_heads, head_dim);
+    rope_kernel<T><<<(unsigned)rows, threads, 0, s>>>(
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(cos),
+        static_cast<const T*>(sin), static_cast<T*>(q_out), static_cast<T*>(k_out), static_cast<T*>(v_out), q_ld,
+        k_ld, v_ld, q_heads, kv_heads, head_dim);
   }
   return cuda_status(cudaGetLastError(), "pkv_rope launch");
 }

@@ -99,14 +99,18 @@ def paged_attention_forward(module, query, key, value, attention_mask=None, scal
     return out.view(b, t, hq, d), None
 
 
-# -- fused elementwise layers -------------------------------------------------
+# -- fused layers ---------------------------------------------------------------
 # Inside a PagedGenerator forward, the decoder layers of a Qwen2-family model
 # on the GPU (bf16 / f16, SiLU MLP) run their RMSNorms (with the residual add
 # folded into the second), rotary embedding and SiLU product as single
 # launches of the library (pkv_rms_norm, pkv_rope, pkv_silu_mul) instead of
-# HF's eager op chains, and hand the rotated q / k to the store without the
-# HF layout transposes.  Outside such a forward every module runs its own HF
-# code unchanged.
+# HF's eager op chains; q / k / v come from one GEMM over the three
+# projections' weights and gate / up from one over the MLP's two (the
+# parameters become views into those packed weights: no extra memory, HF's
+# modules see the same values), the MLP's residual add rides in the down
+# projection's GEMM (addmm), and the rotated q / k reach the store without
+# the HF layout transposes.  Outside such a forward every module runs its own
+# HF code unchanged.
 
 def _dtype_code(t: torch.Tensor) -> int:
     from ._lib import PKV_BF16, PKV_F16
@@ -148,9 +152,31 @@ def fused_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.T
     sin = sin.contiguous()
     qo = torch.empty((rows, hq, head_dim), dtype=q.dtype, device=q.device)
     ko = torch.empty((rows, hkv, head_dim), dtype=k.dtype, device=k.device)
-    raise_for_status(lib.pkv_rope(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
-                                  ko.data_ptr(), rows, hq, hkv, head_dim, _dtype_code(q), _stream()))
+    raise_for_status(lib.pkv_rope(q.data_ptr(), k.data_ptr(), None, cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
+                                  ko.data_ptr(), None, rows, hq * head_dim, hkv * head_dim, 0, hq, hkv, head_dim,
+                                  _dtype_code(q), _stream()))
     return qo, ko
+
+
+def fused_rope_qkv(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, hq: int, hkv: int, head_dim: int):
+    """One packed projection row per token, [..., (Hq + 2 Hkv) * D] = q | k | v -> rotated q [rows, Hq, D],
+    rotated k and v [rows, Hkv, D], contiguous."""
+    from ._lib import lib, raise_for_status
+
+    ld = qkv.shape[-1]
+    rows = qkv.numel() // ld
+    qkv = qkv.contiguous()
+    cos = cos.contiguous()
+    sin = sin.contiguous()
+    qo = torch.empty((rows, hq, head_dim), dtype=qkv.dtype, device=qkv.device)
+    ko = torch.empty((rows, hkv, head_dim), dtype=qkv.dtype, device=qkv.device)
+    vo = torch.empty((rows, hkv, head_dim), dtype=qkv.dtype, device=qkv.device)
+    esz = qkv.element_size()
+    base = qkv.data_ptr()
+    raise_for_status(lib.pkv_rope(base, base + hq * head_dim * esz, base + (hq + hkv) * head_dim * esz,
+                                  cos.data_ptr(), sin.data_ptr(), qo.data_ptr(), ko.data_ptr(), vo.data_ptr(), rows,
+                                  ld, ld, ld, hq, hkv, head_dim, _dtype_code(qkv), _stream()))
+    return qo, ko, vo
 
 
 def fused_silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -166,6 +192,21 @@ def fused_silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def fused_silu_mul_packed(gate_up: torch.Tensor) -> torch.Tensor:
+    """SiLU(gate) * up from one packed row [..., 2 * I] = gate | up -> [rows, I]."""
+    from ._lib import lib, raise_for_status
+
+    gate_up = gate_up.contiguous()
+    ld = gate_up.shape[-1]
+    cols = ld // 2
+    rows = gate_up.numel() // ld
+    out = torch.empty((rows, cols), dtype=gate_up.dtype, device=gate_up.device)
+    base = gate_up.data_ptr()
+    raise_for_status(lib.pkv_silu_mul(base, base + cols * gate_up.element_size(), out.data_ptr(), rows, cols, ld,
+                                      _dtype_code(gate_up), _stream()))
+    return out
+
+
 def _fused_norm_forward(self, hidden_states):
     if getattr(_local, "phase", None) is None:
         return type(self).forward(self, hidden_states)
@@ -175,7 +216,15 @@ def _fused_norm_forward(self, hidden_states):
 def _fused_mlp_forward(self, x):
     if getattr(_local, "phase", None) is None:
         return type(self).forward(self, x)
-    return self.down_proj(fused_silu_mul(self.gate_proj(x), self.up_proj(x)))
+    act = fused_silu_mul_packed(torch.nn.functional.linear(x, self._pkv_gate_up))
+    return self.down_proj(act).view(*x.shape[:-1], -1)
+
+
+def _fused_mlp_residual(mlp, x, residual):
+    """residual + mlp(x), the add done by the down projection's GEMM (addmm, beta = 1)."""
+    act = fused_silu_mul_packed(torch.nn.functional.linear(x, mlp._pkv_gate_up))
+    res = residual.reshape(-1, residual.shape[-1])
+    return torch.addmm(res, act, mlp.down_proj.weight.t()).view(residual.shape)
 
 
 def _fused_attention_forward(self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
@@ -188,9 +237,9 @@ def _fused_attention_forward(self, hidden_states, position_embeddings, attention
     b, t = int(input_shape[0]), int(input_shape[1])
     d = int(self.head_dim)
     cos, sin = position_embeddings
-    q, k = fused_rope(self.q_proj(hidden_states), self.k_proj(hidden_states), cos, sin, d)
-    v = self.v_proj(hidden_states)
-    v = v.reshape(b * t, v.shape[-1] // d, d)
+    w, bias, hq, hkv = self._pkv_qkv
+    qkv = torch.nn.functional.linear(hidden_states, w, bias)
+    q, k, v = fused_rope_qkv(qkv, cos, sin, hq, hkv, d)
     out = _paged_rows(ph, int(self.layer_idx), q, k, v, b, t, self.scaling)
     return self.o_proj(out.reshape(*input_shape, -1)), None
 
@@ -206,7 +255,35 @@ def _fused_layer_forward(self, hidden_states, attention_mask=None, position_ids=
                           past_key_values=past_key_values, use_cache=use_cache,
                           position_embeddings=position_embeddings, **kwargs)
     h2, hidden = fused_rms_norm(a, self.post_attention_layernorm, residual=hidden_states)
+    if getattr(self.mlp.down_proj, "bias", None) is None:
+        return _fused_mlp_residual(self.mlp, h2, hidden)
     return hidden + self.mlp(h2)
+
+
+def _pack_weights(layer) -> None:
+    """q / k / v (and their biases) and gate / up weights concatenated once; the modules' parameters
+    become views into the packed tensors (the same values, no extra memory)."""
+    attn, mlp = layer.self_attn, layer.mlp
+    if not hasattr(attn, "_pkv_qkv"):
+        projs = (attn.q_proj, attn.k_proj, attn.v_proj)
+        d = int(attn.head_dim)
+        w = torch.cat([p.weight for p in projs], 0)
+        has_bias = all(getattr(p, "bias", None) is not None for p in projs)
+        b = torch.cat([p.bias for p in projs], 0) if has_bias else None
+        o = 0
+        for p in projs:
+            n = p.weight.shape[0]
+            p.weight.data = w[o:o + n]
+            if has_bias:
+                p.bias.data = b[o:o + n]
+            o += n
+        attn._pkv_qkv = (w, b, attn.q_proj.weight.shape[0] // d, attn.k_proj.weight.shape[0] // d)
+    if not hasattr(mlp, "_pkv_gate_up"):
+        gu = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0)
+        n = mlp.gate_proj.weight.shape[0]
+        mlp.gate_proj.weight.data = gu[:n]
+        mlp.up_proj.weight.data = gu[n:]
+        mlp._pkv_gate_up = gu
 
 
 def install_fused_layers(model) -> bool:
@@ -226,8 +303,12 @@ def install_fused_layers(model) -> bool:
         parts = (getattr(layer, "input_layernorm", None), getattr(layer, "post_attention_layernorm", None))
         if (attn is None or mlp is None or None in parts or not all(hasattr(n, "variance_epsilon") for n in parts)
                 or not all(hasattr(attn, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj", "head_dim"))
-                or not all(hasattr(mlp, a) for a in ("gate_proj", "up_proj", "down_proj"))):
+                or not all(hasattr(mlp, a) for a in ("gate_proj", "up_proj", "down_proj"))
+                or getattr(mlp.gate_proj, "bias", None) is not None or getattr(mlp.up_proj, "bias", None) is not None):
             return False
+    with torch.no_grad():
+        for layer in layers:
+            _pack_weights(layer)
     for layer in layers:
         layer.forward = types.MethodType(_fused_layer_forward, layer)
         layer.self_attn.forward = types.MethodType(_fused_attention_forward, layer.self_attn)

@@ -79,17 +79,44 @@ def test_rope_equals_hf(cuda_device, dtype, hq, hkv, d, b, t):
     assert torch.equal(got_k.view(b, t, hkv, d), want_k.transpose(1, 2))
 
 
+@pytest.mark.parametrize("hq,hkv,d,b,t", [(12, 2, 128, 32, 1), (28, 4, 128, 1, 70), (14, 2, 64, 2, 9)])
+def test_rope_on_a_packed_qkv_row_equals_hf(cuda_device, hq, hkv, d, b, t):
+    """One packed projection row q | k | v per token (the concatenated-weight GEMM's output)."""
+    from randomrepo_b200.hf import fused_rope_qkv
+    from transformers import Qwen2Config
+    from transformers.models.qwen2 import modeling_qwen2 as m
+
+    dtype = torch.bfloat16
+    g = torch.Generator(device=cuda_device).manual_seed(hq + d + t)
+    qkv = torch.randn((b, t, (hq + 2 * hkv) * d), generator=g, device=cuda_device).to(dtype)
+    q, k, v = qkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+    cfg = Qwen2Config(hidden_size=hq * d, num_attention_heads=hq, num_key_value_heads=hkv, head_dim=d,
+                      rope_theta=1e6, max_position_embeddings=32768)
+    rot = m.Qwen2RotaryEmbedding(cfg).to(cuda_device)
+    pos = torch.randint(0, 4000, (b, t), generator=g, device=cuda_device)
+    cos, sin = rot(qkv, pos)
+    want_q, want_k = m.apply_rotary_pos_emb(q.reshape(b, t, hq, d).transpose(1, 2),
+                                            k.reshape(b, t, hkv, d).transpose(1, 2), cos, sin)
+    got_q, got_k, got_v = fused_rope_qkv(qkv, cos, sin, hq, hkv, d)
+    torch.cuda.synchronize()
+    assert torch.equal(got_q.view(b, t, hq, d), want_q.transpose(1, 2))
+    assert torch.equal(got_k.view(b, t, hkv, d), want_k.transpose(1, 2))
+    assert torch.equal(got_v.view(b, t, hkv * d), v)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("rows,cols", [(32, 8960), (5, 18944), (700, 4864), (1, 3)])
 def test_silu_mul_equals_hf(cuda_device, dtype, rows, cols):
-    from randomrepo_b200.hf import fused_silu_mul
+    from randomrepo_b200.hf import fused_silu_mul, fused_silu_mul_packed
 
     g = torch.Generator(device=cuda_device).manual_seed(rows + cols)
     gate = (torch.randn((rows, cols), generator=g, device=cuda_device) * 4).to(dtype)
     up = torch.randn((rows, cols), generator=g, device=cuda_device).to(dtype)
     want = torch.nn.functional.silu(gate) * up
     got = fused_silu_mul(gate, up)
+    packed = fused_silu_mul_packed(torch.cat([gate, up], dim=-1))
     torch.cuda.synchronize()
+    assert torch.equal(packed, got)
     u = _ulps(got, want)
     assert int(u.max()) <= 1
     assert float((u == 0).float().mean()) >= 0.999
@@ -103,7 +130,9 @@ def test_layer_ops_reject_bad_arguments(cuda_device):
                             None) == PKV_ERR_ARG
     assert lib.pkv_rms_norm(x.data_ptr(), x.data_ptr(), None, x.data_ptr(), x.data_ptr(), 2, 16, 1e-6, PKV_BF16,
                             None) == PKV_ERR_ARG
-    assert lib.pkv_rope(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 2, 1, 1,
-                        15, PKV_BF16, None) == PKV_ERR_ARG
+    p = x.data_ptr()
+    assert lib.pkv_rope(p, p, None, p, p, p, p, None, 2, 16, 16, 0, 1, 1, 15, PKV_BF16, None) == PKV_ERR_ARG  # odd D
+    assert lib.pkv_rope(p, p, None, p, p, p, p, None, 2, 8, 16, 0, 1, 1, 16, PKV_BF16, None) == PKV_ERR_ARG  # q_ld
+    assert lib.pkv_rope(p, p, p, p, p, p, p, None, 2, 16, 16, 16, 1, 1, 16, PKV_BF16, None) == PKV_ERR_ARG  # v alone
     assert lib.pkv_silu_mul(x.data_ptr(), x.data_ptr(), x.data_ptr(), 2, 16, 8, PKV_BF16, None) == PKV_ERR_ARG
     assert lib.pkv_silu_mul(x.data_ptr(), x.data_ptr(), x.data_ptr(), 2, 16, 16, PKV_F32, None) == PKV_ERR_UNSUPPORTED
