@@ -609,7 +609,8 @@ def run_rollout(device: torch.device, seed: int, iters: int = 2) -> tuple[dict, 
                     f"{rs['temperature']}, seed {seed}",
         "tokens_per_s": ours_tps,
         "path": "PagedGenerator: packed prefill kernel, one prefill per group + copy-on-write forks, CUDA-graph "
-                "decode steps (fused append + paged decode per layer), fp32 logits, device sampling kernel",
+                "decode steps (fused append + paged decode per layer; fused RMSNorm / rotary / SiLU launches and "
+                "packed q|k|v and gate|up GEMMs), fp32 logits, device sampling kernel",
         "hf_generate_tokens_per_s": hf_tps,
         "hf_generate_path": "stock HF generate on the same model and batch (SDPA + DynamicCache, left-padded)",
         "speedup_vs_hf_generate": ours_tps / hf_tps,
@@ -702,8 +703,9 @@ def run_decode_7b(device: torch.device, seed: int) -> dict:
                     f"(mean context {float(ctx.mean()):.0f}), temperature {sh['temperature']}, seed {seed}",
         "tokens_per_s": n * 1e3 / ms,
         "ms_per_step": ms,
-        "path": "PagedGenerator.decode_step (CUDA graph: 28 x fused append + paged decode, HF projections / "
-                "MLPs through cuBLAS, fp32 LM head) + DeviceSampler.sample",
+        "path": "PagedGenerator.decode_step (CUDA graph: 28 x fused append + paged decode, fused RMSNorm / "
+                "rotary / SiLU launches, packed q|k|v and gate|up GEMMs through cuBLAS, fp32 LM head) + "
+                "DeviceSampler.sample",
         "bytes_per_step": step_bytes,
         "bytes_rule": "weights except the input embedding (+ the 512 embedding rows read) + K/V of every "
                       "sequence's context + the appended K/V + fp32 logits",
