@@ -18,8 +18,13 @@
 //    for every q and k head of a token row, written head-major [rows][heads][D];
 //  * silu_mul: out = to_dtype(to_dtype(g / (1 + exp(-g))) * u).
 //
-// All three are bandwidth-bound: one CTA per token row (norm, rope) or per
-// 2048 columns of a row (silu_mul).
+// All three are bandwidth-bound and, at decode batch sizes, latency-bound
+// (a step's rows are 100 KB-1 MB): the fast paths move 16-byte vectors of
+// eight elements -- a warp per row for the norm (shuffles only, no block
+// barrier), eight consecutive columns per thread for the SiLU product, and
+// for rope eight columns of a head's first half with the eight they pair with
+// in its second half -- and general kernels take shapes whose rows are not
+// multiples of eight elements.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -98,6 +103,132 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
   }
 }
 
+// Eight elements of T in one 16-byte vector.
+template <typename T>
+struct Vec8 {
+  uint4 raw;
+  __device__ __forceinline__ float get(int i) const {
+    const T* e = reinterpret_cast<const T*>(&raw);
+    return Cvt<T>::f(e[i]);
+  }
+  __device__ __forceinline__ void set(int i, float v) {
+    T* e = reinterpret_cast<T*>(&raw);
+    e[i] = Cvt<T>::t(v);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ Vec8<T> ld8(const T* p) {
+  Vec8<T> v;
+  v.raw = *reinterpret_cast<const uint4*>(p);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const Vec8<T>& v) {
+  *reinterpret_cast<uint4*>(p) = v.raw;
+}
+
+constexpr int kNormWarps = 4;
+
+// A warp per row; hidden % 8 == 0 and 16-byte aligned rows.  Pass 1 folds the
+// residual (storing the sum) and accumulates x^2; pass 2 re-reads the row
+// (its own sum writes, or the input, from L1 / L2) and writes the output.
+template <typename T>
+__global__ void __launch_bounds__(kNormWarps * 32) rms_norm_warp_kernel(const T* __restrict__ a,
+                                                                        const T* __restrict__ b,
+                                                                        T* __restrict__ sum_out,
+                                                                        const T* __restrict__ w,
+                                                                        T* __restrict__ out, int64_t rows,
+                                                                        int hidden, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int nvec = hidden >> 3;
+  const T* ar = a + row * hidden;
+  const T* br = b ? b + row * hidden : nullptr;
+  T* sr = sum_out ? sum_out + row * hidden : nullptr;
+  float ss = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    Vec8<T> x = ld8(ar + 8 * v);
+    if (br) {
+      const Vec8<T> y = ld8(br + 8 * v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x.set(i, x.get(i) + y.get(i));
+      st8(sr + 8 * v, x);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(x.get(i), x.get(i), ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float inv = rsqrtf(ss / (float)hidden + eps);
+  const T* src = sr ? sr : ar;
+  T* orow = out + row * hidden;
+  for (int v = lane; v < nvec; v += 32) {
+    const Vec8<T> x = ld8(src + 8 * v);
+    const Vec8<T> g = ld8(w + 8 * v);
+    Vec8<T> o;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o.set(i, g.get(i) * rnd<T>(x.get(i) * inv));
+    st8(orow + 8 * v, o);
+  }
+}
+
+// Rope on 16-byte vectors: a thread takes columns [8j, 8j + 8) of a head's
+// first half and the eight they pair with in its second half (d % 16 == 0,
+// row strides multiples of 8 elements).  One CTA per token row.
+template <typename T>
+__global__ void rope_vec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                                const T* __restrict__ cosv, const T* __restrict__ sinv, T* __restrict__ q_out,
+                                T* __restrict__ k_out, T* __restrict__ v_out, int64_t q_ld, int64_t k_ld,
+                                int64_t v_ld, int hq, int hkv, int d) {
+  const int64_t row = blockIdx.x;
+  const int half = d >> 1, per_head = half >> 3;
+  const T* c = cosv + row * d;
+  const T* s = sinv + row * d;
+  const int n = (hq + hkv) * per_head;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int h = i / per_head, e = (i - h * per_head) * 8;
+    const bool is_q = h < hq;
+    const T* x = is_q ? q + row * q_ld + h * d : k + row * k_ld + (h - hq) * d;
+    T* o = is_q ? q_out + (row * hq + h) * d : k_out + (row * hkv + (h - hq)) * d;
+    const Vec8<T> lo = ld8(x + e), hi = ld8(x + e + half);
+    const Vec8<T> cl = ld8(c + e), ch = ld8(c + e + half), sl = ld8(s + e), sh = ld8(s + e + half);
+    Vec8<T> ol, oh;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // rotate_half: first half pairs with -second half, second half with first half.
+      ol.set(j, rnd<T>(lo.get(j) * cl.get(j)) + rnd<T>(-hi.get(j) * sl.get(j)));
+      oh.set(j, rnd<T>(hi.get(j) * ch.get(j)) + rnd<T>(lo.get(j) * sh.get(j)));
+    }
+    st8(o + e, ol);
+    st8(o + e + half, oh);
+  }
+  if (v) {
+    for (int i = threadIdx.x; i < hkv * d / 8; i += blockDim.x) st8(v_out + row * hkv * d + 8 * i, ld8(v + row * v_ld + 8 * i));
+  }
+}
+
+// SiLU product on 16-byte vectors (cols % 8 == 0, ld_in % 8 == 0): a CTA
+// takes 2048 columns of one row, a thread eight of them.
+template <typename T>
+__global__ void silu_mul_vec_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ out, int chunks,
+                                    int64_t ld_in, int cols) {
+  const int64_t r = blockIdx.x / chunks;
+  const int c0 = (int)(blockIdx.x - r * chunks) * 2048;
+  const int c = c0 + 8 * threadIdx.x;
+  if (c >= cols) return;
+  const Vec8<T> gv = ld8(g + r * ld_in + c), uv = ld8(u + r * ld_in + c);
+  Vec8<T> o;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float x = gv.get(j);
+    o.set(j, rnd<T>(x / (1.f + expf(-x))) * uv.get(j));
+  }
+  st8(out + r * (int64_t)cols + c, o);
+}
+
 // One CTA per token row: q heads, then k heads (rotated), then v heads
 // (copied, when given); inputs rows q_ld / k_ld / v_ld elements apart (one
 // packed q|k|v projection row, or three tensors), outputs contiguous.
@@ -145,6 +276,8 @@ __global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u
   }
 }
 
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
 int32_t cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return PKV_OK;
   pkv_set_error(std::string(what) + ": " + cudaGetErrorString(e));
@@ -172,6 +305,23 @@ int32_t pkv_rms_norm(const void* x, const void* residual, void* sum_out, const v
   }
   if (rows == 0) return PKV_OK;
   auto s = static_cast<cudaStream_t>(stream);
+  const bool vec = hidden % 8 == 0 && aligned16(x) && aligned16(weight) && aligned16(out) && aligned16(residual) &&
+                   aligned16(sum_out);
+  if (vec) {
+    const unsigned blocks = (unsigned)((rows + kNormWarps - 1) / kNormWarps);
+    if (dtype == PKV_BF16) {
+      using T = __nv_bfloat16;
+      rms_norm_warp_kernel<T><<<blocks, kNormWarps * 32, 0, s>>>(
+          static_cast<const T*>(x), static_cast<const T*>(residual), static_cast<T*>(sum_out),
+          static_cast<const T*>(weight), static_cast<T*>(out), rows, hidden, eps);
+    } else {
+      using T = __half;
+      rms_norm_warp_kernel<T><<<blocks, kNormWarps * 32, 0, s>>>(
+          static_cast<const T*>(x), static_cast<const T*>(residual), static_cast<T*>(sum_out),
+          static_cast<const T*>(weight), static_cast<T*>(out), rows, hidden, eps);
+    }
+    return cuda_status(cudaGetLastError(), "pkv_rms_norm launch");
+  }
   if (dtype == PKV_BF16) {
     using T = __nv_bfloat16;
     rms_norm_kernel<T><<<(unsigned)rows, kNormThreads, 0, s>>>(
@@ -202,6 +352,26 @@ int32_t pkv_rope(const void* q, const void* k, const void* v, const void* cos, c
   }
   if (rows == 0) return PKV_OK;
   auto s = static_cast<cudaStream_t>(stream);
+  const bool vec = head_dim % 16 == 0 && q_ld % 8 == 0 && k_ld % 8 == 0 && (!v || v_ld % 8 == 0) && aligned16(q) &&
+                   aligned16(k) && aligned16(v) && aligned16(cos) && aligned16(sin) && aligned16(q_out) &&
+                   aligned16(k_out) && aligned16(v_out);
+  if (vec) {
+    const int threads = 128;
+    if (dtype == PKV_BF16) {
+      using T = __nv_bfloat16;
+      rope_vec_kernel<T><<<(unsigned)rows, threads, 0, s>>>(
+          static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(cos),
+          static_cast<const T*>(sin), static_cast<T*>(q_out), static_cast<T*>(k_out), static_cast<T*>(v_out), q_ld,
+          k_ld, v_ld, q_heads, kv_heads, head_dim);
+    } else {
+      using T = __half;
+      rope_vec_kernel<T><<<(unsigned)rows, threads, 0, s>>>(
+          static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(cos),
+          static_cast<const T*>(sin), static_cast<T*>(q_out), static_cast<T*>(k_out), static_cast<T*>(v_out), q_ld,
+          k_ld, v_ld, q_heads, kv_heads, head_dim);
+    }
+    return cuda_status(cudaGetLastError(), "pkv_rope launch");
+  }
   const int threads = 256;
   if (dtype == PKV_BF16) {
     using T = __nv_bfloat16;
@@ -238,6 +408,18 @@ int32_t pkv_silu_mul(const void* gate, const void* up, void* out, int64_t rows, 
   }
   auto s = static_cast<cudaStream_t>(stream);
   const unsigned blocks = (unsigned)(rows * chunks);
+  if (cols % 8 == 0 && ld_in % 8 == 0 && aligned16(gate) && aligned16(up) && aligned16(out)) {
+    if (dtype == PKV_BF16) {
+      using T = __nv_bfloat16;
+      silu_mul_vec_kernel<T><<<blocks, kSiluCols / 8, 0, s>>>(static_cast<const T*>(gate), static_cast<const T*>(up),
+                                                              static_cast<T*>(out), chunks, ld_in, (int)cols);
+    } else {
+      using T = __half;
+      silu_mul_vec_kernel<T><<<blocks, kSiluCols / 8, 0, s>>>(static_cast<const T*>(gate), static_cast<const T*>(up),
+                                                              static_cast<T*>(out), chunks, ld_in, (int)cols);
+    }
+    return cuda_status(cudaGetLastError(), "pkv_silu_mul launch");
+  }
   const int threads = 256;
   if (dtype == PKV_BF16) {
     using T = __nv_bfloat16;

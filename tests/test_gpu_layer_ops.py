@@ -34,7 +34,7 @@ def _ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("hidden,rows", [(1536, 32), (3584, 7), (896, 513)])
+@pytest.mark.parametrize("hidden,rows", [(1536, 32), (3584, 7), (896, 513), (100, 9)])  # 100: the general kernel
 def test_rms_norm_matches_hf(cuda_device, dtype, hidden, rows):
     from randomrepo_b200.hf import fused_rms_norm
 
@@ -57,7 +57,8 @@ def test_rms_norm_matches_hf(cuda_device, dtype, hidden, rows):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("hq,hkv,d,b,t", [(12, 2, 128, 32, 1), (28, 4, 128, 1, 300), (14, 2, 64, 3, 17)])
+@pytest.mark.parametrize("hq,hkv,d,b,t", [(12, 2, 128, 32, 1), (28, 4, 128, 1, 300), (14, 2, 64, 3, 17),
+                                          (4, 2, 40, 2, 5)])  # d = 40: the general kernel
 def test_rope_equals_hf(cuda_device, dtype, hq, hkv, d, b, t):
     from randomrepo_b200.hf import fused_rope
     from transformers import Qwen2Config
