@@ -199,3 +199,27 @@ def test_paged_generator_reproduces_the_reference_orchestrator_c1():
     assert [len(t) for t in got] == [len(w) for w in want]
     assert same / total >= 0.99, (same, total)
     assert got == want
+
+
+def test_packed_projection_weights_keep_the_model_unchanged():
+    """The fused layers pack q / k / v and gate / up weights into one tensor each; the modules' parameters
+    become views into them, so HF's own forward gives bit-identical logits, and no extra copy stays alive."""
+    from randomrepo_b200.hf import _pack_weights, install_fused_layers
+
+    model = _tiny_model()
+    ids = torch.randint(0, 128, (1, 17), generator=torch.Generator().manual_seed(4))
+    with torch.no_grad():
+        before = model(input_ids=ids).logits
+        for layer in model.model.layers:
+            _pack_weights(layer)
+        after = model(input_ids=ids).logits
+    assert torch.equal(before, after)
+    for layer in model.model.layers:
+        w, b, hq, hkv = layer.self_attn._pkv_qkv
+        attn = layer.self_attn
+        assert attn.q_proj.weight.data_ptr() == w.data_ptr()
+        assert attn.k_proj.weight.data_ptr() == w[hq * 16:].data_ptr()
+        assert attn.v_proj.bias.data_ptr() == b[(hq + hkv) * 16:].data_ptr()
+        assert layer.mlp.up_proj.weight.data_ptr() == layer.mlp._pkv_gate_up[128:].data_ptr()
+    # A CPU / fp32 model keeps HF's forwards: the fused kernels are for bf16 / f16 on the GPU.
+    assert install_fused_layers(_tiny_model()) is False
