@@ -377,7 +377,11 @@ class PagedGenerator:
     """Rollout loop of a causal LM over the paged store (continuous.py:363-504 without the per-sequence caches).
 
     Token selection and log-probabilities go through ``sampler`` (by default
-    the library's ``DeviceSampler`` kernels, created on first use).
+    the library's ``DeviceSampler`` kernels, created on first use).  With
+    ``fused_layers`` (the default) a Qwen2-family model on the GPU gets the
+    fused decoder-layer forwards (``install_fused_layers``): per model
+    instance, so a model fused once stays fused for other generators, and
+    active only inside these generators' forwards.
     """
 
     def __init__(self, model, store, *, prefill_chunk_size: int = 512, eos_token_id: int | None = None,
