@@ -27,7 +27,7 @@
 // sample, a Gumbel-max race: key = x / T + g with g = -log(-log u) and u
 // uniform in (0, 1); the column with the largest key is a draw from
 // softmax(x / T) (Gumbel 1954; the "Gumbel-max trick").  u comes from a
-// counter-based hash of (seed, offset, row, column): SplitMix64's output
+// counter-based hash of (seed, offset, row, column pair): SplitMix64's output
 // function (Steele, Lea & Flood 2014), so a draw needs no RNG state.
 #include <cuda_runtime.h>
 #include <math.h>
@@ -67,21 +67,34 @@ __device__ __forceinline__ uint64_t row_key(uint64_t seed, uint64_t offset, uint
   return mix64(mix64(seed + 0x9e3779b97f4a7c15ull * (offset + 1)) ^ (row * 4 + stream));
 }
 
-// u in (0, 1) from 23 hashed bits: (i + 1/2) 2^-23, so -log u > 0 always.
-__device__ __forceinline__ float uniform_open(uint64_t h) {
-  return ((float)(uint32_t)(h >> 41) + 0.5f) * 0x1p-23f;
-}
-
 // u in [0, 1) (the range torch.rand draws from).
 __device__ __forceinline__ float uniform_co(uint64_t h) { return (float)(uint32_t)(h >> 40) * 0x1p-24f; }
 
-// g = -log(-log u).  The inner log is the accurate one: u near 1 gives the
-// small -log u that wins races, so it needs relative accuracy there; the
-// outer log only shifts keys by its absolute error (~1e-7).
-__device__ __forceinline__ float gumbel(uint64_t key, int v) {
-  const float u = uniform_open(mix64(key + (uint64_t)(uint32_t)v * 0xd1b54a32d192ed03ull));
-  return -__logf(-logf(u));
+// Column v's 23 random bits: one SplitMix64 output serves the column pair
+// (2m, 2m + 1), bits 41..63 for the even column and 18..40 for the odd one,
+// so a race over consecutive columns hashes once per two.
+__device__ __forceinline__ uint64_t pair_hash(uint64_t key, int v) {
+  return mix64(key + (uint64_t)((uint32_t)v >> 1) * 0xd1b54a32d192ed03ull);
 }
+__device__ __forceinline__ uint32_t pair_bits(uint64_t h, int v) {
+  return (uint32_t)((v & 1) ? (h >> 18) : (h >> 41)) & 0x7fffffu;
+}
+
+// g = -log(E), E = -log(u), u = (i + 1/2) 2^-23.  E needs relative accuracy
+// where it is small (u near 1: the keys that win races): there it is the
+// Taylor series of -log(1 - w) in w = 1 - u (exact in float), five terms
+// below w = 2^-6 (truncation ~w^5 / 6 relative), elsewhere the fast log,
+// whose ~1e-7 absolute error is then a relative one below 1e-5.  The outer
+// log only shifts keys by its absolute error.
+__device__ __forceinline__ float gumbel_of(uint32_t i) {
+  const float u = ((float)i + 0.5f) * 0x1p-23f;
+  const float w = ((float)(0x7fffffu - i) + 0.5f) * 0x1p-23f;
+  const float series = w * (1.f + w * (0.5f + w * (1.f / 3.f + w * (0.25f + w * 0.2f))));
+  const float e = w < 0x1p-6f ? series : -__logf(u);
+  return -__logf(e);
+}
+
+__device__ __forceinline__ float gumbel(uint64_t key, int v) { return gumbel_of(pair_bits(pair_hash(key, v), v)); }
 
 // ---------------------------------------------------------------------------
 // Reductions.
@@ -273,14 +286,20 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(const RowArgs a) {
       }
     }
     if (RACE) {
+      // Vector loads give consecutive columns, so pairs (2m, 2m + 1) share one hash.
 #pragma unroll
-      for (int q = 0; q < kGroup; ++q) {
-        const float v = RACE == 2 ? rx[q] : x[q];
-        if (v == -INFINITY) continue;
-        const float kk = fmaf(v, a.race_scale, gumbel(key, col[q]));
-        if (kk > t.rkey) {
-          t.rkey = kk;
-          t.ridx = col[q];
+      for (int q = 0; q < kGroup; q += 2) {
+        const uint64_t h = VEC ? pair_hash(key, col[q]) : 0;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float v = RACE == 2 ? rx[q + p] : x[q + p];
+          if (v == -INFINITY) continue;
+          const uint64_t hh = VEC ? h : pair_hash(key, col[q + p]);
+          const float kk = fmaf(v, a.race_scale, gumbel_of(pair_bits(hh, col[q + p])));
+          if (kk > t.rkey) {
+            t.rkey = kk;
+            t.ridx = col[q + p];
+          }
         }
       }
     }
