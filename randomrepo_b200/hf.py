@@ -216,13 +216,21 @@ def _fused_norm_forward(self, hidden_states):
 def _fused_mlp_forward(self, x):
     if getattr(_local, "phase", None) is None:
         return type(self).forward(self, x)
-    act = fused_silu_mul_packed(torch.nn.functional.linear(x, self._pkv_gate_up))
+    act = fused_silu_mul_packed(torch.nn.functional.linear(x, _gate_up(self)))
     return self.down_proj(act).view(*x.shape[:-1], -1)
+
+
+def _gate_up(mlp) -> torch.Tensor:
+    """The packed gate | up weight, packed again if the parameters were re-allocated."""
+    if mlp.gate_proj.weight.data_ptr() != mlp._pkv_gate_up.data_ptr():
+        with torch.no_grad():
+            _pack_gate_up(mlp)
+    return mlp._pkv_gate_up
 
 
 def _fused_mlp_residual(mlp, x, residual):
     """residual + mlp(x), the add done by the down projection's GEMM (addmm, beta = 1)."""
-    act = fused_silu_mul_packed(torch.nn.functional.linear(x, mlp._pkv_gate_up))
+    act = fused_silu_mul_packed(torch.nn.functional.linear(x, _gate_up(mlp)))
     res = residual.reshape(-1, residual.shape[-1])
     return torch.addmm(res, act, mlp.down_proj.weight.t()).view(residual.shape)
 
@@ -238,6 +246,11 @@ def _fused_attention_forward(self, hidden_states, position_embeddings, attention
     d = int(self.head_dim)
     cos, sin = position_embeddings
     w, bias, hq, hkv = self._pkv_qkv
+    if self.q_proj.weight.data_ptr() != w.data_ptr():
+        # The parameters were re-allocated (moved, cast, replaced): pack them again.
+        with torch.no_grad():
+            _pack_qkv(self)
+        w, bias, hq, hkv = self._pkv_qkv
     qkv = torch.nn.functional.linear(hidden_states, w, bias)
     q, k, v = fused_rope_qkv(qkv, cos, sin, hq, hkv, d)
     out = _paged_rows(ph, int(self.layer_idx), q, k, v, b, t, self.scaling)
@@ -260,30 +273,39 @@ def _fused_layer_forward(self, hidden_states, attention_mask=None, position_ids=
     return hidden + self.mlp(h2)
 
 
+def _pack_qkv(attn) -> None:
+    """q / k / v weights (and biases) concatenated; the projections' parameters become views into them."""
+    projs = (attn.q_proj, attn.k_proj, attn.v_proj)
+    d = int(attn.head_dim)
+    w = torch.cat([p.weight for p in projs], 0)
+    has_bias = all(getattr(p, "bias", None) is not None for p in projs)
+    b = torch.cat([p.bias for p in projs], 0) if has_bias else None
+    o = 0
+    for p in projs:
+        n = p.weight.shape[0]
+        p.weight.data = w[o:o + n]
+        if has_bias:
+            p.bias.data = b[o:o + n]
+        o += n
+    attn._pkv_qkv = (w, b, attn.q_proj.weight.shape[0] // d, attn.k_proj.weight.shape[0] // d)
+
+
+def _pack_gate_up(mlp) -> None:
+    """gate / up weights concatenated; the projections' parameters become views into them."""
+    gu = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0)
+    n = mlp.gate_proj.weight.shape[0]
+    mlp.gate_proj.weight.data = gu[:n]
+    mlp.up_proj.weight.data = gu[n:]
+    mlp._pkv_gate_up = gu
+
+
 def _pack_weights(layer) -> None:
     """q / k / v (and their biases) and gate / up weights concatenated once; the modules' parameters
     become views into the packed tensors (the same values, no extra memory)."""
-    attn, mlp = layer.self_attn, layer.mlp
-    if not hasattr(attn, "_pkv_qkv"):
-        projs = (attn.q_proj, attn.k_proj, attn.v_proj)
-        d = int(attn.head_dim)
-        w = torch.cat([p.weight for p in projs], 0)
-        has_bias = all(getattr(p, "bias", None) is not None for p in projs)
-        b = torch.cat([p.bias for p in projs], 0) if has_bias else None
-        o = 0
-        for p in projs:
-            n = p.weight.shape[0]
-            p.weight.data = w[o:o + n]
-            if has_bias:
-                p.bias.data = b[o:o + n]
-            o += n
-        attn._pkv_qkv = (w, b, attn.q_proj.weight.shape[0] // d, attn.k_proj.weight.shape[0] // d)
-    if not hasattr(mlp, "_pkv_gate_up"):
-        gu = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0)
-        n = mlp.gate_proj.weight.shape[0]
-        mlp.gate_proj.weight.data = gu[:n]
-        mlp.up_proj.weight.data = gu[n:]
-        mlp._pkv_gate_up = gu
+    if not hasattr(layer.self_attn, "_pkv_qkv"):
+        _pack_qkv(layer.self_attn)
+    if not hasattr(layer.mlp, "_pkv_gate_up"):
+        _pack_gate_up(layer.mlp)
 
 
 def install_fused_layers(model) -> bool:

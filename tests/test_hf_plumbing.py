@@ -221,5 +221,12 @@ def test_packed_projection_weights_keep_the_model_unchanged():
         assert attn.k_proj.weight.data_ptr() == w[hq * 16:].data_ptr()
         assert attn.v_proj.bias.data_ptr() == b[(hq + hkv) * 16:].data_ptr()
         assert layer.mlp.up_proj.weight.data_ptr() == layer.mlp._pkv_gate_up[128:].data_ptr()
+    # Re-allocated parameters (a move or cast) are packed again on next use.
+    from randomrepo_b200.hf import _gate_up
+
+    mlp = model.model.layers[0].mlp
+    old = mlp._pkv_gate_up
+    mlp.gate_proj.weight.data = mlp.gate_proj.weight.data.clone()
+    assert _gate_up(mlp) is not old and mlp._pkv_gate_up.data_ptr() == mlp.gate_proj.weight.data_ptr()
     # A CPU / fp32 model keeps HF's forwards: the fused kernels are for bf16 / f16 on the GPU.
     assert install_fused_layers(_tiny_model()) is False
