@@ -142,6 +142,24 @@ int32_t pkv_allocator_decode_step(pkv_allocator* a, const int64_t* sequence_ids,
  * the current one is a ValueError; an unknown id a KeyError. */
 int32_t pkv_allocator_truncate(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* token_counts,
                                int64_t n);
+/* pkv_allocator_truncate plus the store's per-block fill bookkeeping in the
+ * same pass (block_fill [fill_n]: tokens stored per block, -1 = none): a
+ * block that becomes free gets -1, a sequence's new partial tail block at
+ * most the tokens it still holds. */
+int32_t pkv_allocator_truncate_fill(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* token_counts,
+                                    int64_t n, int32_t* block_fill, int64_t fill_n);
+/* Token counts of n sequences (KeyError for an unknown id): the
+ * PagedKVSequenceView.token_count of each, without building the views. */
+int32_t pkv_allocator_token_counts(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int64_t* counts_out);
+/* Layout of a prefill / verify chunk per sequence -- its last q_lens[i]
+ * tokens (no reference counterpart: the reference prefills into HF caches):
+ * the table row, the tokens before the chunk (past), and the pool slot
+ * (block * block_size + offset) of every chunk token, packed in order into
+ * slots_out (capacity slots_capacity); block_fill (optional) is raised to
+ * cover the chunk tokens.  A chunk longer than its sequence is a ValueError. */
+int32_t pkv_allocator_chunk_slots(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* q_lens, int64_t n,
+                                  int32_t* rows_out, int32_t* past_out, int64_t* slots_out, int64_t slots_capacity,
+                                  int32_t* block_fill, int64_t fill_n);
 /* Record the length and last table entry of the given rows as pending device
  * updates. */
 int32_t pkv_allocator_touch_rows(pkv_allocator* a, const int32_t* rows, int64_t n);

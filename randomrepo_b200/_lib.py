@@ -103,6 +103,11 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "pkv_allocator_touch_rows": (c_int32, [c_void_p, c_void_p, c_int64]),
     "pkv_allocator_truncate": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64]),
+    "pkv_allocator_truncate_fill": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64]),
+    "pkv_allocator_token_counts": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "pkv_allocator_chunk_slots": (
+        c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64]
+    ),
     "pkv_allocator_pending_updates": (c_int32, [c_void_p, I64P, I64P, I64P, I64P]),
     "pkv_allocator_drain_updates": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
     "pkv_pool_bytes": (c_int64, [POINTER(PoolGeom)]),

@@ -474,6 +474,95 @@ int32_t pkv_allocator_truncate(pkv_allocator* a, const int64_t* sequence_ids, co
   return PKV_OK;
 }
 
+int32_t pkv_allocator_truncate_fill(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* token_counts,
+                                    int64_t n, int32_t* block_fill, int64_t fill_n) {
+  pkv_clear_error();
+  const int64_t bs = a->block_size;
+  for (int64_t i = 0; i < n; ++i) {
+    if (token_counts[i] < 0) {
+      pkv_set_error("token_count must be >= 0.");
+      return PKV_ERR_VALUE;
+    }
+    auto it = a->seqs.find(sequence_ids[i]);
+    if (it == a->seqs.end()) {
+      pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
+      return PKV_ERR_KEY;
+    }
+    Sequence& s = it->second;
+    if (token_counts[i] > s.tokens) {
+      pkv_set_error("truncate cannot grow a sequence (" + std::to_string(token_counts[i]) + " > " +
+                    std::to_string(s.tokens) + " tokens)");
+      return PKV_ERR_VALUE;
+    }
+    const int64_t keep = a->required(token_counts[i]);
+    while ((int64_t)s.blocks.size() > keep) {
+      const int32_t b = s.blocks.back();
+      s.blocks.pop_back();
+      a->set_ref(b, a->refcount[b] - 1);
+      if (a->refcount[b] == 0) {
+        a->set_free(b);
+        if (block_fill && b >= 0 && b < fill_n) block_fill[b] = -1;
+      }
+    }
+    s.tokens = token_counts[i];
+    a->mark_len(s.row);
+    const int32_t part = (int32_t)(token_counts[i] % bs);
+    if (block_fill && keep > 0 && part) {
+      const int32_t t = s.blocks.back();
+      if (t >= 0 && t < fill_n && block_fill[t] > part) block_fill[t] = part;
+    }
+  }
+  return PKV_OK;
+}
+
+int32_t pkv_allocator_token_counts(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int64_t* counts_out) {
+  pkv_clear_error();
+  for (int64_t i = 0; i < n; ++i) {
+    auto it = a->seqs.find(sequence_ids[i]);
+    if (it == a->seqs.end()) {
+      pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
+      return PKV_ERR_KEY;
+    }
+    counts_out[i] = it->second.tokens;
+  }
+  return PKV_OK;
+}
+
+int32_t pkv_allocator_chunk_slots(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* q_lens, int64_t n,
+                                  int32_t* rows_out, int32_t* past_out, int64_t* slots_out, int64_t slots_capacity,
+                                  int32_t* block_fill, int64_t fill_n) {
+  pkv_clear_error();
+  const int64_t bs = a->block_size;
+  int64_t k = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    auto it = a->seqs.find(sequence_ids[i]);
+    if (it == a->seqs.end()) {
+      pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
+      return PKV_ERR_KEY;
+    }
+    const Sequence& s = it->second;
+    if (q_lens[i] < 0 || q_lens[i] > s.tokens) {
+      pkv_set_error("sequence " + std::to_string(sequence_ids[i]) + " holds " + std::to_string(s.tokens) +
+                    " tokens, fewer than its chunk of " + std::to_string(q_lens[i]));
+      return PKV_ERR_VALUE;
+    }
+    if (k + q_lens[i] > slots_capacity) {
+      pkv_set_error("pkv_allocator_chunk_slots: slot buffer too small");
+      return PKV_ERR_ARG;
+    }
+    rows_out[i] = s.row;
+    const int64_t past = s.tokens - q_lens[i];
+    past_out[i] = (int32_t)past;
+    for (int64_t pos = past; pos < s.tokens; ++pos) {
+      const int32_t blk = s.blocks[pos / bs];
+      const int32_t in_blk = (int32_t)(pos % bs);
+      slots_out[k++] = (int64_t)blk * bs + in_blk;
+      if (block_fill && blk >= 0 && blk < fill_n && block_fill[blk] < in_blk + 1) block_fill[blk] = in_blk + 1;
+    }
+  }
+  return PKV_OK;
+}
+
 int32_t pkv_allocator_touch_rows(pkv_allocator* a, const int32_t* rows, int64_t n) {
   pkv_clear_error();
   for (int64_t i = 0; i < n; ++i) {

@@ -462,6 +462,20 @@ class PagedGenerator:
     def _token_count(self, sid: int) -> int:
         return int(self.store.token_count(sid))
 
+    def _token_counts(self, ids) -> list[int]:
+        bulk = getattr(self.store, "token_counts", None)
+        if bulk is not None:
+            return [int(c) for c in bulk(ids)]
+        return [self._token_count(s) for s in ids]
+
+    def _append_many(self, ids, counts) -> None:
+        bulk = getattr(self.store, "append_many", None)
+        if bulk is not None:
+            bulk(ids, counts)
+        else:
+            for sid, n in zip(ids, counts):
+                self.store.append_tokens(sid, n)
+
     def extend_hidden(self, sequence_ids, chunks) -> tuple[torch.Tensor, np.ndarray]:
         """Append one chunk of tokens to each (existing) sequence and run one packed forward
         over all chunks: returns (final hidden states [sum of chunk lengths, hidden], chunk
@@ -471,9 +485,8 @@ class PagedGenerator:
         if len(ids) != len(toks):
             raise ValueError("one chunk per sequence id")
         q_lens = np.array([t.numel() for t in toks], dtype=np.int64)
-        past = [self._token_count(sid) for sid in ids]
-        for sid, t in zip(ids, toks):
-            self.store.append_tokens(sid, t.numel())
+        past = self._token_counts(ids)
+        self._append_many(ids, [t.numel() for t in toks])
         input_ids = torch.cat(toks).to(self.device).unsqueeze(0)
         pos = torch.cat([torch.arange(p0, p0 + t.numel()) for p0, t in zip(past, toks)]).to(self.device)
         h = self._forward(input_ids, pos.unsqueeze(0), _Phase("prefill", self.store, sequence_ids=ids, q_lens=q_lens))
@@ -516,10 +529,9 @@ class PagedGenerator:
         # _placeholders counted one decode token per placeholder: these take L instead.
         for p in pads:
             self._pad_len[p] -= 1
-        past = [self._token_count(s) for s in ids] + [self._pad_len[p] for p in pads]
+        past = self._token_counts(ids) + [self._pad_len[p] for p in pads]
         all_ids = ids + pads
-        for sid in all_ids:
-            store.append_tokens(sid, L)
+        self._append_many(all_ids, [L] * len(all_ids))
         toks = torch.tensor([t for c in chunks for t in c] + [0] * (L * len(pads)), dtype=torch.long)
         pos = torch.tensor([p0 + j for p0 in past for j in range(L)], dtype=torch.long)
         q_lens = np.full(nb, L, dtype=np.int64)
@@ -758,7 +770,7 @@ class PagedGenerator:
 
     def _score_rest(self, seq, rows, need, out, ids, max_logit_rows: int) -> None:
         cs = self.prefill_chunk_size
-        pos = [self._token_count(s) for s in seq]
+        pos = self._token_counts(seq)
         need_sets = [set(n) for n in need]
         while True:
             members = [b for b in range(len(seq)) if pos[b] < len(rows[b])]

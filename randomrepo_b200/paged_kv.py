@@ -240,6 +240,20 @@ class PagedKVAllocator:
             raise ValueError("sequence_ids and token_counts must have the same length")
         _lib.raise_for_status(lib.pkv_allocator_truncate(self._handle, p_ids, p_counts, ids.size))
 
+    def append_many(self, sequence_ids, token_counts) -> None:
+        """``append_tokens(sid, n)`` for each pair, in order, without building the views it returns."""
+        h = self._handle
+        for sid, n in zip(sequence_ids, token_counts):
+            _lib.raise_for_status(lib.pkv_allocator_append_tokens(h, int(sid), int(n)))
+
+    def token_counts(self, sequence_ids) -> np.ndarray:
+        """Token counts of several sequences (int64), without building their views."""
+        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
+        out = np.empty(ids.size, dtype=np.int64)
+        _lib.raise_for_status(lib.pkv_allocator_token_counts(self._handle, ids.ctypes.data, ids.size,
+                                                             out.ctypes.data))
+        return out
+
     def refcount(self, block_id: int) -> int:
         out = ctypes.c_int32()
         _lib.raise_for_status(lib.pkv_allocator_refcount(self._handle, int(block_id), ctypes.byref(out)))
@@ -369,7 +383,15 @@ class PagedKVCacheStore:
 
     def token_count(self, sequence_id: int) -> int:
         """Tokens the sequence holds (KeyError if unknown)."""
-        return self.allocator.view(sequence_id).token_count
+        return int(self.allocator.token_counts([sequence_id])[0])
+
+    def token_counts(self, sequence_ids) -> np.ndarray:
+        """Tokens each sequence holds (KeyError for an unknown id)."""
+        return self.allocator.token_counts(sequence_ids)
+
+    def append_many(self, sequence_ids, token_counts) -> None:
+        """``append_tokens`` for each (sequence, count) pair, in order, without returning views."""
+        self.allocator.append_many(sequence_ids, token_counts)
 
     def release(self, sequence_id: int) -> None:
         """paged_kv.py:205-213: drop the resident cache, the stored blocks and the table."""
@@ -531,21 +553,16 @@ class PagedKVCacheStore:
 
     def truncate(self, sequence_ids, token_counts) -> None:
         """Shrink sequences (see ``PagedKVAllocator.truncate``); stored chunks are trimmed to match."""
-        ids = np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64))
-        counts = np.atleast_1d(np.asarray(token_counts, dtype=np.int64))
-        bs = self.allocator.block_size_tokens
-        tails = []
-        for sid, n in zip(ids.tolist(), counts.tolist()):
-            view = self.allocator.view(sid)
-            keep = -(-n // bs)
-            tails.append((view.physical_blocks[:keep], view.physical_blocks[keep:], n))
-        self.allocator.truncate(ids, counts)
-        for kept, dropped, n in tails:
-            for b in dropped:
-                if self.allocator.refcount(b) == 0:
-                    self._block_fill[b] = -1
-            if kept and n % bs and self._block_fill[kept[-1]] > n % bs:
-                self._block_fill[kept[-1]] = n % bs
+        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
+        counts = np.ascontiguousarray(np.atleast_1d(np.asarray(token_counts, dtype=np.int64)))
+        if ids.shape != counts.shape:
+            raise ValueError("sequence_ids and token_counts must have the same length")
+        # One native pass: the blocks past each new end are released, a freed
+        # block's fill becomes -1 and a new partial tail keeps what it still holds.
+        fill = self._block_fill
+        _lib.raise_for_status(lib.pkv_allocator_truncate_fill(self.allocator._handle, ids.ctypes.data,
+                                                              counts.ctypes.data, ids.size, fill.ctypes.data,
+                                                              fill.size))
 
     # -- device decode path (extension) -----------------------------------------
     def decode(self, sequence_ids, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, *, layer: int = 0,
@@ -753,29 +770,22 @@ class PagedKVCacheStore:
         hq = int(num_q_heads)
         if hq <= 0 or hq % pool.num_kv_heads:
             raise ValueError("num_q_heads must be a positive multiple of the pool's KV heads")
-        bs = self.allocator.block_size_tokens
         # Device tables up to date and copy-on-write copies applied (they carry
         # their source block's fill) before the chunk's fills are recorded.
         self._sync()
+        q_lens = np.ascontiguousarray(q_lens, dtype=np.int64)
         rows = np.empty(n, dtype=np.int32)
         past = np.empty(n, dtype=np.int32)
-        slot_parts = []
-        for i, sid in enumerate(ids.tolist()):
-            view = self.allocator.view(sid)
-            p0 = view.token_count - int(q_lens[i])
-            if p0 < 0:
-                raise ValueError(f"sequence {sid} holds {view.token_count} tokens, fewer than its chunk of {q_lens[i]}")
-            rows[i] = self.allocator.row(sid)
-            past[i] = p0
-            if q_lens[i]:
-                pos = np.arange(p0, view.token_count, dtype=np.int64)
-                blocks = np.asarray(view.physical_blocks, dtype=np.int64)[pos // bs]
-                slot_parts.append(blocks * bs + pos % bs)
-                np.maximum.at(self._block_fill, blocks, (pos % bs + 1).astype(np.int32))
         total_q = int(q_lens.sum())
+        slots = np.empty(total_q, dtype=np.int64)
+        fill = self._block_fill
+        # Rows, past lengths and chunk slots in one native pass (fills raised to cover the chunks).
+        _lib.raise_for_status(lib.pkv_allocator_chunk_slots(self.allocator._handle, ids.ctypes.data,
+                                                            q_lens.ctypes.data, n, rows.ctypes.data,
+                                                            past.ctypes.data, slots.ctypes.data, slots.size,
+                                                            fill.ctypes.data, fill.size))
         if total_q == 0:
             return PrefillStep(ids, q_lens, hq, 0, None, None, None)
-        slots = np.concatenate(slot_parts)
         plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
             if buffers is None:
