@@ -45,6 +45,45 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
+class PinnedStaging:
+    """Host-to-device copies of a step's small inputs (positions, token ids, slots, work items)
+    through a ring of page-locked buffers.  A copy from pageable memory makes the host wait until
+    the stream has drained up to it; from page-locked memory it is queued and the host runs on.
+    A buffer is written again only after the copy that read it has run (one event per slot)."""
+
+    def __init__(self, slots: int = 16) -> None:
+        self._bufs: list[torch.Tensor | None] = [None] * slots
+        self._events: list = [None] * slots
+        self._next = 0
+
+    def to_device(self, x, device: torch.device, dtype: torch.dtype | None = None) -> torch.Tensor:
+        src = torch.as_tensor(x)
+        if dtype is not None and src.dtype != dtype:
+            src = src.to(dtype)
+        if device.type != "cuda":
+            return src.to(device)
+        src = src.contiguous()
+        nbytes = src.numel() * src.element_size()
+        out = torch.empty(src.shape, dtype=src.dtype, device=device)
+        if nbytes == 0:
+            return out
+        i = self._next
+        self._next = (i + 1) % len(self._bufs)
+        ev = self._events[i]
+        if ev is not None:
+            ev.synchronize()  # the copy that last read this buffer has run
+        buf = self._bufs[i]
+        if buf is None or buf.numel() < nbytes:
+            buf = self._bufs[i] = torch.empty(max(nbytes, 4096), dtype=torch.uint8).pin_memory()
+        staged = buf[:nbytes].view(src.dtype).view(src.shape)
+        staged.copy_(src)
+        out.copy_(staged, non_blocking=True)
+        if ev is None:
+            ev = self._events[i] = torch.cuda.Event()
+        ev.record()
+        return out
+
+
 class KVPool:
     """KV pool plus device block tables for one ``PagedKVAllocator``."""
 
@@ -77,6 +116,7 @@ class KVPool:
         # Error word of the prefill / verify kernel (0 = none).
         self.prefill_error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._prefill_ws = torch.empty(0, dtype=torch.uint8, device=self.device)
+        self.h2d = PinnedStaging()
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         # Kernel launches issued from Python through this pool (the stepper counts its own).
         self.launches = 0

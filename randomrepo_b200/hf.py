@@ -411,6 +411,9 @@ class PagedGenerator:
         use_paged_attention(model)
         # Fused norm / rotary / SiLU launches inside this generator's forwards (Qwen2-family models on the GPU).
         self.fused_layers = bool(fused_layers) and install_fused_layers(model)
+        from .device import PinnedStaging
+
+        self._h2d = PinnedStaging()
         self.model = model
         self.store = store
         self.prefill_chunk_size = int(prefill_chunk_size)
@@ -487,8 +490,9 @@ class PagedGenerator:
         q_lens = np.array([t.numel() for t in toks], dtype=np.int64)
         past = self._token_counts(ids)
         self._append_many(ids, [t.numel() for t in toks])
-        input_ids = torch.cat(toks).to(self.device).unsqueeze(0)
-        pos = torch.cat([torch.arange(p0, p0 + t.numel()) for p0, t in zip(past, toks)]).to(self.device)
+        input_ids = self._h2d.to_device(torch.cat(toks), self.device).unsqueeze(0)
+        pos = self._h2d.to_device(torch.cat([torch.arange(p0, p0 + t.numel()) for p0, t in zip(past, toks)]),
+                                  self.device)
         h = self._forward(input_ids, pos.unsqueeze(0), _Phase("prefill", self.store, sequence_ids=ids, q_lens=q_lens))
         return h[0], q_lens
 
@@ -553,8 +557,8 @@ class PagedGenerator:
                     bufs = {"slots": step.slots.clone(), "records": step.records.clone(),
                             "n_items": step.plan.n_items}
                     step = store.prefill_step(all_ids, q_lens, hq, buffers=bufs)
-                tok_s = toks.to(self.device).unsqueeze(0)
-                pos_s = pos.to(self.device).unsqueeze(0)
+                tok_s = self._h2d.to_device(toks, self.device).unsqueeze(0)
+                pos_s = self._h2d.to_device(pos, self.device).unsqueeze(0)
                 ph = _Phase("prefill", store, step=step, sequence_ids=all_ids, q_lens=q_lens)
                 cur = torch.cuda.current_stream(self.device)
                 side = torch.cuda.Stream(device=self.device)
@@ -568,8 +572,8 @@ class PagedGenerator:
                 self._ext_graphs[key] = (graph, tok_s, pos_s, logits_s, bufs)
             else:
                 graph, tok_s, pos_s, logits_s, _ = entry
-                tok_s.copy_(toks.unsqueeze(0), non_blocking=True)
-                pos_s.copy_(pos.unsqueeze(0), non_blocking=True)
+                tok_s.copy_(self._h2d.to_device(toks, self.device).unsqueeze(0))
+                pos_s.copy_(self._h2d.to_device(pos, self.device).unsqueeze(0))
                 graph.replay()
                 out = logits_s.clone()
         finally:
@@ -611,8 +615,9 @@ class PagedGenerator:
         if self.cuda_graphs:
             return self._decode_step_graph(sequence_ids, tokens)
         step = self.store.decode_step(sequence_ids)
-        pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
-        h = self._forward(tokens.reshape(-1, 1).to(self.device), pos.reshape(-1, 1),
+        pos = self._h2d.to_device(torch.from_numpy(step.host_lens.astype(np.int64) - 1), self.device)
+        h = self._forward(self._h2d.to_device(tokens.reshape(-1, 1), self.device) if not tokens.is_cuda
+                          else tokens.reshape(-1, 1), pos.reshape(-1, 1),
                           _Phase("decode", self.store, step=step))
         return self.logits(h[:, -1])
 
@@ -661,8 +666,10 @@ class PagedGenerator:
             # Decode graphs hold the fixed step block, which a new capacity replaces.
             self._graphs.clear()
             self._graph_fixed = pool.fixed_serial
-        pos = torch.from_numpy(step.host_lens.astype(np.int64) - 1).to(self.device)
-        tok = tokens.reshape(-1).to(self.device)
+        pos = self._h2d.to_device(torch.from_numpy(step.host_lens.astype(np.int64) - 1), self.device)
+        tok = tokens.reshape(-1)
+        if tok.device != self.device:
+            tok = self._h2d.to_device(tok, self.device)
         if pads:
             tok = torch.cat([tok, tok.new_zeros(len(pads))])
         tok = tok.reshape(-1, 1)

@@ -789,15 +789,15 @@ class PagedKVCacheStore:
         plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
             if buffers is None:
-                slots_d = torch.from_numpy(slots).to(pool.device, non_blocking=True)
-                records_d = torch.from_numpy(plan.records).to(pool.device, non_blocking=True)
+                slots_d = pool.h2d.to_device(torch.from_numpy(slots), pool.device)
+                records_d = pool.h2d.to_device(torch.from_numpy(plan.records), pool.device)
             else:
                 if plan.n_combine or plan.n_items != buffers["n_items"] or slots.size > buffers["slots"].numel():
                     raise ValueError("the prefill plan does not fit the recorded launch")
                 slots_d = buffers["slots"][:slots.size]
                 records_d = buffers["records"][:plan.n_items]
-                slots_d.copy_(torch.from_numpy(slots), non_blocking=True)
-                records_d.copy_(torch.from_numpy(plan.records), non_blocking=True)
+                slots_d.copy_(pool.h2d.to_device(torch.from_numpy(slots), pool.device))
+                records_d.copy_(pool.h2d.to_device(torch.from_numpy(plan.records), pool.device))
         return PrefillStep(ids, q_lens, hq, total_q, plan, slots_d, records_d)
 
     def prefill_attention(self, sequence_ids, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,

@@ -81,15 +81,17 @@ class PagedSpeculativeGenerator:
         """k draft proposals per sequence: (tokens [n, k] int64, logits [n, k, vocab] float32)."""
         draft, sampler = self.draft, self.sampler
         dev = draft.device
+        h2d = draft._h2d
         if draft.cuda_graphs:
             # Graphed decode steps only: sequences two tokens behind take one
             # step on their own first (its logits are not needed).
             two = [j for j, p in enumerate(pending) if len(p) == 2]
             if two:
-                draft.decode_step([ids[j] for j in two], torch.tensor([pending[j][0] for j in two], device=dev))
-            first = draft.decode_step(ids, torch.tensor([p[-1] for p in pending], device=dev))
+                draft.decode_step([ids[j] for j in two], h2d.to_device([pending[j][0] for j in two], dev,
+                                                                       torch.long))
+            first = draft.decode_step(ids, h2d.to_device([p[-1] for p in pending], dev, torch.long))
         elif all(len(p) == 1 for p in pending):
-            first = draft.decode_step(ids, torch.tensor([p[0] for p in pending], device=dev))
+            first = draft.decode_step(ids, h2d.to_device([p[0] for p in pending], dev, torch.long))
         else:
             first = draft.extend(ids, pending)
         n, vocab = first.shape
