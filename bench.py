@@ -830,14 +830,17 @@ def run_speculative(device: torch.device, seed: int, iters: int = 2) -> dict:
     spec = PagedSpeculativeGenerator(tgen, dgen, k=k)
     stats = {}
 
-    def ours(it):
+    def ours(it, seed):
         r = spec.generate(prompts, group_size=group, max_new_tokens=new, first_id=it * 10000,
-                          sampling=SamplingConfig(do_sample=True, temperature=ss["temperature"], seed=it))
+                          sampling=SamplingConfig(do_sample=True, temperature=ss["temperature"], seed=seed))
         stats.update(rounds=r["rounds"], proposed=r["proposed"], accepted=r["accepted"])
         return sum(len(t) for t in r["tokens"])
 
-    ours(0)
-    runs = [_timed(device, lambda it=it: ours(it)) for it in range(1, iters + 1)]
+    # Warm-up on the timed draws: sequences finish at different rounds, and
+    # each batch size the shrinking batch reaches records its CUDA graphs once.
+    for it in range(1, iters + 1):
+        ours(100 + it, it)
+    runs = [_timed(device, lambda it=it: ours(it, it)) for it in range(1, iters + 1)]
     spec_tps = sum(n for n, _ in runs) / sum(t for _, t in runs)
     for st in (t_store, d_store):
         if st.pool.decode_error_flag() or st.pool.prefill_error_flag():
@@ -872,7 +875,8 @@ def run_speculative(device: torch.device, seed: int, iters: int = 2) -> dict:
                            "round cost is the measured machinery, the acceptance rate is the weights'",
         "plain_paged_tokens_per_s": plain_tps,
         "plain_paged_path": "PagedGenerator on the same target and batch, CUDA-graph decode steps",
-        "timing": f"CUDA events around whole rollouts, mean of {iters} after one warm-up each",
+        "timing": f"CUDA events around whole rollouts, mean of {iters}, each after a warm-up rollout with the "
+                  "same draws (a shrinking batch records each batch size's graphs once)",
     }
     if hf_tps is not None:
         out["hf_assisted_tokens_per_s"] = hf_tps
