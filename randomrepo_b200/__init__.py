@@ -8,7 +8,11 @@ Public API (drop-in for ``agentrl.generation.paged_kv``):
   ``verify_attention`` (chunked prefill and speculative verify on tcgen05),
   copy-on-write ``fork`` and ``truncate``;
 * ``PagedGenerator`` (``randomrepo_b200.hf``): HF Qwen2-family models
-  prefilling and decoding through the store;
+  prefilling and decoding through the store (CUDA-graph decode steps, fused
+  norm / rotary / SiLU launches);
+* ``host_input_tensor``: page-locked, write-combined host memory for the
+  q / k / v a host hands to ``PagedKVCacheStore.decode`` (the host-buffer
+  decode path);
 * ``assign_groups`` / ``StepGather`` (``randomrepo_b200.sharding``): GRPO
   groups per GPU and the per-step gather of sampled tokens and logprobs.
 
