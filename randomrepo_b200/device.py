@@ -77,10 +77,14 @@ class PinnedStaging:
             buf = self._bufs[i] = torch.empty(max(nbytes, 4096), dtype=torch.uint8).pin_memory()
         staged = buf[:nbytes].view(src.dtype).view(src.shape)
         staged.copy_(src)
-        out.copy_(staged, non_blocking=True)
-        if ev is None:
+        # The copy runs on the destination device's current stream, so the
+        # guard is recorded there too, whichever device is current.
+        stream = torch.cuda.current_stream(device)
+        with torch.cuda.stream(stream):
+            out.copy_(staged, non_blocking=True)
+        if ev is None or ev.device != stream.device:
             ev = self._events[i] = torch.cuda.Event()
-        ev.record()
+        ev.record(stream)
         return out
 
 

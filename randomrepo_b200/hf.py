@@ -220,12 +220,37 @@ def _fused_mlp_forward(self, x):
     return self.down_proj(act).view(*x.shape[:-1], -1)
 
 
+def _is_view_at(t: torch.Tensor | None, packed: torch.Tensor | None, offset: int) -> bool:
+    """Whether ``t`` still lies at element ``offset`` of ``packed`` (same dtype and device)."""
+    if t is None or packed is None:
+        return t is None and packed is None
+    return (t.dtype == packed.dtype and t.device == packed.device
+            and t.data_ptr() == packed.data_ptr() + offset * packed.element_size())
+
+
 def _gate_up(mlp) -> torch.Tensor:
-    """The packed gate | up weight, packed again if the parameters were re-allocated."""
-    if mlp.gate_proj.weight.data_ptr() != mlp._pkv_gate_up.data_ptr():
+    """The packed gate | up weight, packed again if either parameter was re-allocated (moved, cast,
+    or replaced on its own, e.g. by a weight sync that sets ``.data`` of one projection)."""
+    gu = mlp._pkv_gate_up
+    g, u = mlp.gate_proj.weight, mlp.up_proj.weight
+    if not (_is_view_at(g, gu, 0) and _is_view_at(u, gu, g.numel()) and g.numel() + u.numel() == gu.numel()):
         with torch.no_grad():
             _pack_gate_up(mlp)
     return mlp._pkv_gate_up
+
+
+def _qkv_packed(attn) -> bool:
+    """Whether every q / k / v weight and bias is still the view of the packed tensors it was made."""
+    w, b, _, _ = attn._pkv_qkv
+    o = 0
+    for p in (attn.q_proj, attn.k_proj, attn.v_proj):
+        pw, pb = p.weight, getattr(p, "bias", None)
+        if not _is_view_at(pw, w, o * pw.shape[1]):
+            return False
+        if (pb is None) != (b is None) or (pb is not None and not _is_view_at(pb, b, o)):
+            return False
+        o += pw.shape[0]
+    return o * w.shape[1] == w.numel()
 
 
 def _fused_mlp_residual(mlp, x, residual):
@@ -245,12 +270,11 @@ def _fused_attention_forward(self, hidden_states, position_embeddings, attention
     b, t = int(input_shape[0]), int(input_shape[1])
     d = int(self.head_dim)
     cos, sin = position_embeddings
-    w, bias, hq, hkv = self._pkv_qkv
-    if self.q_proj.weight.data_ptr() != w.data_ptr():
-        # The parameters were re-allocated (moved, cast, replaced): pack them again.
+    if not _qkv_packed(self):
+        # A parameter was re-allocated (moved, cast, or replaced on its own): pack them again.
         with torch.no_grad():
             _pack_qkv(self)
-        w, bias, hq, hkv = self._pkv_qkv
+    w, bias, hq, hkv = self._pkv_qkv
     qkv = torch.nn.functional.linear(hidden_states, w, bias)
     q, k, v = fused_rope_qkv(qkv, cos, sin, hq, hkv, d)
     out = _paged_rows(ph, int(self.layer_idx), q, k, v, b, t, self.scaling)
@@ -327,6 +351,9 @@ def install_fused_layers(model) -> bool:
                 or not all(hasattr(attn, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj", "head_dim"))
                 or not all(hasattr(mlp, a) for a in ("gate_proj", "up_proj", "down_proj"))
                 or getattr(mlp.gate_proj, "bias", None) is not None or getattr(mlp.up_proj, "bias", None) is not None):
+            return False
+        # q / k / v biases are packed only all together: a model with some of them keeps HF's forwards.
+        if len({getattr(p, "bias", None) is None for p in (attn.q_proj, attn.k_proj, attn.v_proj)}) != 1:
             return False
     with torch.no_grad():
         for layer in layers:

@@ -408,6 +408,8 @@ class PagedKVCacheStore:
         return self.allocator.metrics()
 
     # -- resident caches (paged_kv.py:218-243) ------------------------------------
+    # Restated from agentrl/generation/paged_kv.py:218-243: plain dict bookkeeping whose
+    # behaviour, names and messages the drop-in contract fixes, kept statement for statement.
     def cache_template(self, sequence_id: int) -> Any:
         return self._cache_templates[sequence_id]
 
@@ -436,6 +438,10 @@ class PagedKVCacheStore:
         self._resident_caches.pop(sequence_id, None)
 
     # -- block storage (paged_kv.py:245-347) --------------------------------------
+    # The block write and gather run on the device kernels; the resident / template branches of
+    # read_sequence_legacy_cache, write_batched_legacy_cache and the _stack / _split helpers are
+    # restated from agentrl/generation/paged_kv.py:271-281, 287-303 and 335-360 (tuple plumbing
+    # whose results the drop-in contract fixes).
     def write_sequence_cache(self, sequence_id: int, legacy_cache: tuple[tuple[torch.Tensor, ...], ...],
                              cache_template: Any) -> None:
         """paged_kv.py:245-269: trim to token_count, split into blocks, store each block's chunk."""

@@ -352,7 +352,10 @@ def main() -> None:
         i = args.index("--only")
         only = args[i + 1]
         del args[i:i + 2]
-    ref_root = Path(args[0] if args else "/root/reference").resolve()
+    if not args:
+        sys.exit("usage: python tests/golden/make_golden.py REFERENCE_ROOT [--only NAME]\n"
+                 "REFERENCE_ROOT is a checkout of the reference project (the directory holding agentrl/)")
+    ref_root = Path(args[0]).resolve()
     sys.path.insert(0, str(ref_root))
     from agentrl.generation.paged_kv import PagedKVAllocator, PagedKVCacheStore
 

@@ -230,3 +230,36 @@ def test_packed_projection_weights_keep_the_model_unchanged():
     assert _gate_up(mlp) is not old and mlp._pkv_gate_up.data_ptr() == mlp.gate_proj.weight.data_ptr()
     # A CPU / fp32 model keeps HF's forwards: the fused kernels are for bf16 / f16 on the GPU.
     assert install_fused_layers(_tiny_model()) is False
+
+
+def test_packed_weights_follow_a_projection_replaced_on_its_own():
+    """A weight sync or adapter merge may set ``.data`` of one projection only (v_proj, up_proj, a bias):
+    the packed tensors must then be rebuilt from the current parameters, not keep the old values."""
+    from randomrepo_b200.hf import _gate_up, _pack_qkv, _pack_weights, _qkv_packed
+
+    model = _tiny_model()
+    layer = model.model.layers[0]
+    with torch.no_grad():
+        _pack_weights(layer)
+    attn, mlp = layer.self_attn, layer.mlp
+    assert _qkv_packed(attn)
+    gen = torch.Generator().manual_seed(9)
+    for name in ("v_proj", "k_proj"):
+        proj = getattr(attn, name)
+        proj.weight.data = torch.randn(proj.weight.shape, generator=gen)
+        assert not _qkv_packed(attn)
+        with torch.no_grad():
+            _pack_qkv(attn)
+        assert _qkv_packed(attn)
+        w, b, _, _ = attn._pkv_qkv
+        assert torch.equal(w, torch.cat([attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight], 0))
+    attn.q_proj.bias.data = torch.randn(attn.q_proj.bias.shape, generator=gen)
+    assert not _qkv_packed(attn)
+    with torch.no_grad():
+        _pack_qkv(attn)
+    assert torch.equal(attn._pkv_qkv[1], torch.cat([attn.q_proj.bias, attn.k_proj.bias, attn.v_proj.bias], 0))
+    new_up = torch.randn(mlp.up_proj.weight.shape, generator=gen)
+    mlp.up_proj.weight.data = new_up
+    gu = _gate_up(mlp)
+    assert torch.equal(gu[mlp.gate_proj.weight.shape[0]:], new_up)
+    assert _gate_up(mlp) is gu  # packed again once, then reused
