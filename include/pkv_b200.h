@@ -151,6 +151,13 @@ int32_t pkv_allocator_truncate_fill(pkv_allocator* a, const int64_t* sequence_id
 /* Token counts of n sequences (KeyError for an unknown id): the
  * PagedKVSequenceView.token_count of each, without building the views. */
 int32_t pkv_allocator_token_counts(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int64_t* counts_out);
+/* Free blocks that appending one token to each of n sequences takes:
+ * need_out[i] = 1 when sequence i's next token starts a new block or lands in
+ * a partial tail block still shared by a fork (copied on write), else 0.  It
+ * generalises the growth test of ContinuousBatchingOrchestrator's admission
+ * (agentrl/generation/continuous.py:915-919: max(1, len) % block_size == 0)
+ * to copy-on-write forks, which the reference does not have. */
+int32_t pkv_allocator_growth_blocks(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int32_t* need_out);
 /* Layout of a prefill / verify chunk per sequence -- its last q_lens[i]
  * tokens (no reference counterpart: the reference prefills into HF caches):
  * the table row, the tokens before the chunk (past), and the pool slot
@@ -303,6 +310,17 @@ int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t
                                      const int32_t* work_items, int32_t n_items, int32_t n_combine, int32_t batch,
                                      int32_t num_q_heads, int32_t pages_per_split, float scale, void* out,
                                      void* stream);
+
+/* The error word of the no-alloc decode calls on the current device (no
+ * counterpart in the reference): 0, or the codes of pkv_decode_attention's
+ * workspace error word -- 1 (a bounded wait gave up), 3 (a work item outside
+ * the launch was skipped), 4 (a block id outside the pool was replaced by
+ * block 0).  Each pkv_decode_attention_noalloc call clears the word when it
+ * starts, so read it after the calls it should cover and before the next
+ * one.  The word is copied in stream order on `stream` (after the calls
+ * issued there so far) and the function waits for that copy; *error_out is 0
+ * when no no-alloc call has run on the device yet. */
+int32_t pkv_decode_noalloc_error(int32_t* error_out, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Chunked prefill / speculative verify over pages                           */
@@ -486,6 +504,11 @@ int32_t pkv_stepper_copies(pkv_stepper* st, int32_t* pairs_out, int64_t capacity
 int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error);
 /* Kernels the stepper has launched so far. */
 int64_t pkv_stepper_launches(pkv_stepper* st);
+/* Nanoseconds the host has spent blocked on the stepper's staging ring so far
+ * (it waits there only when it runs eight steps ahead of the device); with a
+ * wall-clock reading around a loop of steps it separates the host's own work
+ * per step from waiting.  No reference counterpart (measurement). */
+int64_t pkv_stepper_host_wait_ns(pkv_stepper* st);
 /* Time `count` of the following attention launches, every `every`-th one,
  * with CUDA events recorded right around the decode kernels on their stream
  * (count 0 turns timing off; sampling keeps the event calls' host time off

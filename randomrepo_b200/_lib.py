@@ -105,6 +105,7 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_allocator_truncate": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64]),
     "pkv_allocator_truncate_fill": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64]),
     "pkv_allocator_token_counts": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "pkv_allocator_growth_blocks": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p]),
     "pkv_allocator_chunk_slots": (
         c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64]
     ),
@@ -143,6 +144,7 @@ _SIGNATURES: dict[str, tuple] = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p,
          c_void_p],
     ),
+    "pkv_decode_noalloc_error": (c_int32, [I32P, c_void_p]),
     "pkv_prefill_positions_per_item": (c_int32, [c_int32, c_int32]),
     "pkv_prefill_plan": (
         c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64,
@@ -183,6 +185,7 @@ _SIGNATURES: dict[str, tuple] = {
     "pkv_stepper_copies": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
     "pkv_stepper_error": (c_int32, [c_void_p, I32P]),
     "pkv_stepper_launches": (c_int64, [c_void_p]),
+    "pkv_stepper_host_wait_ns": (c_int64, [c_void_p]),
     "pkv_stepper_time_launches": (c_int32, [c_void_p, c_int64, c_int64]),
     "pkv_stepper_launch_times": (c_int32, [c_void_p, c_void_p, c_int64, I64P]),
     "pkv_rms_norm": (

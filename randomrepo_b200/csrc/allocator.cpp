@@ -528,6 +528,27 @@ int32_t pkv_allocator_token_counts(pkv_allocator* a, const int64_t* sequence_ids
   return PKV_OK;
 }
 
+int32_t pkv_allocator_growth_blocks(pkv_allocator* a, const int64_t* sequence_ids, int64_t n, int32_t* need_out) {
+  pkv_clear_error();
+  const int64_t bs = a->block_size;
+  for (int64_t i = 0; i < n; ++i) {
+    auto it = a->seqs.find(sequence_ids[i]);
+    if (it == a->seqs.end()) {
+      pkv_set_error("Unknown sequence_id " + std::to_string(sequence_ids[i]) + ".");
+      return PKV_ERR_KEY;
+    }
+    const Sequence& s = it->second;
+    // One more token takes a fresh block at a block boundary, or a copy of a
+    // partial tail block that forks still share; otherwise it fits in place.
+    if ((int64_t)s.blocks.size() < a->required(s.tokens + 1)) {
+      need_out[i] = 1;
+    } else {
+      need_out[i] = (s.tokens % bs != 0 && a->refcount[s.blocks.back()] > 1) ? 1 : 0;
+    }
+  }
+  return PKV_OK;
+}
+
 int32_t pkv_allocator_chunk_slots(pkv_allocator* a, const int64_t* sequence_ids, const int64_t* q_lens, int64_t n,
                                   int32_t* rows_out, int32_t* past_out, int64_t* slots_out, int64_t slots_capacity,
                                   int32_t* block_fill, int64_t fill_n) {

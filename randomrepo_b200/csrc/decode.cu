@@ -45,6 +45,7 @@
 #include "pkv_internal.h"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -143,13 +144,15 @@ struct Item {
   int blk;  // this lane's block: page pg0 + lane
 };
 
-// Take the next item from the launch's counter.  The warp that takes the
-// last out-of-range index resets the counters for the next launch (by then
-// no warp of this launch fetches again).
-__device__ __forceinline__ int fetch_item(const DecodeParams& p, int lane, int total_warps) {
+// Take the next item.  A warp's first item is its global warp index (no
+// atomic round trip before its first copy); later ones come from the
+// launch's counter, past the first items.  Each warp draws until it gets an
+// out-of-range index, once; the warp that does so last resets the counters
+// for the next launch (by then no warp of this launch draws again).
+__device__ __forceinline__ int fetch_item(const DecodeParams& p, int lane, int gwarp, int total_warps, bool first) {
   int idx = 0;
   if (lane == 0) {
-    idx = atomicAdd(p.ws_sched, 1);
+    idx = first ? gwarp : total_warps + atomicAdd(p.ws_sched, 1);
     if (idx >= p.n_items) {
       const int done = atomicAdd(p.ws_sched + 1, 1);
       if (done == total_warps - 1) {
@@ -163,10 +166,11 @@ __device__ __forceinline__ int fetch_item(const DecodeParams& p, int lane, int t
 }
 
 template <int HPC>
-__device__ __forceinline__ Item next_item(const DecodeParams& p, int lane, int total_warps) {
+__device__ __forceinline__ Item next_item(const DecodeParams& p, int lane, int gwarp, int total_warps, bool first) {
   Item m;
   for (;;) {
-    m.idx = fetch_item(p, lane, total_warps);
+    m.idx = fetch_item(p, lane, gwarp, total_warps, first);
+    first = false;
     if (m.idx < 0) return m;
     const int4 it = p.items[m.idx];
     if (item_ok<HPC>(it, p)) {
@@ -222,6 +226,7 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int total_warps = gridDim.x * C::kWarps;
+  const int gwarp = blockIdx.x * C::kWarps + warp;
   uint8_t* ring = smem + warp * S * C::kStageBytes;
   uint64_t* full = bars + warp * S;
   if (lane == 0) {
@@ -230,6 +235,10 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
   }
   __syncwarp();
 
+  // Launched as a programmatic dependent of the previous step's kernels
+  // (PKV_DECODE_PDL), this CTA got resident and set up its barriers while
+  // they ran; wait for them here, before the first global access.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // Let the split-K combine grid get resident now; it waits in hardware for
   // this grid to complete before it reads the partials.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -252,10 +261,10 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
   const int group = p.group;
   const char* layer_base = p.pool + (int64_t)p.layer * p.num_blocks * p.hkv * C::kHeadBytes;
 
-  Item cur = next_item<HPC>(p, lane, total_warps);
+  Item cur = next_item<HPC>(p, lane, gwarp, total_warps, true);
   Item nxt;
   nxt.idx = -1;
-  if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, total_warps);
+  if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, gwarp, total_warps, false);
   int issued = 0, consumed = 0;
   bool iss_next = false;
   int iss_pg = cur.pg0;
@@ -484,7 +493,7 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
       iss_pg = cur.pg0;
     }
     nxt.idx = -1;
-    if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, total_warps);
+    if (cur.idx >= 0) nxt = next_item<HPC>(p, lane, gwarp, total_warps, false);
   }
 }
 
@@ -499,15 +508,18 @@ __global__ void __launch_bounds__(Cfg<D, HPC>::kWarps * 32, 1) paged_decode_kern
 // decode grid has completed and its partials are visible.
 constexpr int kCombineThreads = 32;
 
+template <int D, int HPC>
+__device__ __forceinline__ bool entry_ok(const DecodeParams& p, const int4 en) {
+  const int b = en.x, hg = en.y, ns = en.z, slot0 = en.w;
+  return b >= 0 && b < p.batch && (hg + 1) * HPC <= p.hkv && ns >= 2 && ns <= kMaxSplitsPerSeq && slot0 >= 0 &&
+         slot0 + ns <= p.n_items;
+}
+
+// Merge one (entry, query head); the entry has been checked.
 template <int D, int HPC, typename T>
 __device__ __forceinline__ void combine_one(const DecodeParams& p, const int4 en, int hh, int gq) {
   const int b = en.x, hg = en.y, ns = en.z, slot0 = en.w;
   const int lane = threadIdx.x;
-  if (b < 0 || b >= p.batch || (hg + 1) * HPC > p.hkv || ns < 2 || ns > kMaxSplitsPerSeq || slot0 < 0 ||
-      slot0 + ns > p.n_items) {
-    if (lane == 0) atomicExch(p.ws_error, kDevBadItem);
-    return;
-  }
   float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
   if (lane < ns) {
     const float* ml = p.ws_ml + ((int64_t)(slot0 + lane) * HPC + hh) * 16;
@@ -561,14 +573,37 @@ __device__ __forceinline__ void combine_one(const DecodeParams& p, const int4 en
 template <int D, int HPC, typename T>
 __global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(const DecodeParams launch_p,
                                                                                const int4* entries) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The step header and the entries come from the step's descriptor, which
+  // was in place before the decode grid started: read them while that grid
+  // still runs, then wait for its partials.
   const DecodeParams p = step_params(launch_p);
   const int pi = blockIdx.y;
   const int hh = pi >> 3, gq = pi & 7;
+  const int e0 = blockIdx.x;
+  const bool live = gq < p.group && e0 < p.n_combine;
+  int4 en = make_int4(0, 0, 0, 0);
+  bool ok = false;
+  if (live) {
+    en = entries[e0];
+    ok = entry_ok<D, HPC>(p, en);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The next step's decode grid may get resident now (it waits in hardware
+  // for this grid before its first global access).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (gq >= p.group) return;
+  if (live && !ok && threadIdx.x == 0) atomicExch(p.ws_error, kDevBadItem);
+  if (ok) combine_one<D, HPC, T>(p, en, hh, gq);
   // One (entry, query head) per block; a fixed-step launch has a fixed grid
   // and strides over however many entries the step has.
-  for (int e = blockIdx.x; e < p.n_combine; e += gridDim.x) combine_one<D, HPC, T>(p, entries[e], hh, gq);
+  for (int e = e0 + gridDim.x; e < p.n_combine; e += gridDim.x) {
+    const int4 x = entries[e];
+    if (entry_ok<D, HPC>(p, x)) {
+      combine_one<D, HPC, T>(p, x, hh, gq);
+    } else if (threadIdx.x == 0) {
+      atomicExch(p.ws_error, kDevBadItem);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -610,26 +645,55 @@ WsLayout ws_layout(int32_t batch, int32_t hkv, int32_t head_dim, int64_t n_items
   return w;
 }
 
+// cudaFuncSetAttribute once per device (the attribute is per device).
+constexpr int kAttrDevices = 64;
+
+template <typename Fn>
+int32_t ensure_smem_attr(Fn* fn, int bytes, std::atomic<bool>* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kAttrDevices) dev = -1;
+  if (dev >= 0 && done[dev].load(std::memory_order_acquire)) return PKV_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    pkv_set_error(std::string("pkv_decode_attention: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
+  }
+  if (dev >= 0) done[dev].store(true, std::memory_order_release);
+  return PKV_OK;
+}
+
 template <int D, int HPC, typename T>
 int32_t launch_decode(const DecodeParams& prm, const int4* entries, cudaStream_t s) {
   using C = Cfg<D, HPC>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<D, HPC, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
-    if (e != cudaSuccess) {
-      pkv_set_error(std::string("pkv_decode_attention: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-      return PKV_ERR_CUDA;
-    }
-    attr_set = true;
-  }
+  static std::atomic<bool> attr_done[kAttrDevices];
+  if (int32_t st = ensure_smem_attr(paged_decode_kernel<D, HPC, T>, C::kSmemBytes, attr_done)) return st;
   // A fixed-step launch does not know its item count on the host: it always
   // runs the persistent grid (idle warps fetch an out-of-range item and
   // leave) and the combine kernel.
   const bool fixed = prm.step_header != nullptr;
   const int grid =
       fixed ? num_sms_cached() : std::max(1, std::min((prm.n_items + C::kWarps - 1) / C::kWarps, num_sms_cached()));
+#if PKV_DECODE_PDL
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::kWarps * 32);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&cfg, paged_decode_kernel<D, HPC, T>, prm);
+    if (le != cudaSuccess) {
+      pkv_set_error(std::string("pkv_decode_attention launch: ") + cudaGetErrorString(le));
+      return PKV_ERR_CUDA;
+    }
+  }
+#else
   paged_decode_kernel<D, HPC, T><<<grid, C::kWarps * 32, C::kSmemBytes, s>>>(prm);
+#endif
   if (fixed || prm.n_combine > 0) {
     cudaLaunchConfig_t cfg = {};
     // One block per (entry, query head): n_combine is the step's count, or
@@ -727,24 +791,45 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
   // (head group, then split).  The items of one sequence are taken by several
   // warps at about the same time, so its split-K partials are complete early
   // and the shortest sequences (one or two small items) come last and even
-  // out the tail.  One sort of packed (pages, sequence) keys.
-  thread_local std::vector<int64_t> keys;
+  // out the tail.  Sequences ordered by (pages descending, index ascending):
+  // a counting sort over the page counts (max_pages buckets) for large
+  // batches, a comparison sort of packed keys for small ones.
+  thread_local std::vector<int32_t> order;
   thread_local std::vector<int32_t> slot_of;
-  keys.resize(batch);
+  thread_local std::vector<int32_t> bucket;
+  order.resize(batch);
   slot_of.resize(batch);
   {
     int32_t sl = 0;
     for (int b = 0; b < batch; ++b) {
-      const int64_t pages = (seq_lens[b] + 15) / 16;
-      keys[b] = ((int64_t)(0x7fffffff - pages) << 32) | b;  // ascending key = descending length
+      const int32_t pages = (seq_lens[b] + 15) / 16;
       slot_of[b] = sl;
-      sl += groups * (int32_t)((pages + pps - 1) / pps);
+      sl += groups * ((pages + pps - 1) / pps);
     }
   }
-  std::sort(keys.begin(), keys.end());
+  if (batch >= 64 && max_pages <= 4 * batch + 64) {
+    bucket.assign(max_pages + 2, 0);
+    for (int b = 0; b < batch; ++b) ++bucket[(seq_lens[b] + 15) / 16];
+    // Start of each page count's run, longest first.
+    int32_t at = 0;
+    for (int32_t pg = max_pages; pg >= 1; --pg) {
+      const int32_t n = bucket[pg];
+      bucket[pg] = at;
+      at += n;
+    }
+    for (int b = 0; b < batch; ++b) order[bucket[(seq_lens[b] + 15) / 16]++] = b;
+  } else {
+    thread_local std::vector<int64_t> keys;
+    keys.resize(batch);
+    for (int b = 0; b < batch; ++b) {
+      const int64_t pages = (seq_lens[b] + 15) / 16;
+      keys[b] = ((int64_t)(0x7fffffff - pages) << 32) | b;  // ascending key = descending length
+    }
+    std::sort(keys.begin(), keys.end());
+    for (int b = 0; b < batch; ++b) order[b] = (int32_t)(keys[b] & 0xffffffff);
+  }
   int32_t* o = items_out;
-  for (int64_t key : keys) {
-    const int32_t b = (int32_t)(key & 0xffffffff);
+  for (int32_t b : order) {
     const int32_t pages = (seq_lens[b] + 15) / 16;
     const int32_t ns = (pages + pps - 1) / pps;
     for (int hg = 0; hg < groups; ++hg) {
@@ -966,6 +1051,41 @@ int32_t pkv_decode_attention_noalloc(const pkv_pool_geom* g, void* pool, int32_t
   return pkv_decode_attention(g, pool, layer, q, k_new, v_new, block_tables, table_stride, table_rows, context_lens,
                               rows, seq_lens, new_blocks, work_items, n_items, n_combine, batch, num_q_heads,
                               pages_per_split, scale, out, scratch, kStaticScratchBytes, stream);
+}
+
+int32_t pkv_decode_noalloc_error(int32_t* error_out, void* stream) {
+  pkv_clear_error();
+  if (!error_out) {
+    pkv_set_error("pkv_decode_noalloc_error: error_out must not be NULL");
+    return PKV_ERR_ARG;
+  }
+  *error_out = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    pkv_set_error(std::string("pkv_decode_noalloc_error: cudaGetDevice: ") + cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    pkv_set_error("pkv_decode_noalloc_error: device index out of range");
+    return PKV_ERR_UNSUPPORTED;
+  }
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    scratch = g_scratch_addr[dev];
+  }
+  if (!scratch) return PKV_OK;  // no no-alloc call on this device yet
+  // The error word is the scratch's first int32; read it in stream order,
+  // after the calls issued so far on `stream`, and wait for the copy.
+  auto s = static_cast<cudaStream_t>(stream);
+  e = cudaMemcpyAsync(error_out, scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    pkv_set_error(std::string("pkv_decode_noalloc_error: ") + cudaGetErrorString(e));
+    return PKV_ERR_CUDA;
+  }
+  return PKV_OK;
 }
 
 }  // extern "C"

@@ -18,6 +18,11 @@
 #ifndef PKV_DECODE_ITEMS_PER_WARP
 #define PKV_DECODE_ITEMS_PER_WARP 3
 #endif
+// Launch the decode grid as a programmatic dependent of the kernel before it
+// on the stream (its CTAs get resident during that kernel's last blocks).
+#ifndef PKV_DECODE_PDL
+#define PKV_DECODE_PDL 0
+#endif
 
 // pkv_decode_attention plus length / refcount updates the decode does not
 // read, applied by the kernel itself: `deferred` holds deferred_refs

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -126,6 +127,9 @@ struct pkv_stepper {
   // Optional per-launch timing of the decode kernels (events around them).
   std::vector<cudaEvent_t> t_start, t_stop;
   int64_t t_cap = 0, t_count = 0, t_every = 1, t_seen = 0;
+  // Host time spent blocked on the staging ring (the host ran kRing steps
+  // ahead of the device), so that callers can tell host work from waiting.
+  int64_t wait_ns = 0;
 
   ~pkv_stepper() {
     if (round_done) {
@@ -161,7 +165,9 @@ struct pkv_stepper {
   // A ring slot with room for `n` int32, its previous upload finished.
   int32_t take_slot(int64_t n, Slot** out) {
     if (next == 0 && round_pending) {
+      const auto t0 = std::chrono::steady_clock::now();
       int32_t st = cuda_status(cudaEventSynchronize(round_done), "stepper ring");
+      wait_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count();
       if (st) return st;
       round_pending = false;
     } else if (next == 0 && round_open) {
@@ -175,15 +181,23 @@ struct pkv_stepper {
     last_taken = next;
     next = (next + 1) % kRing;
     if (s.cap < n) {
-      const int64_t cap = std::max<int64_t>(n, 2 * s.cap);
-      if (s.host) cudaFreeHost(s.host);
-      if (s.dev) cudaFree(s.dev);  // implicit device sync: only when a slot grows
-      s.host = nullptr;
-      s.dev = nullptr;
-      int32_t st = cuda_status(cudaHostAlloc((void**)&s.host, cap * 4, cudaHostAllocDefault), "cudaHostAlloc");
-      if (!st) st = cuda_status(cudaMalloc((void**)&s.dev, cap * 4), "cudaMalloc");
-      if (st) return st;
-      s.cap = cap;
+      // Grow this slot and every later one of the round together (none of
+      // them is in flight: the round began after the previous one's copies
+      // ended), so that a run of steps allocates once, not once per slot.
+      const int64_t cap = std::max<int64_t>({n + n / 4, 2 * s.cap, 4096});
+      for (int j = last_taken; j < kRing; ++j) {
+        Slot& x = slot[j];
+        if (x.cap >= cap) continue;
+        if (x.host) cudaFreeHost(x.host);
+        if (x.dev) cudaFree(x.dev);  // implicit device sync: only when slots grow
+        x.host = nullptr;
+        x.dev = nullptr;
+        x.cap = 0;
+        int32_t st = cuda_status(cudaHostAlloc((void**)&x.host, cap * 4, cudaHostAllocDefault), "cudaHostAlloc");
+        if (!st) st = cuda_status(cudaMalloc((void**)&x.dev, cap * 4), "cudaMalloc");
+        if (st) return st;
+        x.cap = cap;
+      }
     }
     *out = &s;
     return PKV_OK;
@@ -314,20 +328,27 @@ struct pkv_stepper {
     const int64_t in_need = qb + 2 * kb;
     Io& e = io[io_next];
     if (e.in_cap < in_need || e.out_cap < qb) {
-      // Grow (rare): after the device has finished with the old buffers.
-      if (e.in || e.out) {
+      // Grow (rare) every entry at once, so that the steps that follow
+      // allocate nothing: after the device has finished with the old buffers.
+      bool any = false;
+      for (const Io& x : io) any = any || x.in || x.out;
+      if (any) {
         if (int32_t st = cuda_status(cudaDeviceSynchronize(), "host-step staging")) return st;
       }
-      if (e.in) cudaFree(e.in);
-      if (e.out) cudaFree(e.out);
-      e.in = e.out = nullptr;
-      e.in_cap = e.out_cap = 0;
       const int64_t in_cap = std::max<int64_t>(in_need, 1 << 20), out_cap = std::max<int64_t>(qb, 1 << 20);
-      int32_t st = cuda_status(cudaMalloc((void**)&e.in, in_cap), "cudaMalloc host-step staging");
-      if (!st) st = cuda_status(cudaMalloc((void**)&e.out, out_cap), "cudaMalloc host-step staging");
-      if (st) return st;
-      e.in_cap = in_cap;
-      e.out_cap = out_cap;
+      for (Io& x : io) {
+        if (x.in) cudaFree(x.in);
+        if (x.out) cudaFree(x.out);
+        x.in = x.out = nullptr;
+        x.in_cap = x.out_cap = 0;
+      }
+      for (Io& x : io) {
+        int32_t st = cuda_status(cudaMalloc((void**)&x.in, in_cap), "cudaMalloc host-step staging");
+        if (!st) st = cuda_status(cudaMalloc((void**)&x.out, out_cap), "cudaMalloc host-step staging");
+        if (st) return st;
+        x.in_cap = in_cap;
+        x.out_cap = out_cap;
+      }
     }
     // First entry of a round r: record the kernels enqueued so far (through
     // round r - 1) and let this round's copies wait for round r - 2's.
@@ -816,6 +837,8 @@ int32_t pkv_stepper_error(pkv_stepper* st, int32_t* device_error) {
 
 int64_t pkv_stepper_launches(pkv_stepper* st) { return st->launches; }
 
+int64_t pkv_stepper_host_wait_ns(pkv_stepper* st) { return st->wait_ns; }
+
 int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every) {
   pkv_clear_error();
   if (count < 0 || every < 1) {
@@ -824,6 +847,13 @@ int32_t pkv_stepper_time_launches(pkv_stepper* st, int64_t count, int64_t every)
   }
   st->t_every = every;
   st->t_seen = 0;
+  st->t_count = 0;
+  if (count <= (int64_t)st->t_start.size()) {
+    // The events made by an earlier call serve again: no CUDA call here, so
+    // timing can be re-armed right before a timed region.
+    st->t_cap = count;
+    return PKV_OK;
+  }
   for (auto e : st->t_start) cudaEventDestroy(e);
   for (auto e : st->t_stop) cudaEventDestroy(e);
   st->t_start.assign(count, nullptr);

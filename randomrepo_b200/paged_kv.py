@@ -254,6 +254,17 @@ class PagedKVAllocator:
                                                              out.ctypes.data))
         return out
 
+    def growth_blocks(self, sequence_ids) -> np.ndarray:
+        """Free blocks one more token takes for each sequence (int32 0 / 1): a new block at a block
+        boundary, or the copy-on-write copy of a partial tail block that forks still share.
+        No reference counterpart (the reference's admission tests len % block_size == 0 only,
+        agentrl/generation/continuous.py:915-919, and has no forks)."""
+        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(sequence_ids, dtype=np.int64)))
+        out = np.empty(ids.size, dtype=np.int32)
+        _lib.raise_for_status(lib.pkv_allocator_growth_blocks(self._handle, ids.ctypes.data, ids.size,
+                                                              out.ctypes.data))
+        return out
+
     def refcount(self, block_id: int) -> int:
         out = ctypes.c_int32()
         _lib.raise_for_status(lib.pkv_allocator_refcount(self._handle, int(block_id), ctypes.byref(out)))
@@ -392,6 +403,14 @@ class PagedKVCacheStore:
     def append_many(self, sequence_ids, token_counts) -> None:
         """``append_tokens`` for each (sequence, count) pair, in order, without returning views."""
         self.allocator.append_many(sequence_ids, token_counts)
+
+    @property
+    def free_block_count(self) -> int:
+        return self.allocator.free_block_count
+
+    def growth_blocks(self, sequence_ids) -> np.ndarray:
+        """Free blocks each sequence's next token takes (``PagedKVAllocator.growth_blocks``)."""
+        return self.allocator.growth_blocks(sequence_ids)
 
     def release(self, sequence_id: int) -> None:
         """paged_kv.py:205-213: drop the resident cache, the stored blocks and the table."""

@@ -19,6 +19,7 @@ from tests.conftest import load_npz
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 2e-2, 1e-2
+HKV_B = 2  # KV heads of the microbench shape
 ATTN = load_npz("attention_sdpa.npz")
 
 
@@ -123,18 +124,73 @@ def test_decode_microbench_shape_and_append_bits(cuda_device):
     out = store.decode_attention(step, 0, q.to(cuda_device), kn.to(cuda_device), vn.to(cuda_device))
     torch.cuda.synchronize()
     _close(out, _oracle(q, ks, vs, 128 ** -0.5))
-    for sid in (0, 77, 255):
+    for sid in range(256):
         got = store.read_sequence_legacy_cache(sid)
         assert torch.equal(got[0][0][0].permute(1, 0, 2).cpu(), ks[sid])
         assert torch.equal(got[0][1][0].permute(1, 0, 2).cpu(), vs[sid])
-    # device tables / lengths written by the fused kernel equal the host allocator
+    _check_device_tables(store, range(256), lengths)
+
+
+def _check_device_tables(store, sids, lengths) -> None:
+    """Device block tables and lengths (written by the fused kernel) equal the host allocator, every row."""
     tables = store.pool.tables.cpu().numpy()
     lens = store.pool.context_lens.cpu().numpy()
-    for sid in (0, 31, 255):
+    for sid in sids:
         view = store.allocator.view(sid)
         row = store.allocator.row(sid)
         assert lens[row] == view.token_count == lengths[sid]
         assert tuple(tables[row, : view.logical_block_count]) == view.physical_blocks
+
+
+def test_decode_on_the_bench_workload(cuda_device):
+    """The microbench's own workload (bench.build_workload): 256 sequences of U[64, 2048] tokens whose
+    blocks follow a random permutation of a 40 000-block pool, pool values N(0, 1).  One fused step through
+    PagedKVCacheStore.decode (the call the bench times): all 256 outputs against the oracle, every
+    sequence's gathered K/V bit-exact (old rows unchanged, the appended row equal to k_new / v_new), every
+    device table row and length equal to the allocator.  Then the same step again with host q / k / v and a
+    host output (the end-to-end path): outputs bit-identical to the device-buffer step."""
+    import bench
+
+    store, lengths, q, kn, vn, _ = bench.build_workload(cuda_device, 0)
+    n = len(lengths)
+    ids = np.arange(n, dtype=np.int64)
+    # The bench fills the pool with N(0, 1) directly; here each sequence's blocks (the bench's random
+    # placement) get seeded K/V through the store, so that the oracle knows them.
+    gen = torch.Generator().manual_seed(23)
+    before = []
+    for b in range(n):
+        k = torch.randn((1, HKV_B, int(lengths[b]), 128), generator=gen).to(torch.bfloat16)
+        v = torch.randn((1, HKV_B, int(lengths[b]), 128), generator=gen).to(torch.bfloat16)
+        store.write_sequence_cache(b, ((k.to(cuda_device), v.to(cuda_device)),), None)
+        before.append((k, v))
+    out, step = store.decode(ids, q, kn, vn, layer=0)
+    torch.cuda.synchronize()
+    assert step.n_items > n  # split-K is exercised
+    ks = [torch.cat([before[b][0][0].permute(1, 0, 2), kn[b:b + 1].cpu()]) for b in range(n)]
+    vs = [torch.cat([before[b][1][0].permute(1, 0, 2), vn[b:b + 1].cpu()]) for b in range(n)]
+    _close(out, _oracle(q.cpu(), ks, vs, 128 ** -0.5))
+    for b in range(n):
+        got = store.read_sequence_legacy_cache(int(b))[0]
+        assert torch.equal(got[0][0].permute(1, 0, 2).cpu(), ks[b])
+        assert torch.equal(got[1][0].permute(1, 0, 2).cpu(), vs[b])
+    _check_device_tables(store, range(n), lengths + 1)
+    assert store.pool.decode_error_flag() == 0
+    # The end-to-end form of the same step (the bench rolls each sequence back the same way).
+    from randomrepo_b200 import host_input_tensor
+
+    store.allocator.truncate(ids, lengths)
+    inp = host_input_tensor((q.numel() + 2 * kn.numel(),), q.dtype)
+    nq, nk = q.numel(), kn.numel()
+    inp[:nq].copy_(q.reshape(-1).cpu())
+    inp[nq:nq + nk].copy_(kn.reshape(-1).cpu())
+    inp[nq + nk:].copy_(vn.reshape(-1).cpu())
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    store.decode(ids, inp[:nq].view(q.shape), inp[nq:nq + nk].view(kn.shape), inp[nq + nk:].view(vn.shape),
+                 layer=0, out=out_h)
+    store.wait_host_outputs()
+    assert torch.equal(out_h, out.cpu())
+    _check_device_tables(store, range(n), lengths + 1)
+    assert store.pool.decode_error_flag() == 0
 
 
 def test_multistep_decode_across_layers(cuda_device):

@@ -7,8 +7,10 @@ them from a fixed scratch array inside the library.  This test calls it
 through the C ABI, twice in a row, and checks each result against
 ``pkv_decode_attention`` given a workspace allocated here, with the decode
 tolerance used throughout (its results are in fact identical: same kernels,
-same plan).  It also checks that an oversized step is refused before anything
-runs.  The file is named to be collected last, and it builds its own store so
+same plan), and reads the calls' device error word through
+``pkv_decode_noalloc_error``.  It also checks that an oversized step is
+refused before anything runs, and that a block id outside the pool is
+reported (error 4) and cleared by the next call.  The file is named to be collected last, and it builds its own store so
 it passes alone in a fresh process as well as after the other tests.
 """
 
@@ -77,6 +79,34 @@ def test_no_alloc_decode_matches_workspace_entry_point(cuda_device):
         raise_for_status(lib.pkv_decode_attention_noalloc(*_args(store, step, q, got), stream))
         torch.cuda.synchronize()
         np.testing.assert_allclose(got.float().cpu().numpy(), want.float().cpu().numpy(), rtol=RTOL, atol=ATOL)
+        assert _noalloc_error(stream) == 0
+
+
+def _noalloc_error(stream) -> int:
+    from randomrepo_b200._lib import lib, raise_for_status
+
+    err = ctypes.c_int32(-1)
+    raise_for_status(lib.pkv_decode_noalloc_error(ctypes.byref(err), stream))
+    return int(err.value)
+
+
+def test_no_alloc_reports_a_bad_block_id_and_clears_it_on_the_next_call(cuda_device):
+    """A table entry outside the pool is replaced by block 0 in the kernel (no access leaves the pool)
+    and reported as error 4; the error word is readable after the call and cleared by the next one."""
+    from randomrepo_b200._lib import lib, raise_for_status
+
+    store, step, q = _setup(cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    pool = store.pool
+    row = int(step.host_rows[3])  # the 17-token sequence: its page 0 comes from the table
+    saved = int(pool.tables[row, 0].item())
+    pool.tables[row, 0] = pool.num_blocks + 5
+    out = torch.empty_like(q)
+    raise_for_status(lib.pkv_decode_attention_noalloc(*_args(store, step, q, out), stream))
+    assert _noalloc_error(stream) == 4
+    pool.tables[row, 0] = saved
+    raise_for_status(lib.pkv_decode_attention_noalloc(*_args(store, step, q, out), stream))
+    assert _noalloc_error(stream) == 0
 
 
 def test_no_alloc_rejects_steps_beyond_its_scratch(cuda_device):
