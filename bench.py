@@ -139,7 +139,10 @@ def ncu_traffic() -> float | None:
 
 
 class ClockSampler:
-    """Samples SM clock, power and throttle reasons via NVML during the timed region."""
+    """Samples SM clock and throttle reasons through NVML on a thread, from before the warm-up
+    to the end of the last timed region; ``summary()`` keeps the samples taken inside the timed
+    regions (``mark_start`` / ``mark_end``).  NVML is set up when the sampler is made, so that its
+    start-up (tens of ms) never leaves the GPU idle right before a timed region."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -147,8 +150,9 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period_s: float = 0.002) -> None:
-        self.samples: list[tuple[int, int]] = []
+    def __init__(self, index: int, period_s: float = 0.001) -> None:
+        self.samples: list[tuple[float, int, int]] = []
+        self.windows: list[list[float]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
@@ -167,12 +171,19 @@ class ClockSampler:
         n = self._nvml
         while not self._stop.is_set():
             try:
+                t = time.perf_counter()
                 mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((mhz, reasons))
+                self.samples.append((0.5 * (t + time.perf_counter()), mhz, reasons))
             except Exception:  # noqa: BLE001
                 pass
             time.sleep(self.period)
+
+    def mark_start(self) -> None:
+        self.windows.append([time.perf_counter(), float("inf")])
+
+    def mark_end(self) -> None:
+        self.windows[-1][1] = time.perf_counter()
 
     def __enter__(self):
         if self._nvml is not None:
@@ -186,15 +197,24 @@ class ClockSampler:
             self._thread.join()
 
     def summary(self) -> dict:
-        if not self.samples:
+        inside = [(m, r) for t, m, r in self.samples if any(a <= t <= b for a, b in self.windows)]
+        where = "inside the timed regions"
+        if not inside and self.samples and self.windows:
+            # Regions shorter than one NVML round trip: the samples nearest to each region.
+            where = "nearest to each timed region (no sample fell inside one)"
+            for a, b in self.windows:
+                _, m, r = min(self.samples, key=lambda x: min(abs(x[0] - a), abs(x[0] - b)))
+                inside.append((m, r))
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
-        mhz = [m for m, _ in self.samples]
+        mhz = [m for m, _ in inside]
         active = 0
-        for _, r in self.samples:
+        for _, r in inside:
             active |= r
         reasons = [k for k, bit in self.REASONS.items() if active & bit and k != "gpu_idle"]
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(mhz)}
+        return {"sm_mhz": statistics.median(mhz), "sm_min_mhz": min(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz), "where": where, "regions": len(self.windows),
+                "region_ms": round(sum(b - a for a, b in self.windows) * 1e3, 3)}
 
 
 def build_workload(device: torch.device, seed: int):
@@ -238,6 +258,8 @@ def build_workload(device: torch.device, seed: int):
 def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     import torch.distributed as dist
 
+    from randomrepo_b200._lib import lib
+
     store, lengths, q, kn, vn, _ = build_workload(device, args.seed + rank)
     ids = np.arange(SEQS, dtype=np.int64)
     out = torch.empty_like(q)
@@ -254,83 +276,104 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             dist.barrier()
         torch.cuda.synchronize(device)
 
-    # ---- device-resident timing --------------------------------------------
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    # Every step sees the same lengths (each sequence is rolled back after its
-    # step), so the algorithmic bytes of one step serve every launch; nothing
-    # but the steps themselves runs inside the timed region.
-    step_bytes = algorithmic_bytes(step().host_lens)
-    barrier()
-    # CUDA events recorded by the library right around every 4th decode launch
-    # of the timed region (an event call costs microseconds of host time).
-    pool.time_launches(args.steps // TIMING_EVERY + 1, TIMING_EVERY)
-    launches0 = pool.launch_count()
-    with ClockSampler(device.index or 0) as clocks:
+    # NVML and the launch-timing events are set up before the warm-up, so
+    # that nothing leaves the GPU idle (and its clocks falling) between the
+    # warm-up and a timed region: each region follows its warm-up steps
+    # through one barrier only.
+    clocks = ClockSampler(device.index or 0)
+    n_timed = args.steps // TIMING_EVERY + 1
+    pool.time_launches(n_timed, TIMING_EVERY)
+    pool.time_launches(0)
+    clocks.__enter__()
+    try:
+        # ---- device-resident timing ----------------------------------------
+        for _ in range(args.warmup - 1):
+            step()
+        # Every step sees the same lengths (each sequence is rolled back after
+        # its step), so the algorithmic bytes of one step serve every launch.
+        step_bytes = algorithmic_bytes(step().host_lens)
+        # CUDA events recorded by the library right around every 4th decode
+        # launch of the timed region (re-armed here without a CUDA call).
+        pool.time_launches(n_timed, TIMING_EVERY)
+        launches0 = pool.launch_count()
+        wait0 = lib.pkv_stepper_host_wait_ns(pool.stepper)
+        barrier()
+        clocks.mark_start()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
+        h0 = time.perf_counter()
         for _ in range(args.steps):
             step()
+        h1 = time.perf_counter()
         t1.record()
         torch.cuda.synchronize(device)
-    launches = pool.launch_count() - launches0
-    elapsed_ms = t0.elapsed_time(t1)
-    kernel_ms = pool.launch_times_ms().tolist()
-    pool.time_launches(0)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    barrier()
-    err = pool.decode_error_flag()
-    if err:
-        raise RuntimeError(f"decode kernel reported device error {err}")
-
-    # ---- end to end through the public API with host buffers ---------------
-    # Every step hands the store pinned host q/k/v (one packed buffer) and a
-    # pinned host output: the native stepper copies the inputs in on its copy
-    # stream ahead of the step descriptor and the output back out on a second
-    # stream, so step i+1's input copy and step i-1's output copy run while
-    # step i's kernels do.  The region ends after the last output copy.
-    from randomrepo_b200 import host_input_tensor
-
-    nq, nk = q.numel(), kn.numel()
-    inp_h = host_input_tensor((nq + 2 * nk,), q.dtype)  # page-locked, write-combined
-    inp_h[:nq].copy_(q.reshape(-1).cpu())
-    inp_h[nq:nq + nk].copy_(kn.reshape(-1).cpu())
-    inp_h[nq + nk:].copy_(vn.reshape(-1).cpu())
-    q_h, k_h, v_h = inp_h[:nq].view(q.shape), inp_h[nq:nq + nk].view(kn.shape), inp_h[nq + nk:].view(vn.shape)
-    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-
-    def e2e_step():
-        store.decode(ids, q_h, k_h, v_h, layer=0, out=out_h)
-        alloc.truncate(ids, lengths)
-
-    for _ in range(args.warmup):
-        e2e_step()
-    store.wait_host_outputs()
-    # Three timed regions of K steps each: PCIe and host time on these shared
-    # hosts vary from run to run (other tenants), so the median is reported
-    # and all three are listed.
-    e2e_runs = []
-    for _ in range(E2E_REPEATS):
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        store.fence_host_outputs()  # every output copy issued in the region ends inside it
-        e1.record()
-        torch.cuda.synchronize(device)
-        ms = e0.elapsed_time(e1)
+        clocks.mark_end()
+        wait_ns = lib.pkv_stepper_host_wait_ns(pool.stepper) - wait0
+        launches = pool.launch_count() - launches0
+        elapsed_ms = t0.elapsed_time(t1)
+        kernel_ms = pool.launch_times_ms().tolist()
+        pool.time_launches(0)
         if world > 1:
-            t = torch.tensor([ms], device=device)
+            t = torch.tensor([elapsed_ms], device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        e2e_runs.append(ms)
+            elapsed_ms = float(t.item())
+        barrier()
+        err = pool.decode_error_flag()
+        if err:
+            raise RuntimeError(f"decode kernel reported device error {err}")
+        host_wall_us = (h1 - h0) * 1e6 / args.steps
+        host_busy_us = ((h1 - h0) * 1e9 - wait_ns) / 1e3 / args.steps
+
+        # ---- end to end through the public API with host buffers -----------
+        # Every step hands the store pinned host q/k/v (one packed buffer) and
+        # a pinned host output: the native stepper copies the inputs in on its
+        # copy stream ahead of the step descriptor and the output back out on
+        # a second stream, so step i+1's input copy and step i-1's output copy
+        # run while step i's kernels do.  The region ends after the last
+        # output copy.
+        from randomrepo_b200 import host_input_tensor
+
+        nq, nk = q.numel(), kn.numel()
+        inp_h = host_input_tensor((nq + 2 * nk,), q.dtype)  # page-locked, write-combined
+        inp_h[:nq].copy_(q.reshape(-1).cpu())
+        inp_h[nq:nq + nk].copy_(kn.reshape(-1).cpu())
+        inp_h[nq + nk:].copy_(vn.reshape(-1).cpu())
+        q_h, k_h, v_h = inp_h[:nq].view(q.shape), inp_h[nq:nq + nk].view(kn.shape), inp_h[nq + nk:].view(vn.shape)
+        out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+        def e2e_step():
+            store.decode(ids, q_h, k_h, v_h, layer=0, out=out_h)
+            alloc.truncate(ids, lengths)
+
+        # Three timed regions of K steps each, each right after its warm-up
+        # steps: PCIe and host time on these shared hosts vary from run to
+        # run (other tenants), so the median is reported and all three are
+        # listed.
+        e2e_runs = []
+        for _ in range(E2E_REPEATS):
+            for _ in range(args.warmup):
+                e2e_step()
+            store.wait_host_outputs()
+            barrier()
+            clocks.mark_start()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                e2e_step()
+            store.fence_host_outputs()  # every output copy issued in the region ends inside it
+            e1.record()
+            torch.cuda.synchronize(device)
+            clocks.mark_end()
+            ms = e0.elapsed_time(e1)
+            if world > 1:
+                t = torch.tensor([ms], device=device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            e2e_runs.append(ms)
+    finally:
+        clocks.__exit__(None, None, None)
     e2e_ms = statistics.median(e2e_runs)
     barrier()
     h2d = inp_h.numel() * inp_h.element_size() + (6 * SEQS + 1) * 4
@@ -387,6 +430,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                     "second stream, every step; the region ends after the last output copy",
         },
         "gpu_launches": launches,
+        "host_us_per_step": host_busy_us,
+        "host_wall_us_per_step": host_wall_us,
+        "host_timing": "host_us_per_step: wall time of the timed loop per step minus the time the host spent "
+                       "blocked on the stepper's staging ring (pkv_stepper_host_wait_ns), i.e. the host's own "
+                       "work per step; host_wall_us_per_step includes those waits",
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_tiles:
@@ -401,7 +449,40 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         result["decode_7b"] = run_decode_7b(device, args.seed)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
+    # Last key of the line, so that a tail of the output still shows it.
+    result["summary"] = summarize(result)
     return result
+
+
+def summarize(result: dict) -> dict:
+    """The line's headline figures in a few short keys (the fractions are of the measured peaks)."""
+
+    def get(*path):
+        d = result
+        for k in path:
+            if not isinstance(d, dict) or k not in d:
+                return None
+            d = d[k]
+        return round(d, 4) if isinstance(d, float) else d
+
+    out = {
+        "decode_tokens_per_s": get("value"),
+        "e2e_tokens_per_s": get("e2e", "value"),
+        "ms_per_step": get("ms_per_step"),
+        "kernel_ms_mean": get("roofline", "kernel_ms_mean"),
+        "decode_hbm_frac": get("roofline", "frac"),
+        "host_us_per_step": get("host_us_per_step"),
+        "prefill_tensor_frac": get("tensor_tiles", "prefill", "roofline", "frac"),
+        "verify_hbm_frac": get("tensor_tiles", "verify", "roofline", "frac"),
+        "logprobs_hbm_frac": get("vocab_rows", "token_logprobs", "roofline", "frac"),
+        "rollout_tokens_per_s": get("rollout", "tokens_per_s"),
+        "speculative_tokens_per_s": get("speculative", "tokens_per_s"),
+        "decode_7b_hbm_bound_frac": get("decode_7b", "frac_of_hbm_bound"),
+        "rollout_7b_tokens_per_s": get("rollout_7b", "tokens_per_s"),
+        "grpo_rollout_tokens_per_s": get("grpo_rollout", "tokens_per_s"),
+        "cpu_baseline_tokens_per_s": get("cpu_baseline", "value"),
+    }
+    return {k: v for k, v in out.items() if v is not None}
 
 
 PREFILL_SHAPE = {"model": "Qwen2.5-7B attention", "hq": 28, "hkv": 4, "d": 128, "prompts": 32, "len_lo": 256,
@@ -969,56 +1050,78 @@ def run_vocab_rows(device: torch.device, seed: int, steps: int, warmup: int) -> 
     }
 
 
-def cpu_baseline(lengths: np.ndarray, seconds: float, sample: int = 32, steps: int | None = None) -> dict:
-    """The reference's resident-cache decode step (oracle restatement) on a bounded sample."""
-    from oracle.decode_step import ResidentDecodeBatch
-
+def _reference_sample(lengths: np.ndarray, sample: int, cls):
+    """A bounded sample of the workload for the reference's CPU path: ``sample`` of its sequences (same
+    length draw), bf16 caches and inputs, and every host core for torch's intra-op threads."""
     cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
     rng = np.random.default_rng(7)
     idx = np.sort(rng.choice(len(lengths), size=sample, replace=False))
-    sub = lengths[idx]
-    batch = ResidentDecodeBatch(sub.tolist(), HQ, HKV, D, seed=3, threads=cores)
-    q = rng.standard_normal((sample, HQ, D), dtype=np.float32)
-    kn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
-    vn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
-    ids = list(range(sample))
+    batch = cls(lengths[idx].tolist(), HQ, HKV, D, seed=3)
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn((sample, HQ, D), generator=g).to(torch.bfloat16)
+    kn = torch.randn((sample, HKV, D), generator=g).to(torch.bfloat16)
+    vn = torch.randn((sample, HKV, D), generator=g).to(torch.bfloat16)
+    return batch, list(range(sample)), q, kn, vn, cores
+
+
+def _time_reference(batch, ids, q, kn, vn, seconds: float | None, steps: int | None = None) -> tuple[float, int]:
+    """Mean seconds per step (step + rollback, so every step sees the workload's lengths)."""
     batch.step(ids, q, kn, vn)
     batch.rollback(ids)
     times = []
-    t_end = time.perf_counter() + seconds
+    t_end = time.perf_counter() + (seconds or 0.0)
     while (steps is None and time.perf_counter() < t_end) or (steps is not None and len(times) < steps):
         t = time.perf_counter()
         batch.step(ids, q, kn, vn)
-        times.append(time.perf_counter() - t)
         batch.rollback(ids)
-    batch.close()
-    per_step = statistics.mean(times)
+        times.append(time.perf_counter() - t)
+    return statistics.mean(times), len(times)
+
+
+REFERENCE_PATH_I = ("the reference's resident-cache decode step in its own torch operations (bf16 caches): "
+                    "torch.cat stack of equal-length buckets, torch.cat append (DynamicLayer.update), "
+                    "scaled_dot_product_attention with GQA, per-sequence clone split, append_tokens "
+                    "(oracle.decode_step.TorchResidentDecodeBatch)")
+REFERENCE_PATH_II = ("the reference's block-store round trip in torch (bf16): read_sequence_legacy_cache (key "
+                     "scan of the whole store + torch.cat of the blocks), torch.cat append, GQA SDPA, "
+                     "append_tokens, write_sequence_cache (split + clone per block) "
+                     "(oracle.decode_step.TorchBlockStoreDecodeBatch)")
+
+
+def cpu_baseline(lengths: np.ndarray, seconds: float, sample: int = 32, steps: int | None = None) -> dict:
+    """The reference's CPU decode paths (torch restatements, bf16) on bounded samples of the workload."""
+    from oracle.decode_step import TorchBlockStoreDecodeBatch, TorchResidentDecodeBatch
+
+    batch, ids, q, kn, vn, cores = _reference_sample(lengths, sample, TorchResidentDecodeBatch)
+    per_step, n = _time_reference(batch, ids, q, kn, vn, seconds, steps)
+    batch2, ids2, q2, kn2, vn2, _ = _reference_sample(lengths, sample, TorchBlockStoreDecodeBatch)
+    per_step2, n2 = _time_reference(batch2, ids2, q2, kn2, vn2, max(1.0, seconds / 4), None if steps is None else 2)
     return {
         "value": sample / per_step,
         "unit": "tokens/s",
         "cores": cores,
         "kind": "port",
-        "sample": f"{sample} of the {SEQS} sequences (ctx from the same U[64,2048] draw), {len(times)} decode "
-                  "steps of the reference's resident-cache path: cat append, fp32 GQA attention, clone, "
-                  "append_tokens; fp16 caches",
+        "dtype": "bf16",
+        "sample": f"{sample} of the {SEQS} sequences (ctx from the same U[64,2048] draw), {n} decode steps of "
+                  + REFERENCE_PATH_I,
         "seconds_per_step": per_step,
+        "block_store_path": {
+            "value": sample / per_step2, "unit": "tokens/s", "seconds_per_step": per_step2,
+            "sample": f"{sample} of the {SEQS} sequences, {n2} decode steps of " + REFERENCE_PATH_II,
+        },
     }
 
 
 def run_reference(args) -> dict:
+    """The reference's CPU path (torch restatement of its resident-cache decode step, bf16) on the host cores:
+    each step is a 32-sequence sample of the workload, so the run ends within a few minutes."""
     gen = torch.Generator().manual_seed(args.seed)
     lengths = torch.randint(64, 2049, (SEQS,), generator=gen).numpy().astype(np.int64)
-    from oracle.decode_step import ResidentDecodeBatch
+    from oracle.decode_step import TorchResidentDecodeBatch
 
-    cores = len(os.sched_getaffinity(0))
     sample = 32
-    rng = np.random.default_rng(7)
-    idx = np.sort(rng.choice(SEQS, size=sample, replace=False))
-    batch = ResidentDecodeBatch(lengths[idx].tolist(), HQ, HKV, D, seed=3, threads=cores)
-    q = rng.standard_normal((sample, HQ, D), dtype=np.float32)
-    kn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
-    vn = rng.standard_normal((sample, HKV, D), dtype=np.float32).astype(np.float16)
-    ids = list(range(sample))
+    batch, ids, q, kn, vn, cores = _reference_sample(lengths, sample, TorchResidentDecodeBatch)
     for _ in range(args.warmup):
         batch.step(ids, q, kn, vn)
         batch.rollback(ids)
@@ -1027,7 +1130,6 @@ def run_reference(args) -> dict:
         batch.step(ids, q, kn, vn)
         batch.rollback(ids)
     elapsed = time.perf_counter() - t
-    batch.close()
     value = sample * args.steps / elapsed
     return {
         "metric": METRIC,
@@ -1046,8 +1148,7 @@ def run_reference(args) -> dict:
         "config": workload_config(1),
         "cpu_baseline": {
             "value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"each step: {sample} of the {SEQS} sequences through the reference's resident-cache "
-                      "decode step (oracle restatement: cat append, fp32 GQA attention, clone, append_tokens)",
+            "sample": f"each step: {sample} of the {SEQS} sequences through " + REFERENCE_PATH_I,
         },
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
