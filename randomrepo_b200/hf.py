@@ -458,6 +458,7 @@ class PagedGenerator:
         self._ext_graphs: dict[tuple[int, int], tuple] = {}
         self.fp32_logits = bool(fp32_logits)
         self._sampler = sampler
+        self._growth_used = 0  # blocks the last admission set aside for its sequences' next tokens
         # Device times of the last generate on a CUDA device: prefill_ms (prompts
         # + forks), decode_ms (the decode loop), token counts.
         self.last_timings: dict = {}
@@ -637,9 +638,10 @@ class PagedGenerator:
                     last_hidden[i] = h[int(ends[j])]
         return self.logits(torch.stack(last_hidden))
 
-    def decode_step(self, sequence_ids, tokens: torch.Tensor) -> torch.Tensor:
-        """Feed one token per sequence; returns next-token logits [n, vocab] (float32)."""
-        if self.cuda_graphs:
+    def decode_step(self, sequence_ids, tokens: torch.Tensor, *, eager: bool = False) -> torch.Tensor:
+        """Feed one token per sequence; returns next-token logits [n, vocab] (float32).  ``eager`` runs
+        the step without its CUDA graph (whose placeholder padding could take blocks a full pool lacks)."""
+        if self.cuda_graphs and not eager:
             return self._decode_step_graph(sequence_ids, tokens)
         step = self.store.decode_step(sequence_ids)
         pos = self._h2d.to_device(torch.from_numpy(step.host_lens.astype(np.int64) - 1), self.device)
@@ -835,7 +837,7 @@ class PagedGenerator:
     # -- rollout ----------------------------------------------------------------
     def generate(self, prompts, *, group_size: int = 1, max_new_tokens: int = 16,
                  sampling: SamplingConfig | None = None, force_tokens=None, first_id: int = 0,
-                 release: bool = True) -> dict:
+                 release: bool = True, step_callback=None) -> dict:
         """Roll out ``group_size`` completions per prompt.
 
         Each prompt is prefilled once; the other members of its group fork the
@@ -843,9 +845,23 @@ class PagedGenerator:
         logits.  Returns ``{"sequence_ids", "tokens" (list per sequence),
         "logprobs" (list per sequence: the temperature-1 log-probability of
         each emitted token, the old-policy value of rollout.py:456-472),
-        "argmax" (per step, the greedy token of each sequence's logits)}``.
-        ``force_tokens[i]`` (optional) feeds sequence i those tokens instead
-        of sampled ones (teacher forcing).
+        "argmax" (per token, the greedy token of the logits it was drawn
+        from), "kv_pressure" (counters, below), "steps" (decode loop
+        iterations)}``.  ``force_tokens[i]`` (optional) feeds sequence i those
+        tokens instead of sampled ones (teacher forcing).
+
+        KV pressure (continuous.py:875-937): before each step, sequences whose
+        next token needs a free block (a block boundary, or a copy-on-write
+        copy of a shared tail) are admitted only while free blocks remain, in
+        order of how long they have waited; the others keep their pending
+        logits for a later step (soft preemption, counted as the reference
+        counts it).  When no sequence can be admitted at all, the sequence
+        holding the most generated tokens is evicted (its blocks released) and
+        re-prefilled from its prompt and tokens once blocks are free again, so
+        a pool too small for the whole batch finishes instead of raising.
+        ``step_callback(sequence_ids, tokens, logprobs)``, if given, is called
+        once per loop iteration with that iteration's sampled rows (device
+        tensors; possibly none).
         """
         cfg = sampling or SamplingConfig()
         sampler = self.sampler
@@ -877,19 +893,71 @@ class PagedGenerator:
         tokens = [[] for _ in range(n)]
         logprobs = [[] for _ in range(n)]
         argmax = [[] for _ in range(n)]
-        active = list(range(n))
-        for step in range(max_new_tokens):
-            if not active:
-                break
-            if force_tokens is not None:
-                nxt = torch.tensor([int(force_tokens[i][step]) for i in active], device=cur.device)
-                _, _, am = sampler.sample(cur)
-                chosen_lp = sampler.token_logprobs(cur, nxt)
+        kv = {"paged_kv_preempted_sequences": 0.0, "paged_kv_max_preempted_sequences": 0.0,
+              "scheduler_decode_growth_block_demand": 0.0, "scheduler_decode_growth_blocks_admitted": 0.0,
+              "paged_kv_evicted_sequences": 0.0, "paged_kv_recomputed_tokens": 0.0}
+        cur_rows = list(range(n))      # sequence index of each row of ``cur``
+        held: dict[int, torch.Tensor] = {}   # deferred sequences' pending logits
+        evicted: list[int] = []        # released sequences to re-prefill, oldest first
+        waited = [0] * n
+        iterations = 0
+        while cur_rows or held or evicted:
+            iterations += 1
+            if evicted:
+                self._restore_evicted(evicted, held, prompts, group_size, seq_ids, tokens, kv,
+                                      resident=len(cur_rows) + len(held))
+            candidates = cur_rows + sorted(held)
+            admitted = self._admit(candidates, seq_ids, waited, kv)
+            while not admitted and candidates:
+                victim = max(candidates, key=lambda i: (len(tokens[i]), i))
+                self.store.release(seq_ids[victim])
+                if victim in held:
+                    del held[victim]
+                else:
+                    pos = cur_rows.index(victim)
+                    cur_rows.pop(pos)
+                    cur = torch.cat([cur[:pos], cur[pos + 1:]])
+                evicted.append(victim)
+                kv["paged_kv_evicted_sequences"] += 1.0
+                candidates = [i for i in candidates if i != victim]
+                admitted = self._admit(candidates, seq_ids, waited, kv)
+            if not admitted:
+                # Everything was evicted: the next iteration restores the oldest, if it fits at all.
+                if not self._fits_alone(evicted[0], prompts, group_size, tokens):
+                    raise RuntimeError("the KV pool cannot hold a single sequence of this rollout")
+                continue
+            if admitted == cur_rows and not held:
+                rows = cur
             else:
-                nxt, chosen_lp, am = sampler.sample(cur, cfg)
+                pos = {i: j for j, i in enumerate(cur_rows)}
+                rows = torch.stack([cur[pos[i]] if i in pos else held[i] for i in admitted])
+                adm = set(admitted)
+                for i in candidates:
+                    if i not in adm and i in pos:
+                        held[i] = cur[pos[i]]
+                for i in admitted:
+                    held.pop(i, None)
+                deferred = len(candidates) - len(admitted)
+                kv["paged_kv_preempted_sequences"] += float(deferred)
+                kv["paged_kv_max_preempted_sequences"] = max(kv["paged_kv_max_preempted_sequences"], float(deferred))
+            if len(admitted) != len(candidates):
+                adm = set(admitted)
+                for i in candidates:
+                    waited[i] = 0 if i in adm else waited[i] + 1
+            elif held or any(waited[i] for i in admitted):
+                for i in admitted:
+                    waited[i] = 0
+            if force_tokens is not None:
+                nxt = torch.tensor([int(force_tokens[i][len(tokens[i])]) for i in admitted], device=rows.device)
+                _, _, am = sampler.sample(rows)
+                chosen_lp = sampler.token_logprobs(rows, nxt)
+            else:
+                nxt, chosen_lp, am = sampler.sample(rows, cfg)
+            if step_callback is not None:
+                step_callback([seq_ids[i] for i in admitted], nxt, chosen_lp)
             nxt_h, lp_h, am_h = nxt.tolist(), chosen_lp.tolist(), am.tolist()
             still = []
-            for j, i in enumerate(active):
+            for j, i in enumerate(admitted):
                 tokens[i].append(nxt_h[j])
                 logprobs[i].append(lp_h[j])
                 argmax[i].append(am_h[j])
@@ -899,11 +967,19 @@ class PagedGenerator:
                     still.append(j)
                 elif release and self.store.has_sequence(seq_ids[i]):
                     self.store.release(seq_ids[i])
+            cur_rows = [admitted[j] for j in still]
             if not still:
-                break
-            keep = torch.tensor(still, device=cur.device)
-            active = [active[j] for j in still]
-            cur = self.decode_step([seq_ids[i] for i in active], nxt[keep])
+                cur = cur[:0]
+                continue
+            keep = torch.tensor(still, device=rows.device)
+            eager = False
+            if self.cuda_graphs:
+                # A graphed step pads to a recorded batch size; placeholders may each take a block.
+                free = getattr(self.store, "free_block_count", None)
+                if free is not None:
+                    k = len(cur_rows)
+                    eager = free - self._growth_used < graph_batch(k) - k + 1
+            cur = self.decode_step([seq_ids[i] for i in cur_rows], nxt[keep], eager=eager)
         if marks is not None:
             marks[2].record()
             marks[2].synchronize()
@@ -918,4 +994,59 @@ class PagedGenerator:
                 if self.store.has_sequence(sid):
                     self.store.release(sid)
             self.release_placeholders()
-        return {"sequence_ids": seq_ids, "tokens": tokens, "logprobs": logprobs, "argmax": argmax}
+        return {"sequence_ids": seq_ids, "tokens": tokens, "logprobs": logprobs, "argmax": argmax,
+                "kv_pressure": kv, "steps": iterations}
+
+    def _admit(self, candidates: list[int], seq_ids: list[int], waited: list[int], kv: dict) -> list[int]:
+        """Growth admission (continuous.py:900-937, with copy-on-write copies counted as growth): the
+        candidates whose next token fits the free blocks, longest-waiting first; in candidate order."""
+        free = getattr(self.store, "free_block_count", None)
+        self._growth_used = 0
+        if free is None or free >= len(candidates):
+            self._growth_used = len(candidates) if free is not None else 0
+            return list(candidates)
+        need = self.store.growth_blocks([seq_ids[i] for i in candidates])
+        order = sorted(range(len(candidates)), key=lambda j: (-waited[candidates[j]], j))
+        used, take = 0, []
+        for j in order:
+            if need[j] and used >= free:
+                continue
+            take.append(j)
+            used += int(need[j])
+        kv["scheduler_decode_growth_block_demand"] += float(need.sum())
+        kv["scheduler_decode_growth_blocks_admitted"] += float(used)
+        self._growth_used = used
+        return [candidates[j] for j in sorted(take)]
+
+    def _block_size(self) -> int:
+        alloc = getattr(self.store, "allocator", None)
+        return int(alloc.block_size_tokens) if alloc is not None else int(getattr(self.store, "block_size", 16))
+
+    def _fits_alone(self, i: int, prompts, group_size: int, tokens: list) -> bool:
+        n = int(torch.as_tensor(prompts[i // group_size]).numel()) + len(tokens[i])
+        return int(self.store.free_block_count) >= -(-n // self._block_size()) + 1
+
+    def _restore_evicted(self, evicted: list[int], held: dict, prompts, group_size: int, seq_ids: list[int],
+                         tokens: list, kv: dict, resident: int) -> None:
+        """Re-prefill evicted sequences (oldest first) while the free blocks cover their tokens plus one
+        block of growth for every resident sequence; their next-token logits join the held rows."""
+        bs = self._block_size()
+        back, rows = [], []
+        free = int(self.store.free_block_count)
+        while evicted:
+            i = evicted[0]
+            toks = torch.cat([torch.as_tensor(prompts[i // group_size], dtype=torch.long).reshape(-1),
+                              torch.tensor(tokens[i], dtype=torch.long)])
+            need = -(-toks.numel() // bs) + 1
+            if free < need + resident + len(back):
+                break
+            evicted.pop(0)
+            free -= need
+            back.append(i)
+            rows.append(toks)
+        if not back:
+            return
+        logits = self.prefill([seq_ids[i] for i in back], rows)
+        for j, i in enumerate(back):
+            held[i] = logits[j]
+            kv["paged_kv_recomputed_tokens"] += float(rows[j].numel())

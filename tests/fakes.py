@@ -24,22 +24,76 @@ class _FakeStep:
 
 
 class FakeStore:
-    def __init__(self, layers: int):
+    """With ``total_blocks`` it also keeps block accounting like the device allocator: blocks of
+    ``block_size`` tokens, forks sharing them by refcount, a shared partial tail copied on the first
+    append, and ``RuntimeError`` when no block is free."""
+
+    def __init__(self, layers: int, total_blocks: int | None = None, block_size: int = 16):
         self.layers = layers
         self.kv = {}    # sid -> list per layer of [k [T,Hkv,D], v]
         self.count = {}
+        self.block_size = block_size
+        self.total_blocks = total_blocks
+        self.blocks = {}  # sid -> list of block ids
+        self.refs = {}    # block id -> refcount
+        self._next_block = 0
+
+    # -- block accounting (only with total_blocks) --
+    @property
+    def free_block_count(self):
+        return None if self.total_blocks is None else self.total_blocks - len(self.refs)
+
+    def _grow(self, sid):
+        if self.total_blocks is None:
+            return
+        blocks, n, bs = self.blocks[sid], self.count[sid], self.block_size
+        if n % bs != 0 and self.refs[blocks[-1]] > 1:
+            self.refs[blocks[-1]] -= 1
+            blocks[-1] = self._alloc()
+        while len(blocks) < -(-(n + 1) // bs):
+            blocks.append(self._alloc())
+
+    def _alloc(self):
+        if len(self.refs) >= self.total_blocks:
+            raise RuntimeError("PagedKVAllocator ran out of free blocks.")
+        b = self._next_block
+        self._next_block += 1
+        self.refs[b] = 1
+        return b
+
+    def _drop(self, blocks):
+        for b in blocks:
+            self.refs[b] -= 1
+            if self.refs[b] == 0:
+                del self.refs[b]
+
+    def growth_blocks(self, ids):
+        out = []
+        for sid in ids:
+            blocks, n, bs = self.blocks[sid], self.count[sid], self.block_size
+            out.append(1 if len(blocks) < -(-(n + 1) // bs) or (n % bs != 0 and self.refs[blocks[-1]] > 1) else 0)
+        return np.array(out, dtype=np.int32)
 
     def reserve(self, sid, n):
         assert sid not in self.count
-        self.count[sid] = n
+        self.count[sid] = 0
+        self.blocks[sid] = []
+        for _ in range(n):
+            self._grow(sid)
+            self.count[sid] += 1
         self.kv[sid] = [[None, None] for _ in range(self.layers)]
 
     def append_tokens(self, sid, n):
-        self.count[sid] += n
+        for _ in range(n):
+            self._grow(sid)
+            self.count[sid] += 1
 
     def fork(self, parent, child):
         self.count[child] = self.count[parent]
         self.kv[child] = [[k.clone(), v.clone()] for k, v in self.kv[parent]]
+        self.blocks[child] = list(self.blocks[parent])
+        for b in self.blocks[child]:
+            self.refs[b] += 1
 
     def has_sequence(self, sid):
         return sid in self.count
@@ -51,15 +105,22 @@ class FakeStore:
         for sid, n in zip(ids, counts):
             assert n <= self.count[sid]
             self.count[sid] = n
+            keep = -(-n // self.block_size)
+            if self.total_blocks is not None:
+                self._drop(self.blocks[sid][keep:])
+            del self.blocks[sid][keep:]
             for ent in self.kv[sid]:
                 if ent[0] is not None:
                     ent[0], ent[1] = ent[0][:n], ent[1][:n]
 
     def release(self, sid):
-        del self.count[sid], self.kv[sid]
+        if self.total_blocks is not None:
+            self._drop(self.blocks[sid])
+        del self.count[sid], self.kv[sid], self.blocks[sid]
 
     def decode_step(self, ids):
         for s in ids:
+            self._grow(s)
             self.count[s] += 1
         return _FakeStep(np.array([self.count[s] for s in ids]), list(ids))
 

@@ -263,3 +263,34 @@ def test_packed_weights_follow_a_projection_replaced_on_its_own():
     gu = _gate_up(mlp)
     assert torch.equal(gu[mlp.gate_proj.weight.shape[0]:], new_up)
     assert _gate_up(mlp) is gu  # packed again once, then reused
+
+
+def test_rollout_under_kv_pressure_defers_evicts_and_keeps_the_tokens():
+    """A pool far too small for the batch: growth admission defers sequences whose next token needs a
+    block (continuous.py:900-937; soft preemptions counted as continuous.py:875-898 counts them), and
+    when no sequence can grow at all one is evicted and re-prefilled later.  Teacher-forced on the tokens
+    of an unpressured run, every position's greedy choice and log-probability equal that run's."""
+    from oracle.sampling import OracleSampler
+    from randomrepo_b200.hf import PagedGenerator
+
+    model = _tiny_model()
+    gen = torch.Generator().manual_seed(21)
+    prompts = [torch.randint(0, 128, (int(n),), generator=gen) for n in (20, 9, 33)]
+    new = 40
+    free_run = PagedGenerator(model, FakeStore(2), prefill_chunk_size=64, sampler=OracleSampler())
+    want = free_run.generate(prompts, group_size=3, max_new_tokens=new)
+    assert want["kv_pressure"]["paged_kv_preempted_sequences"] == 0 and want["steps"] == new
+    # 9 sequences of up to 73 tokens need ~40 blocks of 16 with the prompts shared; give them 14.
+    store = FakeStore(2, total_blocks=14)
+    tight = PagedGenerator(model, store, prefill_chunk_size=64, sampler=OracleSampler())
+    got = tight.generate(prompts, group_size=3, max_new_tokens=new, force_tokens=want["tokens"])
+    kv = got["kv_pressure"]
+    assert kv["paged_kv_preempted_sequences"] > 0 and kv["paged_kv_max_preempted_sequences"] >= 1
+    assert kv["paged_kv_evicted_sequences"] > 0 and kv["paged_kv_recomputed_tokens"] > 0
+    assert kv["scheduler_decode_growth_blocks_admitted"] <= kv["scheduler_decode_growth_block_demand"]
+    assert got["steps"] > new
+    assert got["tokens"] == want["tokens"]
+    assert got["argmax"] == want["argmax"]
+    for a, b in zip(got["logprobs"], want["logprobs"]):
+        np.testing.assert_allclose(a, b, atol=1e-4)
+    assert store.refs == {}  # every block returned
