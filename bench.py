@@ -379,6 +379,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     h2d = inp_h.numel() * inp_h.element_size() + (6 * SEQS + 1) * 4
     d2h = out_h.numel() * out_h.element_size()
 
+    # The sharded rollout runs on every rank (its gathers are collectives): at N > 1 before rank 0
+    # goes on alone; at N = 1 after the other lines.
+    grpo = None
+    if world > 1 and not args.no_rollout:
+        grpo = run_grpo_rollout(device, args.seed, rank, world)
     if rank != 0:
         return None
     ms_per_step = elapsed_ms / args.steps
@@ -447,6 +452,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         result["rollout"], result["old_policy"] = run_rollout(device, args.seed)
         result["speculative"] = run_speculative(device, args.seed)
         result["decode_7b"] = run_decode_7b(device, args.seed)
+        result["rollout_7b"] = run_rollout_7b(device, args.seed)
+    if world == 1 and not args.no_rollout:
+        grpo = run_grpo_rollout(device, args.seed, rank, world)
+    if grpo is not None:
+        result["grpo_rollout"] = grpo
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(lengths, args.cpu_seconds)
     # Last key of the line, so that a tail of the output still shows it.
@@ -701,6 +711,189 @@ def run_rollout(device: torch.device, seed: int, iters: int = 2) -> tuple[dict, 
     del gen, store, model
     torch.cuda.empty_cache()
     return rollout, old
+
+
+def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, iters: int = 2) -> dict:
+    """GRPO rollout sharded by groups, one rank per GPU, with the per-step gather the trainer needs.
+
+    Every rank draws the same 4 x world prompts (Qwen2.5-1.5B architecture, random-init bf16, prompts
+    U[64, 256], group 8, 128 new tokens, temperature 1.0), owns the groups ``assign_groups`` gives it
+    (balanced by prompt tokens x group size), rolls them out with PagedGenerator (CUDA-graph decode
+    steps, its own KV pool) and, at every decode step, gathers the step's (sequence id, token,
+    log-probability) rows of all ranks with one NCCL all_gather_into_tensor (StepGather); no KV crosses
+    GPUs.  Ranks whose loops ran fewer steps make empty gathers after it, so every rank makes the same
+    collectives.  Timed with CUDA events per rank, max over ranks; tokens are summed over ranks."""
+    import torch.distributed as dist
+
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
+    from randomrepo_b200.sharding import StepGather, assign_groups, balance_ratio, groups_of_rank
+
+    rs = ROLLOUT_SHAPE
+    group, new = rs["group"], rs["new_tokens"]
+    n_prompts = rs["prompts"] * world
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(rs["len_lo"], rs["len_hi"] + 1, size=n_prompts)
+    prompts = [torch.from_numpy(rng.integers(0, QWEN_1P5B["vocab_size"], size=int(n))) for n in lens]
+    assignment = assign_groups(lens, group, world)
+    mine = groups_of_rank(assignment, rank)
+    model = _qwen(device, QWEN_1P5B, seed)
+    store = make_store(model, total_blocks=4096)
+    gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
+    max_rows = group * max(len(groups_of_rank(assignment, r)) for r in range(world))
+    gather = StepGather(max_rows, device) if world > 1 else None
+    host = {"s": 0.0, "rows": 0}
+
+    def hook(ids, tok, lp):
+        if gather is None:
+            return
+        t = time.perf_counter()
+        gather.start(torch.tensor(ids, dtype=torch.int64), tok, lp)
+        host["s"] += time.perf_counter() - t
+
+    def rollout(it: int) -> tuple[int, float, float]:
+        host["s"] = 0.0
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = gen.generate([prompts[g] for g in mine], group_size=group, max_new_tokens=new, first_id=it * 100000,
+                         sampling=SamplingConfig(do_sample=True, temperature=rs["temperature"], seed=it),
+                         step_callback=hook)
+        if gather is not None:
+            steps = torch.tensor([r["steps"]], device=device)
+            dist.all_reduce(steps, op=dist.ReduceOp.MAX)
+            empty = torch.zeros(0, dtype=torch.int64)
+            for _ in range(int(steps.item()) - r["steps"]):
+                hook([], empty, torch.zeros(0))
+            t = time.perf_counter()
+            rows = gather.finish()
+            host["s"] += time.perf_counter() - t
+            host["rows"] = sum(len(x.tokens) for x in rows)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        return sum(len(t) for t in r["tokens"]), ms, host["s"] * 1e3
+
+    rollout(0)  # records the decode-step graphs
+    runs = [rollout(it) for it in range(1, iters + 1)]
+    if store.pool.decode_error_flag() or store.pool.prefill_error_flag():
+        raise RuntimeError("rollout kernels reported a device error")
+    tokens = sum(n for n, _, _ in runs)
+    ms = sum(t for _, t, _ in runs)
+    gather_ms = sum(g for _, _, g in runs)
+    if world > 1:
+        t = torch.tensor([float(tokens), ms, gather_ms], device=device, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tokens, ms, gather_ms = float(t[0].item()), float(mx[1].item()), float(mx[2].item())
+    del gen, store, model
+    torch.cuda.empty_cache()
+    return {
+        "workload": f"GRPO rollout sharded by groups: {rs['prompts']} prompts x group {group} per GPU "
+                    f"({n_prompts} prompts on {world} GPU(s)), Qwen2.5-1.5B architecture, random-init bf16, "
+                    f"prompts U[{rs['len_lo']},{rs['len_hi']}], {new} new tokens, temperature "
+                    f"{rs['temperature']}, seed {seed}",
+        "tokens_per_s": tokens / (ms * 1e-3),
+        "tokens_per_s_per_gpu": tokens / (ms * 1e-3) / world,
+        "ms_per_rollout": ms / iters,
+        "gather_host_ms_per_rollout": gather_ms / iters,
+        "gathered_rows_per_rollout": host["rows"],
+        "group_balance": balance_ratio(lens, group, assignment, world),
+        "path": "per rank: PagedGenerator with CUDA-graph decode steps on its own KV pool; per decode step one "
+                "NCCL all_gather_into_tensor of (sequence id, token, log-probability) rows (StepGather.start: it "
+                "runs behind the next step's work; StepGather.finish collects every step's rows at the end)"
+                if world > 1 else "PagedGenerator with CUDA-graph decode steps (no collective at one GPU)",
+        "timing": f"CUDA events around whole rollouts (every gather completed inside), {iters} after one warm-up; "
+                  "max over ranks of the time, sum over ranks of the tokens; gather_host_ms = host time in the "
+                  "gather calls (max over ranks)",
+    }
+
+
+ROLLOUT_7B_SHAPE = {"prompts": 64, "group": 8, "len_lo": 256, "len_hi": 4096, "new_tokens": 1024,
+                    "temperature": 1.0, "pool_fraction": 0.6}
+
+
+def run_rollout_7b(device: torch.device, seed: int) -> dict:
+    """The Qwen2.5-7B rollout under KV pressure: 64 prompts x group 8 = 512 sequences, prompts
+    U[256, 4096], 1024 new tokens, temperature 1.0, random-init bf16, through PagedGenerator with a
+    KV pool of 60 % of the blocks the rollout's peak would hold (shared prompt blocks + every
+    sequence's generated blocks), so growth admission defers sequences and evicts / re-prefills when
+    nothing can grow.  Timed once with CUDA events after a short warm-up rollout that records the
+    decode graphs."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from randomrepo_b200.hf import PagedGenerator, SamplingConfig, kv_geometry, make_store
+
+    sh = ROLLOUT_7B_SHAPE
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(sh["len_lo"], sh["len_hi"] + 1, size=sh["prompts"])
+    prompts = [torch.from_numpy(rng.integers(0, QWEN_7B["vocab_size"], size=int(n))) for n in lens]
+    group, new, bs = sh["group"], sh["new_tokens"], 16
+    peak_blocks = int(sum(-(-int(n) // bs) for n in lens)) + sh["prompts"] * group * (-(-new // bs) + 1)
+    blocks = int(peak_blocks * sh["pool_fraction"])
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen2ForCausalLM._from_config(Qwen2Config(**QWEN_7B, attn_implementation="sdpa"),
+                                              dtype=torch.bfloat16).eval()
+    store = make_store(model, total_blocks=blocks)
+    gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
+    cfg = SamplingConfig(do_sample=True, temperature=sh["temperature"], seed=1)
+    gen.generate(prompts[:8], group_size=group, max_new_tokens=32, sampling=cfg)  # records graphs
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    r = gen.generate(prompts, group_size=group, max_new_tokens=new, first_id=100000, sampling=cfg)
+    e1.record()
+    torch.cuda.synchronize(device)
+    s = e0.elapsed_time(e1) / 1e3
+    if store.pool.decode_error_flag() or store.pool.prefill_error_flag():
+        raise RuntimeError("rollout kernels reported a device error")
+    n_tok = sum(len(t) for t in r["tokens"])
+    layers, hkv, d = kv_geometry(model.config)
+    per_block = layers * hkv * d * 2 * 2 * bs
+    timings = dict(gen.last_timings)
+    # The same rollout with a pool that holds its peak (no pressure), for comparison.
+    del gen, store
+    torch.cuda.empty_cache()
+    store = make_store(model, total_blocks=peak_blocks + 512)
+    gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
+    gen.generate(prompts[:8], group_size=group, max_new_tokens=32, sampling=cfg)
+    torch.cuda.synchronize(device)
+    e0.record()
+    r2 = gen.generate(prompts, group_size=group, max_new_tokens=new, first_id=200000, sampling=cfg)
+    e1.record()
+    torch.cuda.synchronize(device)
+    s2 = e0.elapsed_time(e1) / 1e3
+    if store.pool.decode_error_flag() or store.pool.prefill_error_flag():
+        raise RuntimeError("rollout kernels reported a device error")
+    out = {
+        "workload": f"GRPO rollout, Qwen2.5-7B architecture (28 layers, 28q/4kv heads, head_dim 128, vocab 152064), "
+                    f"random-init bf16, {sh['prompts']} prompts x group {group} = {sh['prompts'] * group} sequences, "
+                    f"prompts U[{sh['len_lo']},{sh['len_hi']}] random ids, {new} new tokens, temperature "
+                    f"{sh['temperature']}, seed {seed}",
+        "tokens_per_s": n_tok / s,
+        "seconds": s,
+        "decode_loop_iterations": r["steps"],
+        "kv_pool_gb": blocks * per_block / 1e9,
+        "kv_pool_blocks": blocks,
+        "kv_peak_demand_blocks": peak_blocks,
+        "kv_pressure": r["kv_pressure"],
+        "prefill_ms": timings.get("prefill_ms"),
+        "decode_ms": timings.get("decode_ms"),
+        "unpressured_tokens_per_s": sum(len(t) for t in r2["tokens"]) / s2,
+        "unpressured_kv_pool_gb": (peak_blocks + 512) * per_block / 1e9,
+        "unpressured_decode_loop_iterations": r2["steps"],
+        "path": "PagedGenerator: packed chunked prefill (512), one prefill per group + copy-on-write forks, CUDA-graph "
+                "decode steps (eager when a full pool could not take a graph's padding), growth admission with soft "
+                "preemption, eviction + re-prefill when more than a quarter of the batch would wait, device sampling",
+        "timing": "CUDA events around one whole rollout after a 32-token warm-up rollout of 8 groups (each pool)",
+        "gpu_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
+    }
+    del gen, store, model
+    torch.cuda.empty_cache()
+    return out
 
 
 QWEN_7B = dict(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,

@@ -855,10 +855,11 @@ class PagedGenerator:
         copy of a shared tail) are admitted only while free blocks remain, in
         order of how long they have waited; the others keep their pending
         logits for a later step (soft preemption, counted as the reference
-        counts it).  When no sequence can be admitted at all, the sequence
-        holding the most generated tokens is evicted (its blocks released) and
-        re-prefilled from its prompt and tokens once blocks are free again, so
-        a pool too small for the whole batch finishes instead of raising.
+        counts it).  When that would leave more than a quarter of the batch
+        waiting (or nothing admitted), the newest sequences are evicted (their
+        blocks released) and re-prefilled from their prompts and tokens once
+        blocks are free again, so a pool too small for the whole batch
+        finishes instead of raising.
         ``step_callback(sequence_ids, tokens, logprobs)``, if given, is called
         once per loop iteration with that iteration's sampled rows (device
         tensors; possibly none).
@@ -908,8 +909,11 @@ class PagedGenerator:
                                       resident=len(cur_rows) + len(held))
             candidates = cur_rows + sorted(held)
             admitted = self._admit(candidates, seq_ids, waited, kv)
-            while not admitted and candidates:
-                victim = max(candidates, key=lambda i: (len(tokens[i]), i))
+            # Deferring most of the batch would leave the step's weight and KV reads serving a few
+            # tokens: evict instead (the newest sequences first, so a group leaves together and its
+            # shared prompt blocks free with its last member) until at most a quarter waits.
+            while candidates and (not admitted or len(candidates) - len(admitted) > max(1, len(candidates) // 4)):
+                victim = max(candidates)
                 self.store.release(seq_ids[victim])
                 if victim in held:
                     del held[victim]
@@ -930,7 +934,10 @@ class PagedGenerator:
                 rows = cur
             else:
                 pos = {i: j for j, i in enumerate(cur_rows)}
-                rows = torch.stack([cur[pos[i]] if i in pos else held[i] for i in admitted])
+                if all(i in pos for i in admitted):
+                    rows = cur.index_select(0, torch.tensor([pos[i] for i in admitted], device=cur.device))
+                else:
+                    rows = torch.stack([cur[pos[i]] if i in pos else held[i] for i in admitted])
                 adm = set(admitted)
                 for i in candidates:
                     if i not in adm and i in pos:

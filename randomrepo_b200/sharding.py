@@ -93,6 +93,55 @@ class StepGather:
         width = 1 + 3 * self.max_rows
         self._send = torch.zeros(width, dtype=torch.int64, device=self.device)
         self._recv = torch.zeros(self.world * width, dtype=torch.int64, device=self.device)
+        self._bufs: list[tuple[torch.Tensor, torch.Tensor]] = []   # per started step (reused after finish)
+        self._pending: list = []
+
+    def _pack(self, send: torch.Tensor, sequence_ids, tokens, logprobs) -> None:
+        ids = torch.as_tensor(sequence_ids, dtype=torch.int64).reshape(-1)
+        tok = torch.as_tensor(tokens, dtype=torch.int64).reshape(-1)
+        lp = torch.as_tensor(logprobs, dtype=torch.float32).reshape(-1)
+        n = ids.numel()
+        if tok.numel() != n or lp.numel() != n:
+            raise ValueError("sequence_ids, tokens and logprobs must have one entry per row")
+        if n > self.max_rows:
+            raise ValueError(f"{n} rows exceed max_rows {self.max_rows}")
+        send.zero_()
+        send[0] = n
+        rows = send[1:1 + 3 * n].view(n, 3)
+        rows[:, 0] = ids.to(self.device)
+        rows[:, 1] = tok.to(self.device)
+        rows[:, 2] = lp.to(self.device).view(torch.int32).to(torch.int64)
+
+    def _unpack(self, recv: torch.Tensor) -> GatheredStep:
+        width = 1 + 3 * self.max_rows
+        recv = recv.view(self.world, width).cpu()
+        counts = [int(c) for c in recv[:, 0].tolist()]
+        parts = [recv[r, 1:1 + 3 * counts[r]].view(counts[r], 3) for r in range(self.world)]
+        allrows = torch.cat(parts) if parts else recv.new_zeros((0, 3))
+        return GatheredStep(sequence_ids=allrows[:, 0].clone(), tokens=allrows[:, 1].clone(),
+                            logprobs=allrows[:, 2].to(torch.int32).view(torch.float32).clone(), counts=counts)
+
+    def start(self, sequence_ids, tokens, logprobs) -> None:
+        """``gather`` without waiting: the collective runs behind the caller's next work (it starts
+        after the work already on the current stream, which does not wait for it); ``finish``
+        returns the steps started so far, in order."""
+        width = 1 + 3 * self.max_rows
+        k = len(self._pending)
+        if k >= len(self._bufs):
+            self._bufs.append((torch.zeros(width, dtype=torch.int64, device=self.device),
+                               torch.zeros(self.world * width, dtype=torch.int64, device=self.device)))
+        send, recv = self._bufs[k]
+        self._pack(send, sequence_ids, tokens, logprobs)
+        work = self.dist.all_gather_into_tensor(recv, send, group=self.group, async_op=True)
+        self._pending.append((work, recv))
+
+    def finish(self) -> list[GatheredStep]:
+        out = []
+        for work, recv in self._pending:
+            work.wait()
+            out.append(self._unpack(recv))
+        self._pending.clear()
+        return out
 
     def gather(self, sequence_ids, tokens, logprobs) -> GatheredStep:
         ids = torch.as_tensor(sequence_ids, dtype=torch.int64).reshape(-1)

@@ -73,6 +73,9 @@ def _gather_worker(rank: int, world: int, port: int, results) -> None:
             got = g.gather(ids, tok, lp)
             out.append((got.counts, got.sequence_ids.tolist(), got.tokens.tolist(),
                         got.logprobs.view(torch.int32).tolist()))
+            g.start(ids, tok, lp)  # the same rows through the non-blocking form
+        for a, b in zip(g.finish(), out):
+            assert (a.counts, a.sequence_ids.tolist(), a.tokens.tolist(), a.logprobs.view(torch.int32).tolist()) == b
         dist.destroy_process_group()
         results[rank] = out
     except Exception:  # noqa: BLE001 - reported to the parent
