@@ -545,13 +545,14 @@ __device__ __forceinline__ void combine_one(const DecodeParams& p, const int4 en
   const float4* src = reinterpret_cast<const float4*>(p.ws_o + (((int64_t)slot0 * HPC + hh) * 8 + gq) * D) + lane;
   const int64_t stride = (int64_t)HPC * 8 * D / 4;  // float4s from one split to the next
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < ns; s0 += 16) {
-    float4 x[16];
+  constexpr int kBatch = PKV_COMBINE_BATCH;  // splits loaded per round
+  for (int s0 = 0; s0 < ns; s0 += kBatch) {
+    float4 x[kBatch];
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
+    for (int k = 0; k < kBatch; ++k)
       x[k] = (active && s0 + k < ns) ? src[(s0 + k) * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
+    for (int k = 0; k < kBatch; ++k) {
       const int sidx = s0 + k;
       const float w = __shfl_sync(0xffffffffu, sidx < 32 ? w0 : w1, sidx & 31);
       if (sidx < ns) {
@@ -578,7 +579,8 @@ __global__ void __launch_bounds__(kCombineThreads) paged_decode_combine_kernel(c
   // still runs, then wait for its partials.
   const DecodeParams p = step_params(launch_p);
   const int pi = blockIdx.y;
-  const int hh = pi >> 3, gq = pi & 7;
+  // blockIdx.y = head of the item's KV-head group x query head of its group
+  const int hh = pi / launch_p.group, gq = pi % launch_p.group;
   const int e0 = blockIdx.x;
   const bool live = gq < p.group && e0 < p.n_combine;
   int4 en = make_int4(0, 0, 0, 0);
@@ -699,7 +701,7 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, cudaStream_t
     // One block per (entry, query head): n_combine is the step's count, or
     // its capacity for a fixed-step launch (whose blocks past the step's
     // count return at once).
-    cfg.gridDim = dim3((unsigned)std::max(1, prm.n_combine), HPC * 8);
+    cfg.gridDim = dim3((unsigned)std::max(1, prm.n_combine), HPC * prm.group);
     cfg.blockDim = dim3(kCombineThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;

@@ -18,6 +18,11 @@
 #ifndef PKV_DECODE_ITEMS_PER_WARP
 #define PKV_DECODE_ITEMS_PER_WARP 3
 #endif
+// Splits of one (sequence, head) the split-K combine loads per round (its
+// registers, hence how many of its blocks stay resident beside the decode CTA).
+#ifndef PKV_COMBINE_BATCH
+#define PKV_COMBINE_BATCH 16
+#endif
 // Launch the decode grid as a programmatic dependent of the kernel before it
 // on the stream (its CTAs get resident during that kernel's last blocks).
 #ifndef PKV_DECODE_PDL
