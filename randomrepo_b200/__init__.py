@@ -14,7 +14,11 @@ Public API (drop-in for ``agentrl.generation.paged_kv``):
   q / k / v a host hands to ``PagedKVCacheStore.decode`` (the host-buffer
   decode path);
 * ``assign_groups`` / ``StepGather`` (``randomrepo_b200.sharding``): GRPO
-  groups per GPU and the per-step gather of sampled tokens and logprobs.
+  groups per GPU and the per-step gather of sampled tokens and logprobs;
+* ``randomrepo_b200.ops``: the kernels as PyTorch operators
+  (``torch.ops.pkv.kv_append`` / ``kv_gather`` / ``copy_blocks`` /
+  ``decode_attention`` / ``prefill_attention``, with fake-tensor shapes),
+  registered when that module is imported.
 
 All device work runs in ``libpkv_b200.so`` (hand-written sm_100a kernels),
 built in-tree by ``python -m randomrepo_b200.build``.  The library is loaded
