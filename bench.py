@@ -719,10 +719,9 @@ def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, ite
     Every rank draws the same 4 x world prompts (Qwen2.5-1.5B architecture, random-init bf16, prompts
     U[64, 256], group 8, 128 new tokens, temperature 1.0), owns the groups ``assign_groups`` gives it
     (balanced by prompt tokens x group size), rolls them out with PagedGenerator (CUDA-graph decode
-    steps, its own KV pool) and, at every decode step, gathers the step's (sequence id, token,
-    log-probability) rows of all ranks with one NCCL all_gather_into_tensor (StepGather); no KV crosses
-    GPUs.  Ranks whose loops ran fewer steps make empty gathers after it, so every rank makes the same
-    collectives.  Timed with CUDA events per rank, max over ranks; tokens are summed over ranks."""
+    steps, its own KV pool) and gathers every decode step's (sequence id, token, log-probability) rows
+    of all ranks, GATHER_EVERY steps per NCCL all_gather_into_tensor (StepGather); no KV crosses GPUs.
+    Ranks whose loops ran fewer steps add empty steps, so every rank makes the same collectives.  Timed with CUDA events per rank, max over ranks; tokens are summed over ranks."""
     import torch.distributed as dist
 
     from randomrepo_b200.hf import PagedGenerator, SamplingConfig, make_store
@@ -740,14 +739,25 @@ def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, ite
     store = make_store(model, total_blocks=4096)
     gen = PagedGenerator(model, store, prefill_chunk_size=512, cuda_graphs=True)
     max_rows = group * max(len(groups_of_rank(assignment, r)) for r in range(world))
-    gather = StepGather(max_rows, device) if world > 1 else None
+    gather = StepGather(max_rows * GATHER_EVERY, device) if world > 1 else None
     host = {"s": 0.0, "rows": 0}
+    pending: list[tuple] = []
+
+    def flush():
+        if pending:
+            ids = torch.cat([torch.tensor(i, dtype=torch.int64) for i, _, _ in pending])
+            gather.start(ids, torch.cat([t for _, t, _ in pending]), torch.cat([lp for _, _, lp in pending]))
+            pending.clear()
 
     def hook(ids, tok, lp):
+        # Every step's rows, gathered GATHER_EVERY steps at a time: one rendezvous of the ranks per
+        # GATHER_EVERY decode steps instead of one per step.
         if gather is None:
             return
         t = time.perf_counter()
-        gather.start(torch.tensor(ids, dtype=torch.int64), tok, lp)
+        pending.append((ids, tok, lp))
+        if len(pending) == GATHER_EVERY:
+            flush()
         host["s"] += time.perf_counter() - t
 
     def rollout(it: int) -> tuple[int, float, float]:
@@ -765,10 +775,11 @@ def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, ite
             dist.all_reduce(steps, op=dist.ReduceOp.MAX)
             empty = torch.zeros(0, dtype=torch.int64)
             for _ in range(int(steps.item()) - r["steps"]):
-                hook([], empty, torch.zeros(0))
+                hook([], empty, torch.zeros(0, device=device))
+            flush()
             t = time.perf_counter()
             rows = gather.finish()
-            host["s"] += time.perf_counter() - t
+            host["wait_s"] = time.perf_counter() - t
             host["rows"] = sum(len(x.tokens) for x in rows)
         e1.record()
         torch.cuda.synchronize(device)
@@ -799,17 +810,21 @@ def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, ite
         "tokens_per_s_per_gpu": tokens / (ms * 1e-3) / world,
         "ms_per_rollout": ms / iters,
         "gather_host_ms_per_rollout": gather_ms / iters,
+        "gather_every_steps": GATHER_EVERY,
         "gathered_rows_per_rollout": host["rows"],
         "group_balance": balance_ratio(lens, group, assignment, world),
-        "path": "per rank: PagedGenerator with CUDA-graph decode steps on its own KV pool; per decode step one "
-                "NCCL all_gather_into_tensor of (sequence id, token, log-probability) rows (StepGather.start: it "
-                "runs behind the next step's work; StepGather.finish collects every step's rows at the end)"
+        "path": "per rank: PagedGenerator with CUDA-graph decode steps on its own KV pool; one "
+                f"NCCL all_gather_into_tensor per {GATHER_EVERY} decode steps of every step's (sequence id, token, "
+                "log-probability) rows (StepGather.start: it runs behind the next steps' work; StepGather.finish "
+                "collects all rows at the end)"
                 if world > 1 else "PagedGenerator with CUDA-graph decode steps (no collective at one GPU)",
         "timing": f"CUDA events around whole rollouts (every gather completed inside), {iters} after one warm-up; "
                   "max over ranks of the time, sum over ranks of the tokens; gather_host_ms = host time in the "
-                  "gather calls (max over ranks)",
+                  "gather calls, the final wait excluded (max over ranks)",
     }
 
+
+GATHER_EVERY = 16  # decode steps whose rows one gather carries
 
 ROLLOUT_7B_SHAPE = {"prompts": 64, "group": 8, "len_lo": 256, "len_hi": 4096, "new_tokens": 1024,
                     "temperature": 1.0, "pool_fraction": 0.6}

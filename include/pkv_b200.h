@@ -244,7 +244,8 @@ int32_t pkv_decode_heads_per_item(int32_t num_kv_heads);
  * up to 32768 tokens.  With items_out == NULL only the counts are returned; else
  * items_out (capacity in quadruples) receives *n_items_out int32 quadruples
  *   {sequence, split << 8 | head_group, splits of the sequence, workspace slot of split 0}
- * (full-size items first, then the rest by decreasing size), followed by
+ * (by decreasing page count: full-size items first, the smallest last, so a
+ * persistent grid's tail holds the shortest items), followed by
  * *n_combine_out quadruples {sequence, head_group, splits, slot of split 0},
  * one per (sequence, head group) cut into several items. */
 int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_heads, int32_t head_dim,

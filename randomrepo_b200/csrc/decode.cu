@@ -669,6 +669,21 @@ int32_t launch_decode(const DecodeParams& prm, const int4* entries, cudaStream_t
   using C = Cfg<D, HPC>;
   static std::atomic<bool> attr_done[kAttrDevices];
   if (int32_t st = ensure_smem_attr(paged_decode_kernel<D, HPC, T>, C::kSmemBytes, attr_done)) return st;
+#if PKV_CARVEOUT_MAX
+  {
+    // Both kernels of a step prefer the largest shared-memory carveout, so an
+    // SM that runs the combine between two decode grids keeps its split.
+    static std::atomic<bool> carve_done[kAttrDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kAttrDevices && !carve_done[dev].load()) {
+      cudaFuncSetAttribute(paged_decode_kernel<D, HPC, T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+      cudaFuncSetAttribute(paged_decode_combine_kernel<D, HPC, T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+      carve_done[dev].store(true);
+    }
+  }
+#endif
   // A fixed-step launch does not know its item count on the host: it always
   // runs the persistent grid (idle warps fetch an out-of-range item and
   // leave) and the combine kernel.
@@ -789,13 +804,11 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
     pkv_set_error("pkv_decode_plan: item buffer too small");
     return PKV_ERR_ARG;
   }
-  // Order: sequences by decreasing length, each sequence's items together
-  // (head group, then split).  The items of one sequence are taken by several
-  // warps at about the same time, so its split-K partials are complete early
-  // and the shortest sequences (one or two small items) come last and even
-  // out the tail.  Sequences ordered by (pages descending, index ascending):
-  // a counting sort over the page counts (max_pages buckets) for large
-  // batches, a comparison sort of packed keys for small ones.
+  // Sequences ordered by (pages descending, index ascending): a counting
+  // sort over the page counts (max_pages buckets) for large batches, a
+  // comparison sort of packed keys for small ones.  With PKV_DECODE_ORDER 1
+  // the items are then placed by decreasing page count (below), else each
+  // sequence's items stay together (head group, then split).
   thread_local std::vector<int32_t> order;
   thread_local std::vector<int32_t> slot_of;
   thread_local std::vector<int32_t> bucket;
@@ -831,6 +844,41 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
     for (int b = 0; b < batch; ++b) order[b] = (int32_t)(keys[b] & 0xffffffff);
   }
   int32_t* o = items_out;
+#if PKV_DECODE_ORDER == 1
+  // Items by decreasing page count: every full-size item (pps pages) first,
+  // in the sequence order above, then the remainders from the largest to the
+  // smallest, so the grid's tail holds the shortest items.  One pass: each
+  // item is written straight to its place among the items of its size.
+  {
+    int64_t start[kMaxPagesPerItem + 2] = {};
+    for (int32_t b : order) {
+      const int32_t pages = (seq_lens[b] + 15) / 16;
+      start[pps] += (int64_t)groups * (pages / pps);
+      if (pages % pps) start[pages % pps] += groups;
+    }
+    int64_t at = 0;
+    for (int32_t pg = pps; pg >= 1; --pg) {
+      const int64_t c = start[pg];
+      start[pg] = at;
+      at += c;
+    }
+    for (int32_t b : order) {
+      const int32_t pages = (seq_lens[b] + 15) / 16;
+      const int32_t ns = (pages + pps - 1) / pps;
+      const int32_t full = pages / pps;
+      for (int hg = 0; hg < groups; ++hg) {
+        for (int sp = 0; sp < ns; ++sp) {
+          int32_t* q = items_out + 4 * start[sp < full ? pps : pages % pps]++;
+          q[0] = b;
+          q[1] = (sp << 8) | hg;
+          q[2] = ns;
+          q[3] = slot_of[b] + hg * ns;
+        }
+      }
+    }
+    o += 4 * n;
+  }
+#else
   for (int32_t b : order) {
     const int32_t pages = (seq_lens[b] + 15) / 16;
     const int32_t ns = (pages + pps - 1) / pps;
@@ -844,6 +892,7 @@ int32_t pkv_decode_plan(const int32_t* seq_lens, int32_t batch, int32_t num_kv_h
       }
     }
   }
+#endif
   // Combine entries {sequence, head_group, nsplits, slot of split 0}.
   int32_t slot = 0;
   for (int b = 0; b < batch; ++b) {

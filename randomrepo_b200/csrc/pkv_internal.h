@@ -23,6 +23,17 @@
 #ifndef PKV_COMBINE_BATCH
 #define PKV_COMBINE_BATCH 16
 #endif
+// Work-item order of the decode plan: 1 = items by decreasing page count
+// (the grid's tail holds the smallest items: 54.8-55.8 vs 55.9-57.1 us per
+// microbench launch); 0 = sequences by decreasing length, each sequence's
+// items together.
+#ifndef PKV_DECODE_ORDER
+#define PKV_DECODE_ORDER 1
+#endif
+// Prefer the largest shared-memory carveout for the decode and combine kernels.
+#ifndef PKV_CARVEOUT_MAX
+#define PKV_CARVEOUT_MAX 0
+#endif
 // Launch the decode grid as a programmatic dependent of the kernel before it
 // on the stream (its CTAs get resident during that kernel's last blocks).
 #ifndef PKV_DECODE_PDL

@@ -44,11 +44,14 @@ def test_plan_covers_every_page_once(hkv, seed):
     for b in range(n):
         for hg in range(groups):
             assert sum(v for (bb, gg, _), v in seen.items() if bb == b and gg == hg) == pages[b]
-    # sequences by decreasing length, each sequence's items contiguous and in split order
-    order = [b for b, _, _, _ in items.tolist()]
-    firsts = [order[i] for i in range(len(order)) if i == 0 or order[i] != order[i - 1]]
-    assert len(firsts) == n and sorted(firsts) == list(range(n))
-    assert [int(pages[b]) for b in firsts] == sorted(pages.tolist(), reverse=True)
+    # items by decreasing page count (the grid's tail holds the smallest); the full-size items follow
+    # their sequences' decreasing length
+    sizes = [min(pps, int(pages[b]) - (y >> 8) * pps) for b, y, _, _ in items.tolist()]
+    assert all(a >= c for a, c in zip(sizes, sizes[1:]))
+    full = [b for (b, _, _, _), sz in zip(items.tolist(), sizes) if sz == pps]
+    firsts = [full[i] for i in range(len(full)) if i == 0 or full[i] != full[i - 1]]
+    assert len(set(firsts)) == len(firsts)
+    assert [int(pages[b]) for b in firsts] == sorted((int(pages[b]) for b in firsts), reverse=True)
     # one combine entry per (sequence, head group) cut into several items, naming its slots
     want = {(b, hg) for (b, hg, s) in seen if -(-pages[b] // pps) > 1}
     got = set()
