@@ -150,12 +150,15 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period_s: float = 0.001) -> None:
+    def __init__(self, index: int, period_s: float = 0.001, enabled: bool = True) -> None:
         self.samples: list[tuple[float, int, int]] = []
         self.windows: list[list[float]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
+        self._nvml = None
+        if not enabled:
+            return
         try:
             import pynvml
 
@@ -280,7 +283,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     # that nothing leaves the GPU idle (and its clocks falling) between the
     # warm-up and a timed region: each region follows its warm-up steps
     # through one barrier only.
-    clocks = ClockSampler(device.index or 0)
+    # Rank 0 samples its GPU's clocks (it prints the line); the other ranks keep NVML off their hosts' CPUs.
+    clocks = ClockSampler(device.index or 0, enabled=rank == 0)
     n_timed = args.steps // TIMING_EVERY + 1
     pool.time_launches(n_timed, TIMING_EVERY)
     pool.time_launches(0)
