@@ -651,7 +651,14 @@ int32_t pkv_allocator_drain_updates(pkv_allocator* a, int32_t* out, int64_t capa
     *p++ = c.first;
     *p++ = c.second;
   }
-  a->dirty_table.clear();
+  // clear() walks the whole bucket array, which keeps the size of the
+  // largest batch of edits ever pending (tens of thousands after a bulk
+  // placement): skip it when nothing is pending, and give the buckets back
+  // after a large drain, so that a decode step's drain stays O(its updates).
+  if (!a->dirty_table.empty()) {
+    a->dirty_table.clear();
+    if (a->dirty_table.bucket_count() > 4096) a->dirty_table.rehash(0);
+  }
   a->ref_dirty_list.clear();
   a->len_dirty_list.clear();
   a->copies.clear();
