@@ -906,7 +906,8 @@ def run_rollout_7b(device: torch.device, seed: int) -> dict:
         "unpressured_decode_loop_iterations": r2["steps"],
         "path": "PagedGenerator: packed chunked prefill (512), one prefill per group + copy-on-write forks, CUDA-graph "
                 "decode steps (eager when a full pool could not take a graph's padding), growth admission with soft "
-                "preemption, eviction + re-prefill when more than a quarter of the batch would wait, device sampling",
+                "preemption, eviction when more than a quarter of the batch would wait, evicted group members re-prefilled "
+                "together (prompt once + forks + their own tokens), device sampling",
         "timing": "CUDA events around one whole rollout after a 32-token warm-up rollout of 8 groups (each pool)",
         "gpu_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
     }

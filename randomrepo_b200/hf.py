@@ -1035,25 +1035,67 @@ class PagedGenerator:
 
     def _restore_evicted(self, evicted: list[int], held: dict, prompts, group_size: int, seq_ids: list[int],
                          tokens: list, kv: dict, resident: int) -> None:
-        """Re-prefill evicted sequences (oldest first) while the free blocks cover their tokens plus one
-        block of growth for every resident sequence; their next-token logits join the held rows."""
+        """Re-prefill evicted sequences, oldest first, while the free blocks cover them plus one block of
+        growth for every resident sequence.  The evicted members of one GRPO group come back together:
+        their prompt is prefilled once and forked (copy-on-write, as at the start of the rollout), then
+        each member is extended by its own tokens; their next-token logits join the held rows."""
         bs = self._block_size()
-        back, rows = [], []
         free = int(self.store.free_block_count)
-        while evicted:
-            i = evicted[0]
-            toks = torch.cat([torch.as_tensor(prompts[i // group_size], dtype=torch.long).reshape(-1),
-                              torch.tensor(tokens[i], dtype=torch.long)])
-            need = -(-toks.numel() // bs) + 1
-            if free < need + resident + len(back):
+        groups: dict[int, list[int]] = {}
+        for i in evicted:
+            groups.setdefault(i // group_size, []).append(i)
+        plan, taken = [], 0
+        for g, members in groups.items():
+            plen = int(torch.as_tensor(prompts[g]).numel())
+            need = -(-plen // bs)
+            take = []
+            for i in members:
+                extra = -(-(plen + len(tokens[i])) // bs) - plen // bs + 1
+                if free < need + extra + resident + taken + len(take) + 1:
+                    break
+                take.append(i)
+                need += extra
+            if not take:
                 break
-            evicted.pop(0)
+            plan.append((g, take))
             free -= need
-            back.append(i)
-            rows.append(toks)
-        if not back:
+            taken += len(take)
+            if len(take) < len(members):
+                break
+        if not plan:
             return
-        logits = self.prefill([seq_ids[i] for i in back], rows)
-        for j, i in enumerate(back):
-            held[i] = logits[j]
-            kv["paged_kv_recomputed_tokens"] += float(rows[j].numel())
+        done = {i for _, take in plan for i in take}
+        evicted[:] = [i for i in evicted if i not in done]
+        prompt_logits = self.prefill([seq_ids[take[0]] for _, take in plan], [prompts[g] for g, _ in plan])
+        kv["paged_kv_recomputed_tokens"] += float(sum(int(torch.as_tensor(prompts[g]).numel()) for g, _ in plan))
+        members, chunks = [], []
+        for j, (g, take) in enumerate(plan):
+            for i in take:
+                if i != take[0]:
+                    self.store.fork(seq_ids[take[0]], seq_ids[i])
+                if tokens[i]:
+                    members.append(i)
+                    chunks.append(torch.tensor(tokens[i], dtype=torch.long))
+                else:
+                    held[i] = prompt_logits[j]
+        if members:
+            logits = self._extend_chunked([seq_ids[i] for i in members], chunks)
+            for j, i in enumerate(members):
+                held[i] = logits[j]
+                kv["paged_kv_recomputed_tokens"] += float(chunks[j].numel())
+
+    def _extend_chunked(self, sequence_ids, chunks) -> torch.Tensor:
+        """``extend`` in rounds of at most ``prefill_chunk_size`` tokens per sequence: logits of each
+        chunk's last token [n, vocab]."""
+        cs = self.prefill_chunk_size
+        last = [None] * len(chunks)
+        rounds = max((c.numel() + cs - 1) // cs for c in chunks)
+        for r in range(rounds):
+            sub = [j for j, c in enumerate(chunks) if c.numel() > r * cs]
+            h, q_lens = self.extend_hidden([sequence_ids[j] for j in sub],
+                                           [chunks[j][r * cs:(r + 1) * cs] for j in sub])
+            ends = np.cumsum(q_lens) - 1
+            for k, j in enumerate(sub):
+                if (r + 1) * cs >= chunks[j].numel():
+                    last[j] = h[int(ends[k])]
+        return self.logits(torch.stack(last))
