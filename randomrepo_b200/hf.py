@@ -78,8 +78,9 @@ def _paged_rows(ph: _Phase, layer: int, q, k, v, b: int, t: int, scaling):
         if t != 1:
             raise ValueError("a decode step feeds one token per sequence")
         return ph.store.decode_attention(ph.step, layer, q, k, v, scale=scaling)
-    if b != 1:
-        raise ValueError("prefill runs packed: batch 1, the chunks of all sequences along the token axis")
+    if b != 1 and (ph.q_lens is None or len(ph.q_lens) != b or any(int(n) != t for n in ph.q_lens)):
+        raise ValueError("prefill runs packed (batch 1, the chunks of all sequences along the token axis) or as a "
+                         "batch of equal chunks, one per sequence")
     if ph.step is None and hasattr(ph.store, "prefill_step"):
         ph.step = ph.store.prefill_step(ph.sequence_ids, ph.q_lens, hq)
     return ph.store.prefill_attention(ph.sequence_ids, q, k, v, q_lens=ph.q_lens, layer=layer, scale=scaling,
@@ -90,7 +91,15 @@ def paged_attention_forward(module, query, key, value, attention_mask=None, scal
     """HF attention-interface entry: q [B, Hq, T, D], k/v [B, Hkv, T, D] -> ([B, T, Hq, D], None)."""
     ph = getattr(_local, "phase", None)
     if ph is None:
-        raise RuntimeError("paged_b200 attention ran outside a PagedGenerator forward")
+        # A forward of an HF model over a PagedCache(kernels=True): set up by the cache at layer 0,
+        # valid for that forward's layers only.
+        ph = getattr(_local, "cache_phase", None)
+        if ph is not None:
+            _local.cache_layers_left -= 1
+            if _local.cache_layers_left <= 0:
+                _local.cache_phase = None
+    if ph is None:
+        raise RuntimeError("paged_b200 attention ran outside a PagedGenerator forward or a PagedCache(kernels=True)")
     b, hq, t, d = query.shape
     hkv = key.shape[1]
     out = _paged_rows(ph, int(module.layer_idx), query.transpose(1, 2).reshape(b * t, hq, d).contiguous(),
@@ -1099,3 +1108,130 @@ class PagedGenerator:
                 if (r + 1) * cs >= chunks[j].numel():
                     last[j] = h[int(ends[k])]
         return self.logits(torch.stack(last))
+
+
+def _paged_cache_classes():
+    """The HF ``Cache`` subclass (built on first use, so that importing this module needs no transformers)."""
+    from transformers.cache_utils import Cache, CacheLayerMixin
+
+    class PagedCacheLayer(CacheLayerMixin):
+        """One decoder layer's view of a ``PagedCache``: its K/V live in the store's pages."""
+
+        is_sliding = False
+        is_compileable = False
+
+        def __init__(self, cache, layer_idx: int) -> None:
+            super().__init__()
+            self._cache = cache
+            self.layer_idx = layer_idx
+            self.is_initialized = True
+
+        def lazy_initialization(self, key_states, value_states) -> None:
+            return None
+
+        def update(self, key_states, value_states, *args, **kwargs):
+            return self._cache._update(key_states, value_states, self.layer_idx)
+
+        def get_mask_sizes(self, query_length: int) -> tuple[int, int]:
+            return self._cache._cached + query_length, 0
+
+        def get_seq_length(self) -> int:
+            return self._cache._cached
+
+        def get_max_cache_shape(self) -> int:
+            return -1
+
+    class PagedCache(Cache):
+        """An HF ``Cache`` whose K/V live in a ``PagedKVCacheStore``'s pages: batch row b is the store's
+        sequence ``sequence_ids[b]`` (reserved beforehand, possibly with cached tokens).
+
+        ``update`` -- HF's per-layer cache call (transformers cache_utils.py:102-120, called at
+        modeling_qwen2.py:225) -- appends the step's tokens to every sequence (allocator, once per
+        forward, at layer 0), writes the layer's new K/V into their pages (scatter kernel) and returns
+        the layer's whole K/V [B, Hkv, T, D] gathered from the pages (gather kernel), so the model's
+        own attention runs unchanged over exactly the values a ``DynamicCache`` would hold.  The
+        batch's sequences must hold equal token counts (as a ``DynamicCache`` batch does: padding is
+        in the attention mask).
+
+        With ``kernels=True`` (the model switched to the ``paged_b200`` attention by
+        ``use_paged_attention``) nothing is gathered: at layer 0 of each forward the cache lays out a
+        decode step (one token per sequence) or a prefill of the batch's equal chunks, ``update``
+        returns the fresh K/V, and the attention appends and attends through the store's kernels
+        (fused append + paged decode, or the chunked-prefill kernel), for that forward's layers.
+        """
+
+        def __init__(self, store, sequence_ids, num_layers: int, kernels: bool = False) -> None:
+            self.store = store
+            self.kernels = bool(kernels)
+            self.ids = np.ascontiguousarray(np.asarray(sequence_ids, dtype=np.int64).reshape(-1))
+            counts = store.token_counts(self.ids) if self.ids.size else np.zeros(0, dtype=np.int64)
+            if counts.size and (counts != counts[0]).any():
+                raise ValueError("the sequences of a PagedCache batch must hold equal token counts")
+            self._cached = int(counts[0]) if counts.size else 0
+            self._num_layers = int(num_layers)
+            self._new_slots = None
+            self._all_slots = None
+            super().__init__(layers=[PagedCacheLayer(self, i) for i in range(self._num_layers)])
+
+        def _update(self, key_states, value_states, layer_idx: int):
+            b, hkv, t, d = key_states.shape
+            if b != self.ids.size:
+                raise ValueError(f"batch of {b} rows for a PagedCache of {self.ids.size} sequences")
+            store = self.store
+            if self.kernels:
+                # The model's paged_b200 attention appends and attends through the store's kernels.
+                if layer_idx == 0:
+                    store._ensure_pool(self._num_layers, hkv, d, key_states.dtype, key_states.device)
+                    if t == 1:
+                        ph = _Phase("decode", store, step=store.decode_step(self.ids))
+                    else:
+                        store.append_many(self.ids, np.full(self.ids.size, t, dtype=np.int64))
+                        ph = _Phase("prefill", store, sequence_ids=self.ids.tolist(),
+                                    q_lens=np.full(self.ids.size, t, dtype=np.int64))
+                    self._cached += t
+                    _local.cache_phase = ph
+                    _local.cache_layers_left = self._num_layers
+                return key_states, value_states
+            if layer_idx == 0:
+                pool = store._ensure_pool(self._num_layers, hkv, d, key_states.dtype, key_states.device)
+                store.append_many(self.ids, np.full(self.ids.size, t, dtype=np.int64))
+                self._cached += t
+                # Slots of the new tokens (their blocks' fills recorded) and of every token.
+                step = store.prefill_step(self.ids, np.full(self.ids.size, t, dtype=np.int64), hkv)
+                self._new_slots = step.slots
+                bs = pool.block_size
+                tok = np.arange(self._cached, dtype=np.int64)
+                rows = []
+                for sid in self.ids.tolist():
+                    blocks = np.asarray(store.allocator.view(sid).physical_blocks, dtype=np.int64)
+                    rows.append(blocks[tok // bs] * bs + tok % bs)
+                self._all_slots = torch.from_numpy(np.concatenate(rows)).to(pool.device)
+            pool = store.pool
+            k_new = key_states.permute(1, 0, 2, 3).reshape(hkv, b * t, d).contiguous()
+            v_new = value_states.permute(1, 0, 2, 3).reshape(hkv, b * t, d).contiguous()
+            pool.scatter(layer_idx, k_new.unsqueeze(0), v_new.unsqueeze(0), self._new_slots)
+            n = self._cached
+            keys = torch.empty((1, hkv, b * n, d), dtype=pool.dtype, device=pool.device)
+            values = torch.empty_like(keys)
+            pool.gather(layer_idx, keys, values, self._all_slots)
+            return (keys[0].view(hkv, b, n, d).permute(1, 0, 2, 3),
+                    values[0].view(hkv, b, n, d).permute(1, 0, 2, 3))
+
+        def get_seq_length(self, layer_idx: int = 0) -> int:
+            return self._cached
+
+        def get_mask_sizes(self, query_length: int, layer_idx: int = 0) -> tuple[int, int]:
+            return self._cached + query_length, 0
+
+    return PagedCache
+
+
+def PagedCache(store, sequence_ids, num_layers: int, kernels: bool = False):  # noqa: N802 - builds that class
+    """An HF ``Cache`` over ``store``'s pages for the sequences ``sequence_ids`` (see the class docstring)."""
+    global _PAGED_CACHE_CLASS
+    if _PAGED_CACHE_CLASS is None:
+        _PAGED_CACHE_CLASS = _paged_cache_classes()
+    return _PAGED_CACHE_CLASS(store, sequence_ids, num_layers, kernels)
+
+
+_PAGED_CACHE_CLASS = None

@@ -350,3 +350,87 @@ def test_rollout_under_kv_pressure_matches_the_unpressured_run(cuda_device, cuda
     np.testing.assert_allclose(np.concatenate(got["logprobs"]), np.concatenate(want["logprobs"]), atol=0.05)
     assert store.pool.decode_error_flag() == 0 and store.pool.prefill_error_flag() == 0
     assert store.allocator.used_block_count == 0
+
+
+def test_hf_generate_with_a_paged_cache_equals_a_dynamic_cache(cuda_device):
+    """HF's own ``generate`` (unchanged model code, SDPA attention) with its K/V in the store's pages
+    through ``PagedCache`` gives the same greedy tokens as with HF's ``DynamicCache``, and the pages then
+    hold bit for bit the K/V the DynamicCache holds."""
+    from randomrepo_b200.hf import PagedCache, make_store
+
+    model = _model(cuda_device, 64, 2)
+    gen = torch.Generator().manual_seed(41)
+    ids = torch.randint(0, 512, (3, 21), generator=gen).to(cuda_device)
+    mask = torch.ones_like(ids)
+    with torch.inference_mode():
+        want = model.generate(ids, attention_mask=mask, max_new_tokens=24, do_sample=False, pad_token_id=0,
+                              return_dict_in_generate=True)
+        store = make_store(model, total_blocks=256)
+        sids = [100, 101, 102]
+        for s in sids:
+            store.reserve(s, 0)
+        cache = PagedCache(store, sids, num_layers=model.config.num_hidden_layers)
+        got = model.generate(ids, attention_mask=mask, past_key_values=cache, max_new_tokens=24, do_sample=False,
+                             pad_token_id=0, return_dict_in_generate=True)
+    assert torch.equal(got.sequences, want.sequences)
+    dyn = want.past_key_values
+    n = cache.get_seq_length()
+    assert n == dyn.get_seq_length() == ids.shape[1] + 24 - 1
+    for b, s in enumerate(sids):
+        pages = store.read_sequence_legacy_cache(s)
+        for layer in range(model.config.num_hidden_layers):
+            assert torch.equal(pages[layer][0][0], dyn.layers[layer].keys[b])
+            assert torch.equal(pages[layer][1][0], dyn.layers[layer].values[b])
+
+
+def test_paged_cache_with_the_paged_kernels_matches_a_dynamic_cache(cuda_device):
+    """The same model switched to the ``paged_b200`` attention, its HF forwards over a
+    ``PagedCache(kernels=True)``: a batched prefill forward and then decode forwards run on the store's
+    kernels (chunked-prefill kernel, fused append + paged decode) and give the logits of the same
+    forwards over a ``DynamicCache`` with SDPA within bf16 (greedy choices equal where not near-ties),
+    and HF ``generate`` runs on them end to end."""
+    from transformers import DynamicCache
+
+    from randomrepo_b200.hf import PagedCache, make_store, use_paged_attention
+
+    ref = _model(cuda_device, 128, 2, 12, 2)
+    ours = copy.deepcopy(ref)
+    use_paged_attention(ours)
+    gen = torch.Generator().manual_seed(43)
+    ids = torch.randint(0, 512, (4, 37), generator=gen).to(cuda_device)
+    store = make_store(ours, total_blocks=256)
+    sids = [7, 8, 9, 10]
+    for s in sids:
+        store.reserve(s, 0)
+    cache = PagedCache(store, sids, num_layers=2, kernels=True)
+    dyn = DynamicCache(config=ref.config)
+    agree, total = 0, 0
+    with torch.inference_mode():
+        x = ids
+        for _ in range(6):
+            a = ref(input_ids=x, past_key_values=dyn, use_cache=True).logits[:, -1].float()
+            b = ours(input_ids=x, past_key_values=cache, use_cache=True).logits[:, -1].float()
+            np.testing.assert_allclose(b.cpu().numpy(), a.cpu().numpy(), atol=0.05, rtol=0.02)
+            top2 = a.topk(2, dim=-1).values
+            decidable = (top2[:, 0] - top2[:, 1]) > 0.02
+            agree += int(((a.argmax(-1) == b.argmax(-1)) | ~decidable).sum())
+            total += a.shape[0]
+            x = a.argmax(-1, keepdim=True)
+    assert agree == total
+    assert cache.get_seq_length() == dyn.get_seq_length() == 37 + 5
+    assert store.pool.decode_error_flag() == 0 and store.pool.prefill_error_flag() == 0
+    # HF generate end to end on the kernels (free-running, so after a bf16 near-tie the continuations may
+    # differ: the per-forward logits above are the numerical check; here the run, its first choices and
+    # its cache length).
+    store2 = make_store(ours, total_blocks=256)
+    for s in sids:
+        store2.reserve(s, 0)
+    cache2 = PagedCache(store2, sids, 2, kernels=True)
+    with torch.inference_mode():
+        out = ours.generate(ids, attention_mask=torch.ones_like(ids), max_new_tokens=16, do_sample=False,
+                            pad_token_id=0, past_key_values=cache2)
+        want = ref.generate(ids, attention_mask=torch.ones_like(ids), max_new_tokens=16, do_sample=False,
+                            pad_token_id=0)
+    assert out.shape == want.shape and torch.equal(out[:, :38], want[:, :38])
+    assert cache2.get_seq_length() == 37 + 15
+    assert store2.pool.decode_error_flag() == 0 and store2.pool.prefill_error_flag() == 0
