@@ -777,7 +777,7 @@ def run_grpo_rollout(device: torch.device, seed: int, rank: int, world: int, ite
         if gather is not None:
             steps = torch.tensor([r["steps"]], device=device)
             dist.all_reduce(steps, op=dist.ReduceOp.MAX)
-            empty = torch.zeros(0, dtype=torch.int64)
+            empty = torch.zeros(0, dtype=torch.int64, device=device)
             for _ in range(int(steps.item()) - r["steps"]):
                 hook([], empty, torch.zeros(0, device=device))
             flush()
