@@ -1223,15 +1223,19 @@ def _paged_cache_classes():
         def get_mask_sizes(self, query_length: int, layer_idx: int = 0) -> tuple[int, int]:
             return self._cached + query_length, 0
 
+    PagedCache.__qualname__, PagedCacheLayer.__qualname__ = "PagedCache", "PagedCacheLayer"
     return PagedCache
 
 
-def PagedCache(store, sequence_ids, num_layers: int, kernels: bool = False):  # noqa: N802 - builds that class
-    """An HF ``Cache`` over ``store``'s pages for the sequences ``sequence_ids`` (see the class docstring)."""
-    global _PAGED_CACHE_CLASS
-    if _PAGED_CACHE_CLASS is None:
-        _PAGED_CACHE_CLASS = _paged_cache_classes()
-    return _PAGED_CACHE_CLASS(store, sequence_ids, num_layers, kernels)
-
-
 _PAGED_CACHE_CLASS = None
+
+
+def __getattr__(name: str):
+    # ``PagedCache`` is a transformers ``Cache`` subclass, defined on first use so that importing
+    # this module does not import transformers.
+    global _PAGED_CACHE_CLASS
+    if name == "PagedCache":
+        if _PAGED_CACHE_CLASS is None:
+            _PAGED_CACHE_CLASS = _paged_cache_classes()
+        return _PAGED_CACHE_CLASS
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -294,3 +294,15 @@ def test_rollout_under_kv_pressure_defers_evicts_and_keeps_the_tokens():
     for a, b in zip(got["logprobs"], want["logprobs"]):
         np.testing.assert_allclose(a, b, atol=1e-4)
     assert store.refs == {}  # every block returned
+
+
+def test_paged_cache_is_a_transformers_cache_class():
+    """``PagedCache`` (defined on first use) is a ``transformers`` ``Cache`` subclass, so HF's loops
+    and ``isinstance`` checks accept it; its behaviour runs on the GPU (tests/test_gpu_hf.py)."""
+    from transformers.cache_utils import Cache
+
+    import randomrepo_b200.hf as hf
+    from randomrepo_b200.hf import PagedCache
+
+    assert isinstance(PagedCache, type) and issubclass(PagedCache, Cache)
+    assert hf.PagedCache is PagedCache and PagedCache.__qualname__ == "PagedCache"
