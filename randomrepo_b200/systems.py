@@ -333,12 +333,22 @@ def run_mode(mode: str, model, prompts, *, group: int, new_tokens: int, steps: i
             decode_tokens = sum(len(t) for t in tokens)
             shared, used = timings.get("shared_blocks_after_prefill", (0, 0))
             pre_ms, dec_ms = timings.get("prefill_ms", 0.0), timings.get("decode_ms", gen_ms)
+            kvp = res.get("kv_pressure", {})
+            preempted = float(kvp.get("paged_kv_preempted_sequences", 0.0))
+            # The runtime controller's rule (agentrl/runtime/controller.py:175-181): a full pool
+            # that preempted sequences makes the step paged-KV bound.
+            if pressure >= 0.9 and preempted > 0:
+                bottleneck = "paged_kv"
+            else:
+                bottleneck = "prefill" if pre_ms > dec_ms else "decode"
             row.update(padding_ratio=0.0, generation_padding_ratio=0.0, sequence_padding_ratio=0.0,
                        prefill_tokens_per_second=prompt_tokens / max(pre_ms, 1e-6) * 1e3 if pre_ms else 0.0,
                        decode_tokens_per_second=decode_tokens / max(dec_ms, 1e-6) * 1e3,
                        cache_reuse_effectiveness=shared / used if used else 0.0,
                        paged_kv_allocator_pressure=pressure,
-                       dominant_runtime_bottleneck="prefill" if pre_ms > dec_ms else "decode")
+                       paged_kv_preempted_sequences=preempted,
+                       paged_kv_max_preempted_sequences=float(kvp.get("paged_kv_max_preempted_sequences", 0.0)),
+                       dominant_runtime_bottleneck=bottleneck)
             if spec is not None:
                 row["speculative_acceptance_rate"] = res["accepted"] / max(res["proposed"], 1)
         total_ms = clock.ms(0, 2)
