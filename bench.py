@@ -509,11 +509,12 @@ VERIFY_SHAPE = {"model": "Qwen2.5-1.5B target attention", "hq": 12, "hkv": 2, "d
                 "prefix_hi": 1280, "k": 4}
 
 
-def _tile_workload(device: torch.device, hq: int, hkv: int, d: int, seqs, seed: int):
+def _tile_workload(device: torch.device, hq: int, hkv: int, d: int, seqs, seed: int, verify: bool = False):
     """A store whose sequences hold ``total`` tokens of seeded N(0,1) K/V and the planned
-    prefill items for the chunks ``(past, q_len)`` of each sequence; q is seeded N(0,1)."""
+    items for the chunks ``(past, q_len)`` of each sequence (``verify``: for pkv_verify_attention,
+    as ``prefill_step`` plans short chunks; else for pkv_prefill_attention); q is seeded N(0,1)."""
     from randomrepo_b200 import PagedKVAllocator, PagedKVCacheStore
-    from randomrepo_b200.device import plan_prefill
+    from randomrepo_b200.device import plan_prefill, plan_verify
 
     total = sum(n for n, _ in seqs)
     store = PagedKVCacheStore(PagedKVAllocator(total // BS + len(seqs) + 64, BS), num_layers=1, num_kv_heads=hkv,
@@ -527,7 +528,8 @@ def _tile_workload(device: torch.device, hq: int, hkv: int, d: int, seqs, seed: 
             past.append(p0)
             qls.append(ql)
     store._sync()
-    plan = plan_prefill(np.array(rows), np.array(past), np.array(qls), hq, hkv, store.pool.num_sms)
+    planner = plan_verify if verify else plan_prefill
+    plan = planner(np.array(rows), np.array(past), np.array(qls), hq, hkv, store.pool.num_sms)
     q = torch.randn((sum(qls), hq, d), device=device,
                     generator=torch.Generator(device=device).manual_seed(seed + 1)).to(torch.bfloat16)
     pos_sum = sum(int((np.arange(p0, p0 + ql, dtype=np.int64) + 1).sum()) for p0, ql in zip(past, qls))
@@ -601,7 +603,12 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
     vs = VERIFY_SHAPE
     pre = rng.integers(vs["prefix_lo"], vs["prefix_hi"] + 1, size=vs["seqs"])
     seqs = [(int(p) + vs["k"], [(int(p) - 1, vs["k"] + 1)]) for p in pre]
+    # The same launch on the 128-query-row prefill kernel, for comparison.
     store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2)
+    ms_rows, _ = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
+    del store, q, records
+    store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2,
+                                                              verify=True)
     ms, launches = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
     achieved = kv_bytes / (ms * 1e-3) / 1e9
     res["verify"] = {
@@ -614,6 +621,8 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
                      "peak_source": f"{hbm_kind} hbm_gbs", "traffic": tiles_traffic("verify"), "bytes_per_launch": kv_bytes,
                      "bytes_rule": "K and V of prefix + k tokens per sequence and KV head"},
         "tflops": flops / (ms * 1e-3) / 1e12,
+        "kernel": "pkv_verify_attention (keys on the tensor-core rows) + combine",
+        "prefill_kernel_ms": ms_rows,
     }
     del store, q, records
     torch.cuda.empty_cache()

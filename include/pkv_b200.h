@@ -377,6 +377,52 @@ int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* pool, int32_t 
                               int32_t num_q_heads, float scale, void* out, int32_t* error_word, void* workspace,
                               int64_t workspace_bytes, int64_t n_slots, void* stream);
 
+/* Positions of a chunk one verify work item covers: 32 / G query columns of
+ * one KV head (G = num_q_heads / num_kv_heads); 0 when G > 32 or the head
+ * counts are invalid. */
+int32_t pkv_verify_positions_per_item(int32_t num_q_heads, int32_t num_kv_heads);
+
+/* Plan a pkv_verify_attention launch (host); arguments as for
+ * pkv_prefill_plan.  A sequence's chunk is cut into items of
+ * pkv_verify_positions_per_item positions, one per KV head.  With num_sms > 0
+ * the launch is a persistent grid of *n_ctas_out = min(num_sms, items) CTAs,
+ * one per SM, each working through a list of items: items longer than half
+ * an SM's share of the KV tiles (of 128 keys) are cut into key ranges of at
+ * least two tiles, each writing a partial into one of *n_slots_out workspace
+ * slots that a combine entry merges, and the items go longest first to the
+ * CTA with the fewest tiles so far.  num_sms = 0 gives one CTA per item and no
+ * combine entries (a fixed record count, as a recorded CUDA graph needs).
+ * Records: int32 [n_items + n_combine][8]; record c < n_ctas is CTA c's first
+ * item, whose last field is (f << 8) | m: the CTA's other m <= 127 items are
+ * records f .. f+m-1 (more CTAs than num_sms only beyond 128 items per SM);
+ * then the combine entries {first slot, slots, query index, kv_head << 16 |
+ * positions}.  An item record is {table row, first position, query index,
+ * kv_head << 16 | positions, first KV tile | (end KV tile << 16) (0: all),
+ * combine entry (-1: none), partial slot (-1: none), list}. */
+int32_t pkv_verify_plan(const int32_t* rows, const int32_t* past_lens, const int32_t* q_lens, int32_t n_seqs,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t num_sms, int32_t* work_items_out,
+                        int64_t items_capacity, int64_t* n_items_out, int64_t* n_ctas_out, int64_t* n_combine_out,
+                        int64_t* n_slots_out);
+
+/* The speculative-verify read (short chunks after long cached prefixes), one
+ * layer: the same result as pkv_prefill_attention, from a kernel that puts the
+ * 128 keys of a KV tile on the tensor-core rows and the <= 32 (position,
+ * head) query columns of an item on N, so that short chunks do not leave a
+ * 128-row query tile mostly empty, and streams each CTA's items through one
+ * pipeline.  Arguments as for pkv_prefill_attention with pkv_verify_plan's
+ * records and n_ctas; workspace pkv_prefill_workspace_bytes(n_slots, 128)
+ * for the key-range partials, merged by a second (programmatic dependent)
+ * launch.
+ * Replaces the attention of the speculative verify forward
+ * (agentrl/generation/speculative.py:229-264, rows prefix_len-1 ..
+ * prefix_len-1+k).  Requires block_size 16, head_dim 128, bf16 or f16, at most
+ * 32 query heads per KV head. */
+int32_t pkv_verify_attention(const pkv_pool_geom* g, const void* pool, int32_t layer, const void* q,
+                             const int32_t* block_tables, int32_t table_stride, int32_t table_rows,
+                             const int32_t* work_items, int32_t n_items, int32_t n_ctas, int32_t n_combine,
+                             int64_t total_q, int32_t num_q_heads, float scale, void* out, int32_t* error_word,
+                             void* workspace, int64_t workspace_bytes, int64_t n_slots, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Native decode-step runtime                                                */
 /* ------------------------------------------------------------------------ */

@@ -156,6 +156,16 @@ _SIGNATURES: dict[str, tuple] = {
         [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32,
          c_int64, c_int32, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
     ),
+    "pkv_verify_positions_per_item": (c_int32, [c_int32, c_int32]),
+    "pkv_verify_plan": (
+        c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, I64P, I64P,
+                  I64P, I64P]
+    ),
+    "pkv_verify_attention": (
+        c_int32,
+        [POINTER(PoolGeom), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32,
+         c_int32, c_int64, c_int32, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
+    ),
     "pkv_stepper_create": (c_void_p, [c_void_p, POINTER(PoolGeom), c_void_p, I32P]),
     "pkv_stepper_destroy": (None, [c_void_p]),
     "pkv_stepper_bind_tables": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),

@@ -43,6 +43,7 @@
 // MMAs and the producer for its copies before tensor memory is freed.
 #include "pkv_device.cuh"
 #include "pkv_error.h"
+#include "pkv_prefill.cuh"
 
 #include <algorithm>
 #include <string>
@@ -52,17 +53,11 @@
 namespace pkv {
 namespace {
 
-constexpr int kRows = 128;             // rows of one query tile (M)
-constexpr int kKeys = 128;             // keys per KV tile (N of S, K of P.V)
-constexpr int kPageRows = 16;          // block_size
-constexpr int kPagesPerTile = kKeys / kPageRows;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 320;
 constexpr int kTileThreads = 128;      // softmax threads per query tile
 constexpr int kTmemCols = 512;         // S_A, S_B (kKeys each), O_A, O_B (head_dim each)
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleLog2 = 8.f;    // keep a stale row maximum while the new one exceeds it by <= 2^8
 #ifndef PKV_PREFILL_POLY_PAIRS
 #define PKV_PREFILL_POLY_PAIRS 0       // of every 8 probability pairs, those whose 2^x runs on the FMA pipes
 #endif
@@ -83,36 +78,6 @@ struct PCfg {
   static constexpr uint32_t kPageSlabBytes = kPageRows * 128;
 };
 
-// Work item (two int4): {table row, position of the item's first query, index
-// of that query in the packed q, kv_head << 16 | positions in the item} and
-// {first KV tile, one past the last KV tile (0: all of them), partial slot
-// (-1: write the output), 0}.  The first `ppi` positions form query tile A,
-// the rest tile B.  An item with a key range or a partial slot has one query
-// tile; it writes its unnormalised (m, l, O) into the workspace slot, and a
-// combine entry {first slot, slots, query index, kv_head << 16 | positions}
-// merges the slots of one query tile.
-struct PrefillParams {
-  const void* q;    // [total_q][hq][D]
-  void* out;        // [total_q][hq][D]
-  const char* pool;
-  const int32_t* tables;
-  const int4* items;
-  int32_t* error;
-  float* partials;  // n_slots x (m[128], l[128], O[128][D]) fp32
-  int32_t n_slots;
-  int64_t total_q;
-  int32_t n_items;
-  int32_t table_stride;
-  int32_t table_rows;
-  int32_t hq;
-  int32_t hkv;
-  int32_t group;
-  int32_t ppi;      // positions per query tile: kRows / group
-  int32_t layer;
-  int32_t num_blocks;
-  float scale_log2;
-};
-
 template <int NK, int NV>
 struct Bars {
   uint64_t q_full[2];    // 128 Q-writer arrivals per query tile
@@ -127,20 +92,6 @@ struct Bars {
   uint32_t tmem_base;
   int32_t abort;
 };
-
-__device__ __forceinline__ void record_error(const PrefillParams& p, volatile int32_t* abort, int32_t code) {
-  *abort = 1;
-  atomicExch(p.error, code);
-}
-
-// Bounded wait unless the CTA already gave up.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const PrefillParams& p,
-                                              volatile int32_t* abort) {
-  if (*abort) return false;
-  if (mbar_wait_bounded(bar, parity)) return true;
-  record_error(p, abort, kDevWaitTimeout);
-  return false;
-}
 
 template <int D, typename T, int kPoly>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid_constant__ PrefillParams p) {
@@ -563,50 +514,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(const __grid
   }
 }
 
-// Merge the key-range partials of one query tile: per row, m = max m_s,
-// O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s, written in the output dtype.
-// One block per combine entry, one thread per tile row.
-template <int D, typename T>
-__global__ void __launch_bounds__(kRows) paged_prefill_combine_kernel(const __grid_constant__ PrefillParams p,
-                                                                     const int4* entries) {
-  const int4 e = entries[2 * blockIdx.x];  // records are two int4 apart
-  const int slot0 = e.x, ns = e.y, qrow0 = e.z, h = e.w >> 16, nt = e.w & 0xffff;
-  const int r = threadIdx.x;
-  const int group = p.group;
-  if (slot0 < 0 || ns < 1 || slot0 + ns > p.n_slots || nt < 1 || nt * group > kRows || qrow0 < 0 ||
-      (int64_t)qrow0 + nt > p.total_q || h < 0 || h >= p.hkv) {
-    if (r == 0) atomicExch(p.error, kDevBadItem);
-    return;
-  }
-  if (r >= nt * group) return;
-  constexpr int kSlotFloats = 2 * kRows + kRows * D;
-  const float* base = p.partials + (int64_t)slot0 * kSlotFloats;
-  float m = -INFINITY;
-  for (int s = 0; s < ns; ++s) m = fmaxf(m, base[(int64_t)s * kSlotFloats + r]);
-  float l = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float ms = base[(int64_t)s * kSlotFloats + r];
-    l += ms == -INFINITY ? 0.f : ex2_approx(ms - m) * base[(int64_t)s * kSlotFloats + kRows + r];
-  }
-  const float inv_l = 1.f / l;
-  T* dst = static_cast<T*>(p.out) + (((int64_t)qrow0 + r / group) * p.hq + (int64_t)h * group + r % group) * D;
-#pragma unroll 1
-  for (int d = 0; d < D; d += 8) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < ns; ++s) {
-      const float* ps = base + (int64_t)s * kSlotFloats;
-      const float ms = ps[r];
-      const float w = ms == -INFINITY ? 0.f : ex2_approx(ms - m) * inv_l;
-      const float4 a = *reinterpret_cast<const float4*>(ps + 2 * kRows + (int64_t)r * D + d);
-      const float4 b = *reinterpret_cast<const float4*>(ps + 2 * kRows + (int64_t)r * D + d + 4);
-      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
-      acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
-    }
-    *reinterpret_cast<uint4*>(dst + d) = make_uint4(MmaOp<T>::pack(acc[0], acc[1]), MmaOp<T>::pack(acc[2], acc[3]),
-                                                    MmaOp<T>::pack(acc[4], acc[5]), MmaOp<T>::pack(acc[6], acc[7]));
-  }
-}
-
 template <int D, typename T>
 cudaError_t launch_prefill(const PrefillParams& prm, int32_t n_combine, cudaStream_t stream) {
   using C = PCfg<D>;
@@ -794,6 +701,7 @@ extern "C" int32_t pkv_prefill_attention(const pkv_pool_geom* g, const void* poo
   prm.layer = layer;
   prm.num_blocks = static_cast<int32_t>(g->num_blocks);
   prm.scale_log2 = scale * kLog2e;
+  prm.n_combine = n_combine;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
   if (g->head_dim == 128)

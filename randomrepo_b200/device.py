@@ -222,7 +222,8 @@ class KVPool:
 
     def prefill(self, layer: int, q: torch.Tensor, plan: "PrefillPlan", records: torch.Tensor, num_q_heads: int,
                 scale: float, out: torch.Tensor) -> None:
-        """Launch paged prefill / verify attention (``pkv_prefill_attention``) on the current stream.
+        """Launch paged prefill / verify attention on the current stream: ``pkv_prefill_attention``
+        for a ``plan_prefill`` plan, ``pkv_verify_attention`` for a ``plan_verify`` one.
 
         ``records`` is the device copy of ``plan.records``; key-range partials
         go to a workspace the pool keeps (grown on demand, never shrunk).
@@ -231,11 +232,15 @@ class KVPool:
         if need > self._prefill_ws.numel():
             self._prefill_ws = torch.empty(_round_up(need, 1 << 20), dtype=torch.uint8, device=self.device)
         rows, cols = self.tables.shape
-        st = lib.pkv_prefill_attention(self._geom_ref, self.pool.data_ptr(), int(layer), q.data_ptr(),
-                                       self.tables.data_ptr(), cols, rows, records.data_ptr(), plan.n_items,
-                                       plan.n_combine, q.shape[0], int(num_q_heads), float(scale), out.data_ptr(),
-                                       self.prefill_error.data_ptr(), self._prefill_ws.data_ptr(),
-                                       self._prefill_ws.numel(), plan.n_slots, _stream_ptr())
+        head = (self._geom_ref, self.pool.data_ptr(), int(layer), q.data_ptr(), self.tables.data_ptr(), cols, rows,
+                records.data_ptr(), plan.n_items)
+        tail = (plan.n_combine, q.shape[0], int(num_q_heads), float(scale), out.data_ptr(),
+                self.prefill_error.data_ptr(), self._prefill_ws.data_ptr(), self._prefill_ws.numel(), plan.n_slots,
+                _stream_ptr())
+        if plan.kind == "verify":
+            st = lib.pkv_verify_attention(*head, plan.n_ctas, *tail)
+        else:
+            st = lib.pkv_prefill_attention(*head, *tail)
         _lib.raise_for_status(st)
         self.launches += 2 if plan.n_combine else 1
 
@@ -295,15 +300,20 @@ def plan_decode(lens: np.ndarray, num_kv_heads: int, num_sms: int,
 
 @dataclass
 class PrefillPlan:
-    """``pkv_prefill_plan`` output: int32 [n_items + n_combine, 8] records and their counts."""
+    """``pkv_prefill_plan`` / ``pkv_verify_plan`` output: int32 [n_items + n_combine, 8] records,
+    their counts, and which kernel they are for (``"prefill"`` or ``"verify"``)."""
 
     records: np.ndarray
     n_items: int
     n_combine: int
     n_slots: int
+    kind: str = "prefill"
+    n_ctas: int = 0  # verify: CTAs of the launch (each works through a list of items)
 
 
 PREFILL_SPLIT_WAVES = 0
+# Chunks of few queries (verify steps) go to pkv_verify_attention where it supports the shape.
+VERIFY_KERNEL = True
 
 
 def plan_prefill(rows: np.ndarray, past_lens: np.ndarray, q_lens: np.ndarray, num_q_heads: int,
@@ -329,3 +339,32 @@ def plan_prefill(rows: np.ndarray, past_lens: np.ndarray, q_lens: np.ndarray, nu
     _lib.raise_for_status(lib.pkv_prefill_plan(*args, records.ctypes.data, records.shape[0], ctypes.byref(n),
                                                ctypes.byref(nc), ctypes.byref(ns)))
     return PrefillPlan(records, int(n.value), int(nc.value), int(ns.value))
+
+
+def verify_supported(num_q_heads: int, num_kv_heads: int, head_dim: int, block_size: int, q_len: int) -> bool:
+    """Whether ``pkv_verify_attention`` takes chunks of ``q_len`` queries in one item per KV head."""
+    ppv = int(lib.pkv_verify_positions_per_item(int(num_q_heads), int(num_kv_heads)))
+    return head_dim == 128 and block_size == 16 and 0 < q_len <= ppv
+
+
+def plan_verify(rows: np.ndarray, past_lens: np.ndarray, q_lens: np.ndarray, num_q_heads: int,
+                num_kv_heads: int, num_sms: int = 0) -> PrefillPlan:
+    """Plan one ``pkv_verify_attention`` launch (``pkv_verify_plan``).
+
+    With ``num_sms`` > 0 the launch is a persistent grid of one CTA per SM,
+    each working through a list of items (long key ranges cut, partials merged
+    by combine entries); 0 gives one CTA per item and no combine entries.
+    """
+    rows = np.ascontiguousarray(rows, dtype=np.int32)
+    past_lens = np.ascontiguousarray(past_lens, dtype=np.int32)
+    q_lens = np.ascontiguousarray(q_lens, dtype=np.int32)
+    if not rows.size == past_lens.size == q_lens.size:
+        raise ValueError("rows, past_lens and q_lens must have one entry per sequence")
+    n, nb, nc, ns = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    args = (rows.ctypes.data, past_lens.ctypes.data, q_lens.ctypes.data, rows.size, num_q_heads, num_kv_heads,
+            int(num_sms))
+    counts = (ctypes.byref(n), ctypes.byref(nb), ctypes.byref(nc), ctypes.byref(ns))
+    _lib.raise_for_status(lib.pkv_verify_plan(*args, None, 0, *counts))
+    records = np.empty((n.value + nc.value, 8), dtype=np.int32)
+    _lib.raise_for_status(lib.pkv_verify_plan(*args, records.ctypes.data, records.shape[0], *counts))
+    return PrefillPlan(records, int(n.value), int(nc.value), int(ns.value), "verify", int(nb.value))

@@ -29,7 +29,8 @@ import torch
 
 from . import _lib
 from ._lib import lib
-from .device import KVPool, PrefillPlan, plan_prefill
+from . import device as _device
+from .device import KVPool, PrefillPlan, plan_prefill, plan_verify, verify_supported
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -811,7 +812,13 @@ class PagedKVCacheStore:
                                                             fill.ctypes.data, fill.size))
         if total_q == 0:
             return PrefillStep(ids, q_lens, hq, 0, None, None, None)
-        plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
+        if _device.VERIFY_KERNEL and verify_supported(hq, pool.num_kv_heads, pool.head_dim, pool.block_size,
+                                                      int(q_lens.max())):
+            # Short chunks (a verify step): the kernel with keys on the tensor-core rows.  A
+            # recorded launch (buffers) needs a fixed record count: no key-range split.
+            plan = plan_verify(rows, past, q_lens, hq, pool.num_kv_heads, 0 if buffers is not None else pool.num_sms)
+        else:
+            plan = plan_prefill(rows, past, q_lens, hq, pool.num_kv_heads, pool.num_sms)
         with _on_device(pool.device):
             if buffers is None:
                 slots_d = pool.h2d.to_device(torch.from_numpy(slots), pool.device)
