@@ -492,6 +492,7 @@ def summarize(result: dict) -> dict:
         "host_us_per_step": get("host_us_per_step"),
         "prefill_tensor_frac": get("tensor_tiles", "prefill", "roofline", "frac"),
         "verify_hbm_frac": get("tensor_tiles", "verify", "roofline", "frac"),
+        "verify_long_hbm_frac": get("tensor_tiles", "verify_long", "roofline", "frac"),
         "logprobs_hbm_frac": get("vocab_rows", "token_logprobs", "roofline", "frac"),
         "rollout_tokens_per_s": get("rollout", "tokens_per_s"),
         "speculative_tokens_per_s": get("speculative", "tokens_per_s"),
@@ -505,6 +506,8 @@ def summarize(result: dict) -> dict:
 
 PREFILL_SHAPE = {"model": "Qwen2.5-7B attention", "hq": 28, "hkv": 4, "d": 128, "prompts": 32, "len_lo": 256,
                  "len_hi": 4096, "chunk": 512}
+VERIFY_LONG_SHAPE = {"model": "Qwen2.5-1.5B target attention", "hq": 12, "hkv": 2, "d": 128, "seqs": 32,
+                     "prefix_lo": 4096, "prefix_hi": 16384, "k": 4}
 VERIFY_SHAPE = {"model": "Qwen2.5-1.5B target attention", "hq": 12, "hkv": 2, "d": 128, "seqs": 64, "prefix_lo": 128,
                 "prefix_hi": 1280, "k": 4}
 
@@ -576,6 +579,38 @@ def _time_prefill(store, q, plan, records, steps: int, warmup: int) -> tuple[flo
     return statistics.mean(times), pool.launch_count() - launches0
 
 
+def _verify_line(device: torch.device, vs: dict, rng, seed: int, steps: int, warmup: int, hbm: float,
+                 hbm_kind: str, name: str) -> dict:
+    """One verify launch shape on the verify kernel, with the 128-query-row prefill kernel timed
+    on the same launch for comparison."""
+    pre = rng.integers(vs["prefix_lo"], vs["prefix_hi"] + 1, size=vs["seqs"])
+    seqs = [(int(p) + vs["k"], [(int(p) - 1, vs["k"] + 1)]) for p in pre]
+    store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2)
+    ms_rows, _ = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
+    del store, q, records
+    store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2,
+                                                              verify=True)
+    ms, launches = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    line = {
+        "workload": f"speculative-verify attention, 1 layer, {vs['model']} ({vs['hq']}q/{vs['hkv']}kv heads, "
+                    f"head_dim {vs['d']}), {vs['seqs']} sequences with prefix U[{vs['prefix_lo']},"
+                    f"{vs['prefix_hi']}], k={vs['k']} drafts: {vs['k'] + 1} causal queries each, bf16, seed {seed}",
+        "ms": ms, "work_items": plan.n_items, "ctas": plan.n_ctas, "combine_entries": plan.n_combine,
+        "gpu_launches": launches,
+        "tokens_per_s": vs["seqs"] * (vs["k"] + 1) / (ms * 1e-3),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{hbm_kind} hbm_gbs", "traffic": tiles_traffic(name), "bytes_per_launch": kv_bytes,
+                     "bytes_rule": "K and V of prefix + k tokens per sequence and KV head"},
+        "tflops": flops / (ms * 1e-3) / 1e12,
+        "kernel": "pkv_verify_attention (keys on the tensor-core rows) + combine",
+        "prefill_kernel_ms": ms_rows,
+    }
+    del store, q, records
+    torch.cuda.empty_cache()
+    return line
+
+
 def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -> dict:
     """The tcgen05 chunked-prefill and speculative-verify attention kernels on their own workloads."""
     hbm, hbm_kind = measured_peaks()
@@ -600,32 +635,8 @@ def run_tensor_tiles(device: torch.device, seed: int, steps: int, warmup: int) -
         "kv_gb_per_launch": kv_bytes / 1e9,
     }
     del store, q, records
-    vs = VERIFY_SHAPE
-    pre = rng.integers(vs["prefix_lo"], vs["prefix_hi"] + 1, size=vs["seqs"])
-    seqs = [(int(p) + vs["k"], [(int(p) - 1, vs["k"] + 1)]) for p in pre]
-    # The same launch on the 128-query-row prefill kernel, for comparison.
-    store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2)
-    ms_rows, _ = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
-    del store, q, records
-    store, q, plan, records, flops, kv_bytes = _tile_workload(device, vs["hq"], vs["hkv"], vs["d"], seqs, seed + 2,
-                                                              verify=True)
-    ms, launches = _time_prefill(store, q, plan, records, max(10, steps // 5), warmup)
-    achieved = kv_bytes / (ms * 1e-3) / 1e9
-    res["verify"] = {
-        "workload": f"speculative-verify attention, 1 layer, {vs['model']} ({vs['hq']}q/{vs['hkv']}kv heads, "
-                    f"head_dim {vs['d']}), {vs['seqs']} sequences with prefix U[{vs['prefix_lo']},"
-                    f"{vs['prefix_hi']}], k={vs['k']} drafts: {vs['k'] + 1} causal queries each, bf16, seed {seed}",
-        "ms": ms, "work_items": plan.n_items, "combine_entries": plan.n_combine, "gpu_launches": launches,
-        "tokens_per_s": vs["seqs"] * (vs["k"] + 1) / (ms * 1e-3),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": f"{hbm_kind} hbm_gbs", "traffic": tiles_traffic("verify"), "bytes_per_launch": kv_bytes,
-                     "bytes_rule": "K and V of prefix + k tokens per sequence and KV head"},
-        "tflops": flops / (ms * 1e-3) / 1e12,
-        "kernel": "pkv_verify_attention (keys on the tensor-core rows) + combine",
-        "prefill_kernel_ms": ms_rows,
-    }
-    del store, q, records
-    torch.cuda.empty_cache()
+    for name, vs in (("verify", VERIFY_SHAPE), ("verify_long", VERIFY_LONG_SHAPE)):
+        res[name] = _verify_line(device, vs, rng, seed, steps, warmup, hbm, hbm_kind, name)
     return res
 
 

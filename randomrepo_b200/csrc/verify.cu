@@ -17,19 +17,25 @@
 // G + head of the item's queries; an item holds 32 / G positions of one
 // sequence and KV head, over a range of its KV tiles.
 //
-// Roles (192 threads, two CTAs per SM: 107 KB of shared memory and 128
-// tensor-memory columns each):
+// The grid is persistent: one CTA per SM (192 threads, 225 KB of shared
+// memory, 128 tensor-memory columns) works through a list of items the host
+// plan balanced across the SMs (record c is CTA c's first item; the rest are
+// copied into shared memory once).  Barrier phases count the CTA's KV tiles
+// g across items.  Roles:
 //   warps 0-3  softmax, thread = key of the tile (its tensor-memory lane): a
-//              32-column tcgen05.ld of S^T, column maxima over the 128 keys (a
-//              shuffle transpose-reduction in each warp, four partials through
-//              shared memory at a barrier), a lazily kept running maximum per
-//              column (O^T rescaled in tensor memory only when a maximum grows by
-//              more than 2^8), P^T stored as the key's 64-byte row; in the
-//              epilogue thread = head_dim row of O^T;
+//              32-column tcgen05.ld of S^T; on an item's first tile the exact
+//              column maxima over the 128 keys (a shuffle transpose-reduction
+//              in each warp, four partials through shared memory at a
+//              barrier), on later tiles only a test whether some logit exceeds
+//              its column's running maximum by more than 2^8 (then the exact
+//              maxima, and O^T rescaled in tensor memory); P^T stored as the
+//              key's 64-byte row; query columns of the items two ahead copied
+//              with cp.async; in the epilogue thread = head_dim row of O^T,
+//              the output staged through shared memory as 16-byte stores;
 //   warp 4     producer, lanes 0-15 for K and 16-31 for V on their own: 2 KB
-//              cp.async.bulk copies of every page's slabs into one-tile K and V
-//              buffers (no tensor map, no multicast), the next tile's block ids
-//              read before the wait for the buffer;
+//              cp.async.bulk copies of every page's slabs into a 3-stage K
+//              and a 2-stage V ring (no tensor map, no multicast), the next
+//              tile's block ids read before the wait for a free stage;
 //   warp 5     allocates tensor memory (S^T double-buffered, O^T); lane 0
 //              issues the next S and the next P V, each as soon as its
 //              operands are in.
@@ -71,6 +77,7 @@ constexpr int kNQ = 3;                   // query buffers: item i in buffer i % 
 constexpr int kPBytes = kKeys * 128;     // P^T of one tile: 128 key rows of 128 bytes (64 used)
 constexpr int kMaxList = 128;            // work items one CTA holds in shared memory
 constexpr int64_t kItemCost = 2;         // fixed work of one item, in KV tiles (plan balance)
+constexpr int64_t kCombineCost = 5;      // the combine launch, in KV tiles (plan: cut or not)
 constexpr int kOffQ = 0;
 constexpr int kOffP = kOffQ + kNQ * kQBytes;       // two buffers, tiles alternate
 constexpr int kOffK = kOffP + 2 * kPBytes;
@@ -817,10 +824,13 @@ extern "C" int32_t pkv_verify_plan(const int32_t* rows, const int32_t* past_lens
   // num_sms > 0: a persistent grid of one CTA per SM, each working through a
   // list of items.  An item costs its KV tiles plus kItemCost tiles' worth of
   // fixed work (its first tile's exact maxima, its epilogue, the hand-over to
-  // the next item).  Items costing more than an SM's share are cut into key
+  // the next item); the items go, costliest first, to the CTA with the least
+  // cost so far.  Two candidate item sets are balanced this way: the items as
+  // they are, and the items costing more than an SM's share cut into key
   // ranges (at least two tiles each; each writes a partial, merged by a
-  // combine entry), then the items go, costliest first, to the CTA with the
-  // least cost so far.  num_sms = 0: one CTA per item.
+  // combine entry in a second launch that costs about kCombineCost tiles).
+  // The cut is kept only when its balanced makespan plus that is the
+  // smaller.  num_sms = 0: one CTA per item, no cut.
   std::vector<Entry> items, combine;
   int32_t n_slots = 0;
   const int64_t cost_total = total + kItemCost * (int64_t)base.size();
@@ -847,7 +857,29 @@ extern "C" int32_t pkv_verify_plan(const int32_t* rows, const int32_t* past_lens
     combine.push_back({0, {n_slots, static_cast<int32_t>(ns), e.v[2], e.v[3], 0, 0, 0, 0}});
     n_slots += static_cast<int32_t>(ns);
   }
-  std::stable_sort(items.begin(), items.end(), [](const Entry& a, const Entry& b) { return a.work > b.work; });
+  auto by_work = [](const Entry& a, const Entry& b) { return a.work > b.work; };
+  if (!combine.empty()) {
+    // Makespan (in tiles) of the costliest-first balance over num_sms CTAs.
+    auto makespan = [&](std::vector<Entry> its) {
+      std::stable_sort(its.begin(), its.end(), by_work);
+      std::priority_queue<int64_t, std::vector<int64_t>, std::greater<int64_t>> loads;
+      for (int64_t c = 0; c < std::min<int64_t>(num_sms, (int64_t)its.size()); ++c) loads.push(0);
+      int64_t worst = 0;
+      for (const Entry& e : its) {
+        const int64_t l = loads.top() + e.work + kItemCost;
+        loads.pop();
+        loads.push(l);
+        worst = std::max(worst, l);
+      }
+      return worst;
+    };
+    if (makespan(items) + kCombineCost >= makespan(base)) {
+      items = base;
+      combine.clear();
+      n_slots = 0;
+    }
+  }
+  std::stable_sort(items.begin(), items.end(), by_work);
   const int64_t n_items = static_cast<int64_t>(items.size());
   if (n_items >= (int64_t(1) << 23)) {
     pkv_set_error("too many verify work items in one launch");

@@ -126,24 +126,36 @@ def _work(rec):
     return ((rng_ >> 16) - (rng_ & 0xFFFF)) if slot >= 0 else -(-(pos0 + (hw & 0xFFFF)) // 128)
 
 
-def test_verify_plan_balances_the_bench_shape():
-    """64 sequences, prefix U[128, 1280], k = 4 at 12/2 heads on 148 SMs: one CTA per SM, and no
-    CTA's cost (its KV tiles plus 2 per item) more than one item above the average (costliest first
-    to the least loaded)."""
+def _costs(plan):
+    items = plan.records[:plan.n_items].tolist()
+    return items, [sum(_work(items[k]) + 2 for k in chain) for chain in _verify_lists(plan)]
+
+
+def test_verify_plan_keeps_short_items_whole():
+    """64 sequences, prefix U[128, 1280], k = 4 at 12/2 heads on 148 SMs: 128 items already balance
+    better than cut ranges would with their combine launch, so each item gets a CTA of its own."""
     from randomrepo_b200.device import plan_verify
 
     rng = np.random.default_rng(0)
     pre = rng.integers(128, 1281, size=64)
     plan = plan_verify(np.arange(64), pre - 1, np.full(64, 5), 12, 2, num_sms=148)
-    assert plan.n_ctas == 148
-    items = plan.records[:plan.n_items].tolist()
-    lists = _verify_lists(plan)
-    loads = [sum(_work(items[k]) + 2 for k in chain) for chain in lists]
+    assert plan.n_combine == 0 and plan.n_slots == 0 and plan.n_items == plan.n_ctas == 128
+
+
+@pytest.mark.parametrize("lo,hi,n", [(2048, 8192, 64), (4096, 16384, 32), (128, 1280, 16)])
+def test_verify_plan_cuts_long_or_few_items(lo, hi, n):
+    """Long prefixes (or few sequences): key ranges are cut, one CTA per SM (or per item), and no
+    CTA's cost (its KV tiles plus 2 per item) is more than one item above the average."""
+    from randomrepo_b200.device import plan_verify
+
+    pre = np.random.default_rng(3).integers(lo, hi + 1, size=n)
+    plan = plan_verify(np.arange(n), pre - 1, np.full(n, 5), 12, 2, num_sms=148)
+    assert plan.n_combine > 0 and plan.n_ctas == min(148, plan.n_items)
+    items, loads = _costs(plan)
     total = sum(_work(r) + 2 for r in items)
     assert total == sum(loads)
-    assert max(loads) <= -(-total // 148) + max(_work(r) + 2 for r in items)
-    # each CTA's list runs longest item first
-    for chain in lists:
+    assert max(loads) <= -(-total // plan.n_ctas) + max(_work(r) + 2 for r in items)
+    for chain in _verify_lists(plan):  # each CTA's list runs longest item first
         works = [_work(items[k]) for k in chain]
         assert works == sorted(works, reverse=True)
 
