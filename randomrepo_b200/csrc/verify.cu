@@ -33,8 +33,8 @@
 //              with cp.async; in the epilogue thread = head_dim row of O^T,
 //              the output staged through shared memory as 16-byte stores;
 //   warp 4     producer, lanes 0-15 for K and 16-31 for V on their own: 2 KB
-//              cp.async.bulk copies of every page's slabs into a 3-stage K
-//              and a 2-stage V ring (no tensor map, no multicast), the next
+//              cp.async.bulk copies of every page's slabs into a 2-stage K
+//              and a 3-stage V ring (no tensor map, no multicast), the next
 //              tile's block ids read before the wait for a free stage;
 //   warp 5     allocates tensor memory (S^T double-buffered, O^T); lane 0
 //              issues the next S and the next P V, each as soon as its
@@ -67,8 +67,8 @@ constexpr int kSoftThreads = 128;
 constexpr int kVProducerWarp = 4;
 constexpr int kVMmaWarp = 5;
 constexpr int kVTmemCols = 128;          // S^T buffers at columns 0 and 32, O^T at 64
-constexpr int kNK = 3;                   // K ring stages (one KV tile each)
-constexpr int kNV = 2;                   // V ring stages
+constexpr int kNK = 2;                   // K ring stages (one KV tile each)
+constexpr int kNV = 3;                   // V ring stages: V(g) waits for P V(g - 3), K(g) only for S(g - 2)
 constexpr int kVSlabBytes = kKeys * 128; // one 64-dim slab of a KV tile
 constexpr int kVTileBytes = 2 * kVSlabBytes;
 constexpr int kQSlab = kCols * 128;      // one 64-dim slab of the query columns
