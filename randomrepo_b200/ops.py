@@ -25,6 +25,10 @@ head_dim, dtype code]`` (the ``pkv_pool_geom`` of the C ABI).
   chunks after a cached past over a ``pkv_prefill_plan`` -- chunked prefill
   (prefill.py:96-104) and the k+1-row speculative verify read
   (speculative.py:229-264).
+* ``verify_attention(...) -> out [T, Hq, D]``: the same read for short chunks
+  (a verify step) over a ``pkv_verify_plan``, on the kernel that puts keys on
+  the tensor-core rows (``PagedKVCacheStore.prefill_step`` picks it when the
+  chunks fit).
 """
 
 from __future__ import annotations
@@ -173,4 +177,29 @@ def prefill_attention(pool: torch.Tensor, geom: list[int], layer: int, q: torch.
 
 @prefill_attention.register_fake
 def _(pool, geom, layer, q, block_tables, work_items, n_items, n_combine, n_slots, scale, error_word, workspace):
+    return torch.empty_like(q)
+
+
+@torch.library.custom_op("pkv::verify_attention", mutates_args=("error_word", "workspace"), device_types="cuda")
+def verify_attention(pool: torch.Tensor, geom: list[int], layer: int, q: torch.Tensor, block_tables: torch.Tensor,
+                     work_items: torch.Tensor, n_items: int, n_ctas: int, n_combine: int, n_slots: int, scale: float,
+                     error_word: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+    """``pkv_verify_attention``: q ``[T, Hq, D]``; work_items the int32 records of ``pkv_verify_plan``
+    ``[n_items + n_combine, 8]`` and its CTA count; workspace ``pkv_prefill_workspace_bytes(n_slots, 128)``
+    bytes (may be empty when n_slots is 0); error_word an int32 device scalar."""
+    _need(q.dim() == 3 and q.is_contiguous(), "q must be a contiguous [T, Hq, D] tensor")
+    g = _geom(geom)
+    out = torch.empty_like(q)
+    _check(lib.pkv_verify_attention(ctypes.byref(g), pool.data_ptr(), int(layer), q.data_ptr(),
+                                    block_tables.data_ptr(), block_tables.shape[1], block_tables.shape[0],
+                                    work_items.data_ptr(), int(n_items), int(n_ctas), int(n_combine), q.shape[0],
+                                    q.shape[1], float(scale), out.data_ptr(), error_word.data_ptr(),
+                                    workspace.data_ptr() if workspace.numel() else None,
+                                    workspace.numel() * workspace.element_size(), int(n_slots), _stream(q)))
+    return out
+
+
+@verify_attention.register_fake
+def _(pool, geom, layer, q, block_tables, work_items, n_items, n_ctas, n_combine, n_slots, scale, error_word,
+      workspace):
     return torch.empty_like(q)

@@ -118,3 +118,34 @@ def test_prefill_attention_op_equals_the_store_path(cuda_device):
                                           plan.n_combine, plan.n_slots, 128 ** -0.5, err, ws)
     torch.cuda.synchronize()
     assert torch.equal(got, want) and int(err.item()) == 0 and pool.prefill_error_flag() == 0
+
+
+@pytest.mark.parametrize("lengths", [[130, 300, 1000], [5000, 9000, 300, 17]])
+def test_verify_attention_op_equals_the_store_path(cuda_device, lengths):
+    """The verify kernel through the operator: whole items, and long prefixes whose key ranges are
+    cut and merged (workspace partials and the combine launch)."""
+    from randomrepo_b200._lib import lib
+    from randomrepo_b200.device import plan_verify
+    from randomrepo_b200.ops import pool_geom
+
+    store, _ = _store(cuda_device, lengths, seed=7)
+    pool = store.pool
+    store._sync()
+    n = len(lengths)
+    rows = np.array([store.allocator.row(s) for s in range(n)])
+    past = np.array([m - 5 for m in lengths])
+    qls = np.full(n, 5)
+    plan = plan_verify(rows, past, qls, 12, 2, pool.num_sms)
+    assert (plan.n_combine > 0) == (max(lengths) > 2000)
+    records = torch.from_numpy(plan.records).to(cuda_device)
+    q = torch.randn((5 * n, 12, 128), generator=torch.Generator().manual_seed(8)).to(torch.bfloat16).to(cuda_device)
+    want = torch.empty_like(q)
+    pool.prefill(0, q, plan, records, 12, 128 ** -0.5, want)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ws = torch.empty(max(1, int(lib.pkv_prefill_workspace_bytes(plan.n_slots, 128))), dtype=torch.uint8,
+                     device=cuda_device)
+    got = torch.ops.pkv.verify_attention(pool.pool, pool_geom(pool), 0, q, pool.tables, records, plan.n_items,
+                                         plan.n_ctas, plan.n_combine, plan.n_slots, 128 ** -0.5, err, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and int(err.item()) == 0 and pool.prefill_error_flag() == 0
+

@@ -10,7 +10,8 @@ import randomrepo_b200.ops  # noqa: F401 - registers the operators
 
 
 def test_operators_are_registered():
-    for name in ("kv_append", "kv_gather", "copy_blocks", "decode_attention", "prefill_attention"):
+    for name in ("kv_append", "kv_gather", "copy_blocks", "decode_attention", "prefill_attention",
+                 "verify_attention"):
         assert hasattr(torch.ops.pkv, name)
 
 
@@ -33,6 +34,10 @@ def test_fake_tensor_shapes():
                                                                         device=dev),
                                             i32(8, 4), i32(3, 8), 3, 0, 0, 0.088, i32(1), pool)
         assert o.shape == (40, 12, 128)
+        o = torch.ops.pkv.verify_attention(pool, geom, 0, torch.empty((15, 12, 128), dtype=torch.bfloat16,
+                                                                       device=dev),
+                                           i32(8, 4), i32(6, 8), 6, 6, 0, 0, 0.088, i32(1), pool)
+        assert o.shape == (15, 12, 128) and o.dtype == torch.bfloat16
     assert mode is not None
 
 
