@@ -1,8 +1,9 @@
 // Pieces shared by the two paged attention kernels for query chunks: the
 // chunked-prefill kernel (prefill.cu, queries on the tensor-core rows) and the
-// speculative-verify kernel (verify.cu, keys on the rows).  Both take the same
-// work-item records and write key-range partials in the same format, merged by
-// paged_prefill_combine_kernel.
+// speculative-verify kernel (verify.cu, keys on the rows).  Both take their
+// launch parameters in PrefillParams and write key-range partials in the same
+// slot format; the records below are the prefill kernel's (verify.cu
+// documents its own, which add per-CTA item lists).
 #pragma once
 
 #include "pkv_device.cuh"
@@ -18,7 +19,7 @@ constexpr int kPagesPerTile = kKeys / kPageRows;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;    // keep a stale running maximum while the new one exceeds it by <= 2^8
 
-// Work item (two int4): {table row, position of the item's first query, index
+// Prefill work item (two int4): {table row, position of the item's first query, index
 // of that query in the packed q, kv_head << 16 | positions in the item} and
 // {first KV tile, one past the last KV tile (0: all of them), partial slot
 // (-1: write the output), 0}.  A combine entry (two int4) is {first slot,
